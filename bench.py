@@ -1,0 +1,415 @@
+"""Benchmark: VQ-MoE decode (and prefill) on B200 through the repo's own API.
+
+Workload ("one vq_switch MoE layer, decode"): hidden 4096,
+512 experts, expert intermediate 1024, top-10 softmax routing from router
+logits ~N(0,1), SwiGLU gate/up [1024 x 4096] and down [4096 x 1024], d=8,
+K=16384 (14-bit packed codes), one fp16 codebook per projection per layer,
+bf16 activations.  Seeded synthetic weights (codes uniform over K, codebook
+~N(0, 0.02), scales ~U(0.5, 1.5), G = 64) and inputs (x ~N(0,1)).
+
+A step is one MoE layer forward (router top-k, gate, up, SwiGLU, down,
+weighted combine) on the headline batch (64 tokens; 1 and 8 are reported
+beside it).  Several independently seeded layers are rotated so the
+weights a step reads are not in L2 from the previous step (the bytes each
+step touches, times the rotation, exceed the 126 MB L2).
+
+Multi-GPU (torchrun, one rank per GPU): each rank runs its own replica of
+the layer on its own tokens (weak scaling, no collective on the data path);
+`value` is all ranks' tokens over the max-over-ranks time.
+
+`--impl reference` times the reference's CPU path (the oracle port of the
+reference arithmetic, OpenMP over all host cores) on a bounded sample of the
+same workload.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import pathlib
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+ROOT = pathlib.Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+HIDDEN, INTER, E, TOPK, D, K, BITS, G = 4096, 1024, 512, 10, 8, 16384, 14, 64
+METRIC = "VQ-MoE decode tokens/s (one MoE layer, C2 shapes)"
+UNIT = "tokens/s"
+
+
+def _peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return float(d["hbm_gbs"]), float(d["bf16_tflops"]), "measured"
+    return 6650.0, 1590.0, "fallback"
+
+
+def _wpr(nsub):
+    return (nsub + 31) // 32 * BITS
+
+
+def proj_bytes(out, inn):
+    """Packed code + scale bytes of one expert's projection."""
+    return out * _wpr(inn // D) * 4 + out * (inn // G) * 2
+
+
+EXPERT_BYTES = {"gate": proj_bytes(INTER, HIDDEN), "up": proj_bytes(INTER, HIDDEN), "down": proj_bytes(HIDDEN, INTER)}
+CODEBOOK_BYTES = K * D * 2
+
+
+# ---------------------------------------------------------------- clocks
+
+class ClockSampler:
+    """nvidia-smi clocks + throttle reasons sampled every 200 ms during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.f = None
+
+    def __enter__(self):
+        try:
+            self.f = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=self.f, stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+        return self
+
+    def __exit__(self, *a):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+
+    def summary(self):
+        if self.proc is None or self.f is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.f.flush()
+        rows = [r.split(",") for r in pathlib.Path(self.f.name).read_text().splitlines() if r.strip()]
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for r in rows:
+            r = [c.strip() for c in r]
+            if len(r) < 9:
+                continue
+            try:
+                sm.append(float(r[1]))
+                mx = float(r[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, r[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# ------------------------------------------------------------------ GPU arm
+
+def make_layer(torch, dev, seed):
+    from vqlab_b200 import VQSwitchLinear
+    from vqlab_b200.moe import VQMoEBlock
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(seed)
+
+    def proj(out, inn):
+        # uniform random words ARE uniform 14-bit codes: K = 2^BITS and NSUB % 32 == 0
+        codes = torch.randint(-2 ** 31, 2 ** 31 - 1, (E, out, _wpr(inn // D)), dtype=torch.int32, device=dev,
+                              generator=gen)
+        cb = (torch.randn((K, D), device=dev, generator=gen) * 0.02).to(torch.float16)
+        sc = (torch.rand((E, out, inn // G), device=dev, generator=gen) + 0.5).to(torch.float16)
+        return VQSwitchLinear(codes, cb, sc, group_size=G, pack_bits=BITS, in_features=inn)
+
+    return VQMoEBlock(proj(INTER, HIDDEN), proj(INTER, HIDDEN), proj(HIDDEN, INTER), TOPK)
+
+
+def distinct_experts(torch, logits):
+    from vqlab_b200.moe import route
+    idx, _ = route(logits, TOPK)
+    return int(torch.unique(idx).numel())
+
+
+def layer_bytes(n_distinct, batch):
+    per_expert = sum(EXPERT_BYTES.values())
+    act = batch * HIDDEN * 2 * 2 + batch * TOPK * INTER * 2 * 3 + batch * TOPK * HIDDEN * 2
+    return n_distinct * per_expert + 3 * CODEBOOK_BYTES + act
+
+
+def time_graph_steps(torch, graphs, steps, warmup):
+    """Replay captured step graphs round-robin; device time of `steps` replays."""
+    s = torch.cuda.current_stream()
+    for i in range(warmup):
+        graphs[i % len(graphs)].replay()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(s)
+    for i in range(steps):
+        graphs[i % len(graphs)].replay()
+    e1.record(s)
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1) / 1e3
+
+
+def gpu_arm(args, rank, world, dev):
+    import torch
+    torch.cuda.set_device(dev)
+    peak_gbs, peak_tf, peak_kind = _peaks()
+    batches = sorted(set([args.batch] + [int(b) for b in args.extra_batches.split(",") if b]))
+    n_layers = args.layers
+    layers = [make_layer(torch, dev, 1000 * rank + l) for l in range(n_layers)]
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(7 + rank)
+    results = {}
+    launches_per_step = None
+    for B in batches:
+        xs = [torch.randn((B, HIDDEN), device=dev, generator=gen).to(torch.bfloat16) for _ in range(n_layers)]
+        lg = [torch.randn((B, E), device=dev, generator=gen) for _ in range(n_layers)]
+        outs = [None] * n_layers
+        # warm the allocator / library, then capture one graph per layer
+        for l in range(n_layers):
+            outs[l] = layers[l](xs[l], lg[l])
+        torch.cuda.synchronize()
+        graphs = []
+        for l in range(n_layers):
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g):
+                outs[l] = layers[l](xs[l], lg[l])
+            graphs.append(g)
+        torch.cuda.synchronize()
+        if world > 1:
+            torch.distributed.barrier()
+        torch.cuda.synchronize()
+        with ClockSampler(dev.index if dev.index is not None else 0) as clk:
+            secs = time_graph_steps(torch, graphs, args.steps, args.warmup)
+        if world > 1:
+            t = torch.tensor([secs], device=dev)
+            torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+            secs = float(t.item())
+        nd = [distinct_experts(torch, lg[l]) for l in range(n_layers)]
+        avg_bytes = statistics.mean(layer_bytes(n, B) for n in nd)
+        results[B] = {"secs": secs, "ms_per_step": secs * 1e3 / args.steps,
+                      "tokens_per_s": B * args.steps * world / secs,
+                      "hbm_gbs": avg_bytes * args.steps / secs / 1e9,
+                      "distinct_experts_mean": statistics.mean(nd), "clocks": clk.summary()}
+        del graphs
+        torch.cuda.synchronize()
+
+    # ---- dominant kernel: the expert decode launch (gate projection), timed alone
+    B = args.batch
+    m = layers[0]
+    x = torch.randn((B, 1, 1, HIDDEN), device=dev, generator=gen).to(torch.bfloat16)
+    lgt = torch.randn((B, E), device=dev, generator=gen)
+    from vqlab_b200.moe import route
+    idx, _ = route(lgt, TOPK)
+    nd = int(torch.unique(idx).numel())
+    projs = [layers[l].gate_proj for l in range(n_layers)]
+    for p in projs:
+        p(x, idx)
+    torch.cuda.synchronize()
+    s = torch.cuda.current_stream()
+    ev = []
+    reps = max(3, args.steps)
+    for i in range(reps):
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(s)
+        projs[i % n_layers](x, idx)
+        b.record(s)
+        ev.append((a, b))
+    torch.cuda.synchronize()
+    # the workspace memset shares the bracket; it is a 256-byte fill
+    dur = statistics.mean(a.elapsed_time(b) for a, b in ev) / 1e3
+    alg = nd * EXPERT_BYTES["gate"] + CODEBOOK_BYTES + B * HIDDEN * 2 + B * TOPK * INTER * 2
+    achieved = alg / dur / 1e9
+    roof = {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak_gbs, "unit": "GB/s",
+            "frac": round(achieved / peak_gbs, 4), "traffic": None,
+            "kernel": "vq_decode_kernel (gate projection, batch %d, %d distinct experts)" % (B, nd),
+            "peak_kind": peak_kind}
+
+    # ---- e2e through the public API with host buffers
+    e2e = None
+    if not args.skip_e2e:
+        xh = torch.randn((B, HIDDEN)).to(torch.bfloat16).pin_memory()
+        lh = torch.randn((B, E)).pin_memory()
+        yh = torch.empty((B, HIDDEN), dtype=torch.bfloat16).pin_memory()
+        for i in range(args.warmup):
+            layers[i % n_layers](xh.to(dev, non_blocking=True), lh.to(dev, non_blocking=True))
+        torch.cuda.synchronize()
+        if world > 1:
+            torch.distributed.barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(s)
+        for i in range(args.steps):
+            xd = xh.to(dev, non_blocking=True)
+            ld = lh.to(dev, non_blocking=True)
+            yd = layers[i % n_layers](xd, ld)
+            yh.copy_(yd, non_blocking=True)
+            s.synchronize()
+        e1.record(s)
+        torch.cuda.synchronize()
+        secs = e0.elapsed_time(e1) / 1e3
+        if world > 1:
+            t = torch.tensor([secs], device=dev)
+            torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+            secs = float(t.item())
+        e2e = {"value": round(B * args.steps * world / secs, 1), "unit": UNIT,
+               "h2d_bytes_per_step": B * HIDDEN * 2 + B * E * 4, "d2h_bytes_per_step": B * HIDDEN * 2,
+               "ms_per_step": round(secs * 1e3 / args.steps, 4)}
+    launches = 3  # per step: the 3 expert decode launches are ours (router/SwiGLU/combine are torch ops)
+    return results, roof, e2e, launches
+
+
+# ------------------------------------------------------------------ CPU arms
+
+def cpu_sample(tokens: int, seed: int = 11):
+    """Time the oracle port of the reference arithmetic on `tokens` tokens of
+    the C2 layer (router, gate/up walk decode, SwiGLU, down, combine) with all
+    host threads.  Weights are generated only for the experts those tokens
+    touch (same distributions as the GPU arm)."""
+    import numpy as np
+
+    from oracle import oracle as orc
+    rng = np.random.default_rng(seed)
+    x = rng.standard_normal((tokens, HIDDEN)).astype(np.float32)
+    lg = rng.standard_normal((tokens, E)).astype(np.float32)
+    idx, w = orc.router_topk(lg, TOPK)
+    used = np.unique(idx)
+    remap = np.zeros(E, dtype=np.uint32)
+    remap[used] = np.arange(used.size, dtype=np.uint32)
+    lidx = remap[idx].reshape(-1)
+    ne = used.size
+
+    def proj(out, inn):
+        words = rng.integers(0, 2 ** 32, (ne, out, _wpr(inn // D)), dtype=np.uint64).astype(np.uint32)
+        cb = (rng.standard_normal((K, D)) * 0.02).astype(np.float16).view(np.uint16)
+        sc = rng.uniform(0.5, 1.5, (ne, out, inn // G)).astype(np.float16).view(np.uint16)
+        return words, cb, sc
+
+    P = [proj(INTER, HIDDEN), proj(INTER, HIDDEN), proj(HIDDEN, INTER)]
+    xb = orc.round_bf16(x)
+
+    def run():
+        xh = orc.f16_bits(xb)
+        g = orc.switch_fused(P[0][0], P[0][1], P[0][2], xh, lidx, TOPK, packed_bits=BITS)
+        u = orc.switch_fused(P[1][0], P[1][1], P[1][2], xh, lidx, TOPK, packed_bits=BITS)
+        h = orc.swiglu_bf16(orc.round_bf16(orc.round_f16(g)), orc.round_bf16(orc.round_f16(u)))
+        dn = orc.switch_fused(P[2][0], P[2][1], P[2][2], orc.f16_bits(h), lidx, 1, packed_bits=BITS)
+        return orc.combine_bf16(orc.round_bf16(orc.round_f16(dn)).reshape(tokens, TOPK, HIDDEN), w)
+
+    run()
+    t0 = time.perf_counter()
+    run()
+    return time.perf_counter() - t0
+
+
+def cpu_baseline_block(tokens):
+    from oracle import oracle as orc
+    secs = cpu_sample(tokens)
+    return {"value": round(tokens / secs, 3), "unit": UNIT, "cores": orc.num_threads(), "kind": "port",
+            "sample": f"{tokens} token(s) of the C2 layer (10 pairs each x gate/up/down, walk-order decode of "
+                      f"packed 14-bit codes, SwiGLU, combine) on the oracle port, {secs:.2f} s"}
+
+
+def reference_arm(args, rank, world):
+    if rank != 0:
+        return 0
+    from oracle import oracle as orc
+    tokens = 1
+    cpu_sample(tokens)  # warm-up (page-in, thread pool)
+    times = []
+    for i in range(args.warmup):
+        cpu_sample(tokens, seed=100 + i)
+    for i in range(args.steps):
+        times.append(cpu_sample(tokens, seed=200 + i))
+    secs = sum(times)
+    value = tokens * args.steps / secs
+    cb = {"value": round(value, 3), "unit": UNIT, "cores": orc.num_threads(), "kind": "port",
+          "sample": f"{tokens} token of the C2 layer per step (router, 3 x 10-pair walk decode, SwiGLU, "
+                    f"combine) on the oracle port of the reference arithmetic"}
+    line = {"metric": METRIC, "value": round(value, 3), "unit": UNIT, "n_gpus": args.gpus, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(secs * 1e3 / args.steps, 3), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32 accumulate over fp16 (bf16 I/O)",
+            "data": "synthetic (seeded)", "impl": "reference",
+            "config": _config(args, world), "cpu_baseline": cb,
+            "e2e": {"value": round(value, 3), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def _config(args, world):
+    return {"workload": f"C2 one VQ-MoE layer decode, batch {args.batch} tokens/GPU (hidden 4096, 512 experts, "
+                        f"inter 1024, top-10, d8 K16384 14-bit, G64)",
+            "global_batch": args.batch * world, "experts": E, "top_k": TOPK, "hidden": HIDDEN,
+            "intermediate": INTER, "dim": D, "codebook": K, "pack_bits": BITS, "group": G,
+            "parallelism": f"replicas{world}" if world > 1 else "single",
+            "l2": f"{args.layers} independently seeded layers rotated per step (weights touched per cycle >> 126 MB L2)"}
+
+
+def main(argv=None) -> int:
+    ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--batch", type=int, default=64)
+    ap.add_argument("--extra-batches", default="1,8")
+    ap.add_argument("--layers", type=int, default=8)
+    ap.add_argument("--skip-e2e", action="store_true")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args(argv)
+    args.warmup = max(3, args.warmup)
+
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+
+    if args.impl == "reference":
+        return reference_arm(args, rank, world)
+
+    import torch
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    if world > 1:
+        import datetime
+        torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                             device_id=dev)
+    from vqlab_b200 import _lib
+    _lib.lib()
+    results, roof, e2e, launches = gpu_arm(args, rank, world, dev)
+    if rank == 0:
+        head = results[args.batch]
+        line = {"metric": METRIC, "value": round(head["tokens_per_s"], 1), "unit": UNIT, "n_gpus": world,
+                "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(head["ms_per_step"], 4),
+                "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+                "dtype": "f32 accumulate over fp16 (bf16 I/O)", "data": "synthetic (seeded)",
+                "config": _config(args, world), "clocks": head["clocks"],
+                "packed_weight_hbm_gbs": round(head["hbm_gbs"], 1),
+                "batches": {str(b): {"tokens_per_s": round(r["tokens_per_s"], 1),
+                                     "ms_per_step": round(r["ms_per_step"], 4),
+                                     "hbm_gbs": round(r["hbm_gbs"], 1),
+                                     "distinct_experts": round(r["distinct_experts_mean"], 1)}
+                            for b, r in results.items()},
+                "roofline": roof, "e2e": e2e, "gpu_launches": launches * args.steps}
+        if not args.no_cpu_baseline:
+            line["cpu_baseline"] = cpu_baseline_block(8)
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        torch.distributed.barrier()
+        torch.distributed.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

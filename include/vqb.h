@@ -1,0 +1,130 @@
+/*
+ * vqb.h -- C ABI of the B200 VQ expert runtime (libvqb200.so).
+ *
+ * The drop-in boundary for the VQLab runtime hot path: the fused
+ * codebook-decode matmul behind `VQSwitchLinear` (routed MoE experts) and
+ * `VQLinear` (dense projections), reading the vq_pack v1 packed layout.
+ *
+ * Every pointer is a DEVICE pointer owned by the caller; every call is
+ * asynchronous on the given stream and allocates nothing.  Calls that need
+ * scratch memory take a caller-supplied workspace whose size the matching
+ * *_workspace_size function returns.  No torch types cross this boundary.
+ *
+ * Tensor formats (identical to the reference's safetensors tensors):
+ *   codes     packed (pack_bits > 0): uint32 [E, OUT, WPR], WPR = ceil(NSUB/32)*BITS,
+ *             code j of a row at bits [j*BITS, (j+1)*BITS) of the row's
+ *             little-endian word stream (src/vqlab/runtime/vq_pack.py:11-27)
+ *             unpacked (pack_bits == 0): uint8 / uint16 [E, OUT, NSUB]
+ *   codebook  fp16 [K, D], D in {2, 4, 8}
+ *   scales    fp16 [E, OUT, IN/G]  (one scale per output row and group of G inputs)
+ *   x         bf16 / fp16 [T, IN]  (token rows)
+ *   indices   uint32 [T, top_k]    (expert of each (token, slot) pair)
+ *   y         [T*top_k, OUT] for the switch, [N, OUT] for dense
+ */
+#ifndef VQB_H_
+#define VQB_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* cudaStream_t without pulling in the CUDA headers. */
+typedef struct CUstream_st* vqb_stream_t;
+
+/* Error convention.  The reference raises on every unsupported geometry and
+ * never falls through to a wrong-memory read (vq_switch.py:3016-3019,
+ * :3106-3109, :3124-3128, :3347-3354, :5285-5296); each raise maps to one
+ * status here. */
+typedef enum vqb_status {
+  VQB_OK = 0,
+  VQB_BAD_SHAPE = 1,              /* inconsistent sizes (IN % G, G % D, ...) */
+  VQB_BAD_WPR = 2,                /* codes row width != ceil(NSUB/32)*BITS (vq_switch.py:3124-3128) */
+  VQB_UNSUPPORTED_GEOMETRY = 3,   /* D not in {2,4,8}, BITS > 16, ... (vq_switch.py:3106-3109) */
+  VQB_CODEBOOK_SHARDED = 4,       /* K differs from the K the module was built with (vq_switch.py:5285-5296) */
+  VQB_CUDA_ERROR = 5,             /* a launch or runtime call failed */
+  VQB_TIMEOUT = 6,                /* a bounded device wait gave up */
+  VQB_BAD_ROUTING = 7,            /* an expert index >= E was seen on the device */
+  VQB_WORKSPACE_TOO_SMALL = 8,
+  VQB_BAD_ALIGNMENT = 9,
+  VQB_NULL_POINTER = 10
+} vqb_status;
+
+typedef enum vqb_dtype { VQB_F16 = 0, VQB_BF16 = 1, VQB_F32 = 2 } vqb_dtype;
+
+/* Kernel path selection.  AUTO follows the reference's cutoffs: the fused
+ * small-N kernel below VQ_FUSED_MAX_N = 512 pairs (vq_switch.py:45, :5313),
+ * the grouped prefill GEMM above it. */
+typedef enum vqb_path { VQB_PATH_AUTO = 0, VQB_PATH_DECODE = 1, VQB_PATH_PREFILL = 2 } vqb_path;
+
+/* One VQ-coded projection: a VQSwitchLinear (E experts) or a VQLinear (E = 1).
+ * Mirrors the module attributes of vq_switch.py:5198-5282 / vq_dense.py:315-344. */
+typedef struct vqb_linear_desc {
+  int32_t num_experts;        /* E (1 for a dense VQLinear) */
+  int32_t out_features;       /* OUT */
+  int32_t in_features;        /* IN */
+  int32_t dim;                /* D, codebook entry width */
+  int32_t num_codes;          /* K, codebook rows */
+  int32_t group_size;         /* G */
+  int32_t pack_bits;          /* BITS; 0 = unpacked codes */
+  int32_t code_bytes;         /* unpacked only: 1 (uint8) or 2 (uint16) */
+  int32_t expected_num_codes; /* K at construction (sharding guard); 0 = no check */
+  int32_t codes_last_dim;     /* caller's codes.shape[-1] (WPR check, vq_switch.py:3124-3128); 0 = no check */
+  const void* codes;
+  const void* codebook;
+  const void* scales;
+  const int32_t* row_table;   /* SKIPZERO row table; must be NULL (not supported yet) */
+} vqb_linear_desc;
+
+/* Optional knobs; pass NULL for defaults. */
+typedef struct vqb_options {
+  int32_t path;               /* vqb_path */
+  int32_t k_split;            /* decode kernel K-slices per row (0 = auto, else 1,2,4,8) */
+  int32_t max_fused_pairs;    /* AUTO cutoff in pairs (0 = 512) */
+  int32_t reserved[5];
+} vqb_options;
+
+/* Library identity and messages. */
+const char* vqb_version(void);
+const char* vqb_status_string(vqb_status status);
+
+/* Device-side vq_pack reader: packed [rows, wpr] -> uint16 codes [rows, nsub].
+ * Replaces vq_pack.unpack (src/vqlab/runtime/vq_pack.py:79-97) and the MLX
+ * reader _unpack_rows (src/vqlab/runtime/vq_dense.py:140-184). */
+vqb_status vqb_unpack(const uint32_t* packed, int64_t rows, int64_t wpr, int32_t nsub,
+                      int32_t bits, uint16_t* out, vqb_stream_t stream);
+
+/* Scratch bytes vqb_switch_forward needs for n_tokens x top_k pairs. */
+size_t vqb_switch_workspace_size(const vqb_linear_desc* desc, int32_t n_tokens, int32_t top_k,
+                                 const vqb_options* opts);
+
+/* y[t*top_k + j, :] = W_{indices[t, j]} x[t, :] for every (token, slot).
+ * Replaces VQSwitchLinear.__call__ (src/vqlab/runtime/vq_switch.py:5284-5423):
+ * x is narrowed to fp16 (the host cast of :5301-5308), accumulation is fp32,
+ * the result is rounded to fp16 and then to y_dtype (:5423). */
+vqb_status vqb_switch_forward(const vqb_linear_desc* desc, const void* x, vqb_dtype x_dtype,
+                              int32_t n_tokens, const uint32_t* indices, int32_t top_k,
+                              void* y, vqb_dtype y_dtype, void* workspace, size_t workspace_bytes,
+                              const vqb_options* opts, vqb_stream_t stream);
+
+/* Scratch bytes vqb_dense_forward needs for n_rows input rows. */
+size_t vqb_dense_workspace_size(const vqb_linear_desc* desc, int64_t n_rows, const vqb_options* opts);
+
+/* y[n, :] = W x[n, :] for a dense VQ projection (E = 1).
+ * Replaces VQLinear.__call__ (src/vqlab/runtime/vq_dense.py:346-441): the
+ * small-N fused kernel narrows x to fp16 in-kernel and stores y_dtype
+ * directly (vq_switch.py:2319-2327); the large-N path materialises
+ * W = fp16(cb*s) in x's dtype tile by tile and runs the GEMM
+ * (_decode_matmul, vq_dense.py:267-312). */
+vqb_status vqb_dense_forward(const vqb_linear_desc* desc, const void* x, vqb_dtype x_dtype,
+                             int64_t n_rows, void* y, vqb_dtype y_dtype,
+                             void* workspace, size_t workspace_bytes,
+                             const vqb_options* opts, vqb_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* VQB_H_ */

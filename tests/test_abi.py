@@ -1,0 +1,136 @@
+"""The C ABI library loads, exports every function include/vqb.h declares,
+and its host-side validation returns the reference's error classes without
+touching a GPU (every case below is rejected before any CUDA call)."""
+import ctypes
+import pathlib
+import re
+
+import numpy as np
+import pytest
+import torch
+
+from vqlab_b200 import _lib
+from vqlab_b200 import VQLinear, VQSwitchLinear
+
+HEADER = pathlib.Path(__file__).resolve().parent.parent / "include" / "vqb.h"
+
+
+def declared_functions():
+    src = HEADER.read_text()
+    src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
+    return sorted(set(re.findall(r"\b(vqb_[a-z0-9_]+)\s*\(", src)))
+
+
+def test_library_exports_every_declared_function():
+    L = _lib.lib()
+    names = declared_functions()
+    assert names, "no declarations parsed"
+    for n in names:
+        assert hasattr(L, n), f"libvqb200.so does not export {n}"
+    assert set(_lib.exported_symbols()) <= set(names)
+
+
+def test_version_and_status_strings():
+    assert "sm_100a" in _lib.version()
+    assert "sharded" in _lib.status_string(_lib.VQB_CODEBOOK_SHARDED)
+    assert _lib.status_string(_lib.VQB_OK) == "ok"
+
+
+def _desc(**kw):
+    d = _lib.LinearDesc()
+    base = dict(num_experts=4, out_features=64, in_features=512, dim=8, num_codes=4096, group_size=64,
+                pack_bits=12, code_bytes=0, expected_num_codes=4096, codes_last_dim=24,
+                codes=0x1000, codebook=0x2000, scales=0x3000, row_table=None)
+    base.update(kw)
+    for k, v in base.items():
+        setattr(d, k, v)
+    return d
+
+
+def _switch(d, n_tokens=1, top_k=2):
+    L = _lib.lib()
+    return L.vqb_switch_forward(ctypes.byref(d), ctypes.c_void_p(0x4000), _lib.VQB_BF16, n_tokens,
+                                ctypes.c_void_p(0x5000), top_k, ctypes.c_void_p(0x6000), _lib.VQB_BF16,
+                                ctypes.c_void_p(0x7000), 1 << 20, None, None)
+
+
+@pytest.mark.parametrize("kw,status", [
+    (dict(dim=3), _lib.VQB_UNSUPPORTED_GEOMETRY),
+    (dict(pack_bits=17), _lib.VQB_UNSUPPORTED_GEOMETRY),
+    (dict(codes_last_dim=23), _lib.VQB_BAD_WPR),
+    (dict(num_codes=2048), _lib.VQB_CODEBOOK_SHARDED),
+    (dict(in_features=500), _lib.VQB_BAD_SHAPE),
+    (dict(group_size=60, in_features=480, codes_last_dim=0), _lib.VQB_BAD_SHAPE),
+    (dict(pack_bits=10), _lib.VQB_BAD_SHAPE),        # 2^10 < K
+    (dict(codes=None), _lib.VQB_NULL_POINTER),
+    (dict(row_table=0x8000), _lib.VQB_UNSUPPORTED_GEOMETRY),
+    (dict(codebook=0x2008), _lib.VQB_BAD_ALIGNMENT),
+    (dict(pack_bits=0, code_bytes=1, num_codes=4096), _lib.VQB_BAD_SHAPE),
+    (dict(pack_bits=0, code_bytes=3), _lib.VQB_UNSUPPORTED_GEOMETRY),
+])
+def test_switch_validation_statuses(kw, status):
+    assert _switch(_desc(**kw)) == status
+
+
+def test_zero_pairs_is_a_noop():
+    assert _switch(_desc(), n_tokens=0) == _lib.VQB_OK
+
+
+def test_workspace_too_small():
+    L = _lib.lib()
+    d = _desc()
+    st = L.vqb_switch_forward(ctypes.byref(d), ctypes.c_void_p(0x4000), _lib.VQB_BF16, 1, ctypes.c_void_p(0x5000),
+                              2, ctypes.c_void_p(0x6000), _lib.VQB_BF16, ctypes.c_void_p(0x7000), 8, None, None)
+    assert st == _lib.VQB_WORKSPACE_TOO_SMALL
+
+
+def test_status_to_exception_classes():
+    with pytest.raises(ValueError):
+        _lib.check(_lib.VQB_BAD_WPR)
+    with pytest.raises(NotImplementedError):
+        _lib.check(_lib.VQB_UNSUPPORTED_GEOMETRY)
+    with pytest.raises(RuntimeError):
+        _lib.check(_lib.VQB_CODEBOOK_SHARDED)
+
+
+def _module(packed=True):
+    E, OUT, IN, D, K = 2, 16, 128, 8, 256
+    bits = 8
+    codes = torch.zeros((E, OUT, (IN // D + 31) // 32 * bits), dtype=torch.int32)
+    cb = torch.zeros((K, D), dtype=torch.float16)
+    sc = torch.ones((E, OUT, IN // 64), dtype=torch.float16)
+    return VQSwitchLinear(codes, cb, sc, group_size=64, pack_bits=bits, in_features=IN)
+
+
+def test_module_properties_and_from_weights():
+    m = _module()
+    assert (m.input_dims, m.output_dims, m.num_experts) == (128, 16, 2)
+    m2 = VQSwitchLinear.from_weights(m.codes, m.codebook, m.vq_scales)
+    assert m2.pack_bits == 8 and m2.input_dims == 128
+    with pytest.raises(ValueError):
+        VQSwitchLinear(m.codes, m.codebook, m.vq_scales, pack_bits=8)  # no in_features
+    with pytest.raises(NotImplementedError):
+        VQSwitchLinear(m.codes, m.codebook, m.vq_scales, pack_bits=8, in_features=128,
+                       row_table=torch.zeros((2, 16), dtype=torch.int32))
+
+
+def test_module_refuses_cpu_tensors():
+    m = _module()
+    x = torch.zeros((1, 1, 1, 128), dtype=torch.bfloat16)
+    with pytest.raises(ValueError, match="CUDA"):
+        m(x, torch.zeros((1, 2), dtype=torch.int32))
+
+
+def test_module_sharding_guard():
+    m = _module()
+    m.codebook = m.codebook[:128]
+    with pytest.raises(RuntimeError, match="sharded"):
+        m(torch.zeros((1, 1, 1, 128), dtype=torch.bfloat16), torch.zeros((1, 2), dtype=torch.int32))
+
+
+def test_dense_module_properties():
+    codes = torch.zeros((32, 64), dtype=torch.uint8)
+    lin = VQLinear(codes, torch.zeros((256, 2), dtype=torch.float16), torch.ones((32, 2), dtype=torch.float16))
+    assert (lin.input_dims, lin.output_dims) == (128, 32)
+    with pytest.raises(ValueError):
+        lin(torch.zeros((1, 128), dtype=torch.bfloat16))

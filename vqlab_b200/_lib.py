@@ -1,0 +1,130 @@
+"""ctypes binding of libvqb200.so (the C ABI declared in include/vqb.h).
+
+The shared library is the product: this module only loads it, mirrors the C
+structs and turns a non-OK `vqb_status` into the exception class the
+reference raises for the same condition (ValueError for shape/format errors,
+NotImplementedError for unsupported geometry, RuntimeError for a sharded
+codebook or a CUDA failure; vq_switch.py:3106-3128, :5285-5296).  There is no
+CPU fallback: if the library cannot be loaded, every call raises.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import pathlib
+import threading
+
+PKG = pathlib.Path(__file__).resolve().parent
+LIB_PATH = PKG / "libvqb200.so"
+
+VQB_OK = 0
+VQB_BAD_SHAPE = 1
+VQB_BAD_WPR = 2
+VQB_UNSUPPORTED_GEOMETRY = 3
+VQB_CODEBOOK_SHARDED = 4
+VQB_CUDA_ERROR = 5
+VQB_TIMEOUT = 6
+VQB_BAD_ROUTING = 7
+VQB_WORKSPACE_TOO_SMALL = 8
+VQB_BAD_ALIGNMENT = 9
+VQB_NULL_POINTER = 10
+
+VQB_F16, VQB_BF16, VQB_F32 = 0, 1, 2
+PATH_AUTO, PATH_DECODE, PATH_PREFILL = 0, 1, 2
+
+
+class LinearDesc(ctypes.Structure):
+    _fields_ = [
+        ("num_experts", ctypes.c_int32),
+        ("out_features", ctypes.c_int32),
+        ("in_features", ctypes.c_int32),
+        ("dim", ctypes.c_int32),
+        ("num_codes", ctypes.c_int32),
+        ("group_size", ctypes.c_int32),
+        ("pack_bits", ctypes.c_int32),
+        ("code_bytes", ctypes.c_int32),
+        ("expected_num_codes", ctypes.c_int32),
+        ("codes_last_dim", ctypes.c_int32),
+        ("codes", ctypes.c_void_p),
+        ("codebook", ctypes.c_void_p),
+        ("scales", ctypes.c_void_p),
+        ("row_table", ctypes.c_void_p),
+    ]
+
+
+class Options(ctypes.Structure):
+    _fields_ = [
+        ("path", ctypes.c_int32),
+        ("k_split", ctypes.c_int32),
+        ("max_fused_pairs", ctypes.c_int32),
+        ("reserved", ctypes.c_int32 * 5),
+    ]
+
+
+class VQBError(RuntimeError):
+    """A non-OK status that maps to no narrower Python exception."""
+
+
+_lock = threading.Lock()
+_lib = None
+
+
+def _bind(L):
+    P, i32, i64, sz = ctypes.c_void_p, ctypes.c_int32, ctypes.c_int64, ctypes.c_size_t
+    L.vqb_version.restype = ctypes.c_char_p
+    L.vqb_status_string.restype = ctypes.c_char_p
+    L.vqb_status_string.argtypes = [i32]
+    L.vqb_unpack.restype = i32
+    L.vqb_unpack.argtypes = [P, i64, i64, i32, i32, P, P]
+    L.vqb_switch_workspace_size.restype = sz
+    L.vqb_switch_workspace_size.argtypes = [P, i32, i32, P]
+    L.vqb_switch_forward.restype = i32
+    L.vqb_switch_forward.argtypes = [P, P, i32, i32, P, i32, P, i32, P, sz, P, P]
+    L.vqb_dense_workspace_size.restype = sz
+    L.vqb_dense_workspace_size.argtypes = [P, i64, P]
+    L.vqb_dense_forward.restype = i32
+    L.vqb_dense_forward.argtypes = [P, P, i32, i64, P, i32, P, sz, P, P]
+    return L
+
+
+def lib():
+    """Load (building first if the toolchain is here and the .so is missing)."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    with _lock:
+        if _lib is None:
+            if not LIB_PATH.exists() or os.environ.get("VQB_REBUILD") == "1":
+                from . import build as _build
+                _build.build()
+            try:
+                _lib = _bind(ctypes.CDLL(str(LIB_PATH)))
+            except OSError as e:  # no silent fallback: the native path is the product
+                raise RuntimeError(f"libvqb200.so could not be loaded from {LIB_PATH}: {e}") from e
+    return _lib
+
+
+def status_string(st: int) -> str:
+    return lib().vqb_status_string(int(st)).decode()
+
+
+def check(st: int, what: str = "") -> None:
+    if st == VQB_OK:
+        return
+    msg = f"{what}: {status_string(st)} (vqb_status {st})" if what else status_string(st)
+    if st in (VQB_BAD_SHAPE, VQB_BAD_WPR, VQB_BAD_ALIGNMENT, VQB_NULL_POINTER,
+              VQB_WORKSPACE_TOO_SMALL, VQB_BAD_ROUTING):
+        raise ValueError(msg)
+    if st == VQB_UNSUPPORTED_GEOMETRY:
+        raise NotImplementedError(msg)
+    raise VQBError(msg)
+
+
+def version() -> str:
+    return lib().vqb_version().decode()
+
+
+def exported_symbols():
+    """Names of every function include/vqb.h declares (for the load test)."""
+    return ["vqb_version", "vqb_status_string", "vqb_unpack", "vqb_switch_workspace_size",
+            "vqb_switch_forward", "vqb_dense_workspace_size", "vqb_dense_forward"]

@@ -1,0 +1,167 @@
+// C ABI of libvqb200.so (declared in include/vqb.h): argument validation with
+// the reference's error classes, path selection, workspace layout, launches.
+#include <cstdio>
+
+#include "vqb_common.cuh"
+#include "vqb_internal.h"
+
+namespace vqb {
+
+// Every geometry rule the reference enforces before it dispatches a kernel:
+// explicit D (vq_switch.py:3106-3109), the packed row width
+// (:3124-3128), IN % G and G % D (the group/subvector structure of
+// vq_pack/fit_moe), the codebook sharding guard (:5285-5296).
+vqb_status validate(const vqb_linear_desc* d, LinearGeometry* g) {
+  if (!d || !d->codes || !d->codebook || !d->scales) return VQB_NULL_POINTER;
+  if (d->row_table) return VQB_UNSUPPORTED_GEOMETRY;
+  if (d->expected_num_codes > 0 && d->num_codes != d->expected_num_codes) return VQB_CODEBOOK_SHARDED;
+  if (d->dim != 2 && d->dim != 4 && d->dim != 8) return VQB_UNSUPPORTED_GEOMETRY;
+  if (d->num_experts < 1 || d->out_features < 1 || d->in_features < 1 || d->group_size < 1 || d->num_codes < 1)
+    return VQB_BAD_SHAPE;
+  if (d->in_features % d->group_size != 0 || d->group_size % d->dim != 0) return VQB_BAD_SHAPE;
+  const int nsub = d->in_features / d->dim;
+  int bits, row_words;
+  if (d->pack_bits > 0) {
+    if (d->pack_bits > 16) return VQB_UNSUPPORTED_GEOMETRY;
+    if ((int64_t(1) << d->pack_bits) < d->num_codes) return VQB_BAD_SHAPE;
+    bits = d->pack_bits;
+    row_words = (nsub + 31) / 32 * bits;
+    if (d->codes_last_dim > 0 && d->codes_last_dim != row_words) return VQB_BAD_WPR;
+  } else {
+    if (d->code_bytes != 1 && d->code_bytes != 2) return VQB_UNSUPPORTED_GEOMETRY;
+    if (d->code_bytes == 1 && d->num_codes > 256) return VQB_BAD_SHAPE;
+    const int64_t row_bytes = int64_t(nsub) * d->code_bytes;
+    // unpacked rows are read as 8/16-bit code streams (byte-identical to
+    // pack_bits 8/16 rows when whole words; vq_switch.py:2975-2996)
+    if (row_bytes % 4 != 0) return VQB_UNSUPPORTED_GEOMETRY;
+    if ((reinterpret_cast<uintptr_t>(d->codes) & 3) != 0) return VQB_BAD_ALIGNMENT;
+    bits = 8 * d->code_bytes;
+    row_words = static_cast<int>(row_bytes / 4);
+    if (d->codes_last_dim > 0 && d->codes_last_dim != nsub) return VQB_BAD_SHAPE;
+  }
+  if ((reinterpret_cast<uintptr_t>(d->codebook) & 15) != 0 || (reinterpret_cast<uintptr_t>(d->scales) & 1) != 0)
+    return VQB_BAD_ALIGNMENT;
+  g->E = d->num_experts;
+  g->OUT = d->out_features;
+  g->IN = d->in_features;
+  g->D = d->dim;
+  g->K = d->num_codes;
+  g->G = d->group_size;
+  g->bits = bits;
+  g->row_words = row_words;
+  g->codes = d->codes;
+  g->codebook = d->codebook;
+  g->scales = d->scales;
+  return VQB_OK;
+}
+
+static bool dtype_ok(int t) { return t == VQB_F16 || t == VQB_BF16 || t == VQB_F32; }
+
+// Workspace: a 256-byte header (device error word at offset 0) followed by
+// per-path scratch.
+constexpr size_t kHeaderBytes = 256;
+
+}  // namespace vqb
+
+using namespace vqb;
+
+extern "C" {
+
+const char* vqb_version(void) { return "vqb200 0.1 sm_100a"; }
+
+const char* vqb_status_string(vqb_status s) {
+  switch (s) {
+    case VQB_OK: return "ok";
+    case VQB_BAD_SHAPE: return "inconsistent tensor shapes for a VQ projection";
+    case VQB_BAD_WPR: return "packed codes row width does not match ceil(NSUB/32)*BITS";
+    case VQB_UNSUPPORTED_GEOMETRY: return "unsupported VQ geometry (D must be 2, 4 or 8; BITS <= 16)";
+    case VQB_CODEBOOK_SHARDED: return "VQ codebook was sharded: K differs from the K the module was built with";
+    case VQB_CUDA_ERROR: return "CUDA launch or runtime error";
+    case VQB_TIMEOUT: return "a bounded device wait timed out";
+    case VQB_BAD_ROUTING: return "an expert index was out of range";
+    case VQB_WORKSPACE_TOO_SMALL: return "workspace too small";
+    case VQB_BAD_ALIGNMENT: return "misaligned tensor pointer";
+    case VQB_NULL_POINTER: return "null tensor pointer";
+  }
+  return "unknown status";
+}
+
+vqb_status vqb_unpack(const uint32_t* packed, int64_t rows, int64_t wpr, int32_t nsub, int32_t bits, uint16_t* out,
+                      vqb_stream_t stream) {
+  if (!packed || !out) return VQB_NULL_POINTER;
+  if (bits < 1 || bits > 16 || nsub < 0 || rows < 0) return VQB_UNSUPPORTED_GEOMETRY;
+  if (wpr != (int64_t(nsub) + 31) / 32 * bits) return VQB_BAD_WPR;
+  return launch_unpack(packed, rows, wpr, nsub, bits, out, reinterpret_cast<cudaStream_t>(stream));
+}
+
+size_t vqb_switch_workspace_size(const vqb_linear_desc* desc, int32_t n_tokens, int32_t top_k,
+                                 const vqb_options* opts) {
+  (void)desc; (void)n_tokens; (void)top_k; (void)opts;
+  return kHeaderBytes;
+}
+
+vqb_status vqb_switch_forward(const vqb_linear_desc* desc, const void* x, vqb_dtype x_dtype, int32_t n_tokens,
+                              const uint32_t* indices, int32_t top_k, void* y, vqb_dtype y_dtype, void* workspace,
+                              size_t workspace_bytes, const vqb_options* opts, vqb_stream_t stream) {
+  LinearGeometry geo;
+  vqb_status st = validate(desc, &geo);
+  if (st != VQB_OK) return st;
+  if (n_tokens < 0 || top_k < 1) return VQB_BAD_SHAPE;
+  if (!dtype_ok(x_dtype) || !dtype_ok(y_dtype)) return VQB_BAD_SHAPE;
+  const int64_t N64 = int64_t(n_tokens) * top_k;
+  if (N64 > 0x7fffffff) return VQB_BAD_SHAPE;
+  const int N = static_cast<int>(N64);
+  if (N == 0) return VQB_OK;
+  if (!x || !indices || !y) return VQB_NULL_POINTER;
+  if (workspace_bytes < vqb_switch_workspace_size(desc, n_tokens, top_k, opts)) return VQB_WORKSPACE_TOO_SMALL;
+  if (!workspace) return VQB_NULL_POINTER;
+  int* err = static_cast<int*>(workspace);
+  const int ks = opts ? opts->k_split : 0;
+  // MoE numerics: x narrowed to fp16, fp32 accumulation, fp16 output rounding
+  // then the caller's dtype (vq_switch.py:5301-5308, :5423).
+  return launch_decode(geo, x, x_dtype, n_tokens, indices, N, top_k, y, y_dtype, /*narrow_x_f16=*/true,
+                       /*round_f16_first=*/true, /*wround=*/0, ks, err, reinterpret_cast<cudaStream_t>(stream));
+}
+
+size_t vqb_dense_workspace_size(const vqb_linear_desc* desc, int64_t n_rows, const vqb_options* opts) {
+  (void)desc; (void)n_rows; (void)opts;
+  return kHeaderBytes;
+}
+
+vqb_status vqb_dense_forward(const vqb_linear_desc* desc, const void* x, vqb_dtype x_dtype, int64_t n_rows, void* y,
+                             vqb_dtype y_dtype, void* workspace, size_t workspace_bytes, const vqb_options* opts,
+                             vqb_stream_t stream) {
+  LinearGeometry geo;
+  vqb_status st = validate(desc, &geo);
+  if (st != VQB_OK) return st;
+  if (geo.E != 1) return VQB_BAD_SHAPE;
+  if (!dtype_ok(x_dtype) || !dtype_ok(y_dtype)) return VQB_BAD_SHAPE;
+  if (n_rows < 0 || n_rows > 0x7fffffff) return VQB_BAD_SHAPE;
+  if (n_rows == 0) return VQB_OK;
+  if (!x || !y) return VQB_NULL_POINTER;
+  if (workspace_bytes < vqb_dense_workspace_size(desc, n_rows, opts)) return VQB_WORKSPACE_TOO_SMALL;
+  if (!workspace) return VQB_NULL_POINTER;
+  const int ks = opts ? opts->k_split : 0;
+  const int path = opts ? opts->path : VQB_PATH_AUTO;
+  // Which reference path serves this call (vq_dense.py:401-441): the fused
+  // dense kernel only for d2/d4 at N <= the per-geometry cutoff
+  // (_fused_max_n, vq_dense.py:94-102: unpacked 12, packed d2 72, packed d4
+  // 32); everything else, and every d8 layer, is _decode_matmul.
+  bool fused;
+  if (path == VQB_PATH_DECODE) fused = true;
+  else if (path == VQB_PATH_PREFILL) fused = false;
+  else {
+    int maxn = desc->pack_bits == 0 ? 12 : (geo.D == 2 ? 72 : (geo.D == 4 ? 32 : 0));
+    if (opts && opts->max_fused_pairs > 0) maxn = opts->max_fused_pairs;
+    fused = geo.D != 8 && n_rows <= maxn;
+  }
+  // fused numerics: x narrowed to fp16 in-kernel, group partials, y stored
+  // directly in the output dtype (vq_switch.py:2319-2327).
+  // _decode_matmul numerics: W = fp16(cb*s) in x's dtype, y = x @ W^T.
+  const int wround = fused ? 0 : (x_dtype == VQB_BF16 ? 1 : 2);
+  return launch_decode(geo, x, x_dtype, static_cast<int>(n_rows), nullptr, static_cast<int>(n_rows), 1, y, y_dtype,
+                       /*narrow_x_f16=*/fused, /*round_f16_first=*/false, wround, ks, static_cast<int*>(workspace),
+                       reinterpret_cast<cudaStream_t>(stream));
+}
+
+}  // extern "C"
