@@ -81,9 +81,13 @@ typedef struct vqb_linear_desc {
 /* Optional knobs; pass NULL for defaults. */
 typedef struct vqb_options {
   int32_t path;               /* vqb_path */
-  int32_t k_split;            /* decode kernel K-slices per row (0 = auto, else 1,2,4,8) */
+  int32_t k_split;            /* decode kernel K-slices per row (0 = auto; grouped kernel 1..16, per-pair 1..8) */
   int32_t max_fused_pairs;    /* AUTO cutoff in pairs (0 = 512) */
-  int32_t reserved[5];
+  int32_t decode_variant;     /* 0 = expert-grouped persistent kernel, 1 = one pair per CTA (reference order) */
+  int32_t stage_codebook;     /* grouped kernel: 0 = auto, 1 = shared-memory prefix (no pair split),
+                                 2 = none, 3 = split the codebook across a CTA pair */
+  int32_t pairs_per_chunk;    /* grouped kernel: tokens sharing one lookup pass (0 = auto, else 1, 2 or 4) */
+  int32_t reserved[2];
 } vqb_options;
 
 /* Library identity and messages. */
@@ -96,7 +100,10 @@ const char* vqb_status_string(vqb_status status);
 vqb_status vqb_unpack(const uint32_t* packed, int64_t rows, int64_t wpr, int32_t nsub,
                       int32_t bits, uint16_t* out, vqb_stream_t stream);
 
-/* Scratch bytes vqb_switch_forward needs for n_tokens x top_k pairs. */
+/* Scratch bytes vqb_switch_forward needs for n_tokens x top_k pairs.  The
+ * first 16 bytes of the workspace are a status block the call rewrites:
+ * int32 [1] is set to VQB_BAD_ROUTING when an expert index >= E was seen
+ * (such a pair is computed as expert 0, never read out of range). */
 size_t vqb_switch_workspace_size(const vqb_linear_desc* desc, int32_t n_tokens, int32_t top_k,
                                  const vqb_options* opts);
 

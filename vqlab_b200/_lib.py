@@ -57,7 +57,10 @@ class Options(ctypes.Structure):
         ("path", ctypes.c_int32),
         ("k_split", ctypes.c_int32),
         ("max_fused_pairs", ctypes.c_int32),
-        ("reserved", ctypes.c_int32 * 5),
+        ("decode_variant", ctypes.c_int32),
+        ("stage_codebook", ctypes.c_int32),
+        ("pairs_per_chunk", ctypes.c_int32),
+        ("reserved", ctypes.c_int32 * 2),
     ]
 
 

@@ -57,9 +57,6 @@ vqb_status validate(const vqb_linear_desc* d, LinearGeometry* g) {
 
 static bool dtype_ok(int t) { return t == VQB_F16 || t == VQB_BF16 || t == VQB_F32; }
 
-// Workspace: a 256-byte header (device error word at offset 0) followed by
-// per-path scratch.
-constexpr size_t kHeaderBytes = 256;
 
 }  // namespace vqb
 
@@ -94,10 +91,62 @@ vqb_status vqb_unpack(const uint32_t* packed, int64_t rows, int64_t wpr, int32_t
   return launch_unpack(packed, rows, wpr, nsub, bits, out, reinterpret_cast<cudaStream_t>(stream));
 }
 
+// Workspace: [routing (status block first)][x as 16-bit rows for the MMA B operand]
+static size_t linear_workspace_bytes(int N, int E, int64_t T, int IN) {
+  return route_workspace_bytes(N, E, kDecodeMaxPairs) + mma_x16_bytes(T, IN);
+}
+
 size_t vqb_switch_workspace_size(const vqb_linear_desc* desc, int32_t n_tokens, int32_t top_k,
                                  const vqb_options* opts) {
-  (void)desc; (void)n_tokens; (void)top_k; (void)opts;
-  return kHeaderBytes;
+  (void)opts;
+  const int64_t T = n_tokens > 0 ? n_tokens : 0;
+  const int64_t N = T * (top_k > 0 ? top_k : 1);
+  const int E = desc ? (desc->num_experts > 0 ? desc->num_experts : 1) : 1;
+  const int IN = desc ? (desc->in_features > 0 ? desc->in_features : 0) : 0;
+  return linear_workspace_bytes(static_cast<int>(N), E, T, IN);
+}
+
+// Shared body of the switch and dense entry points once shapes are valid.
+static vqb_status run_linear(const LinearGeometry& geo, const void* x, int x_dtype, int n_tokens,
+                             const uint32_t* indices, int krep, int N, void* y, int y_dtype, void* workspace,
+                             const vqb_options* opts, bool narrow_x_f16, bool round_f16_first, int wround,
+                             cudaStream_t stream) {
+  RouteWorkspace rw = carve_route_workspace(workspace, N, geo.E);
+  if (cudaMemsetAsync(rw.meta, 0, sizeof(int) * 4, stream) != cudaSuccess) return VQB_CUDA_ERROR;
+  const int ks = opts ? opts->k_split : 0;
+  const int variant = opts ? opts->decode_variant : 0;
+  if (variant == 1) {
+    // one pair per CTA, the reference walk order (kept for exact-order checks)
+    return launch_decode(geo, x, x_dtype, n_tokens, indices, N, krep, y, y_dtype, narrow_x_f16, round_f16_first,
+                         wround, ks, rw.meta + 1, stream);
+  }
+  if (!mma_decode_supported(geo, wround, x_dtype)) {
+    // geometries outside the tensor-core kernel (group not a multiple of 64,
+    // IN not a multiple of 512, unaligned rows) take the per-pair kernel
+    return launch_decode(geo, x, x_dtype, n_tokens, indices, N, krep, y, y_dtype, narrow_x_f16, round_f16_first,
+                         wround, ks > 8 ? 8 : ks, rw.meta + 1, stream);
+  }
+  const int pmax = decode_pairs_per_chunk(N, geo.E, geo.K, geo.D, geo.IN, opts ? opts->pairs_per_chunk : 0);
+  vqb_status st = launch_route_small(indices, N, geo.E, pmax, rw, stream);
+  if (st != VQB_OK) return st;
+  GroupedDecodeArgs a{};
+  a.x = x;
+  a.x_dtype = x_dtype;
+  a.krep = krep;
+  a.route = &rw;
+  a.N = N;
+  a.y = y;
+  a.y_dtype = y_dtype;
+  a.narrow_x_f16 = narrow_x_f16;
+  a.round_f16_first = round_f16_first;
+  a.wround = wround;
+  a.ks = ks;
+  const int stage = opts ? opts->stage_codebook : 0;
+  a.stage_codebook = stage == 1 ? 1 : (stage == 2 ? 0 : (stage == 3 ? 3 : -1));
+  a.pmax = pmax;
+  uint16_t* x16 = reinterpret_cast<uint16_t*>(static_cast<char*>(workspace) +
+                                              route_workspace_bytes(N, geo.E, kDecodeMaxPairs));
+  return launch_decode_mma(geo, a, x16, n_tokens, stream);
 }
 
 vqb_status vqb_switch_forward(const vqb_linear_desc* desc, const void* x, vqb_dtype x_dtype, int32_t n_tokens,
@@ -115,17 +164,18 @@ vqb_status vqb_switch_forward(const vqb_linear_desc* desc, const void* x, vqb_dt
   if (!x || !indices || !y) return VQB_NULL_POINTER;
   if (workspace_bytes < vqb_switch_workspace_size(desc, n_tokens, top_k, opts)) return VQB_WORKSPACE_TOO_SMALL;
   if (!workspace) return VQB_NULL_POINTER;
-  int* err = static_cast<int*>(workspace);
-  const int ks = opts ? opts->k_split : 0;
   // MoE numerics: x narrowed to fp16, fp32 accumulation, fp16 output rounding
   // then the caller's dtype (vq_switch.py:5301-5308, :5423).
-  return launch_decode(geo, x, x_dtype, n_tokens, indices, N, top_k, y, y_dtype, /*narrow_x_f16=*/true,
-                       /*round_f16_first=*/true, /*wround=*/0, ks, err, reinterpret_cast<cudaStream_t>(stream));
+  return run_linear(geo, x, x_dtype, n_tokens, indices, top_k, N, y, y_dtype, workspace, opts,
+                    /*narrow_x_f16=*/true, /*round_f16_first=*/true, /*wround=*/0,
+                    reinterpret_cast<cudaStream_t>(stream));
 }
 
 size_t vqb_dense_workspace_size(const vqb_linear_desc* desc, int64_t n_rows, const vqb_options* opts) {
-  (void)desc; (void)n_rows; (void)opts;
-  return kHeaderBytes;
+  (void)opts;
+  const int n = static_cast<int>(n_rows > 0 ? (n_rows > 0x7fffffff ? 0x7fffffff : n_rows) : 0);
+  const int IN = desc ? (desc->in_features > 0 ? desc->in_features : 0) : 0;
+  return linear_workspace_bytes(n, 1, n, IN);
 }
 
 vqb_status vqb_dense_forward(const vqb_linear_desc* desc, const void* x, vqb_dtype x_dtype, int64_t n_rows, void* y,
@@ -141,7 +191,6 @@ vqb_status vqb_dense_forward(const vqb_linear_desc* desc, const void* x, vqb_dty
   if (!x || !y) return VQB_NULL_POINTER;
   if (workspace_bytes < vqb_dense_workspace_size(desc, n_rows, opts)) return VQB_WORKSPACE_TOO_SMALL;
   if (!workspace) return VQB_NULL_POINTER;
-  const int ks = opts ? opts->k_split : 0;
   const int path = opts ? opts->path : VQB_PATH_AUTO;
   // Which reference path serves this call (vq_dense.py:401-441): the fused
   // dense kernel only for d2/d4 at N <= the per-geometry cutoff
@@ -158,10 +207,11 @@ vqb_status vqb_dense_forward(const vqb_linear_desc* desc, const void* x, vqb_dty
   // fused numerics: x narrowed to fp16 in-kernel, group partials, y stored
   // directly in the output dtype (vq_switch.py:2319-2327).
   // _decode_matmul numerics: W = fp16(cb*s) in x's dtype, y = x @ W^T.
+  if (!fused && x_dtype == VQB_F32) return VQB_UNSUPPORTED_GEOMETRY;
   const int wround = fused ? 0 : (x_dtype == VQB_BF16 ? 1 : 2);
-  return launch_decode(geo, x, x_dtype, static_cast<int>(n_rows), nullptr, static_cast<int>(n_rows), 1, y, y_dtype,
-                       /*narrow_x_f16=*/fused, /*round_f16_first=*/false, wround, ks, static_cast<int*>(workspace),
-                       reinterpret_cast<cudaStream_t>(stream));
+  const int n = static_cast<int>(n_rows);
+  return run_linear(geo, x, x_dtype, n, nullptr, 1, n, y, y_dtype, workspace, opts, /*narrow_x_f16=*/fused,
+                    /*round_f16_first=*/false, wround, reinterpret_cast<cudaStream_t>(stream));
 }
 
 }  // extern "C"

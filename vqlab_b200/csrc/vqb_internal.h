@@ -19,11 +19,67 @@ struct LinearGeometry {
 
 vqb_status validate(const vqb_linear_desc* d, LinearGeometry* out);
 
+// Pairs grouped by expert (vq_route.cu).
+struct RouteWorkspace {
+  int* meta;      // [0] chunk count, [1] error flag
+  int* counts;    // [E]
+  int* offsets;   // [E+1]
+  int* sorted;    // [N] pair ids grouped by expert
+  int4* chunks;   // (expert, first sorted slot, pairs, 0)
+};
+
+size_t route_workspace_bytes(int N, int E, int max_pairs);
+RouteWorkspace carve_route_workspace(void* base, int N, int E);
+vqb_status launch_route_small(const uint32_t* idx, int N, int E, int max_pairs, const RouteWorkspace& ws,
+                              cudaStream_t stream);
+
+// One pair per CTA, CUDA-core walk in the reference's order (vq_decode.cu).
 vqb_status launch_decode(const LinearGeometry& geo, const void* x, int x_dtype, int T, const uint32_t* idx,
                          int N, int krep, void* y, int y_dtype, bool narrow_x_f16, bool round_f16_first,
                          int wround, int ks, int* err, cudaStream_t stream);
 
 vqb_status launch_unpack(const uint32_t* packed, int64_t rows, int64_t wpr, int nsub, int bits, uint16_t* out,
                          cudaStream_t stream);
+
+constexpr int kDecodeMaxPairs = 16;  // route workspace sizing bound (chunks <= N + E either way)
+
+// Expert-grouped decode on the tensor cores (vq_decode_mma.cu).
+struct GroupedDecodeArgs {
+  const void* x;          // token rows [T, IN] (x_dtype)
+  int x_dtype;
+  int krep;               // pair p reads token p / krep
+  const RouteWorkspace* route;
+  int N;                  // pairs
+  void* y;                // [N, OUT]
+  int y_dtype;
+  bool narrow_x_f16;
+  bool round_f16_first;
+  int wround;
+  int ks;                 // 0 = auto
+  int stage_codebook;     // -1 auto, 0 none, 1 prefix only (no split), 3 split across a CTA pair
+  int pmax;               // tokens per chunk the route step used (<= 16)
+};
+bool mma_decode_supported(const LinearGeometry& geo, int wround, int x_dtype);
+size_t mma_x16_bytes(int64_t T, int IN);
+vqb_status launch_decode_mma(const LinearGeometry& geo, const GroupedDecodeArgs& a, uint16_t* x16, int T,
+                             cudaStream_t stream);
+
+// Tokens that share one pass over an expert's rows (one MMA n-tile holds 8).
+inline int decode_pairs_per_chunk(int N, int E, int K, int D, int IN, int override_pairs) {
+  int pm;
+  if (override_pairs == 1 || override_pairs == 2 || override_pairs == 4 || override_pairs == 8 ||
+      override_pairs == 16)
+    pm = override_pairs;
+  else if (E == 1) pm = N > 8 ? 16 : 8;
+  else if (N <= E) pm = 2;
+  else if (N <= 4 * static_cast<int64_t>(E)) pm = 4;
+  else pm = 8;
+  // a codebook that does not fit shared memory keeps the x staging small so
+  // more of the table stays resident
+  if (E > 1 && static_cast<int64_t>(K) * D * 2 > 160 * 1024 && pm > 4 && override_pairs == 0) pm = 4;
+  const int64_t fit = (64 * 1024) / ((static_cast<int64_t>(IN) + 8) * 2);
+  if (pm > fit) pm = fit < 1 ? 1 : static_cast<int>(fit >= 16 ? 16 : (fit >= 8 ? 8 : (fit >= 4 ? 4 : (fit >= 2 ? 2 : 1))));
+  return pm;
+}
 
 }  // namespace vqb

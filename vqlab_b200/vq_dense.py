@@ -91,7 +91,7 @@ class VQLinear(torch.nn.Module):
         optp = ctypes.byref(self.options) if self.options is not None else None
         L = _lib.lib()
         ws_bytes = L.vqb_dense_workspace_size(ctypes.byref(d), n, optp)
-        ws = torch.zeros(ws_bytes, dtype=torch.uint8, device=x.device)
+        ws = torch.empty(ws_bytes, dtype=torch.uint8, device=x.device)
         st = L.vqb_dense_forward(ctypes.byref(d), ctypes.c_void_p(xf.data_ptr()), _DTYPES[x.dtype], n,
                                  ctypes.c_void_p(y.data_ptr()), _DTYPES[x.dtype], ctypes.c_void_p(ws.data_ptr()),
                                  ws_bytes, optp, _stream_ptr(x.device))

@@ -38,9 +38,11 @@ def _stream_ptr(dev) -> ctypes.c_void_p:
     return ctypes.c_void_p(torch.cuda.current_stream(dev).cuda_stream)
 
 
-def make_options(path: int = 0, k_split: int = 0, max_fused_pairs: int = 0):
+def make_options(path: int = 0, k_split: int = 0, max_fused_pairs: int = 0, decode_variant: int = 0,
+                 stage_codebook: int = 0, pairs_per_chunk: int = 0):
     o = _lib.Options()
     o.path, o.k_split, o.max_fused_pairs = path, k_split, max_fused_pairs
+    o.decode_variant, o.stage_codebook, o.pairs_per_chunk = decode_variant, stage_codebook, pairs_per_chunk
     return o
 
 
@@ -173,14 +175,14 @@ class VQSwitchLinear(torch.nn.Module):
         optp = ctypes.byref(opts) if opts is not None else None
         L = _lib.lib()
         ws_bytes = L.vqb_switch_workspace_size(ctypes.byref(d), ntok, krep, optp)
-        ws = torch.zeros(ws_bytes, dtype=torch.uint8, device=x.device)
+        ws = torch.empty(ws_bytes, dtype=torch.uint8, device=x.device)
         st = L.vqb_switch_forward(ctypes.byref(d), ctypes.c_void_p(x2.data_ptr()), _DTYPES[x.dtype], ntok,
                                   ctypes.c_void_p(idx.data_ptr()), krep, ctypes.c_void_p(y.data_ptr()),
                                   _DTYPES[x.dtype], ctypes.c_void_p(ws.data_ptr()), ws_bytes, optp,
                                   _stream_ptr(x.device))
         _lib.check(st, "vqb_switch_forward")
         if os.environ.get("VQB_CHECK_ROUTING") == "1":
-            if int(ws[:4].view(torch.int32).item()) != 0:
+            if int(ws[:16].view(torch.int32)[1].item()) != 0:
                 raise ValueError("an expert index was out of range for this VQSwitchLinear")
         return y.reshape(*indices.shape, 1, OUT)
 
