@@ -91,9 +91,15 @@ vqb_status vqb_unpack(const uint32_t* packed, int64_t rows, int64_t wpr, int32_t
   return launch_unpack(packed, rows, wpr, nsub, bits, out, reinterpret_cast<cudaStream_t>(stream));
 }
 
-// Workspace: [routing (status block first)][x as 16-bit rows for the MMA B operand]
+// Workspace: [routing (status block first)][x as 16-bit rows: the token rows
+// for the decode kernel's B operand, or all pairs' rows in expert order for
+// the grouped GEMM -- whichever is larger]
+static size_t x_region_bytes(int N, int64_t T, int IN) {
+  const size_t a = mma_x16_bytes(T, IN), b = tc_prefill_x_bytes(N, IN);
+  return a > b ? a : b;
+}
 static size_t linear_workspace_bytes(int N, int E, int64_t T, int IN) {
-  return route_workspace_bytes(N, E, kDecodeMaxPairs) + mma_x16_bytes(T, IN);
+  return route_workspace_bytes(N, E, kDecodeMaxPairs) + x_region_bytes(N, T, IN);
 }
 
 size_t vqb_switch_workspace_size(const vqb_linear_desc* desc, int32_t n_tokens, int32_t top_k,
@@ -110,11 +116,20 @@ size_t vqb_switch_workspace_size(const vqb_linear_desc* desc, int32_t n_tokens, 
 static vqb_status run_linear(const LinearGeometry& geo, const void* x, int x_dtype, int n_tokens,
                              const uint32_t* indices, int krep, int N, void* y, int y_dtype, void* workspace,
                              const vqb_options* opts, bool narrow_x_f16, bool round_f16_first, int wround,
-                             cudaStream_t stream) {
+                             bool large, cudaStream_t stream) {
   RouteWorkspace rw = carve_route_workspace(workspace, N, geo.E);
   if (cudaMemsetAsync(rw.meta, 0, sizeof(int) * 4, stream) != cudaSuccess) return VQB_CUDA_ERROR;
   const int ks = opts ? opts->k_split : 0;
   const int variant = opts ? opts->decode_variant : 0;
+  uint16_t* xbuf = reinterpret_cast<uint16_t*>(static_cast<char*>(workspace) +
+                                               route_workspace_bytes(N, geo.E, kDecodeMaxPairs));
+  if (large && variant == 0 && tc_prefill_supported(geo) && x_dtype != VQB_F32) {
+    // grouped tcgen05 GEMM: tiles of up to 256 of one expert's tokens
+    vqb_status st = launch_route_small(indices, N, geo.E, kPrefillTileTokens, rw, stream);
+    if (st != VQB_OK) return st;
+    return launch_prefill_tc(geo, x, x_dtype, krep, rw, N, xbuf, y, y_dtype, round_f16_first,
+                             /*bf16_operands=*/wround == 1, rw.meta, stream);
+  }
   if (variant == 1) {
     // one pair per CTA, the reference walk order (kept for exact-order checks)
     return launch_decode(geo, x, x_dtype, n_tokens, indices, N, krep, y, y_dtype, narrow_x_f16, round_f16_first,
@@ -144,9 +159,7 @@ static vqb_status run_linear(const LinearGeometry& geo, const void* x, int x_dty
   const int stage = opts ? opts->stage_codebook : 0;
   a.stage_codebook = stage == 1 ? 1 : (stage == 2 ? 0 : (stage == 3 ? 3 : -1));
   a.pmax = pmax;
-  uint16_t* x16 = reinterpret_cast<uint16_t*>(static_cast<char*>(workspace) +
-                                              route_workspace_bytes(N, geo.E, kDecodeMaxPairs));
-  return launch_decode_mma(geo, a, x16, n_tokens, stream);
+  return launch_decode_mma(geo, a, xbuf, n_tokens, stream);
 }
 
 vqb_status vqb_switch_forward(const vqb_linear_desc* desc, const void* x, vqb_dtype x_dtype, int32_t n_tokens,
@@ -164,10 +177,15 @@ vqb_status vqb_switch_forward(const vqb_linear_desc* desc, const void* x, vqb_dt
   if (!x || !indices || !y) return VQB_NULL_POINTER;
   if (workspace_bytes < vqb_switch_workspace_size(desc, n_tokens, top_k, opts)) return VQB_WORKSPACE_TOO_SMALL;
   if (!workspace) return VQB_NULL_POINTER;
+  // Path: the fused small-N kernel up to VQ_FUSED_MAX_N = 512 pairs, the
+  // grouped GEMM above it (vq_switch.py:45, :5313-5315).
+  const int path = opts ? opts->path : VQB_PATH_AUTO;
+  const int max_fused = (opts && opts->max_fused_pairs > 0) ? opts->max_fused_pairs : 512;
+  const bool large = path == VQB_PATH_PREFILL || (path == VQB_PATH_AUTO && N > max_fused);
   // MoE numerics: x narrowed to fp16, fp32 accumulation, fp16 output rounding
   // then the caller's dtype (vq_switch.py:5301-5308, :5423).
   return run_linear(geo, x, x_dtype, n_tokens, indices, top_k, N, y, y_dtype, workspace, opts,
-                    /*narrow_x_f16=*/true, /*round_f16_first=*/true, /*wround=*/0,
+                    /*narrow_x_f16=*/true, /*round_f16_first=*/true, /*wround=*/0, large,
                     reinterpret_cast<cudaStream_t>(stream));
 }
 
@@ -210,8 +228,11 @@ vqb_status vqb_dense_forward(const vqb_linear_desc* desc, const void* x, vqb_dty
   if (!fused && x_dtype == VQB_F32) return VQB_UNSUPPORTED_GEOMETRY;
   const int wround = fused ? 0 : (x_dtype == VQB_BF16 ? 1 : 2);
   const int n = static_cast<int>(n_rows);
+  // the grouped GEMM once the decode kernel would need more than one pass of
+  // 16 tokens over the weights
+  const bool large = path == VQB_PATH_PREFILL || (!fused && n > 16);
   return run_linear(geo, x, x_dtype, n, nullptr, 1, n, y, y_dtype, workspace, opts, /*narrow_x_f16=*/fused,
-                    /*round_f16_first=*/false, wround, reinterpret_cast<cudaStream_t>(stream));
+                    /*round_f16_first=*/false, wround, large, reinterpret_cast<cudaStream_t>(stream));
 }
 
 }  // extern "C"

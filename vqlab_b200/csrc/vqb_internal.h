@@ -64,6 +64,14 @@ size_t mma_x16_bytes(int64_t T, int IN);
 vqb_status launch_decode_mma(const LinearGeometry& geo, const GroupedDecodeArgs& a, uint16_t* x16, int T,
                              cudaStream_t stream);
 
+// Grouped tcgen05 GEMM for large token counts (vq_prefill_tc.cu).
+bool tc_prefill_supported(const LinearGeometry& geo);
+size_t tc_prefill_x_bytes(int64_t N, int IN);
+vqb_status launch_prefill_tc(const LinearGeometry& geo, const void* x, int x_dtype, int krep, const RouteWorkspace& rw,
+                             int N, uint16_t* xs, void* y, int y_dtype, bool round_f16_first, bool bf16_operands,
+                             int* status, cudaStream_t stream);
+constexpr int kPrefillTileTokens = 256;
+
 // Tokens that share one pass over an expert's rows (one MMA n-tile holds 8).
 inline int decode_pairs_per_chunk(int N, int E, int K, int D, int IN, int override_pairs) {
   int pm;
