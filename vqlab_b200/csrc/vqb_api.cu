@@ -58,62 +58,19 @@ vqb_status validate(const vqb_linear_desc* d, LinearGeometry* g) {
 static bool dtype_ok(int t) { return t == VQB_F16 || t == VQB_BF16 || t == VQB_F32; }
 
 
-}  // namespace vqb
-
-using namespace vqb;
-
-extern "C" {
-
-const char* vqb_version(void) { return "vqb200 0.1 sm_100a"; }
-
-const char* vqb_status_string(vqb_status s) {
-  switch (s) {
-    case VQB_OK: return "ok";
-    case VQB_BAD_SHAPE: return "inconsistent tensor shapes for a VQ projection";
-    case VQB_BAD_WPR: return "packed codes row width does not match ceil(NSUB/32)*BITS";
-    case VQB_UNSUPPORTED_GEOMETRY: return "unsupported VQ geometry (D must be 2, 4 or 8; BITS <= 16)";
-    case VQB_CODEBOOK_SHARDED: return "VQ codebook was sharded: K differs from the K the module was built with";
-    case VQB_CUDA_ERROR: return "CUDA launch or runtime error";
-    case VQB_TIMEOUT: return "a bounded device wait timed out";
-    case VQB_BAD_ROUTING: return "an expert index was out of range";
-    case VQB_WORKSPACE_TOO_SMALL: return "workspace too small";
-    case VQB_BAD_ALIGNMENT: return "misaligned tensor pointer";
-    case VQB_NULL_POINTER: return "null tensor pointer";
-  }
-  return "unknown status";
-}
-
-vqb_status vqb_unpack(const uint32_t* packed, int64_t rows, int64_t wpr, int32_t nsub, int32_t bits, uint16_t* out,
-                      vqb_stream_t stream) {
-  if (!packed || !out) return VQB_NULL_POINTER;
-  if (bits < 1 || bits > 16 || nsub < 0 || rows < 0) return VQB_UNSUPPORTED_GEOMETRY;
-  if (wpr != (int64_t(nsub) + 31) / 32 * bits) return VQB_BAD_WPR;
-  return launch_unpack(packed, rows, wpr, nsub, bits, out, reinterpret_cast<cudaStream_t>(stream));
-}
-
 // Workspace: [routing (status block first)][x as 16-bit rows: the token rows
 // for the decode kernel's B operand, or all pairs' rows in expert order for
 // the grouped GEMM -- whichever is larger]
-static size_t x_region_bytes(int N, int64_t T, int IN) {
+size_t x_region_bytes(int N, int64_t T, int IN) {
   const size_t a = mma_x16_bytes(T, IN), b = tc_prefill_x_bytes(N, IN);
   return a > b ? a : b;
 }
-static size_t linear_workspace_bytes(int N, int E, int64_t T, int IN) {
+size_t linear_workspace_bytes(int N, int E, int64_t T, int IN) {
   return route_workspace_bytes(N, E, kDecodeMaxPairs) + x_region_bytes(N, T, IN);
 }
 
-size_t vqb_switch_workspace_size(const vqb_linear_desc* desc, int32_t n_tokens, int32_t top_k,
-                                 const vqb_options* opts) {
-  (void)opts;
-  const int64_t T = n_tokens > 0 ? n_tokens : 0;
-  const int64_t N = T * (top_k > 0 ? top_k : 1);
-  const int E = desc ? (desc->num_experts > 0 ? desc->num_experts : 1) : 1;
-  const int IN = desc ? (desc->in_features > 0 ? desc->in_features : 0) : 0;
-  return linear_workspace_bytes(static_cast<int>(N), E, T, IN);
-}
-
 // Shared body of the switch and dense entry points once shapes are valid.
-static vqb_status run_linear(const LinearGeometry& geo, const void* x, int x_dtype, int n_tokens,
+vqb_status run_linear(const LinearGeometry& geo, const void* x, int x_dtype, int n_tokens,
                              const uint32_t* indices, int krep, int N, void* y, int y_dtype, void* workspace,
                              const vqb_options* opts, bool narrow_x_f16, bool round_f16_first, int wround,
                              bool large, cudaStream_t stream) {
@@ -160,6 +117,49 @@ static vqb_status run_linear(const LinearGeometry& geo, const void* x, int x_dty
   a.stage_codebook = stage == 1 ? 1 : (stage == 2 ? 0 : (stage == 3 ? 3 : -1));
   a.pmax = pmax;
   return launch_decode_mma(geo, a, xbuf, n_tokens, stream);
+}
+
+}  // namespace vqb
+
+using namespace vqb;
+
+extern "C" {
+
+const char* vqb_version(void) { return "vqb200 0.1 sm_100a"; }
+
+const char* vqb_status_string(vqb_status s) {
+  switch (s) {
+    case VQB_OK: return "ok";
+    case VQB_BAD_SHAPE: return "inconsistent tensor shapes for a VQ projection";
+    case VQB_BAD_WPR: return "packed codes row width does not match ceil(NSUB/32)*BITS";
+    case VQB_UNSUPPORTED_GEOMETRY: return "unsupported VQ geometry (D must be 2, 4 or 8; BITS <= 16)";
+    case VQB_CODEBOOK_SHARDED: return "VQ codebook was sharded: K differs from the K the module was built with";
+    case VQB_CUDA_ERROR: return "CUDA launch or runtime error";
+    case VQB_TIMEOUT: return "a bounded device wait timed out";
+    case VQB_BAD_ROUTING: return "an expert index was out of range";
+    case VQB_WORKSPACE_TOO_SMALL: return "workspace too small";
+    case VQB_BAD_ALIGNMENT: return "misaligned tensor pointer";
+    case VQB_NULL_POINTER: return "null tensor pointer";
+  }
+  return "unknown status";
+}
+
+vqb_status vqb_unpack(const uint32_t* packed, int64_t rows, int64_t wpr, int32_t nsub, int32_t bits, uint16_t* out,
+                      vqb_stream_t stream) {
+  if (!packed || !out) return VQB_NULL_POINTER;
+  if (bits < 1 || bits > 16 || nsub < 0 || rows < 0) return VQB_UNSUPPORTED_GEOMETRY;
+  if (wpr != (int64_t(nsub) + 31) / 32 * bits) return VQB_BAD_WPR;
+  return launch_unpack(packed, rows, wpr, nsub, bits, out, reinterpret_cast<cudaStream_t>(stream));
+}
+
+size_t vqb_switch_workspace_size(const vqb_linear_desc* desc, int32_t n_tokens, int32_t top_k,
+                                 const vqb_options* opts) {
+  (void)opts;
+  const int64_t T = n_tokens > 0 ? n_tokens : 0;
+  const int64_t N = T * (top_k > 0 ? top_k : 1);
+  const int E = desc ? (desc->num_experts > 0 ? desc->num_experts : 1) : 1;
+  const int IN = desc ? (desc->in_features > 0 ? desc->in_features : 0) : 0;
+  return linear_workspace_bytes(static_cast<int>(N), E, T, IN);
 }
 
 vqb_status vqb_switch_forward(const vqb_linear_desc* desc, const void* x, vqb_dtype x_dtype, int32_t n_tokens,

@@ -72,6 +72,12 @@ vqb_status launch_prefill_tc(const LinearGeometry& geo, const void* x, int x_dty
                              int* status, cudaStream_t stream);
 constexpr int kPrefillTileTokens = 256;
 
+// Workspace layout and the shared body of the switch / dense entry points (vqb_api.cu).
+size_t linear_workspace_bytes(int N, int E, int64_t T, int IN);
+vqb_status run_linear(const LinearGeometry& geo, const void* x, int x_dtype, int n_tokens, const uint32_t* indices,
+                      int krep, int N, void* y, int y_dtype, void* workspace, const vqb_options* opts,
+                      bool narrow_x_f16, bool round_f16_first, int wround, bool large, cudaStream_t stream);
+
 // Tokens that share one pass over an expert's rows (one MMA n-tile holds 8).
 inline int decode_pairs_per_chunk(int N, int E, int K, int D, int IN, int override_pairs) {
   int pm;
