@@ -116,6 +116,27 @@ vqb_status vqb_switch_forward(const vqb_linear_desc* desc, const void* x, vqb_dt
                               void* y, vqb_dtype y_dtype, void* workspace, size_t workspace_bytes,
                               const vqb_options* opts, vqb_stream_t stream);
 
+/* vqb_switch_forward without a workspace argument: the call allocates
+ * nothing and takes its scratch from an 8 MiB array inside the library's
+ * device image.  No counterpart in the reference (its runtime allocates
+ * through MLX).  For callers that cannot hand the library device memory:
+ * a host program that reaches the GPU only through this ABI and has no
+ * device allocator, or a serving loop that allows no allocation after
+ * start-up.  Limits:
+ *   - scratch = routing tables for n_tokens*top_k pairs + n_tokens*in_features
+ *     fp16 values must fit in 8 MiB, else VQB_WORKSPACE_TOO_SMALL;
+ *   - it always runs the decode (small-N) kernel;
+ *   - the array is one per GPU and is reused by every call: calls that
+ *     overlap on the GPU race on it and must be serialized by the caller;
+ *   - the first call on a device looks the array's address up (once per
+ *     device, that device current); make it before any stream capture.
+ * The status block (int32 [1] = VQB_BAD_ROUTING on a bad expert index) sits
+ * at the start of that array and is not readable through this ABI. */
+vqb_status vqb_switch_forward_static(const vqb_linear_desc* desc, const void* x, vqb_dtype x_dtype,
+                                     int32_t n_tokens, const uint32_t* indices, int32_t top_k,
+                                     void* y, vqb_dtype y_dtype, const vqb_options* opts,
+                                     vqb_stream_t stream);
+
 /* Scratch bytes vqb_dense_forward needs for n_rows input rows. */
 size_t vqb_dense_workspace_size(const vqb_linear_desc* desc, int64_t n_rows, const vqb_options* opts);
 

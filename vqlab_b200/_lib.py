@@ -87,6 +87,8 @@ def _bind(L):
     L.vqb_dense_workspace_size.argtypes = [P, i64, P]
     L.vqb_dense_forward.restype = i32
     L.vqb_dense_forward.argtypes = [P, P, i32, i64, P, i32, P, sz, P, P]
+    L.vqb_switch_forward_static.restype = i32
+    L.vqb_switch_forward_static.argtypes = [P, P, i32, i32, P, i32, P, i32, P, P]
     return L
 
 
@@ -130,4 +132,4 @@ def version() -> str:
 def exported_symbols():
     """Names of every function include/vqb.h declares (for the load test)."""
     return ["vqb_version", "vqb_status_string", "vqb_unpack", "vqb_switch_workspace_size",
-            "vqb_switch_forward", "vqb_dense_workspace_size", "vqb_dense_forward"]
+            "vqb_switch_forward", "vqb_dense_workspace_size", "vqb_dense_forward", "vqb_switch_forward_static"]
