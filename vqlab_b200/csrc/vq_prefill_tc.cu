@@ -41,7 +41,7 @@ constexpr int kTileM = 128;
 constexpr int kChunkK = 64;          // K per pipeline stage (one 128-byte swizzle row of fp16)
 constexpr int kMaxN = 256;           // tokens per tile
 constexpr int kBStages = 3;
-constexpr int kAStages = 2;
+constexpr int kAStages = 4;         // two chunks decoded per iteration, double-buffered
 constexpr int kThreads = 256;        // warp 0: TMA + TMEM alloc, warp 1: MMA, warps 4-7: decode + epilogue
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kSpinLimit = 1u << 26;
@@ -174,7 +174,7 @@ __device__ __forceinline__ uint32_t make_idesc(int n, bool bf16) {
 // -------------------------------------------------------------- the kernel
 
 template <int D>
-__device__ __forceinline__ void decode_chunk(const TParams& prm, const uint16_t* cb_s, BitWalker<true>& wk,
+__device__ __forceinline__ void decode_chunk(const TParams& prm, const uint16_t* cb_s, PrefetchWalker& wk,
                                              uint32_t mask, __half2 s2, uint32_t* out) {
   // 64 k of one row -> 32 fp16x2 words, W = fp16(cb * s)
   constexpr int CODES = kChunkK / D;
@@ -342,20 +342,27 @@ __global__ void __launch_bounds__(kThreads, 1) vq_prefill_tc_kernel(const __grid
       const uint32_t* row = prm.codes + static_cast<int64_t>(e) * prm.expert_words +
                             static_cast<int64_t>(rr) * prm.row_words;
       const uint16_t* srow = prm.scales + (static_cast<int64_t>(e) * prm.OUT + rr) * prm.NGRP;
-      BitWalker<true> wk;
-      wk.init(row, 0);
+      PrefetchWalker wk;
+      wk.init(row, prm.row_words);
       bool ok = true;
-      for (int kc = 0; kc < n_k; ++kc) {
-        uint32_t w[32];
-        const __half s = __ushort_as_half(__ldg(srow + (kc * kChunkK) / prm.G));
-        decode_chunk<D>(prm, cb_s, wk, mask, __halves2half2(s, s), w);
-        if (!mbar_wait(&a_empty[astage], aphase ^ 1u, abort_flag)) { ok = false; break; }
-        tc_fence_after();
-        tc_st_x32(tmem_a + lane_off + astage * 32, w);
-        tc_wait_st();
-        tc_fence_before();
-        mbar_arrive(&a_full[astage]);
-        if (++astage == kAStages) { astage = 0; aphase ^= 1u; }
+      // two chunks per iteration: both chunks' lookups are in flight together
+      for (int kc = 0; kc < n_k; kc += 2) {
+        const bool two = kc + 1 < n_k;
+        uint32_t w0[32], w1[32];
+        const __half s0 = __ushort_as_half(__ldg(srow + (kc * kChunkK) / prm.G));
+        const __half s1 = two ? __ushort_as_half(__ldg(srow + ((kc + 1) * kChunkK) / prm.G)) : s0;
+        decode_chunk<D>(prm, cb_s, wk, mask, __halves2half2(s0, s0), w0);
+        if (two) decode_chunk<D>(prm, cb_s, wk, mask, __halves2half2(s1, s1), w1);
+        for (int h = 0; h < (two ? 2 : 1); ++h) {
+          if (!mbar_wait(&a_empty[astage], aphase ^ 1u, abort_flag)) { ok = false; break; }
+          tc_fence_after();
+          tc_st_x32(tmem_a + lane_off + astage * 32, h == 0 ? w0 : w1);
+          tc_wait_st();
+          tc_fence_before();
+          mbar_arrive(&a_full[astage]);
+          if (++astage == kAStages) { astage = 0; aphase ^= 1u; }
+        }
+        if (!ok) break;
       }
       if (!ok) break;
       // epilogue: D columns [0, n) of this lane's row

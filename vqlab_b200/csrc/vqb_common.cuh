@@ -118,4 +118,54 @@ struct BitWalker {
   }
 };
 
+// BitWalker with one 16-byte load in flight ahead of the one being consumed,
+// so a long sequential walk never waits on a load it could have issued
+// earlier.  Rows must be 16-byte aligned with a multiple of 4 words; loads
+// past the row's end are not issued (they read as zero).
+struct PrefetchWalker {
+  const uint4* p;     // next chunk to request
+  const uint4* end;   // one past the row's last chunk
+  uint4 cur, nxt;
+  int qi;             // next word of cur
+  uint64_t buf;
+  int nb;
+
+  __device__ __forceinline__ uint4 fetch() {
+    uint4 v = make_uint4(0, 0, 0, 0);
+    if (p < end) v = ldg_stream_v4(p);
+    ++p;
+    return v;
+  }
+  __device__ __forceinline__ uint32_t next_word() {
+    if (qi == 4) {
+      cur = nxt;
+      nxt = fetch();
+      qi = 0;
+    }
+    const uint32_t w = qi == 0 ? cur.x : (qi == 1 ? cur.y : (qi == 2 ? cur.z : cur.w));
+    ++qi;
+    return w;
+  }
+  // start at word 0 of a row of `row_words` words (a multiple of 4)
+  __device__ __forceinline__ void init(const uint32_t* row, int row_words) {
+    p = reinterpret_cast<const uint4*>(row);
+    end = p + row_words / 4;
+    cur = fetch();
+    nxt = fetch();
+    qi = 0;
+    buf = next_word();
+    nb = 32;
+  }
+  __device__ __forceinline__ uint32_t next(int bits, uint32_t mask) {
+    if (nb < bits) {
+      buf |= static_cast<uint64_t>(next_word()) << nb;
+      nb += 32;
+    }
+    const uint32_t c = static_cast<uint32_t>(buf) & mask;
+    buf >>= bits;
+    nb -= bits;
+    return c;
+  }
+};
+
 }  // namespace vqb
