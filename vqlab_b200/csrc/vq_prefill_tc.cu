@@ -1,25 +1,35 @@
 // Grouped VQ GEMM for large token counts on the 5th-generation tensor cores
 // (sm_100a: tcgen05.mma with the accumulator and the A operand in tensor
-// memory, B staged by TMA).  The B200 counterpart of the reference's
-// segmented, count-sorted prefill GEMM (gemmseg2, vq_switch.py:3687-4310,
-// dispatched by _gemmseg_prefill :4569-4722) and of the dense large-N path
-// (_decode_matmul, vq_dense.py:267-312).
+// memory, B and the code stream staged by TMA).  The B200 counterpart of the
+// reference's segmented, count-sorted prefill GEMM (gemmseg2,
+// vq_switch.py:3687-4310, dispatched by _gemmseg_prefill :4569-4722) and of
+// the dense large-N path (_decode_matmul, vq_dense.py:267-312).
 //
 // Work: pairs are sorted by expert and x is gathered into that order (fp16,
-// or bf16 for the dense bf16 arm); a tile is (expert e, 128 output rows,
-// up to 256 of e's tokens).  Per tile and K chunk of 64:
-//   * 4 decode warps (thread = output row = TMEM lane) walk their row's packed
-//     code stream, look each code up in the codebook (shared-memory prefix,
-//     rest through L1), scale it -- W = fp16(cb * s), one RNE rounding -- and
-//     store the 64 weights of the chunk into a TMEM A buffer (tcgen05.st);
-//   * a TMA warp loads the 64-wide token tile of x into shared memory
-//     (128-byte swizzle, the canonical K-major UMMA layout);
+// or bf16 for the dense bf16 arm).  A tile is (expert e, 128 output rows, up
+// to 128 of e's tokens); a CTA runs tiles one after another (persistent grid,
+// one CTA per SM).  Per tile and K chunk of 64:
+//   * 16 decode warps in 4 sets: set s decodes chunk s of every window of 4
+//     chunks.  In a set, thread = output row = TMEM lane; it extracts the
+//     chunk's codes from the window of packed rows a TMA warp staged in
+//     shared memory, looks each one up in the shared-memory codebook, scales
+//     it -- W = fp16(cb * s), one RNE rounding -- and stores the 64 weights of
+//     its row into a TMEM A stage (tcgen05.st);
+//   * a TMA warp loads the tile's tokens x[:, chunk] (boxes of 32 rows, only
+//     as many as the tile has tokens; 128-byte swizzle, the canonical K-major
+//     UMMA layout);
 //   * one elected thread of the MMA warp issues four tcgen05.mma (K = 16 each)
 //     D[128 x N] += A_tmem[128 x 16] . B_smem[16 x N] and commits to the
 //     barriers that free the A and B buffers.
-// After the last chunk the decode warps read D from TMEM (tcgen05.ld) and
-// store y[pair, row] with the output rounding.  N is the tile's real token
-// count rounded up to 16, so small experts cost only their own columns.
+// Codebooks larger than the shared-memory slice (d8/K16384 is 256 KB) run in
+// passes: pass h keeps entries [h*KP, (h+1)*KP) resident (a bulk copy by a
+// loader warp), codes outside the slice contribute zero weights, and the
+// accumulator collects every pass -- each weight is non-zero in exactly one
+// pass, so the product sum is the single-pass one in another order.  Every
+// lookup is a shared-memory read.  Consecutive tiles walk the slices in
+// alternating order so one reload serves two passes.
+// Two TMEM accumulators let the epilogue of one tile (tcgen05.ld, y[pair, row]
+// with the output rounding) overlap the next tile's MMAs.
 //
 // Numerics: the weights take one fp16 rounding of cb*s (the reference's
 // non-ACCS / dense arms round the same product; its ACCS arm applies s to
@@ -27,7 +37,8 @@
 // bf16(fp16(cb*s)) weights (dense bf16, vq_dense.py:294), accumulation fp32.
 //
 // Every mbarrier wait is bounded: on expiry the CTA records VQB_TIMEOUT in
-// the status word, stops issuing, frees its tensor memory and returns.
+// the status word, stops issuing, waits for its copies in flight, frees its
+// tensor memory and returns.
 #include <cuda.h>
 
 #include "vqb_common.cuh"
@@ -38,31 +49,52 @@ namespace vqb {
 namespace {
 
 constexpr int kTileM = 128;
-constexpr int kChunkK = 64;          // K per pipeline stage (one 128-byte swizzle row of fp16)
-constexpr int kMaxN = 256;           // tokens per tile
-constexpr int kBStages = 3;
-constexpr int kAStages = 4;         // two chunks decoded per iteration, double-buffered
-constexpr int kThreads = 256;        // warp 0: TMA + TMEM alloc, warp 1: MMA, warps 4-7: decode + epilogue
+constexpr int kChunkK = 64;                          // K per A stage (one 128-byte swizzle row of fp16)
+constexpr int kMaxN = kPrefillTileTokens;            // tokens per tile
+constexpr int kBoxRows = 32;                         // x rows per TMA box
+constexpr int kBStageBytes = kMaxN * kChunkK * 2;    // 16 KB
+constexpr int kBStages = 4;                          // position g -> B stage g % 4
+constexpr int kAStages = 8;                          // position g -> A stage g % 8 (two per decode set)
+constexpr int kWStages = 2;                          // code/scale windows
+constexpr int kSets = 4;                             // window = kSets chunks, one per set
+constexpr int kIssuers = 2;                          // MMA issuing threads, one accumulator each
+constexpr int kDecodeWarps = 4 * kSets;              // 4 TMEM lane quarters per set
+// warp roles (a warp reaches TMEM lanes 32 * (warp % 4) ...; the issuers sit on different SM sub-partitions)
+constexpr int kWarpTmaX = 0, kWarpMma0 = 1, kWarpTmaCode = 2, kWarpMma1 = 3, kWarpCbLoad = 4;
+constexpr int kFirstDecodeWarp = 5;
+constexpr int kThreads = (kFirstDecodeWarp + kDecodeWarps) * 32;
 constexpr uint32_t kTmemCols = 512;
+constexpr uint32_t kTmemA = kIssuers * kMaxN;        // columns: [0,128) D0, [128,256) D1, then 8 A stages of 32
 constexpr uint32_t kSpinLimit = 1u << 26;
+constexpr int kScaleRowBytes = 16;                   // 8 fp16 scales per row per window
+constexpr int kNumBars = kBStages + 2 * kAStages + 2 * kWStages + 2 + kIssuers + 1 + kIssuers;
 
 struct TParams {
   const uint32_t* codes;
   const uint16_t* codebook;
   const uint16_t* scales;
   const int* sorted;       // pair ids grouped by expert
-  const int4* chunks;      // (expert, first sorted slot, tokens <= 256, 0)
+  const int4* chunks;      // (expert, first sorted slot, tokens <= 128, 0)
   const int* meta;         // [0] chunk count
   int* status;             // [1] <- VQB_TIMEOUT on a bounded-wait expiry
   void* y;
-  int64_t expert_words;
-  int row_words;
-  int OUT, IN, G, NGRP, bits;
-  int ns;                  // codebook entries staged in shared memory
+  int OUT, IN, G, NGRP, bits, K;
+  int n_k;                 // real K chunks (IN / 64)
+  int n_pos;               // A stages per tile per pass (n_k rounded up to whole windows)
   int row_tiles;
   int y_dtype;
   int round_f16_first;
   int b_bf16;              // B (x) and A are bf16 (dense bf16 arm)
+  int W;                   // code window pitch in words (W / 4 odd: conflict-free 16-byte reads)
+  int wpw;                 // code words per window of the packed row
+  int code_stage_bytes;
+  int win_stage_bytes;
+  int scale_tma;           // scales staged with the codes (else read from global)
+  int log2g;
+  int kp_log2;             // codebook entries per pass = 1 << kp_log2 (npass > 1)
+  int kp;
+  int npass;
+  int off_win, off_cb, off_bar;
 };
 
 // ------------------------------------------------------------ PTX helpers
@@ -87,7 +119,7 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
                : "=r"(ok) : "r"(smem_u32(bar)), "r"(parity) : "memory");
   return ok != 0;
 }
-// bounded wait: false when the limit expired (the caller aborts)
+// bounded wait: false when the limit expired or another role aborted
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag) {
   for (uint32_t i = 0; i < kSpinLimit; ++i) {
     if (mbar_try_wait(bar, parity)) return true;
@@ -96,11 +128,26 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
   *abort_flag = 1;
   return false;
 }
+// the same for a whole warp: every lane waits, the warp agrees on the outcome
+__device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag) {
+  return __all_sync(0xffffffffu, mbar_wait(bar, parity, abort_flag)) != 0;
+}
+// bounded drain used at teardown (no abort check: a copy in flight must land)
+__device__ __forceinline__ void mbar_drain(uint64_t* bar, uint32_t parity) {
+  for (uint32_t i = 0; i < kSpinLimit && !mbar_try_wait(bar, parity); ++i) {
+  }
+}
 
 __device__ __forceinline__ void tma_load_2d(const CUtensorMap* map, uint64_t* bar, void* dst, int x, int y) {
   asm volatile(
       "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];"
       :: "r"(smem_u32(dst)), "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(x), "r"(y) : "memory");
+}
+// plain (non-tensor) bulk copy global -> shared; 16-byte aligned, size % 16 == 0
+__device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+      :: "r"(smem_u32(dst)), "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(smem_u32(bar)) : "memory");
 }
 
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
@@ -171,36 +218,111 @@ __device__ __forceinline__ uint32_t make_idesc(int n, bool bf16) {
   return d;
 }
 
-// -------------------------------------------------------------- the kernel
+// Codebook slice a tile-pass reads: consecutive tiles of a CTA walk the
+// slices in alternating order, so the slice resident at the end of one tile is
+// the first one the next tile uses.
+__device__ __forceinline__ int pass_slice(int npass, int tile_local, int pass) {
+  return npass == 1 ? 0 : ((tile_local & 1) ? npass - 1 - pass : pass);
+}
 
+// ------------------------------------------------------------ decode side
+
+// Look one code up in the shared-memory codebook slice.  With several passes
+// a code outside the resident slice yields a zero weight; with one pass the
+// index is clamped to the table so a corrupt code cannot read past it.
 template <int D>
-__device__ __forceinline__ void decode_chunk(const TParams& prm, const uint16_t* cb_s, PrefetchWalker& wk,
-                                             uint32_t mask, __half2 s2, uint32_t* out) {
-  // 64 k of one row -> 32 fp16x2 words, W = fp16(cb * s)
-  constexpr int CODES = kChunkK / D;
-  constexpr int WPC = D / 2;
-  uint32_t c[CODES];
+__device__ __forceinline__ void lookup(const uint16_t* cb_s, uint32_t c, bool masked, int kp_log2, int h,
+                                      uint32_t kmax, uint32_t* out) {
+  bool hit = true;
+  uint32_t li;
+  if (masked) {
+    hit = static_cast<int>(c >> kp_log2) == h;
+    li = c & ((1u << kp_log2) - 1u);
+  } else {
+    li = min(c, kmax);
+  }
+  if constexpr (D == 8) {
+    uint4 v = make_uint4(0, 0, 0, 0);
+    if (hit) v = reinterpret_cast<const uint4*>(cb_s)[li];
+    out[0] = v.x; out[1] = v.y; out[2] = v.z; out[3] = v.w;
+  } else if constexpr (D == 4) {
+    uint2 v = make_uint2(0, 0);
+    if (hit) v = reinterpret_cast<const uint2*>(cb_s)[li];
+    out[0] = v.x; out[1] = v.y;
+  } else {
+    uint32_t v = 0;
+    if (hit) v = reinterpret_cast<const uint32_t*>(cb_s)[li];
+    out[0] = v;
+  }
+}
+
+// One row's 64 weights of one chunk -> 32 fp16x2 (or bf16x2) words.
+// crow: the row in the staged code window (16-byte aligned, pitch W words);
+// b0: bit offset of the chunk's first code in it (the same for every row).
+// BITS > 0: the code width is a compile-time constant -- the chunk's bits are
+// read with conflict-free 16-byte loads, aligned to bit 0 with a funnel
+// shift, and every code sits at a fixed bit position.  BITS == 0: any width,
+// a sequential bit walk.
+template <int D, int BITS>
+__device__ __forceinline__ void decode_chunk(const TParams& prm, const uint16_t* cb_s, const uint32_t* crow, int b0,
+                                             __half2 s2, int h, uint32_t* out) {
+  constexpr int CPC = kChunkK / D;   // codes per chunk
+  constexpr int WPC = D / 2;         // output words per code
+  const bool masked = prm.npass > 1;
+  const uint32_t kmax = static_cast<uint32_t>(prm.K - 1);
+  if constexpr (BITS > 0) {
+    constexpr uint32_t MASK = (1u << BITS) - 1u;
+    constexpr int NB = CPC * BITS;             // bits of the chunk
+    constexpr int NW = (NB + 31) / 32 + 1;     // words holding them after word alignment (+ straddle)
+    constexpr int NQ = (NW + 3 + 3) / 4;       // 16-byte loads that cover a start anywhere in a 16-byte unit
+    const int w0 = b0 >> 5, sh = b0 & 31, dw = w0 & 3;
+    const uint4* src = reinterpret_cast<const uint4*>(crow) + (w0 >> 2);
+    uint32_t q[4 * NQ];
 #pragma unroll
-  for (int i = 0; i < CODES; ++i) c[i] = wk.next(prm.bits, mask);
+    for (int i = 0; i < NQ; ++i) {
+      const uint4 v = src[i];
+      q[4 * i] = v.x; q[4 * i + 1] = v.y; q[4 * i + 2] = v.z; q[4 * i + 3] = v.w;
+    }
+    // drop the dw leading words (dw is the same for the whole warp)
+    uint32_t t[4 * NQ - 2];
 #pragma unroll
-  for (int i = 0; i < CODES; ++i) {
-    if constexpr (D == 8) {
-      const uint4 v = c[i] < static_cast<uint32_t>(prm.ns) ? reinterpret_cast<const uint4*>(cb_s)[c[i]]
-                                                           : __ldg(reinterpret_cast<const uint4*>(prm.codebook) + c[i]);
-      out[WPC * i] = v.x; out[WPC * i + 1] = v.y; out[WPC * i + 2] = v.z; out[WPC * i + 3] = v.w;
-    } else if constexpr (D == 4) {
-      const uint2 v = c[i] < static_cast<uint32_t>(prm.ns) ? reinterpret_cast<const uint2*>(cb_s)[c[i]]
-                                                           : __ldg(reinterpret_cast<const uint2*>(prm.codebook) + c[i]);
-      out[WPC * i] = v.x; out[WPC * i + 1] = v.y;
-    } else {
-      out[i] = c[i] < static_cast<uint32_t>(prm.ns) ? reinterpret_cast<const uint32_t*>(cb_s)[c[i]]
-                                                    : __ldg(reinterpret_cast<const uint32_t*>(prm.codebook) + c[i]);
+    for (int i = 0; i < 4 * NQ - 2; ++i) t[i] = (dw & 2) ? q[i + 2] : q[i];
+    uint32_t r[NW];
+#pragma unroll
+    for (int i = 0; i < NW; ++i) r[i] = (dw & 1) ? t[i + 1] : t[i];
+    uint32_t n[NW - 1];
+#pragma unroll
+    for (int i = 0; i < NW - 1; ++i) n[i] = __funnelshift_r(r[i], r[i + 1], sh);
+#pragma unroll
+    for (int i = 0; i < CPC; ++i) {
+      constexpr int dummy = 0;
+      (void)dummy;
+      const int bit = i * BITS, wi = bit >> 5, bs = bit & 31;
+      const uint32_t v = (bs + BITS <= 32) ? (n[wi] >> bs) : __funnelshift_r(n[wi], n[wi + 1], bs);
+      lookup<D>(cb_s, v & MASK, masked, prm.kp_log2, h, kmax, out + WPC * i);
+    }
+  } else {
+    const int bits = prm.bits;
+    const uint32_t mask = (1u << bits) - 1u;
+    const uint32_t* p = crow + (b0 >> 5);
+    uint64_t buf = static_cast<uint64_t>(*p++) >> (b0 & 31);
+    int nb = 32 - (b0 & 31);
+#pragma unroll 8
+    for (int i = 0; i < CPC; ++i) {
+      if (nb < bits) {
+        buf |= static_cast<uint64_t>(*p++) << nb;
+        nb += 32;
+      }
+      const uint32_t c = static_cast<uint32_t>(buf) & mask;
+      buf >>= bits;
+      nb -= bits;
+      lookup<D>(cb_s, c, masked, prm.kp_log2, h, kmax, out + WPC * i);
     }
   }
 #pragma unroll
   for (int i = 0; i < 32; ++i) {
-    __half2 h = __hmul2(*reinterpret_cast<__half2*>(&out[i]), s2);
-    out[i] = *reinterpret_cast<uint32_t*>(&h);
+    __half2 v = __hmul2(*reinterpret_cast<__half2*>(&out[i]), s2);
+    out[i] = *reinterpret_cast<uint32_t*>(&v);
   }
   if (prm.b_bf16) {
 #pragma unroll
@@ -212,33 +334,44 @@ __device__ __forceinline__ void decode_chunk(const TParams& prm, const uint16_t*
   }
 }
 
-template <int D>
-__global__ void __launch_bounds__(kThreads, 1) vq_prefill_tc_kernel(const __grid_constant__ CUtensorMap xmap,
-                                                                  const TParams prm) {
+// -------------------------------------------------------------- the kernel
+
+template <int D, int BITS>
+__global__ void __launch_bounds__(kThreads, 1)
+    vq_prefill_tc_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_constant__ CUtensorMap cmap,
+                         const __grid_constant__ CUtensorMap smap, const TParams prm) {
   extern __shared__ __align__(16) unsigned char smem_dyn[];
-  // layout: [B stages (1024-aligned: the 128-byte swizzle atom)][codebook prefix][barriers][tmem addr][flags]
-  unsigned char* smem_raw = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_dyn) + 1023) & ~uintptr_t(1023));
-  const size_t b_stage_bytes = static_cast<size_t>(kMaxN) * kChunkK * 2;  // 32 KB
-  unsigned char* b_base = smem_raw;
-  uint16_t* cb_s = reinterpret_cast<uint16_t*>(smem_raw + kBStages * b_stage_bytes);
-  const size_t cb_bytes = (static_cast<size_t>(prm.ns) * D * 2 + 15) & ~size_t(15);
-  uint64_t* bars = reinterpret_cast<uint64_t*>(reinterpret_cast<unsigned char*>(cb_s) + ((cb_bytes + 7) & ~size_t(7)));
-  uint64_t* b_full = bars;                      // [kBStages]
-  uint64_t* b_empty = bars + kBStages;          // [kBStages]
-  uint64_t* a_full = bars + 2 * kBStages;       // [kAStages]
-  uint64_t* a_empty = a_full + kAStages;        // [kAStages]
-  uint64_t* acc_full = a_empty + kAStages;      // [1]
-  uint64_t* mma_done = acc_full + 1;            // [1] teardown: every issued MMA has completed
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_done + 1);
+  // [B stages][2 code/scale windows][codebook slice][barriers][tmem addr][flag]; 1024-aligned (swizzle atom)
+  // (pointer arithmetic on the shared array keeps the compiler's knowledge
+  // that every access below is a shared-memory access)
+  unsigned char* base = smem_dyn + ((1024u - (smem_u32(smem_dyn) & 1023u)) & 1023u);
+  unsigned char* b_base = base;
+  unsigned char* w_base = base + prm.off_win;
+  uint16_t* cb_s = reinterpret_cast<uint16_t*>(base + prm.off_cb);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(base + prm.off_bar);
+  uint64_t* b_full = bars;                         // [kBStages] x tile landed
+  uint64_t* a_full = b_full + kBStages;            // [kAStages] the 4 warps of a set stored it
+  uint64_t* st_free = a_full + kAStages;           // [kAStages] MMAs of position g done: A stage g%8, B stage g%4 free
+  uint64_t* w_full = st_free + kAStages;           // [kWStages] code/scale window landed
+  uint64_t* w_empty = w_full + kWStages;           // [kWStages] all 16 decode warps read it
+  uint64_t* cb_full = w_empty + kWStages;          // [1] codebook slice landed
+  uint64_t* cb_empty = cb_full + 1;                // [1] all decode warps done with the slice
+  uint64_t* acc_full = cb_empty + 1;               // [kIssuers] issuer i's accumulator complete
+  uint64_t* acc_empty = acc_full + kIssuers;       // [1] epilogue read both accumulators
+  uint64_t* mma_done = acc_empty + 1;              // [kIssuers] teardown: every issued MMA completed
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + kNumBars);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
   if (threadIdx.x == 0) {
-    for (int i = 0; i < kBStages; ++i) { mbar_init(&b_full[i], 1); mbar_init(&b_empty[i], 1); }
-    for (int i = 0; i < kAStages; ++i) { mbar_init(&a_full[i], 128); mbar_init(&a_empty[i], 1); }
-    mbar_init(acc_full, 1);
-    mbar_init(mma_done, 1);
+    for (int i = 0; i < kBStages; ++i) mbar_init(&b_full[i], 1);
+    for (int i = 0; i < kAStages; ++i) { mbar_init(&a_full[i], 4); mbar_init(&st_free[i], 1); }
+    for (int i = 0; i < kWStages; ++i) { mbar_init(&w_full[i], 1); mbar_init(&w_empty[i], kDecodeWarps); }
+    mbar_init(cb_full, 1);
+    mbar_init(cb_empty, kDecodeWarps);
+    for (int i = 0; i < kIssuers; ++i) { mbar_init(&acc_full[i], 1); mbar_init(&mma_done[i], 1); }
+    mbar_init(acc_empty, kDecodeWarps);
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
@@ -247,145 +380,246 @@ __global__ void __launch_bounds__(kThreads, 1) vq_prefill_tc_kernel(const __grid
                  :: "r"(smem_u32(tmem_slot)), "r"(kTmemCols) : "memory");
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
   }
-  // codebook prefix -> shared memory
-  {
-    const uint4* src = reinterpret_cast<const uint4*>(prm.codebook);
-    uint4* dst = reinterpret_cast<uint4*>(cb_s);
-    const int n16 = static_cast<int>((static_cast<size_t>(prm.ns) * D * 2) / 16);
-    for (int i = threadIdx.x; i < n16; i += kThreads) dst[i] = __ldg(src + i);
-  }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
-  // TMEM columns: [0, 256) accumulator D, [256, 256 + 32 * kAStages) A buffers
-  const uint32_t tmem_d = tmem_base;
-  const uint32_t tmem_a = tmem_base + kMaxN;
 
   const int nchunks = prm.meta[0];
   const int64_t nitems = static_cast<int64_t>(nchunks) * prm.row_tiles;
-  const int n_k = prm.IN / kChunkK;
+  const int nwin = prm.n_pos / kSets;
 
-  if (warp == 0) {
-    // ---------------- TMA producer: token tiles of x, kBStages deep
+  if (warp == kWarpTmaX) {
+    // ---------------- TMA producer: token tiles of x, position g -> B stage g % 4
     if (lane == 0) {
       asm volatile("prefetch.tensormap [%0];" :: "l"(reinterpret_cast<uint64_t>(&xmap)) : "memory");
-      uint32_t stage = 0, phase = 0;
-      int filled[kBStages] = {};
-      uint32_t fill_phase[kBStages] = {};
-      for (int64_t it = blockIdx.x; it < nitems && !*abort_flag; it += gridDim.x) {
-        const int chunk = static_cast<int>(it / prm.row_tiles);
-        const int4 ch = prm.chunks[chunk];
-        for (int kc = 0; kc < n_k; ++kc) {
-          if (!mbar_wait(&b_empty[stage], phase ^ 1u, abort_flag)) break;
-          mbar_expect_tx(&b_full[stage], static_cast<uint32_t>(b_stage_bytes));
-          tma_load_2d(&xmap, &b_full[stage], b_base + stage * b_stage_bytes, kc * kChunkK, ch.y);
-          filled[stage] = 1;
-          fill_phase[stage] = phase;
-          if (++stage == kBStages) { stage = 0; phase ^= 1u; }
+      uint32_t g = 0;
+      bool ok = true;
+      for (int64_t it = blockIdx.x; it < nitems && ok; it += gridDim.x) {
+        const int4 ch = prm.chunks[static_cast<int>(it / prm.row_tiles)];
+        const int ncopy = (ch.z + kBoxRows - 1) / kBoxRows;
+        const uint32_t bytes = static_cast<uint32_t>(ncopy * kBoxRows * kChunkK * 2);
+        for (int pass = 0; pass < prm.npass && ok; ++pass) {
+          for (int p = 0; p < prm.n_pos; ++p, ++g) {
+            // the stage was last read by position g - 4
+            if (g >= kBStages &&
+                !mbar_wait(&st_free[(g - kBStages) % kAStages], ((g - kBStages) / kAStages) & 1u, abort_flag)) {
+              ok = false;
+              break;
+            }
+            const uint32_t bs = g % kBStages;
+            mbar_expect_tx(&b_full[bs], bytes);
+            unsigned char* dst = b_base + bs * kBStageBytes;
+            for (int c = 0; c < ncopy; ++c)
+              tma_load_2d(&xmap, &b_full[bs], dst + c * kBoxRows * kChunkK * 2, p * kChunkK, ch.y + c * kBoxRows);
+          }
         }
       }
       // no copy may still be writing shared memory when the CTA exits
-      for (int s2 = 0; s2 < kBStages; ++s2) {
-        if (filled[s2]) {
-          for (uint32_t i = 0; i < kSpinLimit && !mbar_try_wait(&b_full[s2], fill_phase[s2]); ++i) {
-          }
-        }
-      }
+      for (uint32_t k = 1; k <= kBStages && k <= g; ++k) mbar_drain(&b_full[(g - k) % kBStages], ((g - k) / kBStages) & 1u);
     }
-  } else if (warp == 1) {
-    // ---------------- MMA issuer (one thread)
+  } else if (warp == kWarpMma0 || warp == kWarpMma1) {
+    // ---------------- MMA issuers: issuer i takes the positions p with (p / 2) % 2 == i
+    // (B stages 2i, 2i+1) and accumulates into its own D_i; the epilogue adds D_0 + D_1.
     if (lane == 0) {
-      uint32_t bstage = 0, bphase = 0, astage = 0, aphase = 0;
-      for (int64_t it = blockIdx.x; it < nitems && !*abort_flag; it += gridDim.x) {
-        const int chunk = static_cast<int>(it / prm.row_tiles);
-        const int4 ch = prm.chunks[chunk];
-        const int n = (ch.z + 15) & ~15;
-        const uint32_t idesc = make_idesc(n, prm.b_bf16 != 0);
-        bool ok = true;
-        for (int kc = 0; kc < n_k && ok; ++kc) {
-          ok = mbar_wait(&a_full[astage], aphase, abort_flag) && mbar_wait(&b_full[bstage], bphase, abort_flag);
-          if (!ok) break;
-          tc_fence_after();
-          const uint32_t b_addr = smem_u32(b_base + bstage * b_stage_bytes);
+      const int iss = warp == kWarpMma0 ? 0 : 1;
+      const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(iss * kMaxN);
+      // descriptor of B stage 0; stage s starts s * 16 KB later (the start-address field counts 16-byte units)
+      const uint64_t bdesc0 = sw128_desc(smem_u32(b_base));
+      uint32_t g = 0;
+      bool ok = true;
+      int j = 0;
+      for (int64_t it = blockIdx.x; it < nitems && ok; it += gridDim.x, ++j) {
+        const int4 ch = prm.chunks[static_cast<int>(it / prm.row_tiles)];
+        if (j >= 1 && !mbar_wait(acc_empty, static_cast<uint32_t>((j - 1) & 1), abort_flag)) break;
+        tc_fence_after();
+        const uint32_t idesc = make_idesc((ch.z + 15) & ~15, prm.b_bf16 != 0);
+        uint32_t acc = 0;
+        for (int pass = 0; pass < prm.npass && ok; ++pass) {
+          for (int p = 2 * iss; p < prm.n_pos; p += 4) {
 #pragma unroll
-          for (int kk = 0; kk < kChunkK / 16; ++kk) {
-            // A: 16 k = 8 columns of packed fp16 pairs; B: advance 32 bytes inside the swizzle row
-            tc_mma_ts(tmem_d, tmem_a + astage * 32 + kk * 8, sw128_desc(b_addr + kk * 32), idesc,
-                      (kc > 0 || kk > 0) ? 1u : 0u);
+            for (int h = 0; h < 2; ++h) {
+              const uint32_t gp = g + static_cast<uint32_t>(p + h);
+              const uint32_t ast = gp % kAStages, bs = gp % kBStages;
+              ok = mbar_wait(&a_full[ast], (gp / kAStages) & 1u, abort_flag) &&
+                   mbar_wait(&b_full[bs], (gp / kBStages) & 1u, abort_flag);
+              if (!ok) break;
+              tc_fence_after();
+              const uint32_t a_tmem = tmem_base + kTmemA + ast * 32;
+              const uint64_t bd = bdesc0 + static_cast<uint64_t>(bs * (kBStageBytes >> 4));
+              tc_mma_ts(d_tmem, a_tmem, bd, idesc, acc);
+              tc_mma_ts(d_tmem, a_tmem + 8, bd + 2, idesc, 1u);    // +32 bytes: next 16 k of the swizzle row
+              tc_mma_ts(d_tmem, a_tmem + 16, bd + 4, idesc, 1u);
+              tc_mma_ts(d_tmem, a_tmem + 24, bd + 6, idesc, 1u);
+              acc = 1u;
+              tc_commit(&st_free[ast]);
+            }
+            if (!ok) break;
           }
-          tc_commit(&b_empty[bstage]);
-          tc_commit(&a_empty[astage]);
-          if (++bstage == kBStages) { bstage = 0; bphase ^= 1u; }
-          if (++astage == kAStages) { astage = 0; aphase ^= 1u; }
+          g += static_cast<uint32_t>(prm.n_pos);
         }
-        if (ok) tc_commit(acc_full);
+        if (ok) tc_commit(&acc_full[iss]);
       }
       // every MMA this thread issued has completed before TMEM is freed
-      tc_commit(mma_done);
-      for (uint32_t i = 0; i < kSpinLimit && !mbar_try_wait(mma_done, 0); ++i) {
-      }
+      tc_commit(&mma_done[iss]);
+      mbar_drain(&mma_done[iss], 0);
     }
-  } else if (warp >= 4) {
-    // ---------------- decode + epilogue (thread = row = TMEM lane)
-    const int q = warp & 3;                       // TMEM lane quarter
+  } else if (warp == kWarpTmaCode) {
+    // ---------------- TMA producer: windows of packed code rows (+ scales)
+    if (lane == 0) {
+      asm volatile("prefetch.tensormap [%0];" :: "l"(reinterpret_cast<uint64_t>(&cmap)) : "memory");
+      uint32_t ws = 0, wp = 0;
+      int filled[kWStages] = {};
+      uint32_t fill_phase[kWStages] = {};
+      const uint32_t bytes = static_cast<uint32_t>(prm.code_stage_bytes + (prm.scale_tma ? kTileM * kScaleRowBytes : 0));
+      bool ok = true;
+      for (int64_t it = blockIdx.x; it < nitems && ok; it += gridDim.x) {
+        const int chunk = static_cast<int>(it / prm.row_tiles);
+        const int rt = static_cast<int>(it - static_cast<int64_t>(chunk) * prm.row_tiles);
+        const int4 ch = prm.chunks[chunk];
+        const int yrow = ch.x * prm.OUT + rt * kTileM;
+        for (int pass = 0; pass < prm.npass && ok; ++pass) {
+          for (int w = 0; w < nwin; ++w) {
+            if (!mbar_wait(&w_empty[ws], wp ^ 1u, abort_flag)) { ok = false; break; }
+            mbar_expect_tx(&w_full[ws], bytes);
+            unsigned char* dst = w_base + ws * prm.win_stage_bytes;
+            tma_load_2d(&cmap, &w_full[ws], dst, (w * prm.wpw) & ~3, yrow);
+            if (prm.scale_tma) {
+              const int g_first = (w * kSets * kChunkK) >> prm.log2g;
+              tma_load_2d(&smap, &w_full[ws], dst + prm.code_stage_bytes, g_first & ~7, yrow);
+            }
+            filled[ws] = 1;
+            fill_phase[ws] = wp;
+            if (++ws == kWStages) { ws = 0; wp ^= 1u; }
+          }
+        }
+      }
+      for (int s = 0; s < kWStages; ++s)
+        if (filled[s]) mbar_drain(&w_full[s], fill_phase[s]);
+    }
+  } else if (warp == kWarpCbLoad) {
+    // ---------------- codebook slice loader
+    if (lane == 0) {
+      int resident = -1;
+      uint32_t loads = 0;
+      bool ok = true;
+      int j = 0;
+      for (int64_t it = blockIdx.x; it < nitems && ok; it += gridDim.x, ++j) {
+        for (int pass = 0; pass < prm.npass; ++pass) {
+          const int h = pass_slice(prm.npass, j, pass);
+          if (h == resident) continue;
+          if (loads > 0 && !mbar_wait(cb_empty, (loads - 1) & 1u, abort_flag)) { ok = false; break; }
+          const int64_t first = static_cast<int64_t>(h) * prm.kp;
+          const int64_t cnt = min(static_cast<int64_t>(prm.kp), static_cast<int64_t>(prm.K) - first);
+          const uint32_t bytes = static_cast<uint32_t>(cnt * D * 2);
+          mbar_expect_tx(cb_full, bytes);
+          const unsigned char* src = reinterpret_cast<const unsigned char*>(prm.codebook) + first * D * 2;
+          for (uint32_t off = 0; off < bytes; off += 32768u)
+            bulk_load(reinterpret_cast<unsigned char*>(cb_s) + off, src + off, min(32768u, bytes - off), cb_full);
+          resident = h;
+          ++loads;
+        }
+      }
+      if (loads > 0) mbar_drain(cb_full, (loads - 1) & 1u);
+    }
+  } else if (warp >= kFirstDecodeWarp) {
+    // ---------------- decode (+ epilogue): set s, TMEM lane quarter q = warp % 4, thread = row
+    const int s = (warp - kFirstDecodeWarp) >> 2;
+    const int q = warp & 3;
     const uint32_t lane_off = static_cast<uint32_t>(q * 32) << 16;
-    const uint32_t mask = (1u << prm.bits) - 1u;
-    uint32_t astage = 0, aphase = 0, accphase = 0;
-    for (int64_t it = blockIdx.x; it < nitems && !*abort_flag; it += gridDim.x) {
+    const int lrow = q * 32 + lane;                 // row inside the tile
+    uint32_t ws = 0, wp = 0;
+    uint32_t g = 0;                                 // position sequence number
+    int cur = -1;
+    uint32_t cb_loads = 0;
+    bool ok = true;
+    int j = 0;
+    for (int64_t it = blockIdx.x; it < nitems && ok; it += gridDim.x, ++j) {
       const int chunk = static_cast<int>(it / prm.row_tiles);
       const int rt = static_cast<int>(it - static_cast<int64_t>(chunk) * prm.row_tiles);
       const int4 ch = prm.chunks[chunk];
-      const int e = ch.x;
-      const int r = rt * kTileM + q * 32 + lane;
+      const int r = rt * kTileM + lrow;
       const int rr = min(r, prm.OUT - 1);
-      const uint32_t* row = prm.codes + static_cast<int64_t>(e) * prm.expert_words +
-                            static_cast<int64_t>(rr) * prm.row_words;
-      const uint16_t* srow = prm.scales + (static_cast<int64_t>(e) * prm.OUT + rr) * prm.NGRP;
-      PrefetchWalker wk;
-      wk.init(row, prm.row_words);
-      bool ok = true;
-      // two chunks per iteration: both chunks' lookups are in flight together
-      for (int kc = 0; kc < n_k; kc += 2) {
-        const bool two = kc + 1 < n_k;
-        uint32_t w0[32], w1[32];
-        const __half s0 = __ushort_as_half(__ldg(srow + (kc * kChunkK) / prm.G));
-        const __half s1 = two ? __ushort_as_half(__ldg(srow + ((kc + 1) * kChunkK) / prm.G)) : s0;
-        decode_chunk<D>(prm, cb_s, wk, mask, __halves2half2(s0, s0), w0);
-        if (two) decode_chunk<D>(prm, cb_s, wk, mask, __halves2half2(s1, s1), w1);
-        for (int h = 0; h < (two ? 2 : 1); ++h) {
-          if (!mbar_wait(&a_empty[astage], aphase ^ 1u, abort_flag)) { ok = false; break; }
+      const uint16_t* srow = prm.scales + (static_cast<int64_t>(ch.x) * prm.OUT + rr) * prm.NGRP;
+      for (int pass = 0; pass < prm.npass && ok; ++pass) {
+        const int h = pass_slice(prm.npass, j, pass);
+        if (h != cur) {
+          if (cur >= 0) {
+            __syncwarp();
+            if (lane == 0) mbar_arrive(cb_empty);
+          }
+          if (!warp_wait(cb_full, cb_loads & 1u, abort_flag)) { ok = false; break; }
+          ++cb_loads;
+          cur = h;
+        }
+        for (int w = 0; w < nwin; ++w) {
+          if (!warp_wait(&w_full[ws], wp, abort_flag)) { ok = false; break; }
+          const unsigned char* wst = w_base + ws * prm.win_stage_bytes;
+          const int p = w * kSets + s;
+          uint32_t out[32];
+          if (p < prm.n_k) {
+            uint16_t sc;
+            if (prm.scale_tma) {
+              const uint4 sv = reinterpret_cast<const uint4*>(wst + prm.code_stage_bytes)[lrow];
+              const int gi = ((p * kChunkK) >> prm.log2g) - (((w * kSets * kChunkK) >> prm.log2g) & ~7);
+              const uint32_t sw = (gi & 4) ? ((gi & 2) ? sv.w : sv.z) : ((gi & 2) ? sv.y : sv.x);
+              sc = static_cast<uint16_t>((gi & 1) ? (sw >> 16) : (sw & 0xFFFFu));
+            } else {
+              sc = __ldg(srow + (p * kChunkK) / prm.G);
+            }
+            const __half sh = __ushort_as_half(sc);
+            const int wstart = w * prm.wpw;
+            const int b0 = (wstart & 3) * 32 + s * (kChunkK / D) * prm.bits;
+            decode_chunk<D, BITS>(prm, cb_s, reinterpret_cast<const uint32_t*>(wst) + lrow * prm.W, b0,
+                                  __halves2half2(sh, sh), h, out);
+          } else {
+#pragma unroll
+            for (int i = 0; i < 32; ++i) out[i] = 0u;  // K padding up to a whole window
+          }
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&w_empty[ws]);
+          if (++ws == kWStages) { ws = 0; wp ^= 1u; }
+          // position p of this tile-pass has sequence number g + p; its A stage
+          // was last read by position g + p - 8
+          const uint32_t gp = g + static_cast<uint32_t>(p);
+          const uint32_t ast = gp % kAStages;
+          if (!warp_wait(&st_free[ast], ((gp / kAStages) & 1u) ^ 1u, abort_flag)) { ok = false; break; }
           tc_fence_after();
-          tc_st_x32(tmem_a + lane_off + astage * 32, h == 0 ? w0 : w1);
+          tc_st_x32(tmem_base + lane_off + kTmemA + ast * 32, out);
           tc_wait_st();
           tc_fence_before();
-          mbar_arrive(&a_full[astage]);
-          if (++astage == kAStages) { astage = 0; aphase ^= 1u; }
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&a_full[ast]);
         }
-        if (!ok) break;
+        g += static_cast<uint32_t>(prm.n_pos);
       }
       if (!ok) break;
-      // epilogue: D columns [0, n) of this lane's row
-      if (!mbar_wait(acc_full, accphase, abort_flag)) break;
-      accphase ^= 1u;
+      // epilogue: y = D_0 + D_1, column blocks of 16 split over the 4 sets
+      if (!warp_wait(&acc_full[0], static_cast<uint32_t>(j & 1), abort_flag) ||
+          !warp_wait(&acc_full[1], static_cast<uint32_t>(j & 1), abort_flag))
+        break;
       tc_fence_after();
       const int ntok = ch.z;
-      for (int c0 = 0; c0 < ntok; c0 += 16) {
-        uint32_t v[16];
-        tc_ld_x16(tmem_d + lane_off + c0, v);
+      const int n = (ntok + 15) & ~15;
+      for (int c0 = s * 16; c0 < n; c0 += kSets * 16) {
+        uint32_t v0[16], v1[16];
+        tc_ld_x16(tmem_base + lane_off + static_cast<uint32_t>(c0), v0);
+        tc_ld_x16(tmem_base + lane_off + static_cast<uint32_t>(kMaxN + c0), v1);
         tc_wait_ld();
         if (r < prm.OUT) {
 #pragma unroll
-          for (int j = 0; j < 16; ++j) {
-            if (c0 + j < ntok) {
-              const int pair = prm.sorted[ch.y + c0 + j];
-              store_y(prm.y, static_cast<int64_t>(pair) * prm.OUT + r, __uint_as_float(v[j]), prm.y_dtype,
-                      prm.round_f16_first != 0);
+          for (int jj = 0; jj < 16; ++jj) {
+            if (c0 + jj < ntok) {
+              const int pair = prm.sorted[ch.y + c0 + jj];
+              store_y(prm.y, static_cast<int64_t>(pair) * prm.OUT + r, __uint_as_float(v0[jj]) + __uint_as_float(v1[jj]),
+                      prm.y_dtype, prm.round_f16_first != 0);
             }
           }
         }
       }
       tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(acc_empty);
     }
   }
 
@@ -397,17 +631,37 @@ __global__ void __launch_bounds__(kThreads, 1) vq_prefill_tc_kernel(const __grid
   if (warp == 0) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" :: "r"(tmem_base), "r"(kTmemCols) : "memory");
 }
 
-// x rows gathered into expert-sorted order as 16-bit B rows: xs[s] = x[sorted[s] / krep]
+// x rows gathered into expert-sorted order as 16-bit B rows: xs[s] = x[sorted[s] / krep].
+// One warp per row, 16 bytes (8 elements) per lane and step; x is fp16 or
+// bf16 with 16-byte aligned rows (IN % 64 == 0 and an aligned base).
 __global__ void gather_sorted_kernel(const void* __restrict__ x, int x_dtype, const int* __restrict__ sorted, int N,
                                      int krep, int IN, int to_bf16, uint16_t* __restrict__ xs) {
-  const int per_row = IN;
-  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
-       i < static_cast<int64_t>(N) * per_row; i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-    const int s = static_cast<int>(i / per_row);
-    const int k = static_cast<int>(i - static_cast<int64_t>(s) * per_row);
+  const int lane = threadIdx.x & 31;
+  const int vec = IN / 8;
+  const bool convert = (x_dtype == VQB_BF16) != (to_bf16 != 0);
+  for (int s = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); s < N; s += gridDim.x * (blockDim.x >> 5)) {
     const int t = sorted[s] / krep;
-    const float v = load_x(x, static_cast<int64_t>(t) * IN + k, x_dtype, false);
-    xs[i] = to_bf16 ? __bfloat16_as_ushort(__float2bfloat16_rn(v)) : __half_as_ushort(__float2half_rn(v));
+    const uint4* src = reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(x) + static_cast<int64_t>(t) * IN);
+    uint4* dst = reinterpret_cast<uint4*>(xs + static_cast<int64_t>(s) * IN);
+    for (int i = lane; i < vec; i += 32) {
+      uint4 v = __ldg(src + i);
+      if (convert) {
+        uint32_t* w = reinterpret_cast<uint32_t*>(&v);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          if (to_bf16) {
+            const float2 f = __half22float2(*reinterpret_cast<__half2*>(&w[j]));
+            __nv_bfloat162 b = __floats2bfloat162_rn(f.x, f.y);
+            w[j] = *reinterpret_cast<uint32_t*>(&b);
+          } else {
+            const float2 f = __bfloat1622float2(*reinterpret_cast<__nv_bfloat162*>(&w[j]));
+            __half2 h = __floats2half2_rn(f.x, f.y);
+            w[j] = *reinterpret_cast<uint32_t*>(&h);
+          }
+        }
+      }
+      dst[i] = v;
+    }
   }
 }
 
@@ -427,7 +681,37 @@ EncodeTiledFn encode_fn() {
   return fn;
 }
 
+bool encode_2d(EncodeTiledFn enc, CUtensorMap* map, CUtensorMapDataType dt, int esize, const void* ptr, uint64_t inner,
+               uint64_t rows, uint32_t box_inner, uint32_t box_rows, CUtensorMapSwizzle swz) {
+  cuuint64_t dims[2] = {static_cast<cuuint64_t>(inner), static_cast<cuuint64_t>(rows)};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(inner) * esize};
+  cuuint32_t box[2] = {box_inner, box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  return enc(map, dt, 2, const_cast<void*>(ptr), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swz,
+             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 int g_sms_tc = 0;
+int g_smem_optin = 0;
+
+template <int D>
+void* pick_kernel(int bits) {
+  // code widths of the shipped geometries get the fixed-position extraction
+  if constexpr (D == 8) {
+    if (bits == 12) return reinterpret_cast<void*>(vq_prefill_tc_kernel<8, 12>);
+    if (bits == 14) return reinterpret_cast<void*>(vq_prefill_tc_kernel<8, 14>);
+    if (bits == 16) return reinterpret_cast<void*>(vq_prefill_tc_kernel<8, 16>);
+    return reinterpret_cast<void*>(vq_prefill_tc_kernel<8, 0>);
+  } else if constexpr (D == 4) {
+    if (bits == 12) return reinterpret_cast<void*>(vq_prefill_tc_kernel<4, 12>);
+    if (bits == 13) return reinterpret_cast<void*>(vq_prefill_tc_kernel<4, 13>);
+    return reinterpret_cast<void*>(vq_prefill_tc_kernel<4, 0>);
+  } else {
+    if (bits == 8) return reinterpret_cast<void*>(vq_prefill_tc_kernel<2, 8>);
+    if (bits == 9) return reinterpret_cast<void*>(vq_prefill_tc_kernel<2, 9>);
+    return reinterpret_cast<void*>(vq_prefill_tc_kernel<2, 0>);
+  }
+}
 
 }  // namespace
 
@@ -436,6 +720,7 @@ bool tc_prefill_supported(const LinearGeometry& geo) {
   if (geo.G % kChunkK != 0) return false;      // one scale per row per 64-k chunk
   if (geo.bits > 16) return false;
   if ((reinterpret_cast<uintptr_t>(geo.codes) & 15) != 0 || geo.row_words % 4 != 0) return false;
+  if ((static_cast<int64_t>(geo.K) * geo.D * 2) % 16 != 0) return false;  // codebook bulk copies
   return true;
 }
 
@@ -449,28 +734,11 @@ vqb_status launch_prefill_tc(const LinearGeometry& geo, const void* x, int x_dty
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess) return VQB_CUDA_ERROR;
     if (cudaDeviceGetAttribute(&g_sms_tc, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return VQB_CUDA_ERROR;
+    if (cudaDeviceGetAttribute(&g_smem_optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev) != cudaSuccess)
+      return VQB_CUDA_ERROR;
   }
   EncodeTiledFn enc = encode_fn();
   if (!enc) return VQB_CUDA_ERROR;
-  // 1. gather x into expert-sorted 16-bit rows
-  {
-    const int64_t n = static_cast<int64_t>(N) * geo.IN;
-    int64_t blocks = (n + 255) / 256;
-    if (blocks > 8 * g_sms_tc) blocks = 8 * g_sms_tc;
-    gather_sorted_kernel<<<static_cast<unsigned>(blocks), 256, 0, stream>>>(x, x_dtype, rw.sorted, N, krep, geo.IN,
-                                                                            bf16_operands ? 1 : 0, xs);
-    if (cudaGetLastError() != cudaSuccess) return VQB_CUDA_ERROR;
-  }
-  // 2. TMA map over xs [N rows, IN] 16-bit: box 64 x 256, 128-byte swizzle
-  CUtensorMap map;
-  cuuint64_t dims[2] = {static_cast<cuuint64_t>(geo.IN), static_cast<cuuint64_t>(N)};
-  cuuint64_t strides[1] = {static_cast<cuuint64_t>(geo.IN) * 2};
-  cuuint32_t box[2] = {kChunkK, kMaxN};
-  cuuint32_t estr[2] = {1, 1};
-  if (enc(&map, bf16_operands ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, xs, dims,
-          strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-          CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
-    return VQB_CUDA_ERROR;
 
   TParams prm{};
   prm.codes = static_cast<const uint32_t*>(geo.codes);
@@ -481,39 +749,93 @@ vqb_status launch_prefill_tc(const LinearGeometry& geo, const void* x, int x_dty
   prm.meta = rw.meta;
   prm.status = status;
   prm.y = y;
-  prm.row_words = geo.row_words;
-  prm.expert_words = static_cast<int64_t>(geo.OUT) * geo.row_words;
   prm.OUT = geo.OUT;
   prm.IN = geo.IN;
   prm.G = geo.G;
   prm.NGRP = geo.IN / geo.G;
   prm.bits = geo.bits;
+  prm.K = geo.K;
+  prm.n_k = geo.IN / kChunkK;
+  prm.n_pos = (prm.n_k + kSets - 1) / kSets * kSets;
   prm.row_tiles = (geo.OUT + kTileM - 1) / kTileM;
   prm.y_dtype = y_dtype;
   prm.round_f16_first = round_f16_first ? 1 : 0;
   prm.b_bf16 = bf16_operands ? 1 : 0;
 
-  const size_t b_bytes = static_cast<size_t>(kBStages) * kMaxN * kChunkK * 2;
-  const size_t tail = 256 + 1024;  // barriers, tmem slot, flags, and the 1024-byte alignment slack
-  const size_t budget = 227 * 1024;
-  const size_t entry = static_cast<size_t>(geo.D) * 2;
-  size_t ns = (budget - b_bytes - tail - 16) / entry;
-  ns = ns / 8 * 8;
-  if (ns > static_cast<size_t>(geo.K)) ns = geo.K;
-  prm.ns = static_cast<int>(ns);
-  const size_t smem = b_bytes + ((ns * entry + 15) & ~size_t(15)) + tail + 16;
+  // code window: kSets chunks = 256 k = (256 / D) codes of every row
+  prm.wpw = (kSets * kChunkK / geo.D) * geo.bits / 32;
+  const int o_max = prm.wpw % 4 == 0 ? 0 : (prm.wpw % 2 == 0 ? 2 : 3);
+  int W = (o_max + prm.wpw + 3) & ~3;
+  if ((W / 4) % 2 == 0) W += 4;
+  prm.W = W;
+  prm.code_stage_bytes = kTileM * W * 4;
+  const bool g_pow2 = (geo.G & (geo.G - 1)) == 0;
+  prm.scale_tma = (prm.NGRP % 8 == 0 && g_pow2 && (reinterpret_cast<uintptr_t>(geo.scales) & 15) == 0) ? 1 : 0;
+  int log2g = 0;
+  while ((1 << (log2g + 1)) <= geo.G) ++log2g;
+  prm.log2g = log2g;
+  prm.win_stage_bytes = prm.code_stage_bytes + (prm.scale_tma ? kTileM * kScaleRowBytes : 0);
 
-  cudaError_t ce;
-  auto launch = [&](auto kern) {
-    ce = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
-    if (ce != cudaSuccess) return;
-    kern<<<g_sms_tc, kThreads, smem, stream>>>(map, prm);
-    ce = cudaGetLastError();
-  };
-  if (geo.D == 8) launch(vq_prefill_tc_kernel<8>);
-  else if (geo.D == 4) launch(vq_prefill_tc_kernel<4>);
-  else launch(vq_prefill_tc_kernel<2>);
-  return ce == cudaSuccess ? VQB_OK : VQB_CUDA_ERROR;
+  // shared memory: B stages, windows, then the largest power-of-two codebook slice that fits
+  const size_t tail = static_cast<size_t>(kNumBars) * 8 + 16;
+  const size_t fixed = 1024 + static_cast<size_t>(kBStages) * kBStageBytes +
+                       static_cast<size_t>(kWStages) * prm.win_stage_bytes + tail + 16;
+  if (static_cast<size_t>(g_smem_optin) <= fixed + 1024) return VQB_UNSUPPORTED_GEOMETRY;
+  const size_t avail = static_cast<size_t>(g_smem_optin) - fixed;
+  const size_t entry = static_cast<size_t>(geo.D) * 2;
+  if (static_cast<size_t>(geo.K) * entry <= avail) {
+    prm.kp = geo.K;
+    prm.kp_log2 = 0;
+    prm.npass = 1;
+  } else {
+    int l = 0;
+    while ((static_cast<size_t>(2) << l) * entry <= avail) ++l;
+    prm.kp_log2 = l;
+    prm.kp = 1 << l;
+    prm.npass = (geo.K + prm.kp - 1) / prm.kp;
+  }
+  const size_t cb_bytes = (static_cast<size_t>(prm.kp) * entry + 15) & ~size_t(15);
+  prm.off_win = kBStages * kBStageBytes;
+  prm.off_cb = prm.off_win + kWStages * prm.win_stage_bytes;
+  prm.off_bar = static_cast<int>(prm.off_cb + cb_bytes);
+  const size_t smem = 1024 + static_cast<size_t>(prm.off_bar) + tail;
+  if (smem > static_cast<size_t>(g_smem_optin)) return VQB_UNSUPPORTED_GEOMETRY;
+
+  // 1. gather x into expert-sorted 16-bit rows
+  {
+    if (x_dtype != VQB_F16 && x_dtype != VQB_BF16) return VQB_UNSUPPORTED_GEOMETRY;
+    if ((reinterpret_cast<uintptr_t>(x) & 15) != 0) return VQB_BAD_ALIGNMENT;
+    int64_t blocks = (static_cast<int64_t>(N) + 7) / 8;
+    if (blocks > 16 * g_sms_tc) blocks = 16 * g_sms_tc;
+    gather_sorted_kernel<<<static_cast<unsigned>(blocks), 256, 0, stream>>>(x, x_dtype, rw.sorted, N, krep, geo.IN,
+                                                                            bf16_operands ? 1 : 0, xs);
+    if (cudaGetLastError() != cudaSuccess) return VQB_CUDA_ERROR;
+  }
+  // 2. TMA maps: xs [N, IN] 16-bit (box 64 x 32, 128-byte swizzle); codes
+  //    [E*OUT, row_words] u32 (box W x 128); scales [E*OUT, NGRP] fp16 (box 8 x 128)
+  CUtensorMap xmap, cmap, smap;
+  if (!encode_2d(enc, &xmap, bf16_operands ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, xs,
+                 static_cast<uint64_t>(geo.IN), static_cast<uint64_t>(N), kChunkK, kBoxRows,
+                 CU_TENSOR_MAP_SWIZZLE_128B))
+    return VQB_CUDA_ERROR;
+  const uint64_t rows = static_cast<uint64_t>(geo.E) * geo.OUT;
+  if (!encode_2d(enc, &cmap, CU_TENSOR_MAP_DATA_TYPE_UINT32, 4, geo.codes, static_cast<uint64_t>(geo.row_words), rows,
+                 static_cast<uint32_t>(W), kTileM, CU_TENSOR_MAP_SWIZZLE_NONE))
+    return VQB_CUDA_ERROR;
+  if (prm.scale_tma) {
+    if (!encode_2d(enc, &smap, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, geo.scales, static_cast<uint64_t>(prm.NGRP), rows, 8,
+                   kTileM, CU_TENSOR_MAP_SWIZZLE_NONE))
+      return VQB_CUDA_ERROR;
+  } else {
+    smap = cmap;  // unused
+  }
+
+  void* kern = geo.D == 8 ? pick_kernel<8>(geo.bits) : (geo.D == 4 ? pick_kernel<4>(geo.bits) : pick_kernel<2>(geo.bits));
+  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)) != cudaSuccess)
+    return VQB_CUDA_ERROR;
+  void* args[] = {&xmap, &cmap, &smap, &prm};
+  if (cudaLaunchKernel(kern, dim3(g_sms_tc), dim3(kThreads), args, smem, stream) != cudaSuccess) return VQB_CUDA_ERROR;
+  return cudaGetLastError() == cudaSuccess ? VQB_OK : VQB_CUDA_ERROR;
 }
 
 }  // namespace vqb

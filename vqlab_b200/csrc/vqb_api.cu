@@ -80,8 +80,9 @@ vqb_status run_linear(const LinearGeometry& geo, const void* x, int x_dtype, int
   const int variant = opts ? opts->decode_variant : 0;
   uint16_t* xbuf = reinterpret_cast<uint16_t*>(static_cast<char*>(workspace) +
                                                route_workspace_bytes(N, geo.E, kDecodeMaxPairs));
-  if (large && variant == 0 && tc_prefill_supported(geo) && x_dtype != VQB_F32) {
-    // grouped tcgen05 GEMM: tiles of up to 256 of one expert's tokens
+  if (large && variant == 0 && tc_prefill_supported(geo) && x_dtype != VQB_F32 &&
+      (reinterpret_cast<uintptr_t>(x) & 15) == 0) {
+    // grouped tcgen05 GEMM: tiles of up to 128 of one expert's tokens
     vqb_status st = launch_route_small(indices, N, geo.E, kPrefillTileTokens, rw, stream);
     if (st != VQB_OK) return st;
     return launch_prefill_tc(geo, x, x_dtype, krep, rw, N, xbuf, y, y_dtype, round_f16_first,

@@ -70,7 +70,7 @@ size_t tc_prefill_x_bytes(int64_t N, int IN);
 vqb_status launch_prefill_tc(const LinearGeometry& geo, const void* x, int x_dtype, int krep, const RouteWorkspace& rw,
                              int N, uint16_t* xs, void* y, int y_dtype, bool round_f16_first, bool bf16_operands,
                              int* status, cudaStream_t stream);
-constexpr int kPrefillTileTokens = 256;
+constexpr int kPrefillTileTokens = 128;
 
 // Workspace layout and the shared body of the switch / dense entry points (vqb_api.cu).
 size_t linear_workspace_bytes(int N, int E, int64_t T, int IN);
