@@ -67,7 +67,7 @@ constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kTmemA = kIssuers * kMaxN;        // columns: [0,128) D0, [128,256) D1, then 8 A stages of 32
 constexpr uint32_t kSpinLimit = 1u << 26;
 constexpr int kScaleRowBytes = 16;                   // 8 fp16 scales per row per window
-constexpr int kNumBars = kBStages + 2 * kAStages + 2 * kWStages + 2 + kIssuers + 1 + kIssuers;
+constexpr int kNumBars = 2 * kBStages + 2 * kAStages + 2 * kWStages + 2 + kIssuers + 1 + kIssuers;
 
 struct TParams {
   const uint32_t* codes;
@@ -143,6 +143,12 @@ __device__ __forceinline__ void tma_load_2d(const CUtensorMap* map, uint64_t* ba
       "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];"
       :: "r"(smem_u32(dst)), "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(x), "r"(y) : "memory");
 }
+__device__ __forceinline__ void tma_load_3d(const CUtensorMap* map, uint64_t* bar, void* dst, int x, int y, int z) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5}], [%2];"
+      :: "r"(smem_u32(dst)), "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(x), "r"(y), "r"(z)
+      : "memory");
+}
 // plain (non-tensor) bulk copy global -> shared; 16-byte aligned, size % 16 == 0
 __device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
   asm volatile(
@@ -217,6 +223,11 @@ __device__ __forceinline__ uint32_t make_idesc(int n, bool bf16) {
   d |= static_cast<uint32_t>(kTileM >> 4) << 24;  // m_dim
   return d;
 }
+
+// Token rows a B slot holds for a tile of n tokens, and the K positions that
+// share one B stage (a stage holds 128 token rows of 64 k).
+__host__ __device__ __forceinline__ int slot_rows(int n) { return n <= 32 ? 32 : (n <= 64 ? 64 : 128); }
+__host__ __device__ __forceinline__ int slot_positions(int rows) { return rows <= 32 ? 4 : (rows <= 64 ? 2 : 1); }
 
 // Codebook slice a tile-pass reads: consecutive tiles of a CTA walk the
 // slices in alternating order, so the slice resident at the end of one tile is
@@ -338,7 +349,8 @@ __device__ __forceinline__ void decode_chunk(const TParams& prm, const uint16_t*
 
 template <int D, int BITS>
 __global__ void __launch_bounds__(kThreads, 1)
-    vq_prefill_tc_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_constant__ CUtensorMap cmap,
+    vq_prefill_tc_kernel(const __grid_constant__ CUtensorMap xmap32, const __grid_constant__ CUtensorMap xmap64,
+                         const __grid_constant__ CUtensorMap xmap128, const __grid_constant__ CUtensorMap cmap,
                          const __grid_constant__ CUtensorMap smap, const TParams prm) {
   extern __shared__ __align__(16) unsigned char smem_dyn[];
   // [B stages][2 code/scale windows][codebook slice][barriers][tmem addr][flag]; 1024-aligned (swizzle atom)
@@ -349,9 +361,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   unsigned char* w_base = base + prm.off_win;
   uint16_t* cb_s = reinterpret_cast<uint16_t*>(base + prm.off_cb);
   uint64_t* bars = reinterpret_cast<uint64_t*>(base + prm.off_bar);
-  uint64_t* b_full = bars;                         // [kBStages] x tile landed
-  uint64_t* a_full = b_full + kBStages;            // [kAStages] the 4 warps of a set stored it
-  uint64_t* st_free = a_full + kAStages;           // [kAStages] MMAs of position g done: A stage g%8, B stage g%4 free
+  uint64_t* b_full = bars;                         // [kBStages] x slot landed
+  uint64_t* b_empty = b_full + kBStages;           // [kBStages] MMAs done with the slot
+  uint64_t* a_full = b_empty + kBStages;           // [kAStages] the 4 warps of a set stored it
+  uint64_t* st_free = a_full + kAStages;           // [kAStages] MMAs of position g done: A stage g % 8 free
   uint64_t* w_full = st_free + kAStages;           // [kWStages] code/scale window landed
   uint64_t* w_empty = w_full + kWStages;           // [kWStages] all 16 decode warps read it
   uint64_t* cb_full = w_empty + kWStages;          // [1] codebook slice landed
@@ -365,7 +378,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
   if (threadIdx.x == 0) {
-    for (int i = 0; i < kBStages; ++i) mbar_init(&b_full[i], 1);
+    for (int i = 0; i < kBStages; ++i) { mbar_init(&b_full[i], 1); mbar_init(&b_empty[i], 1); }
     for (int i = 0; i < kAStages; ++i) { mbar_init(&a_full[i], 4); mbar_init(&st_free[i], 1); }
     for (int i = 0; i < kWStages; ++i) { mbar_init(&w_full[i], 1); mbar_init(&w_empty[i], kDecodeWarps); }
     mbar_init(cb_full, 1);
@@ -390,43 +403,44 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int nwin = prm.n_pos / kSets;
 
   if (warp == kWarpTmaX) {
-    // ---------------- TMA producer: token tiles of x, position g -> B stage g % 4
+    // ---------------- TMA producer: x slots (slot_positions(n) consecutive K positions per B stage)
     if (lane == 0) {
-      asm volatile("prefetch.tensormap [%0];" :: "l"(reinterpret_cast<uint64_t>(&xmap)) : "memory");
-      uint32_t g = 0;
+      asm volatile("prefetch.tensormap [%0];" :: "l"(reinterpret_cast<uint64_t>(&xmap32)) : "memory");
+      asm volatile("prefetch.tensormap [%0];" :: "l"(reinterpret_cast<uint64_t>(&xmap64)) : "memory");
+      asm volatile("prefetch.tensormap [%0];" :: "l"(reinterpret_cast<uint64_t>(&xmap128)) : "memory");
+      uint32_t gs = 0;  // slot sequence number
       bool ok = true;
       for (int64_t it = blockIdx.x; it < nitems && ok; it += gridDim.x) {
         const int4 ch = prm.chunks[static_cast<int>(it / prm.row_tiles)];
-        const int ncopy = (ch.z + kBoxRows - 1) / kBoxRows;
-        const uint32_t bytes = static_cast<uint32_t>(ncopy * kBoxRows * kChunkK * 2);
+        const int rows = slot_rows(ch.z);
+        const int pp = slot_positions(rows);
+        // one box per slot: 64 k x rows tokens x pp chunks, laid out [chunk][token][k]
+        const CUtensorMap* map = rows == 32 ? &xmap32 : (rows == 64 ? &xmap64 : &xmap128);
+        const uint32_t bytes = static_cast<uint32_t>(pp * rows * kChunkK * 2);
         for (int pass = 0; pass < prm.npass && ok; ++pass) {
-          for (int p = 0; p < prm.n_pos; ++p, ++g) {
-            // the stage was last read by position g - 4
-            if (g >= kBStages &&
-                !mbar_wait(&st_free[(g - kBStages) % kAStages], ((g - kBStages) / kAStages) & 1u, abort_flag)) {
-              ok = false;
-              break;
-            }
-            const uint32_t bs = g % kBStages;
+          for (int p0 = 0; p0 < prm.n_pos; p0 += pp, ++gs) {
+            const uint32_t bs = gs % kBStages;
+            if (!mbar_wait(&b_empty[bs], ((gs / kBStages) & 1u) ^ 1u, abort_flag)) { ok = false; break; }
             mbar_expect_tx(&b_full[bs], bytes);
             unsigned char* dst = b_base + bs * kBStageBytes;
-            for (int c = 0; c < ncopy; ++c)
-              tma_load_2d(&xmap, &b_full[bs], dst + c * kBoxRows * kChunkK * 2, p * kChunkK, ch.y + c * kBoxRows);
+            tma_load_3d(map, &b_full[bs], dst, 0, ch.y, p0);
           }
         }
       }
       // no copy may still be writing shared memory when the CTA exits
-      for (uint32_t k = 1; k <= kBStages && k <= g; ++k) mbar_drain(&b_full[(g - k) % kBStages], ((g - k) / kBStages) & 1u);
+      for (uint32_t k = 1; k <= kBStages && k <= gs; ++k) mbar_drain(&b_full[(gs - k) % kBStages], ((gs - k) / kBStages) & 1u);
     }
   } else if (warp == kWarpMma0 || warp == kWarpMma1) {
-    // ---------------- MMA issuers: issuer i takes the positions p with (p / 2) % 2 == i
-    // (B stages 2i, 2i+1) and accumulates into its own D_i; the epilogue adds D_0 + D_1.
+    // ---------------- MMA issuers.  A tile's K positions come in slots of pp
+    // positions sharing one B stage (pp > 1 for tiles of <= 64 tokens); the
+    // slots alternate between the two issuers, each accumulating into its own
+    // D_i, and the epilogue adds D_0 + D_1.
     if (lane == 0) {
       const int iss = warp == kWarpMma0 ? 0 : 1;
       const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(iss * kMaxN);
-      // descriptor of B stage 0; stage s starts s * 16 KB later (the start-address field counts 16-byte units)
+      // descriptor of B stage 0; later stages / positions start further on (the start-address field counts 16-byte units)
       const uint64_t bdesc0 = sw128_desc(smem_u32(b_base));
-      uint32_t g = 0;
+      uint32_t g = 0, gs = 0;
       bool ok = true;
       int j = 0;
       for (int64_t it = blockIdx.x; it < nitems && ok; it += gridDim.x, ++j) {
@@ -434,19 +448,22 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (j >= 1 && !mbar_wait(acc_empty, static_cast<uint32_t>((j - 1) & 1), abort_flag)) break;
         tc_fence_after();
         const uint32_t idesc = make_idesc((ch.z + 15) & ~15, prm.b_bf16 != 0);
+        const int rows = slot_rows(ch.z);
+        const int pp = slot_positions(rows);
         uint32_t acc = 0;
+        int k = 0;  // slot index inside the tile
         for (int pass = 0; pass < prm.npass && ok; ++pass) {
-          for (int p = 2 * iss; p < prm.n_pos; p += 4) {
-#pragma unroll
-            for (int h = 0; h < 2; ++h) {
-              const uint32_t gp = g + static_cast<uint32_t>(p + h);
-              const uint32_t ast = gp % kAStages, bs = gp % kBStages;
-              ok = mbar_wait(&a_full[ast], (gp / kAStages) & 1u, abort_flag) &&
-                   mbar_wait(&b_full[bs], (gp / kBStages) & 1u, abort_flag);
-              if (!ok) break;
+          for (int p0 = 0; p0 < prm.n_pos; p0 += pp, ++gs, ++k) {
+            if ((k & 1) != iss) continue;
+            const uint32_t bs = gs % kBStages;
+            if (!(ok = mbar_wait(&b_full[bs], (gs / kBStages) & 1u, abort_flag))) break;
+            for (int q = 0; q < pp; ++q) {
+              const uint32_t gp = g + static_cast<uint32_t>(p0 + q);
+              const uint32_t ast = gp % kAStages;
+              if (!(ok = mbar_wait(&a_full[ast], (gp / kAStages) & 1u, abort_flag))) break;
               tc_fence_after();
               const uint32_t a_tmem = tmem_base + kTmemA + ast * 32;
-              const uint64_t bd = bdesc0 + static_cast<uint64_t>(bs * (kBStageBytes >> 4));
+              const uint64_t bd = bdesc0 + static_cast<uint64_t>((bs * kBStageBytes + q * rows * kChunkK * 2) >> 4);
               tc_mma_ts(d_tmem, a_tmem, bd, idesc, acc);
               tc_mma_ts(d_tmem, a_tmem + 8, bd + 2, idesc, 1u);    // +32 bytes: next 16 k of the swizzle row
               tc_mma_ts(d_tmem, a_tmem + 16, bd + 4, idesc, 1u);
@@ -455,6 +472,7 @@ __global__ void __launch_bounds__(kThreads, 1)
               tc_commit(&st_free[ast]);
             }
             if (!ok) break;
+            tc_commit(&b_empty[bs]);
           }
           g += static_cast<uint32_t>(prm.n_pos);
         }
@@ -594,13 +612,14 @@ __global__ void __launch_bounds__(kThreads, 1)
         g += static_cast<uint32_t>(prm.n_pos);
       }
       if (!ok) break;
-      // epilogue: y = D_0 + D_1, column blocks of 16 split over the 4 sets
+      // epilogue: y = D_0 (+ D_1 when both issuers took part), column blocks of 16 split over the 4 sets
       if (!warp_wait(&acc_full[0], static_cast<uint32_t>(j & 1), abort_flag) ||
           !warp_wait(&acc_full[1], static_cast<uint32_t>(j & 1), abort_flag))
         break;
       tc_fence_after();
       const int ntok = ch.z;
       const int n = (ntok + 15) & ~15;
+      const bool two = prm.npass * prm.n_pos / slot_positions(slot_rows(ntok)) > 1;
       for (int c0 = s * 16; c0 < n; c0 += kSets * 16) {
         uint32_t v0[16], v1[16];
         tc_ld_x16(tmem_base + lane_off + static_cast<uint32_t>(c0), v0);
@@ -611,8 +630,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int jj = 0; jj < 16; ++jj) {
             if (c0 + jj < ntok) {
               const int pair = prm.sorted[ch.y + c0 + jj];
-              store_y(prm.y, static_cast<int64_t>(pair) * prm.OUT + r, __uint_as_float(v0[jj]) + __uint_as_float(v1[jj]),
-                      prm.y_dtype, prm.round_f16_first != 0);
+              const float acc = two ? __uint_as_float(v0[jj]) + __uint_as_float(v1[jj]) : __uint_as_float(v0[jj]);
+              store_y(prm.y, static_cast<int64_t>(pair) * prm.OUT + r, acc, prm.y_dtype, prm.round_f16_first != 0);
             }
           }
         }
@@ -689,6 +708,19 @@ bool encode_2d(EncodeTiledFn enc, CUtensorMap* map, CUtensorMapDataType dt, int 
   cuuint32_t estr[2] = {1, 1};
   return enc(map, dt, 2, const_cast<void*>(ptr), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swz,
              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// xs [N, IN] 16-bit as a 3-d tensor (64 k, N tokens, IN / 64 chunks): a box
+// {64, rows, pp} lands as pp consecutive [rows][64] K-major swizzled tiles
+bool encode_x3d(EncodeTiledFn enc, CUtensorMap* map, bool bf16, const void* xs, int IN, int N, uint32_t rows,
+                uint32_t pp) {
+  cuuint64_t dims[3] = {static_cast<cuuint64_t>(kChunkK), static_cast<cuuint64_t>(N), static_cast<cuuint64_t>(IN / kChunkK)};
+  cuuint64_t strides[2] = {static_cast<cuuint64_t>(IN) * 2, static_cast<cuuint64_t>(kChunkK) * 2};
+  cuuint32_t box[3] = {static_cast<cuuint32_t>(kChunkK), rows, pp};
+  cuuint32_t estr[3] = {1, 1, 1};
+  return enc(map, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, const_cast<void*>(xs), dims,
+             strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
 int g_sms_tc = 0;
@@ -811,13 +843,15 @@ vqb_status launch_prefill_tc(const LinearGeometry& geo, const void* x, int x_dty
                                                                             bf16_operands ? 1 : 0, xs);
     if (cudaGetLastError() != cudaSuccess) return VQB_CUDA_ERROR;
   }
-  // 2. TMA maps: xs [N, IN] 16-bit (box 64 x 32, 128-byte swizzle); codes
+  // 2. TMA maps: xs [N, IN] 16-bit seen as [chunk][token][64 k] (boxes of
+  //    32 x 4, 64 x 2 and 128 x 1 tokens x chunks, 128-byte swizzle); codes
   //    [E*OUT, row_words] u32 (box W x 128); scales [E*OUT, NGRP] fp16 (box 8 x 128)
-  CUtensorMap xmap, cmap, smap;
-  if (!encode_2d(enc, &xmap, bf16_operands ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, xs,
-                 static_cast<uint64_t>(geo.IN), static_cast<uint64_t>(N), kChunkK, kBoxRows,
-                 CU_TENSOR_MAP_SWIZZLE_128B))
-    return VQB_CUDA_ERROR;
+  CUtensorMap xmaps[3], cmap, smap;
+  for (int i = 0; i < 3; ++i) {
+    const uint32_t rows = 32u << i;
+    if (!encode_x3d(enc, &xmaps[i], bf16_operands, xs, geo.IN, N, rows, static_cast<uint32_t>(slot_positions(rows))))
+      return VQB_CUDA_ERROR;
+  }
   const uint64_t rows = static_cast<uint64_t>(geo.E) * geo.OUT;
   if (!encode_2d(enc, &cmap, CU_TENSOR_MAP_DATA_TYPE_UINT32, 4, geo.codes, static_cast<uint64_t>(geo.row_words), rows,
                  static_cast<uint32_t>(W), kTileM, CU_TENSOR_MAP_SWIZZLE_NONE))
@@ -833,7 +867,7 @@ vqb_status launch_prefill_tc(const LinearGeometry& geo, const void* x, int x_dty
   void* kern = geo.D == 8 ? pick_kernel<8>(geo.bits) : (geo.D == 4 ? pick_kernel<4>(geo.bits) : pick_kernel<2>(geo.bits));
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)) != cudaSuccess)
     return VQB_CUDA_ERROR;
-  void* args[] = {&xmap, &cmap, &smap, &prm};
+  void* args[] = {&xmaps[0], &xmaps[1], &xmaps[2], &cmap, &smap, &prm};
   if (cudaLaunchKernel(kern, dim3(g_sms_tc), dim3(kThreads), args, smem, stream) != cudaSuccess) return VQB_CUDA_ERROR;
   return cudaGetLastError() == cudaSuccess ? VQB_OK : VQB_CUDA_ERROR;
 }
