@@ -9,7 +9,9 @@ bf16 activations.  Seeded synthetic weights (codes uniform over K, codebook
 
 A step is one MoE layer forward (router top-k, gate, up, SwiGLU, down,
 weighted combine) on the headline batch (64 tokens; 1 and 8 are reported
-beside it).  Several independently seeded layers are rotated so the
+beside it).  The prefill leg runs the same layer on 4096
+tokens with top-10 routing drawn from Zipf(1.1) expert popularity and
+reports TFLOP/s of the three expert projections.  Several independently seeded layers are rotated so the
 weights a step reads are not in L2 from the previous step (the bytes each
 step touches, times the rotation, exceed the 126 MB L2).
 
@@ -163,6 +165,93 @@ def time_graph_steps(torch, graphs, steps, warmup):
     return e0.elapsed_time(e1) / 1e3
 
 
+def kernel_seconds(torch, stream, call, reps):
+    """Mean device time of the dominant kernel of `call(i)`: the library
+    records two events on the launch stream around that kernel alone."""
+    from vqlab_b200 import _lib
+    pairs = []
+    for i in range(reps):
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)  # creates the events
+        b.record(stream)
+        pairs.append((a, b))
+    torch.cuda.synchronize()
+    for i, (a, b) in enumerate(pairs):
+        _lib.time_next_kernel(a, b)
+        call(i)
+    torch.cuda.synchronize()
+    return statistics.mean(a.elapsed_time(b) for a, b in pairs) / 1e3
+
+
+def profiled_traffic(kernel):
+    """DRAM bytes per launch of `kernel` from the committed ncu summary
+    (profiles/*.txt lines `traffic_bytes_per_launch <kernel> <bytes>`), else None."""
+    for f in sorted((ROOT / "profiles").glob("*.txt")):
+        for line in f.read_text().splitlines():
+            parts = line.split()
+            if len(parts) == 3 and parts[0] == "traffic_bytes_per_launch" and parts[1] == kernel:
+                return int(float(parts[2]))
+    return None
+
+
+def zipf_logits(torch, dev, gen, T, alpha=1.1):
+    """Router logits whose top-10 is a draw without replacement from Zipf(alpha)
+    expert popularity: log(popularity) + Gumbel noise (the Gumbel-top-k trick)."""
+    perm = torch.randperm(E, device=dev, generator=gen)
+    pop = torch.empty(E, device=dev)
+    pop[perm] = 1.0 / torch.arange(1, E + 1, device=dev, dtype=torch.float32) ** alpha
+    u = torch.rand((T, E), device=dev, generator=gen).clamp_(1e-12, 1.0 - 1e-7)
+    return pop.log()[None, :] - torch.log(-torch.log(u))
+
+
+def prefill_leg(torch, dev, args, peak_tf, peak_kind, rank, world):
+    """one MoE layer on 4096 tokens, Zipf(1.1) routing."""
+    T = 4096
+    layer = make_layer(torch, dev, 5000 + rank)
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(17 + rank)
+    x = torch.randn((T, HIDDEN), device=dev, generator=gen).to(torch.bfloat16)
+    lg = zipf_logits(torch, dev, gen, T)
+    for _ in range(2):
+        layer(x, lg)
+    torch.cuda.synchronize()
+    steps = max(3, args.steps // 5)
+    s = torch.cuda.current_stream()
+    if world > 1:
+        torch.distributed.barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(dev.index if dev.index is not None else 0) as clk:
+        e0.record(s)
+        for _ in range(steps):
+            layer(x, lg)
+        e1.record(s)
+        torch.cuda.synchronize()
+    secs = e0.elapsed_time(e1) / 1e3
+    if world > 1:
+        t = torch.tensor([secs], device=dev)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        secs = float(t.item())
+    flops = 3 * 2 * INTER * HIDDEN * T * TOPK
+    from vqlab_b200.moe import route
+    idx, _ = route(lg, TOPK)
+    counts = torch.bincount(idx.reshape(-1).long(), minlength=E)
+    xg = x[:, None, None, :]
+    dur = kernel_seconds(torch, s, lambda i: layer.gate_proj(xg, idx), 5)
+    kflops = 2 * INTER * HIDDEN * T * TOPK
+    ach = kflops / dur / 1e12
+    return {"metric": "VQ-MoE prefill TFLOP/s (one MoE layer, C3: 4096 tokens, Zipf(1.1) top-10)",
+            "value": round(flops * steps * world / secs / 1e12, 2), "unit": "TFLOP/s", "steps": steps,
+            "ms_per_layer": round(secs * 1e3 / steps, 3), "tokens_per_s": round(T * steps * world / secs, 1),
+            "tokens_per_expert": {"max": int(counts.max()), "median": float(counts.float().median()),
+                                  "min": int(counts.min())},
+            "flops_per_layer": flops, "clocks": clk.summary(),
+            "roofline": {"bound": "tensor", "achieved": round(ach, 1), "peak": peak_tf, "unit": "TFLOP/s",
+                         "frac": round(ach / peak_tf, 4), "traffic": profiled_traffic("vq_prefill_tc_kernel"),
+                         "kernel": "vq_prefill_tc_kernel (gate projection, 40960 pairs), timed alone",
+                         "us_per_launch": round(dur * 1e6, 1), "peak_kind": f"{peak_kind} burst bf16 GEMM"}}
+
+
 def gpu_arm(args, rank, world, dev):
     import torch
     torch.cuda.set_device(dev)
@@ -206,6 +295,7 @@ def gpu_arm(args, rank, world, dev):
                       "distinct_experts_mean": statistics.mean(nd), "clocks": clk.summary()}
         del graphs
         torch.cuda.synchronize()
+        xs_last, lg_last = xs, lg
 
     # ---- dominant kernel: the expert decode launch (gate projection), timed alone
     B = args.batch
@@ -220,23 +310,15 @@ def gpu_arm(args, rank, world, dev):
         p(x, idx)
     torch.cuda.synchronize()
     s = torch.cuda.current_stream()
-    ev = []
-    reps = max(3, args.steps)
-    for i in range(reps):
-        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        a.record(s)
-        projs[i % n_layers](x, idx)
-        b.record(s)
-        ev.append((a, b))
-    torch.cuda.synchronize()
-    # the workspace memset shares the bracket; it is a 256-byte fill
-    dur = statistics.mean(a.elapsed_time(b) for a, b in ev) / 1e3
+    dur = kernel_seconds(torch, s, lambda i: projs[i % n_layers](x, idx), max(3, args.steps))
     alg = nd * EXPERT_BYTES["gate"] + CODEBOOK_BYTES + B * HIDDEN * 2 + B * TOPK * INTER * 2
     achieved = alg / dur / 1e9
+    traffic = profiled_traffic("vq_decode_mma_kernel")
     roof = {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak_gbs, "unit": "GB/s",
-            "frac": round(achieved / peak_gbs, 4), "traffic": None,
-            "kernel": "vq_decode_kernel (gate projection, batch %d, %d distinct experts)" % (B, nd),
-            "peak_kind": peak_kind}
+            "frac": round(achieved / peak_gbs, 4), "traffic": traffic,
+            "kernel": "vq_decode_mma_kernel (gate projection, batch %d, %d distinct experts), timed alone" % (B, nd),
+            "algorithmic_bytes_per_launch": alg, "us_per_launch": round(dur * 1e6, 2),
+            "peak_kind": f"{peak_kind} burst copy bandwidth"}
 
     # ---- e2e through the public API with host buffers
     e2e = None
@@ -267,7 +349,12 @@ def gpu_arm(args, rank, world, dev):
         e2e = {"value": round(B * args.steps * world / secs, 1), "unit": UNIT,
                "h2d_bytes_per_step": B * HIDDEN * 2 + B * E * 4, "d2h_bytes_per_step": B * HIDDEN * 2,
                "ms_per_step": round(secs * 1e3 / args.steps, 4)}
-    launches = 3  # per step: the 3 expert decode launches are ours (router/SwiGLU/combine are torch ops)
+    # our kernels per step, counted by the library on one eager step
+    from vqlab_b200 import _lib
+    c0 = _lib.launch_count()
+    layers[0](xs_last[0], lg_last[0])
+    torch.cuda.synchronize()
+    launches = _lib.launch_count() - c0
     return results, roof, e2e, launches
 
 
@@ -368,6 +455,9 @@ def main(argv=None) -> int:
     ap.add_argument("--layers", type=int, default=8)
     ap.add_argument("--skip-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--skip-prefill", action="store_true")
+    ap.add_argument("--cpu-tokens", type=int, default=1024,
+                    help="tokens of the CPU baseline sample (~10 s of oracle work on 16 host threads)")
     args = ap.parse_args(argv)
     args.warmup = max(3, args.warmup)
 
@@ -388,6 +478,10 @@ def main(argv=None) -> int:
     from vqlab_b200 import _lib
     _lib.lib()
     results, roof, e2e, launches = gpu_arm(args, rank, world, dev)
+    prefill = None
+    if not args.skip_prefill:
+        _, peak_tf, peak_kind = _peaks()
+        prefill = prefill_leg(torch, dev, args, peak_tf, peak_kind, rank, world)
     if rank == 0:
         head = results[args.batch]
         line = {"metric": METRIC, "value": round(head["tokens_per_s"], 1), "unit": UNIT, "n_gpus": world,
@@ -401,9 +495,12 @@ def main(argv=None) -> int:
                                      "hbm_gbs": round(r["hbm_gbs"], 1),
                                      "distinct_experts": round(r["distinct_experts_mean"], 1)}
                             for b, r in results.items()},
-                "roofline": roof, "e2e": e2e, "gpu_launches": launches * args.steps}
+                "roofline": roof, "e2e": e2e, "gpu_launches": launches * args.steps,
+                "gpu_launches_per_step": launches}
+        if prefill is not None:
+            line["prefill"] = prefill
         if not args.no_cpu_baseline:
-            line["cpu_baseline"] = cpu_baseline_block(8)
+            line["cpu_baseline"] = cpu_baseline_block(args.cpu_tokens)
         print(json.dumps(line), flush=True)
     if world > 1:
         torch.distributed.barrier()

@@ -54,9 +54,12 @@ typedef enum vqb_status {
 
 typedef enum vqb_dtype { VQB_F16 = 0, VQB_BF16 = 1, VQB_F32 = 2 } vqb_dtype;
 
-/* Kernel path selection.  AUTO follows the reference's cutoffs: the fused
- * small-N kernel below VQ_FUSED_MAX_N = 512 pairs (vq_switch.py:45, :5313),
- * the grouped prefill GEMM above it. */
+/* Kernel path selection.  AUTO for vqb_switch_forward: the fused small-N
+ * kernel up to VQ_FUSED_MAX_N = 512 pairs as in the reference
+ * (vq_switch.py:45, :5313), the grouped prefill GEMM above it only when the
+ * experts also average more than 3 pairs each (below that density the
+ * expert-grouped decode kernel is faster on a B200).  AUTO for
+ * vqb_dense_forward follows the reference's dense cutoffs. */
 typedef enum vqb_path { VQB_PATH_AUTO = 0, VQB_PATH_DECODE = 1, VQB_PATH_PREFILL = 2 } vqb_path;
 
 /* One VQ-coded projection: a VQSwitchLinear (E experts) or a VQLinear (E = 1).
@@ -136,6 +139,20 @@ vqb_status vqb_switch_forward_static(const vqb_linear_desc* desc, const void* x,
                                      int32_t n_tokens, const uint32_t* indices, int32_t top_k,
                                      void* y, vqb_dtype y_dtype, const vqb_options* opts,
                                      vqb_stream_t stream);
+
+/* Measurement aids; neither has a counterpart in the reference, whose Metal
+ * runtime exposes no launch accounting or per-kernel timing.
+ *
+ * vqb_launch_count: kernels this library has launched in the process so far
+ * (every route, conversion, decode and GEMM kernel; not graph replays).
+ *
+ * vqb_time_next_kernel: arm a one-shot timer for the calling host thread.  The
+ * next vqb_switch_forward / vqb_dense_forward call on this thread records
+ * start_event (a cudaEvent_t) on its stream immediately before its dominant
+ * kernel -- the decode or grouped-GEMM kernel -- and stop_event immediately
+ * after it, then disarms.  Both NULL disarms; one NULL is VQB_NULL_POINTER. */
+uint64_t vqb_launch_count(void);
+vqb_status vqb_time_next_kernel(void* start_event, void* stop_event);
 
 /* Scratch bytes vqb_dense_forward needs for n_rows input rows. */
 size_t vqb_dense_workspace_size(const vqb_linear_desc* desc, int64_t n_rows, const vqb_options* opts);

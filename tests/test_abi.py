@@ -134,3 +134,13 @@ def test_dense_module_properties():
     assert (lin.input_dims, lin.output_dims) == (128, 32)
     with pytest.raises(ValueError):
         lin(torch.zeros((1, 128), dtype=torch.bfloat16))
+
+
+def test_measurement_aids_host_side():
+    """vqb_launch_count / vqb_time_next_kernel need no GPU for these paths:
+    the count is readable, a half-armed timer is refused, NULL/NULL disarms."""
+    L = _lib.lib()
+    assert L.vqb_launch_count() >= 0
+    assert L.vqb_time_next_kernel(ctypes.c_void_p(16), None) == 10  # VQB_NULL_POINTER
+    assert L.vqb_time_next_kernel(None, ctypes.c_void_p(16)) == 10
+    assert L.vqb_time_next_kernel(None, None) == 0

@@ -1,0 +1,46 @@
+"""The library's measurement aids on a B200: the launch counter counts our
+kernels, and the one-shot timer brackets exactly the dominant kernel."""
+import numpy as np
+import pytest
+import torch
+
+from oracle import oracle as orc
+from vqlab_b200 import VQSwitchLinear, _lib
+from vq_cases import make_layer, to_torch
+
+pytestmark = pytest.mark.gpu
+
+
+def _layer():
+    L = make_layer(E=8, OUT=256, IN=512, D=8, K=4096, G=64, seed=5)
+    codes, cb, sc = to_torch(L)
+    return L, VQSwitchLinear(codes, cb, sc, group_size=64, pack_bits=L.bits, in_features=512)
+
+
+@pytest.mark.parametrize("T", [4, 600])  # decode kernel, grouped tcgen05 GEMM
+def test_launch_count_and_kernel_timer(T):
+    L, m = _layer()
+    rng = np.random.default_rng(T)
+    idx = torch.from_numpy(rng.integers(0, 8, (T, 2)).astype(np.int32)).cuda()
+    x = torch.from_numpy(rng.standard_normal((T, 1, 1, 512)).astype(np.float32)).cuda().to(torch.bfloat16)
+    m(x, idx)
+    torch.cuda.synchronize()
+    c0 = _lib.launch_count()
+    y = m(x, idx)
+    torch.cuda.synchronize()
+    assert _lib.launch_count() - c0 == 3  # route + x conversion/gather + decode/GEMM kernel
+    s = torch.cuda.current_stream()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record(s)
+    b.record(s)
+    torch.cuda.synchronize()
+    _lib.time_next_kernel(a, b)
+    y2 = m(x, idx)
+    torch.cuda.synchronize()
+    assert a.elapsed_time(b) > 0.0
+    assert torch.equal(y, y2)
+    # the timer is one-shot: a further call leaves the events alone
+    t = a.elapsed_time(b)
+    m(x, idx)
+    torch.cuda.synchronize()
+    assert a.elapsed_time(b) == t

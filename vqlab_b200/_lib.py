@@ -89,6 +89,10 @@ def _bind(L):
     L.vqb_dense_forward.argtypes = [P, P, i32, i64, P, i32, P, sz, P, P]
     L.vqb_switch_forward_static.restype = i32
     L.vqb_switch_forward_static.argtypes = [P, P, i32, i32, P, i32, P, i32, P, P]
+    L.vqb_launch_count.restype = ctypes.c_uint64
+    L.vqb_launch_count.argtypes = []
+    L.vqb_time_next_kernel.restype = i32
+    L.vqb_time_next_kernel.argtypes = [P, P]
     return L
 
 
@@ -132,4 +136,17 @@ def version() -> str:
 def exported_symbols():
     """Names of every function include/vqb.h declares (for the load test)."""
     return ["vqb_version", "vqb_status_string", "vqb_unpack", "vqb_switch_workspace_size",
-            "vqb_switch_forward", "vqb_dense_workspace_size", "vqb_dense_forward", "vqb_switch_forward_static"]
+            "vqb_switch_forward", "vqb_dense_workspace_size", "vqb_dense_forward", "vqb_switch_forward_static",
+            "vqb_launch_count", "vqb_time_next_kernel"]
+
+
+def launch_count() -> int:
+    """Kernels libvqb200.so has launched in this process (graph replays excluded)."""
+    return int(lib().vqb_launch_count())
+
+
+def time_next_kernel(start_event, stop_event) -> None:
+    """Record two torch.cuda.Event objects around the dominant kernel of this
+    thread's next projection call (on the call's stream), then disarm."""
+    check(lib().vqb_time_next_kernel(ctypes.c_void_p(start_event.cuda_event), ctypes.c_void_p(stop_event.cuda_event)),
+          "vqb_time_next_kernel")

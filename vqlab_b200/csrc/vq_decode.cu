@@ -275,8 +275,11 @@ vqb_status launch_decode(const LinearGeometry& geo, const void* x, int x_dtype, 
                                 static_cast<int>(smem));                                            \
       if (ce != cudaSuccess) break;                                                                 \
     }                                                                                               \
+    timer_before(stream);                                                                           \
     kern<<<grid, 256, smem, stream>>>(prm);                                                         \
+    timer_after(stream);                                                                            \
     ce = cudaGetLastError();                                                                        \
+    if (ce == cudaSuccess) note_launch();                                                           \
   } while (0)
 #define VQB_LAUNCH(DD, VV)                  \
   do {                                      \

@@ -520,6 +520,7 @@ vqb_status launch_decode_mma(const LinearGeometry& geo, const GroupedDecodeArgs&
     if (blocks > 4 * nsm) blocks = 4 * nsm;
     x_to_16bit_kernel<<<static_cast<unsigned>(blocks), 256, 0, stream>>>(a.x, a.x_dtype, n, WR == 1 ? 1 : 0, x16);
     if (cudaGetLastError() != cudaSuccess) return VQB_CUDA_ERROR;
+    note_launch();
   }
   MParams prm{};
   prm.codes = static_cast<const uint32_t*>(geo.codes);
@@ -624,7 +625,10 @@ vqb_status launch_decode_mma(const LinearGeometry& geo, const GroupedDecodeArgs&
     attr[0].val.clusterDim.z = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
+    timer_before(stream);
     ce = cudaLaunchKernelEx(&cfg, kern, prm);
+    timer_after(stream);
+    if (ce == cudaSuccess) note_launch();
   };
 #define VQB_M1(DD, WW, NN)                                                               \
   do {                                                                                   \

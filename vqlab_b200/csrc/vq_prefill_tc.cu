@@ -842,6 +842,7 @@ vqb_status launch_prefill_tc(const LinearGeometry& geo, const void* x, int x_dty
     gather_sorted_kernel<<<static_cast<unsigned>(blocks), 256, 0, stream>>>(x, x_dtype, rw.sorted, N, krep, geo.IN,
                                                                             bf16_operands ? 1 : 0, xs);
     if (cudaGetLastError() != cudaSuccess) return VQB_CUDA_ERROR;
+    note_launch();
   }
   // 2. TMA maps: xs [N, IN] 16-bit seen as [chunk][token][64 k] (boxes of
   //    32 x 4, 64 x 2 and 128 x 1 tokens x chunks, 128-byte swizzle); codes
@@ -868,8 +869,12 @@ vqb_status launch_prefill_tc(const LinearGeometry& geo, const void* x, int x_dty
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)) != cudaSuccess)
     return VQB_CUDA_ERROR;
   void* args[] = {&xmaps[0], &xmaps[1], &xmaps[2], &cmap, &smap, &prm};
-  if (cudaLaunchKernel(kern, dim3(g_sms_tc), dim3(kThreads), args, smem, stream) != cudaSuccess) return VQB_CUDA_ERROR;
-  return cudaGetLastError() == cudaSuccess ? VQB_OK : VQB_CUDA_ERROR;
+  timer_before(stream);
+  const cudaError_t ce = cudaLaunchKernel(kern, dim3(g_sms_tc), dim3(kThreads), args, smem, stream);
+  timer_after(stream);
+  if (ce != cudaSuccess || cudaGetLastError() != cudaSuccess) return VQB_CUDA_ERROR;
+  note_launch();
+  return VQB_OK;
 }
 
 }  // namespace vqb

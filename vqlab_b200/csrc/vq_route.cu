@@ -6,32 +6,72 @@
 // produces, in the caller's workspace:
 //   counts[E]          pairs per expert
 //   offsets[E+1]       exclusive prefix of counts
-//   sorted[N]          pair ids grouped by expert (order inside an expert is
-//                      not fixed; every pair's output is computed on its own,
-//                      so results do not depend on it)
+//   sorted[N]          pair ids grouped by expert, ascending inside an expert
+//                      (a stable counting sort, like the reference's stable
+//                      argsort), so tile contents -- and with them the
+//                      GEMM's summation order -- are the same on every call
 //   chunks[*]          (expert, first sorted slot, pair count <= max_pairs)
 //   meta[0]            number of chunks; meta[1] error flag (expert id >= E)
-// One CTA handles the whole batch (decode sizes: N up to a few thousand).
+// One CTA handles the whole batch.  Warp w owns the contiguous pair range
+// [w*per, (w+1)*per): it counts its pairs per expert into its own row of a
+// [32][E] shared table (lanes of a warp that share an expert are grouped with
+// __match_any_sync, the lowest lane adds the group's size), the table is
+// scanned over warps per expert, and the warp walks its range again placing
+// each pair at its expert's running slot.
 #include "vqb_common.cuh"
 #include "vqb_internal.h"
 
 namespace vqb {
 
-__global__ void __launch_bounds__(1024) route_small_kernel(const uint32_t* __restrict__ idx, int N, int E,
-                                                            int max_pairs, RouteWorkspace ws) {
+namespace {
+
+constexpr int kRouteThreads = 1024;
+constexpr int kRouteWarps = kRouteThreads / 32;
+
+__device__ __forceinline__ uint32_t expert_of(const uint32_t* idx, int p, int E, int* meta) {
+  uint32_t e = idx ? idx[p] : 0u;
+  if (e >= static_cast<uint32_t>(E)) {
+    meta[1] = VQB_BAD_ROUTING;  // reported; the pair is routed to expert 0 so no read goes out of range
+    e = 0;
+  }
+  return e;
+}
+
+}  // namespace
+
+__global__ void __launch_bounds__(kRouteThreads) route_small_kernel(const uint32_t* __restrict__ idx, int N, int E,
+                                                                     int max_pairs, RouteWorkspace ws) {
   extern __shared__ int sh[];
-  int* cnt = sh;            // [E]
-  int* cur = sh + E;        // [E]
-  int* nch = sh + 2 * E;    // [E] chunks per expert, then its exclusive scan
-  for (int e = threadIdx.x; e < E; e += blockDim.x) cnt[e] = 0;
+  int* cnt = sh;                 // [E]
+  int* nch = sh + E;             // [E] chunk-count prefix
+  int* tab = sh + 2 * E;         // [kRouteWarps][E] per-warp counts, then per-warp running slots
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+  const int per = (N + kRouteWarps - 1) / kRouteWarps;
+  const int lo = min(N, wid * per), hi = min(N, lo + per);
+  const uint32_t lt = (1u << lane) - 1u;
+
+  for (int i = threadIdx.x; i < kRouteWarps * E; i += blockDim.x) tab[i] = 0;
   __syncthreads();
-  for (int p = threadIdx.x; p < N; p += blockDim.x) {
-    uint32_t e = idx ? idx[p] : 0u;
-    if (e >= static_cast<uint32_t>(E)) {
-      ws.meta[1] = VQB_BAD_ROUTING;  // reported; the pair is routed to expert 0 so no read goes out of range
-      e = 0;
+  // 1. per-warp counts
+  int* row = tab + wid * E;
+  for (int b = lo; b < hi; b += 32) {
+    const int p = b + lane;
+    const bool valid = p < hi;
+    const uint32_t e = valid ? expert_of(idx, p, E, ws.meta) : 0xFFFFFFFFu;
+    const uint32_t peers = __match_any_sync(0xFFFFFFFFu, e);
+    if (valid && (peers & lt) == 0) row[e] += __popc(peers);
+    __syncwarp();
+  }
+  __syncthreads();
+  // 2. per expert: total, and exclusive prefix over warps
+  for (int e = threadIdx.x; e < E; e += blockDim.x) {
+    int run = 0;
+    for (int w = 0; w < kRouteWarps; ++w) {
+      const int c = tab[w * E + e];
+      tab[w * E + e] = run;
+      run += c;
     }
-    atomicAdd(&cnt[e], 1);
+    cnt[e] = run;
   }
   __syncthreads();
   {
@@ -39,11 +79,10 @@ __global__ void __launch_bounds__(1024) route_small_kernel(const uint32_t* __res
     // each thread scans a contiguous run of experts, the run totals are
     // scanned across the block through warp shuffles.
     __shared__ int2 wsum[32];
-    const int per = (E + blockDim.x - 1) / blockDim.x;
-    const int e0 = threadIdx.x * per, e1 = min(E, e0 + per);
+    const int pe = (E + blockDim.x - 1) / blockDim.x;
+    const int e0 = threadIdx.x * pe, e1 = min(E, e0 + pe);
     int a = 0, b = 0;
     for (int e = e0; e < e1; ++e) { a += cnt[e]; b += (cnt[e] + max_pairs - 1) / max_pairs; }
-    const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
     int ia = a, ib = b;
     for (int o = 1; o < 32; o <<= 1) {
       const int ta = __shfl_up_sync(0xffffffffu, ia, o), tb = __shfl_up_sync(0xffffffffu, ib, o);
@@ -64,7 +103,7 @@ __global__ void __launch_bounds__(1024) route_small_kernel(const uint32_t* __res
     int chunks = (wid > 0 ? wsum[wid - 1].y : 0) + ib - b;
     for (int e = e0; e < e1; ++e) {
       ws.offsets[e] = run;
-      cur[e] = run;
+      for (int w = 0; w < kRouteWarps; ++w) tab[w * E + e] += run;  // running slot of warp w in expert e
       run += cnt[e];
       nch[e] = chunks;
       chunks += (cnt[e] + max_pairs - 1) / max_pairs;
@@ -88,11 +127,20 @@ __global__ void __launch_bounds__(1024) route_small_kernel(const uint32_t* __res
       ws.chunks[base++] = ch;
     }
   }
-  for (int p = threadIdx.x; p < N; p += blockDim.x) {
-    uint32_t e = idx ? idx[p] : 0u;
-    if (e >= static_cast<uint32_t>(E)) e = 0;
-    const int slot = atomicAdd(&cur[e], 1);
-    ws.sorted[slot] = p;
+  // 3. stable placement: warp w walks its range again in order
+  for (int b = lo; b < hi; b += 32) {
+    const int p = b + lane;
+    const bool valid = p < hi;
+    uint32_t e = 0xFFFFFFFFu;
+    if (valid) {
+      e = idx ? idx[p] : 0u;
+      if (e >= static_cast<uint32_t>(E)) e = 0;
+    }
+    const uint32_t peers = __match_any_sync(0xFFFFFFFFu, e);
+    if (valid) ws.sorted[row[e] + __popc(peers & lt)] = p;
+    __syncwarp();
+    if (valid && (peers & lt) == 0) row[e] += __popc(peers);
+    __syncwarp();
   }
 }
 
@@ -122,15 +170,17 @@ RouteWorkspace carve_route_workspace(void* base, int N, int E) {
 
 vqb_status launch_route_small(const uint32_t* idx, int N, int E, int max_pairs, const RouteWorkspace& ws,
                               cudaStream_t stream) {
-  const size_t smem = sizeof(int) * 3 * static_cast<size_t>(E);
+  const size_t smem = sizeof(int) * (2 + kRouteWarps) * static_cast<size_t>(E);
   if (smem > 200 * 1024) return VQB_UNSUPPORTED_GEOMETRY;
   cudaError_t ce = cudaSuccess;
   if (smem > 48 * 1024)
     ce = cudaFuncSetAttribute(route_small_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                               static_cast<int>(smem));
   if (ce != cudaSuccess) return VQB_CUDA_ERROR;
-  route_small_kernel<<<1, 1024, smem, stream>>>(idx, N, E, max_pairs, ws);
-  return cudaGetLastError() == cudaSuccess ? VQB_OK : VQB_CUDA_ERROR;
+  route_small_kernel<<<1, kRouteThreads, smem, stream>>>(idx, N, E, max_pairs, ws);
+  if (cudaGetLastError() != cudaSuccess) return VQB_CUDA_ERROR;
+  note_launch();
+  return VQB_OK;
 }
 
 }  // namespace vqb

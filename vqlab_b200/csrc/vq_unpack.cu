@@ -33,7 +33,9 @@ vqb_status launch_unpack(const uint32_t* packed, int64_t rows, int64_t wpr, int 
   int64_t blocks = (total + 255) / 256;
   if (blocks > 148 * 64) blocks = 148 * 64;
   vq_unpack_kernel<<<static_cast<unsigned>(blocks), 256, 0, stream>>>(packed, rows, wpr, nsub, bits, out);
-  return cudaGetLastError() == cudaSuccess ? VQB_OK : VQB_CUDA_ERROR;
+  if (cudaGetLastError() != cudaSuccess) return VQB_CUDA_ERROR;
+  note_launch();
+  return VQB_OK;
 }
 
 }  // namespace vqb

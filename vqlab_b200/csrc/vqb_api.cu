@@ -1,5 +1,6 @@
 // C ABI of libvqb200.so (declared in include/vqb.h): argument validation with
 // the reference's error classes, path selection, workspace layout, launches.
+#include <atomic>
 #include <cstdio>
 
 #include "vqb_common.cuh"
@@ -53,6 +54,22 @@ vqb_status validate(const vqb_linear_desc* d, LinearGeometry* g) {
   g->codebook = d->codebook;
   g->scales = d->scales;
   return VQB_OK;
+}
+
+namespace {
+std::atomic<uint64_t> g_launches{0};
+thread_local cudaEvent_t t_timer_start = nullptr, t_timer_stop = nullptr;
+}  // namespace
+
+void note_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
+
+void timer_before(cudaStream_t stream) {
+  if (t_timer_start) cudaEventRecord(t_timer_start, stream);
+}
+
+void timer_after(cudaStream_t stream) {
+  if (t_timer_stop) cudaEventRecord(t_timer_stop, stream);
+  t_timer_start = t_timer_stop = nullptr;
 }
 
 static bool dtype_ok(int t) { return t == VQB_F16 || t == VQB_BF16 || t == VQB_F32; }
@@ -128,6 +145,15 @@ extern "C" {
 
 const char* vqb_version(void) { return "vqb200 0.1 sm_100a"; }
 
+uint64_t vqb_launch_count(void) { return g_launches.load(std::memory_order_relaxed); }
+
+vqb_status vqb_time_next_kernel(void* start_event, void* stop_event) {
+  if ((start_event == nullptr) != (stop_event == nullptr)) return VQB_NULL_POINTER;
+  t_timer_start = static_cast<cudaEvent_t>(start_event);
+  t_timer_stop = static_cast<cudaEvent_t>(stop_event);
+  return VQB_OK;
+}
+
 const char* vqb_status_string(vqb_status s) {
   switch (s) {
     case VQB_OK: return "ok";
@@ -178,11 +204,18 @@ vqb_status vqb_switch_forward(const vqb_linear_desc* desc, const void* x, vqb_dt
   if (!x || !indices || !y) return VQB_NULL_POINTER;
   if (workspace_bytes < vqb_switch_workspace_size(desc, n_tokens, top_k, opts)) return VQB_WORKSPACE_TOO_SMALL;
   if (!workspace) return VQB_NULL_POINTER;
-  // Path: the fused small-N kernel up to VQ_FUSED_MAX_N = 512 pairs, the
-  // grouped GEMM above it (vq_switch.py:45, :5313-5315).
+  // Path: the reference runs the fused small-N kernel up to VQ_FUSED_MAX_N =
+  // 512 pairs and the grouped GEMM above it (vq_switch.py:45, :5313-5315).
+  // The grouped GEMM decodes every routed expert's full weight tile, so on a
+  // B200 it only pays once experts average more than kGemmPairsPerExpert
+  // pairs (measured crossover on the 512-expert, 1024 x 4096 gate: the decode
+  // kernel is faster at <= 2.5 pairs per expert, the GEMM at >= 5); AUTO takes
+  // the GEMM when both cutoffs are passed.
+  constexpr int64_t kGemmPairsPerExpert = 3;
   const int path = opts ? opts->path : VQB_PATH_AUTO;
   const int max_fused = (opts && opts->max_fused_pairs > 0) ? opts->max_fused_pairs : 512;
-  const bool large = path == VQB_PATH_PREFILL || (path == VQB_PATH_AUTO && N > max_fused);
+  const bool large = path == VQB_PATH_PREFILL ||
+                     (path == VQB_PATH_AUTO && N > max_fused && N > kGemmPairsPerExpert * geo.E);
   // MoE numerics: x narrowed to fp16, fp32 accumulation, fp16 output rounding
   // then the caller's dtype (vq_switch.py:5301-5308, :5423).
   return run_linear(geo, x, x_dtype, n_tokens, indices, top_k, N, y, y_dtype, workspace, opts,

@@ -72,6 +72,14 @@ vqb_status launch_prefill_tc(const LinearGeometry& geo, const void* x, int x_dty
                              int* status, cudaStream_t stream);
 constexpr int kPrefillTileTokens = 128;
 
+// Launch accounting and the one-shot kernel timer (vqb_api.cu): every kernel
+// launch of the library calls note_launch(); the dominant kernel of a call
+// (the decode or grouped-GEMM kernel) is bracketed by timer_before/after,
+// which record the events armed by vqb_time_next_kernel on its stream.
+void note_launch();
+void timer_before(cudaStream_t stream);
+void timer_after(cudaStream_t stream);
+
 // Workspace layout and the shared body of the switch / dense entry points (vqb_api.cu).
 size_t linear_workspace_bytes(int N, int E, int64_t T, int IN);
 vqb_status run_linear(const LinearGeometry& geo, const void* x, int x_dtype, int n_tokens, const uint32_t* indices,
