@@ -15,9 +15,13 @@ reports TFLOP/s of the three expert projections.  Several independently seeded l
 weights a step reads are not in L2 from the previous step (the bytes each
 step touches, times the rotation, exceed the 126 MB L2).
 
-Multi-GPU (torchrun, one rank per GPU): each rank runs its own replica of
-the layer on its own tokens (weak scaling, no collective on the data path);
-`value` is all ranks' tokens over the max-over-ranks time.
+Multi-GPU (torchrun, one rank per GPU): expert parallelism (BASELINE config
+5): rank r holds experts [r*E/N, (r+1)*E/N) of every projection, each rank
+brings its own batch of tokens (weak scaling), and every layer dispatches the
+(token, slot) pairs to the owning ranks and combines the outputs back with
+NCCL all-to-alls (vqlab_b200.ep).  `value` is all ranks' tokens over the
+max-over-ranks time.  The dispatch reads its split sizes on the host, so
+multi-GPU steps run eagerly (single-GPU steps replay CUDA graphs).
 
 `--impl reference` times the reference's CPU path (the oracle port of the
 reference arithmetic, OpenMP over all host cores) on a bounded sample of the
@@ -83,7 +87,12 @@ class ClockSampler:
             self.f = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                 "-lms", "200"], stdout=self.f, stderr=subprocess.DEVNULL)
+                 "-lms", "100"], stdout=self.f, stderr=subprocess.DEVNULL)
+            # the timed region starts once the sampler is producing rows
+            t0 = time.time()
+            while time.time() - t0 < 3.0 and pathlib.Path(self.f.name).stat().st_size == 0:
+                time.sleep(0.02)
+            self.skip = len(pathlib.Path(self.f.name).read_text().splitlines())
         except Exception:
             self.proc = None
         return self
@@ -100,7 +109,8 @@ class ClockSampler:
         if self.proc is None or self.f is None:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
         self.f.flush()
-        rows = [r.split(",") for r in pathlib.Path(self.f.name).read_text().splitlines() if r.strip()]
+        rows = [r.split(",") for r in pathlib.Path(self.f.name).read_text().splitlines()[getattr(self, "skip", 0):]
+                if r.strip()]
         sm, mx, reasons = [], None, set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
         for r in rows:
@@ -121,21 +131,30 @@ class ClockSampler:
 
 # ------------------------------------------------------------------ GPU arm
 
-def make_layer(torch, dev, seed):
+def make_layer(torch, dev, seed, rank=0, world=1):
+    """One seeded MoE layer; with world > 1 this rank's expert shard of it
+    wrapped in the expert-parallel block (codebooks are per layer, so every
+    rank builds the same ones)."""
     from vqlab_b200 import VQSwitchLinear
     from vqlab_b200.moe import VQMoEBlock
+    from vqlab_b200.ep import EPMoEBlock
+    e_local = E // world
     gen = torch.Generator(device=dev)
-    gen.manual_seed(seed)
+    gen.manual_seed(seed * 1009 + rank)
+    cgen = torch.Generator(device=dev)
+    cgen.manual_seed(seed)
 
     def proj(out, inn):
         # uniform random words ARE uniform 14-bit codes: K = 2^BITS and NSUB % 32 == 0
-        codes = torch.randint(-2 ** 31, 2 ** 31 - 1, (E, out, _wpr(inn // D)), dtype=torch.int32, device=dev,
+        codes = torch.randint(-2 ** 31, 2 ** 31 - 1, (e_local, out, _wpr(inn // D)), dtype=torch.int32, device=dev,
                               generator=gen)
-        cb = (torch.randn((K, D), device=dev, generator=gen) * 0.02).to(torch.float16)
-        sc = (torch.rand((E, out, inn // G), device=dev, generator=gen) + 0.5).to(torch.float16)
+        cb = (torch.randn((K, D), device=dev, generator=cgen) * 0.02).to(torch.float16)
+        sc = (torch.rand((e_local, out, inn // G), device=dev, generator=gen) + 0.5).to(torch.float16)
         return VQSwitchLinear(codes, cb, sc, group_size=G, pack_bits=BITS, in_features=inn)
 
-    return VQMoEBlock(proj(INTER, HIDDEN), proj(INTER, HIDDEN), proj(HIDDEN, INTER), TOPK)
+    if world == 1:
+        return VQMoEBlock(proj(INTER, HIDDEN), proj(INTER, HIDDEN), proj(HIDDEN, INTER), TOPK)
+    return EPMoEBlock(proj(INTER, HIDDEN), proj(INTER, HIDDEN), proj(HIDDEN, INTER), TOPK, num_experts=E)
 
 
 def distinct_experts(torch, logits):
@@ -148,6 +167,24 @@ def layer_bytes(n_distinct, batch):
     per_expert = sum(EXPERT_BYTES.values())
     act = batch * HIDDEN * 2 * 2 + batch * TOPK * INTER * 2 * 3 + batch * TOPK * HIDDEN * 2
     return n_distinct * per_expert + 3 * CODEBOOK_BYTES + act
+
+
+def time_eager_steps(torch, layers, xs, lg, steps, warmup):
+    """Eager layer steps (the expert-parallel dispatch reads split sizes on the host)."""
+    s = torch.cuda.current_stream()
+    n = len(layers)
+    for i in range(warmup):
+        layers[i % n](xs[i % n], lg[i % n])
+    torch.cuda.synchronize()
+    torch.distributed.barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(s)
+    for i in range(steps):
+        layers[i % n](xs[i % n], lg[i % n])
+    e1.record(s)
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1) / 1e3
 
 
 def time_graph_steps(torch, graphs, steps, warmup):
@@ -207,7 +244,7 @@ def zipf_logits(torch, dev, gen, T, alpha=1.1):
 def prefill_leg(torch, dev, args, peak_tf, peak_kind, rank, world):
     """one MoE layer on 4096 tokens, Zipf(1.1) routing."""
     T = 4096
-    layer = make_layer(torch, dev, 5000 + rank)
+    layer = make_layer(torch, dev, 5000, rank, world)
     gen = torch.Generator(device=dev)
     gen.manual_seed(17 + rank)
     x = torch.randn((T, HIDDEN), device=dev, generator=gen).to(torch.bfloat16)
@@ -215,7 +252,7 @@ def prefill_leg(torch, dev, args, peak_tf, peak_kind, rank, world):
     for _ in range(2):
         layer(x, lg)
     torch.cuda.synchronize()
-    steps = max(3, args.steps // 5)
+    steps = max(5, args.steps // 10)
     s = torch.cuda.current_stream()
     if world > 1:
         torch.distributed.barrier()
@@ -236,9 +273,13 @@ def prefill_leg(torch, dev, args, peak_tf, peak_kind, rank, world):
     from vqlab_b200.moe import route
     idx, _ = route(lg, TOPK)
     counts = torch.bincount(idx.reshape(-1).long(), minlength=E)
-    xg = x[:, None, None, :]
-    dur = kernel_seconds(torch, s, lambda i: layer.gate_proj(xg, idx), 5)
-    kflops = 2 * INTER * HIDDEN * T * TOPK
+    if world == 1:
+        xg, gidx = x[:, None, None, :], idx
+    else:
+        xr, er = layer.last_recv
+        xg, gidx = xr.reshape(-1, 1, 1, HIDDEN), er.reshape(-1, 1)
+    dur = kernel_seconds(torch, s, lambda i: layer.gate_proj(xg, gidx), 5)
+    kflops = 2 * INTER * HIDDEN * int(gidx.numel())
     ach = kflops / dur / 1e12
     return {"metric": "VQ-MoE prefill TFLOP/s (one MoE layer, C3: 4096 tokens, Zipf(1.1) top-10)",
             "value": round(flops * steps * world / secs / 1e12, 2), "unit": "TFLOP/s", "steps": steps,
@@ -247,8 +288,9 @@ def prefill_leg(torch, dev, args, peak_tf, peak_kind, rank, world):
                                   "min": int(counts.min())},
             "flops_per_layer": flops, "clocks": clk.summary(),
             "roofline": {"bound": "tensor", "achieved": round(ach, 1), "peak": peak_tf, "unit": "TFLOP/s",
-                         "frac": round(ach / peak_tf, 4), "traffic": profiled_traffic("vq_prefill_tc_kernel"),
-                         "kernel": "vq_prefill_tc_kernel (gate projection, 40960 pairs), timed alone",
+                         "frac": round(ach / peak_tf, 4),
+                         "traffic": profiled_traffic("vq_prefill_tc_kernel") if world == 1 else None,
+                         "kernel": "vq_prefill_tc_kernel (gate projection, %d pairs on this rank), timed alone" % int(gidx.numel()),
                          "us_per_launch": round(dur * 1e6, 1), "peak_kind": f"{peak_kind} burst bf16 GEMM"}}
 
 
@@ -258,7 +300,7 @@ def gpu_arm(args, rank, world, dev):
     peak_gbs, peak_tf, peak_kind = _peaks()
     batches = sorted(set([args.batch] + [int(b) for b in args.extra_batches.split(",") if b]))
     n_layers = args.layers
-    layers = [make_layer(torch, dev, 1000 * rank + l) for l in range(n_layers)]
+    layers = [make_layer(torch, dev, 1000 + l, rank, world) for l in range(n_layers)]
     gen = torch.Generator(device=dev)
     gen.manual_seed(7 + rank)
     results = {}
@@ -272,17 +314,18 @@ def gpu_arm(args, rank, world, dev):
             outs[l] = layers[l](xs[l], lg[l])
         torch.cuda.synchronize()
         graphs = []
-        for l in range(n_layers):
-            g = torch.cuda.CUDAGraph()
-            with torch.cuda.graph(g):
-                outs[l] = layers[l](xs[l], lg[l])
-            graphs.append(g)
-        torch.cuda.synchronize()
-        if world > 1:
-            torch.distributed.barrier()
+        if world == 1:
+            for l in range(n_layers):
+                g = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(g):
+                    outs[l] = layers[l](xs[l], lg[l])
+                graphs.append(g)
         torch.cuda.synchronize()
         with ClockSampler(dev.index if dev.index is not None else 0) as clk:
-            secs = time_graph_steps(torch, graphs, args.steps, args.warmup)
+            if world == 1:
+                secs = time_graph_steps(torch, graphs, args.steps, args.warmup)
+            else:
+                secs = time_eager_steps(torch, layers, xs, lg, args.steps, args.warmup)
         if world > 1:
             t = torch.tensor([secs], device=dev)
             torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
@@ -291,7 +334,8 @@ def gpu_arm(args, rank, world, dev):
         avg_bytes = statistics.mean(layer_bytes(n, B) for n in nd)
         results[B] = {"secs": secs, "ms_per_step": secs * 1e3 / args.steps,
                       "tokens_per_s": B * args.steps * world / secs,
-                      "hbm_gbs": avg_bytes * args.steps / secs / 1e9,
+                      # packed weight bytes of the experts a step touches (one GPU holds them all)
+                      "hbm_gbs": avg_bytes * args.steps / secs / 1e9 if world == 1 else None,
                       "distinct_experts_mean": statistics.mean(nd), "clocks": clk.summary()}
         del graphs
         torch.cuda.synchronize()
@@ -299,24 +343,31 @@ def gpu_arm(args, rank, world, dev):
 
     # ---- dominant kernel: the expert decode launch (gate projection), timed alone
     B = args.batch
-    m = layers[0]
-    x = torch.randn((B, 1, 1, HIDDEN), device=dev, generator=gen).to(torch.bfloat16)
-    lgt = torch.randn((B, E), device=dev, generator=gen)
-    from vqlab_b200.moe import route
-    idx, _ = route(lgt, TOPK)
-    nd = int(torch.unique(idx).numel())
     projs = [layers[l].gate_proj for l in range(n_layers)]
+    if world == 1:
+        x = torch.randn((B, 1, 1, HIDDEN), device=dev, generator=gen).to(torch.bfloat16)
+        lgt = torch.randn((B, E), device=dev, generator=gen)
+        from vqlab_b200.moe import route
+        idx, _ = route(lgt, TOPK)
+    else:
+        # the pairs this rank's experts received in the last expert-parallel step
+        xr, er = layers[0].last_recv
+        x, idx = xr.reshape(-1, 1, 1, HIDDEN), er.reshape(-1, 1)
+    npairs = int(idx.numel())
+    nd = int(torch.unique(idx).numel())
     for p in projs:
         p(x, idx)
     torch.cuda.synchronize()
     s = torch.cuda.current_stream()
     dur = kernel_seconds(torch, s, lambda i: projs[i % n_layers](x, idx), max(3, args.steps))
-    alg = nd * EXPERT_BYTES["gate"] + CODEBOOK_BYTES + B * HIDDEN * 2 + B * TOPK * INTER * 2
+    alg = nd * EXPERT_BYTES["gate"] + CODEBOOK_BYTES + x.shape[0] * HIDDEN * 2 + npairs * INTER * 2
     achieved = alg / dur / 1e9
-    traffic = profiled_traffic("vq_decode_mma_kernel")
+    traffic = profiled_traffic("vq_decode_mma_kernel") if world == 1 else None
     roof = {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak_gbs, "unit": "GB/s",
             "frac": round(achieved / peak_gbs, 4), "traffic": traffic,
-            "kernel": "vq_decode_mma_kernel (gate projection, batch %d, %d distinct experts), timed alone" % (B, nd),
+            "kernel": "%s (gate projection, %d pairs, %d distinct experts), timed alone" % (
+                "vq_decode_mma_kernel" if npairs <= 512 or npairs <= 3 * projs[0].num_experts else "vq_prefill_tc_kernel",
+                npairs, nd),
             "algorithmic_bytes_per_launch": alg, "us_per_launch": round(dur * 1e6, 2),
             "peak_kind": f"{peak_kind} burst copy bandwidth"}
 
@@ -440,14 +491,14 @@ def _config(args, world):
                         f"inter 1024, top-10, d8 K16384 14-bit, G64)",
             "global_batch": args.batch * world, "experts": E, "top_k": TOPK, "hidden": HIDDEN,
             "intermediate": INTER, "dim": D, "codebook": K, "pack_bits": BITS, "group": G,
-            "parallelism": f"replicas{world}" if world > 1 else "single",
+            "parallelism": f"ep{world} (experts sharded, NCCL all-to-all dispatch/combine)" if world > 1 else "single",
             "l2": f"{args.layers} independently seeded layers rotated per step (weights touched per cycle >> 126 MB L2)"}
 
 
 def main(argv=None) -> int:
     ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--batch", type=int, default=64)
@@ -489,17 +540,17 @@ def main(argv=None) -> int:
                 "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
                 "dtype": "f32 accumulate over fp16 (bf16 I/O)", "data": "synthetic (seeded)",
                 "config": _config(args, world), "clocks": head["clocks"],
-                "packed_weight_hbm_gbs": round(head["hbm_gbs"], 1),
+                "packed_weight_hbm_gbs": round(head["hbm_gbs"], 1) if head["hbm_gbs"] else None,
                 "batches": {str(b): {"tokens_per_s": round(r["tokens_per_s"], 1),
                                      "ms_per_step": round(r["ms_per_step"], 4),
-                                     "hbm_gbs": round(r["hbm_gbs"], 1),
+                                     "hbm_gbs": round(r["hbm_gbs"], 1) if r["hbm_gbs"] else None,
                                      "distinct_experts": round(r["distinct_experts_mean"], 1)}
                             for b, r in results.items()},
                 "roofline": roof, "e2e": e2e, "gpu_launches": launches * args.steps,
                 "gpu_launches_per_step": launches}
         if prefill is not None:
             line["prefill"] = prefill
-        if not args.no_cpu_baseline:
+        if not args.no_cpu_baseline and world == 1:
             line["cpu_baseline"] = cpu_baseline_block(args.cpu_tokens)
         print(json.dumps(line), flush=True)
     if world > 1:

@@ -1,0 +1,136 @@
+"""Expert parallelism for the VQ MoE block: experts sharded across ranks,
+tokens dispatched to the rank that owns each routed expert and the expert
+outputs combined back, one all-to-all each way per layer.
+
+The reference runs every expert on one device (its multi-node path pipelines
+whole layers, it never shards experts); the layer it computes is the
+`ref_moe` block (tests/test_qwen3_5_parity.py:180-204): fp32 softmax router,
+top-k, renormalised weights, per (token, slot) pair gate/up/down and the
+weighted sum over slots.  EPMoEBlock computes the same pairs, only on the
+rank that holds the pair's expert:
+
+  rank r holds experts [r * E_local, (r + 1) * E_local)   (E_local = E / world)
+  1. route locally: idx [T, k] global expert ids, weights [T, k]
+  2. order the T*k pairs by destination rank (stable), exchange the per-rank
+     pair counts (an all-to-all of `world` integers), then one all-to-all of
+     the pairs' token rows and one of their local expert ids
+  3. gate / up / SwiGLU / down on the received pairs (x given per pair)
+  4. the reverse all-to-all returns each pair's output row to the rank that
+     owns the token, which restores pair order and sums over the k slots.
+
+The collectives are torch.distributed all_to_all_single (NCCL over NVLink on
+B200 ranks; gloo for the CPU tests).  The expert compute is pluggable so the
+dispatch/combine logic can be tested without a GPU: `experts(x_pairs [R, H],
+local_ids [R]) -> y_pairs [R, H]`; the default runs the three VQSwitchLinear
+projections of this rank.
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass
+from typing import Callable, Optional
+
+import torch
+import torch.distributed as dist
+
+from .moe import route
+
+
+@dataclass
+class DispatchPlan:
+    order: torch.Tensor        # [P] flat pair ids sorted by destination rank (stable)
+    dest_counts: torch.Tensor  # [world] pairs this rank sends to each rank
+    send_counts: list          # host copy of dest_counts
+    recv_counts: list          # pairs this rank receives from each rank
+
+
+def dispatch_plan(idx: torch.Tensor, experts_per_rank: int, world: int, group=None) -> DispatchPlan:
+    """Stable order of the flat (token, slot) pairs by owning rank, and the
+    split sizes of both all-to-alls (one small all-to-all of counts, read on
+    the host: the data all-to-alls need them as lists)."""
+    dest = idx.reshape(-1).long() // experts_per_rank
+    order = torch.sort(dest, stable=True).indices
+    counts = torch.bincount(dest, minlength=world)
+    recv = torch.empty_like(counts)
+    if world > 1:
+        dist.all_to_all_single(recv, counts, group=group)
+    else:
+        recv.copy_(counts)
+    return DispatchPlan(order=order, dest_counts=counts, send_counts=counts.tolist(), recv_counts=recv.tolist())
+
+
+def _a2a(t: torch.Tensor, out_rows: int, out_split, in_split, group) -> torch.Tensor:
+    out = t.new_empty((out_rows,) + tuple(t.shape[1:]))
+    dist.all_to_all_single(out, t.contiguous(), output_split_sizes=out_split, input_split_sizes=in_split, group=group)
+    return out
+
+
+class EPMoEBlock(torch.nn.Module):
+    """One MoE layer with its experts sharded over the ranks of `group`.
+
+    gate_proj / up_proj / down_proj are this rank's VQSwitchLinear shards
+    (E_local experts each); num_experts is the global E (E % world == 0).
+    """
+
+    def __init__(self, gate_proj, up_proj, down_proj, top_k: int, num_experts: int, group=None,
+                 experts: Optional[Callable[[torch.Tensor, torch.Tensor], torch.Tensor]] = None):
+        super().__init__()
+        self.gate_proj, self.up_proj, self.down_proj = gate_proj, up_proj, down_proj
+        self.top_k = int(top_k)
+        self.group = group
+        self.world = dist.get_world_size(group) if dist.is_initialized() else 1
+        self.rank = dist.get_rank(group) if dist.is_initialized() else 0
+        if num_experts % self.world != 0:
+            raise ValueError(f"num_experts={num_experts} is not a multiple of the {self.world} ranks")
+        self.num_experts = int(num_experts)
+        self.experts_per_rank = self.num_experts // self.world
+        if gate_proj is not None and gate_proj.num_experts != self.experts_per_rank:
+            raise ValueError(f"rank shard holds {gate_proj.num_experts} experts, expected {self.experts_per_rank}")
+        self._experts = experts if experts is not None else self._vq_experts
+
+    def _vq_experts(self, xp: torch.Tensor, local: torch.Tensor) -> torch.Tensor:
+        """gate/up/SwiGLU/down of R pairs (x per pair) on this rank's VQ shards."""
+        R, H = xp.shape
+        if R == 0:
+            return xp.new_empty((0, self.down_proj.output_dims))
+        ids = local.to(torch.int32).reshape(R, 1)
+        xe = xp.reshape(R, 1, 1, H)
+        g = self.gate_proj(xe, ids)
+        u = self.up_proj(xe, ids)
+        h = (torch.nn.functional.silu(g.float()) * u.float()).to(xp.dtype)
+        return self.down_proj(h, ids).reshape(R, -1)
+
+    def forward(self, x: torch.Tensor, router_logits: torch.Tensor) -> torch.Tensor:
+        """x [T, H], router_logits [T, E] (this rank's tokens) -> y [T, H] in x's dtype."""
+        T, H = x.shape
+        k = self.top_k
+        idx, w = route(router_logits, k)
+        plan = dispatch_plan(idx, self.experts_per_rank, self.world, self.group)
+        flat = idx.reshape(-1).long()
+        tok = plan.order // k                                   # token of each sorted pair
+        send_x = x.index_select(0, tok)
+        send_e = (flat.index_select(0, plan.order) % self.experts_per_rank).to(torch.int32)
+        n_recv = sum(plan.recv_counts)
+        if self.world > 1:
+            recv_x = _a2a(send_x, n_recv, plan.recv_counts, plan.send_counts, self.group)
+            recv_e = _a2a(send_e, n_recv, plan.recv_counts, plan.send_counts, self.group)
+        else:
+            recv_x, recv_e = send_x, send_e
+        self.last_recv = (recv_x, recv_e)  # the pairs this rank computed (kept for measurement)
+        y_recv = self._experts(recv_x, recv_e)
+        if self.world > 1:
+            back = _a2a(y_recv, T * k, plan.send_counts, plan.recv_counts, self.group)
+        else:
+            back = y_recv
+        y_pairs = torch.empty_like(back)
+        y_pairs.index_copy_(0, plan.order, back)
+        y = (y_pairs.reshape(T, k, y_pairs.shape[1]).float() * w.unsqueeze(-1)).sum(dim=1)
+        return y.to(x.dtype)
+
+
+def shard_experts(codes: torch.Tensor, scales: torch.Tensor, rank: int, world: int):
+    """This rank's slice [rank*E/world, (rank+1)*E/world) of per-expert codes and scales."""
+    E = codes.shape[0]
+    if E % world != 0:
+        raise ValueError(f"{E} experts do not split over {world} ranks")
+    n = E // world
+    return codes[rank * n:(rank + 1) * n].contiguous(), scales[rank * n:(rank + 1) * n].contiguous()
