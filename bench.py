@@ -252,7 +252,7 @@ def prefill_leg(torch, dev, args, peak_tf, peak_kind, rank, world):
     for _ in range(2):
         layer(x, lg)
     torch.cuda.synchronize()
-    steps = max(5, args.steps // 10)
+    steps = max(10, args.steps // 5)
     s = torch.cuda.current_stream()
     if world > 1:
         torch.distributed.barrier()

@@ -140,6 +140,20 @@ vqb_status vqb_switch_forward_static(const vqb_linear_desc* desc, const void* x,
                                      void* y, vqb_dtype y_dtype, const vqb_options* opts,
                                      vqb_stream_t stream);
 
+/* The MoE block's elementwise work around the projections (the reference's
+ * block: tests/test_qwen3_5_parity.py:180-204; mlx_lm SwitchGLU), one pass each.
+ *
+ * vqb_swiglu: out[i] = dtype( silu(f32(gate[i])) * f32(up[i]) ) for n
+ * elements, silu(v) = v / (1 + exp(-v)) in fp32.
+ *
+ * vqb_moe_combine: out[t, :] = dtype( sum_{j<top_k} w[t, j] * f32(d[t, j, :]) ),
+ * expert outputs d [n_tokens, top_k, hidden], weights fp32 [n_tokens, top_k],
+ * the slot sum in fp32 in slot order (each product rounded, no fused
+ * multiply-add). */
+vqb_status vqb_swiglu(const void* gate, const void* up, void* out, int64_t n, vqb_dtype dtype, vqb_stream_t stream);
+vqb_status vqb_moe_combine(const void* expert_out, const float* weights, void* out, int32_t n_tokens,
+                           int32_t top_k, int32_t hidden, vqb_dtype dtype, vqb_stream_t stream);
+
 /* Measurement aids; neither has a counterpart in the reference, whose Metal
  * runtime exposes no launch accounting or per-kernel timing.
  *

@@ -1,0 +1,51 @@
+"""The whole MoE block on the GPU (router, gate/up/down VQ projections,
+fused SwiGLU, fused slot combine) against the oracle's composition of the
+same steps (router_topk, switch_fused walk, swiglu_bf16, combine_bf16 -- the
+reference block of tests/test_qwen3_5_parity.py:180-204)."""
+import numpy as np
+import pytest
+import torch
+
+from oracle import oracle as orc
+from vqlab_b200 import VQSwitchLinear
+from vqlab_b200.moe import VQMoEBlock
+
+pytestmark = pytest.mark.gpu
+
+E, H, I, K, BITS, G, TOPK = 16, 512, 256, 4096, 12, 64, 4
+
+
+def _proj(rng, out, inn):
+    codes = rng.integers(0, K, (E, out, inn // 8)).astype(np.uint16)
+    cb = (rng.standard_normal((K, 8)) * 0.02).astype(np.float16)
+    sc = rng.uniform(0.5, 1.5, (E, out, inn // G)).astype(np.float16)
+    return codes, orc.pack(codes, BITS), cb, sc
+
+
+def _vq(p, inn):
+    _, packed, cb, sc = p
+    return VQSwitchLinear(torch.from_numpy(packed.view(np.int32)).cuda(), torch.from_numpy(cb).cuda(),
+                          torch.from_numpy(sc).cuda(), group_size=G, pack_bits=BITS, in_features=inn)
+
+
+@pytest.mark.parametrize("T", [3, 64, 300])  # decode kernel, decode kernel, grouped GEMM (> 512 pairs, 75/expert)
+def test_moe_block_matches_oracle_composition(T):
+    rng = np.random.default_rng(T)
+    P = [_proj(rng, I, H), _proj(rng, I, H), _proj(rng, H, I)]
+    blk = VQMoEBlock(_vq(P[0], H), _vq(P[1], H), _vq(P[2], I), TOPK)
+    x = orc.round_bf16(rng.standard_normal((T, H)).astype(np.float32))
+    lg = rng.standard_normal((T, E)).astype(np.float32)
+    y = blk(torch.from_numpy(x).cuda().to(torch.bfloat16), torch.from_numpy(lg).cuda()).float().cpu().numpy()
+
+    idx, w = orc.router_topk(lg, TOPK)
+    li = idx.reshape(-1)
+    xh = orc.f16_bits(x)
+    out = lambda a: orc.round_bf16(orc.round_f16(a))
+    g = out(orc.switch_fused(P[0][0], P[0][2].view(np.uint16), P[0][3].view(np.uint16), xh, li, TOPK))
+    u = out(orc.switch_fused(P[1][0], P[1][2].view(np.uint16), P[1][3].view(np.uint16), xh, li, TOPK))
+    h = orc.swiglu_bf16(g, u)
+    d = out(orc.switch_fused(P[2][0], P[2][2].view(np.uint16), P[2][3].view(np.uint16), orc.f16_bits(h), li, 1))
+    ref = orc.combine_bf16(d.reshape(T, TOPK, H), w)
+    # bf16 outputs at every stage: 2e-3 of the output scale plus one bf16 ulp of each value
+    tol = 2e-3 * np.abs(ref).max() + np.abs(ref) * 2.0 ** -7 + 1e-6
+    assert np.all(np.abs(y - ref) <= 4 * tol), float(np.max(np.abs(y - ref) / tol))

@@ -89,6 +89,10 @@ def _bind(L):
     L.vqb_dense_forward.argtypes = [P, P, i32, i64, P, i32, P, sz, P, P]
     L.vqb_switch_forward_static.restype = i32
     L.vqb_switch_forward_static.argtypes = [P, P, i32, i32, P, i32, P, i32, P, P]
+    L.vqb_swiglu.restype = i32
+    L.vqb_swiglu.argtypes = [P, P, P, i64, i32, P]
+    L.vqb_moe_combine.restype = i32
+    L.vqb_moe_combine.argtypes = [P, P, P, i32, i32, i32, i32, P]
     L.vqb_launch_count.restype = ctypes.c_uint64
     L.vqb_launch_count.argtypes = []
     L.vqb_time_next_kernel.restype = i32
@@ -137,7 +141,7 @@ def exported_symbols():
     """Names of every function include/vqb.h declares (for the load test)."""
     return ["vqb_version", "vqb_status_string", "vqb_unpack", "vqb_switch_workspace_size",
             "vqb_switch_forward", "vqb_dense_workspace_size", "vqb_dense_forward", "vqb_switch_forward_static",
-            "vqb_launch_count", "vqb_time_next_kernel"]
+            "vqb_launch_count", "vqb_time_next_kernel", "vqb_swiglu", "vqb_moe_combine"]
 
 
 def launch_count() -> int:

@@ -1,0 +1,179 @@
+// The elementwise work of the MoE block around the three VQ projections, one
+// pass each instead of a chain of framework ops (the reference block:
+// tests/test_qwen3_5_parity.py:180-204, mlx_lm SwitchGLU):
+//   swiglu:  h = dtype( silu(f32(gate)) * f32(up) ),  silu(v) = v / (1 + exp(-v))
+//   combine: y[t, :] = dtype( sum_j w[t, j] * f32(d[t, j, :]) ), j = 0 .. k-1 in order, fp32
+// Both are HBM-bound streams; 16-byte vectors when the tensors allow it.
+#include "vqb_common.cuh"
+#include "vqb_internal.h"
+
+namespace vqb {
+
+namespace {
+
+template <typename T>
+__device__ __forceinline__ float to_f(T v);
+template <>
+__device__ __forceinline__ float to_f<__nv_bfloat16>(__nv_bfloat16 v) { return __bfloat162float(v); }
+template <>
+__device__ __forceinline__ float to_f<__half>(__half v) { return __half2float(v); }
+template <>
+__device__ __forceinline__ float to_f<float>(float v) { return v; }
+
+template <typename T>
+__device__ __forceinline__ T from_f(float v);
+template <>
+__device__ __forceinline__ __nv_bfloat16 from_f<__nv_bfloat16>(float v) { return __float2bfloat16_rn(v); }
+template <>
+__device__ __forceinline__ __half from_f<__half>(float v) { return __float2half_rn(v); }
+template <>
+__device__ __forceinline__ float from_f<float>(float v) { return v; }
+
+__device__ __forceinline__ float silu(float v) { return v / (1.0f + expf(-v)); }
+
+// VEC elements of T per thread-step (16 bytes when VEC * sizeof(T) == 16)
+template <typename T, int VEC>
+__global__ void swiglu_kernel(const T* __restrict__ g, const T* __restrict__ u, T* __restrict__ h, int64_t n) {
+  const int64_t nv = n / VEC;
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < nv;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    T gv[VEC], uv[VEC], hv[VEC];
+    if constexpr (VEC * sizeof(T) == 16) {
+      *reinterpret_cast<uint4*>(gv) = __ldg(reinterpret_cast<const uint4*>(g) + i);
+      *reinterpret_cast<uint4*>(uv) = __ldg(reinterpret_cast<const uint4*>(u) + i);
+    } else {
+#pragma unroll
+      for (int j = 0; j < VEC; ++j) { gv[j] = g[i * VEC + j]; uv[j] = u[i * VEC + j]; }
+    }
+#pragma unroll
+    for (int j = 0; j < VEC; ++j) hv[j] = from_f<T>(__fmul_rn(silu(to_f(gv[j])), to_f(uv[j])));
+    if constexpr (VEC * sizeof(T) == 16) {
+      reinterpret_cast<uint4*>(h)[i] = *reinterpret_cast<uint4*>(hv);
+    } else {
+#pragma unroll
+      for (int j = 0; j < VEC; ++j) h[i * VEC + j] = hv[j];
+    }
+  }
+}
+
+// one thread = VEC consecutive hidden elements of one token
+template <typename T, int VEC>
+__global__ void combine_kernel(const T* __restrict__ d, const float* __restrict__ w, T* __restrict__ y, int Tn, int k,
+                               int H) {
+  const int per_tok = H / VEC;
+  const int64_t total = static_cast<int64_t>(Tn) * per_tok;
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int t = static_cast<int>(i / per_tok);
+    const int c = static_cast<int>(i - static_cast<int64_t>(t) * per_tok);
+    float acc[VEC];
+#pragma unroll
+    for (int e = 0; e < VEC; ++e) acc[e] = 0.0f;
+    for (int j = 0; j < k; ++j) {
+      const float wj = __ldg(w + static_cast<int64_t>(t) * k + j);
+      const T* row = d + (static_cast<int64_t>(t) * k + j) * H + static_cast<int64_t>(c) * VEC;
+      T v[VEC];
+      if constexpr (VEC * sizeof(T) == 16) {
+        *reinterpret_cast<uint4*>(v) = __ldg(reinterpret_cast<const uint4*>(row));
+      } else {
+#pragma unroll
+        for (int e = 0; e < VEC; ++e) v[e] = row[e];
+      }
+#pragma unroll
+      for (int e = 0; e < VEC; ++e) acc[e] = __fadd_rn(acc[e], __fmul_rn(to_f(v[e]), wj));  // product rounded, no fma
+    }
+    T o[VEC];
+#pragma unroll
+    for (int e = 0; e < VEC; ++e) o[e] = from_f<T>(acc[e]);
+    T* out = y + static_cast<int64_t>(t) * H + static_cast<int64_t>(c) * VEC;
+    if constexpr (VEC * sizeof(T) == 16) {
+      *reinterpret_cast<uint4*>(out) = *reinterpret_cast<uint4*>(o);
+    } else {
+#pragma unroll
+      for (int e = 0; e < VEC; ++e) out[e] = o[e];
+    }
+  }
+}
+
+int g_sms_ops = 0;
+
+vqb_status ensure_sms() {
+  if (g_sms_ops == 0) {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return VQB_CUDA_ERROR;
+    if (cudaDeviceGetAttribute(&g_sms_ops, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return VQB_CUDA_ERROR;
+  }
+  return VQB_OK;
+}
+
+unsigned grid_for(int64_t work) {
+  int64_t b = (work + 255) / 256;
+  if (b > 8 * static_cast<int64_t>(g_sms_ops)) b = 8 * static_cast<int64_t>(g_sms_ops);
+  return static_cast<unsigned>(b < 1 ? 1 : b);
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+
+template <typename T>
+vqb_status launch_swiglu(const void* g, const void* u, void* h, int64_t n, cudaStream_t s) {
+  constexpr int V = 16 / sizeof(T);
+  if (n % V == 0 && aligned16(g) && aligned16(u) && aligned16(h)) {
+    swiglu_kernel<T, V><<<grid_for(n / V), 256, 0, s>>>(static_cast<const T*>(g), static_cast<const T*>(u),
+                                                        static_cast<T*>(h), n);
+  } else {
+    swiglu_kernel<T, 1><<<grid_for(n), 256, 0, s>>>(static_cast<const T*>(g), static_cast<const T*>(u),
+                                                    static_cast<T*>(h), n);
+  }
+  if (cudaGetLastError() != cudaSuccess) return VQB_CUDA_ERROR;
+  note_launch();
+  return VQB_OK;
+}
+
+template <typename T>
+vqb_status launch_combine(const void* d, const float* w, void* y, int Tn, int k, int H, cudaStream_t s) {
+  constexpr int V = 16 / sizeof(T);
+  if (H % V == 0 && aligned16(d) && aligned16(y)) {
+    combine_kernel<T, V><<<grid_for(static_cast<int64_t>(Tn) * (H / V)), 256, 0, s>>>(
+        static_cast<const T*>(d), w, static_cast<T*>(y), Tn, k, H);
+  } else {
+    combine_kernel<T, 1><<<grid_for(static_cast<int64_t>(Tn) * H), 256, 0, s>>>(static_cast<const T*>(d), w,
+                                                                               static_cast<T*>(y), Tn, k, H);
+  }
+  if (cudaGetLastError() != cudaSuccess) return VQB_CUDA_ERROR;
+  note_launch();
+  return VQB_OK;
+}
+
+}  // namespace
+
+}  // namespace vqb
+
+using namespace vqb;
+
+extern "C" vqb_status vqb_swiglu(const void* gate, const void* up, void* out, int64_t n, vqb_dtype dtype,
+                                 vqb_stream_t stream) {
+  if (n < 0) return VQB_BAD_SHAPE;
+  if (n == 0) return VQB_OK;
+  if (!gate || !up || !out) return VQB_NULL_POINTER;
+  vqb_status st = ensure_sms();
+  if (st != VQB_OK) return st;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  if (dtype == VQB_BF16) return launch_swiglu<__nv_bfloat16>(gate, up, out, n, s);
+  if (dtype == VQB_F16) return launch_swiglu<__half>(gate, up, out, n, s);
+  if (dtype == VQB_F32) return launch_swiglu<float>(gate, up, out, n, s);
+  return VQB_BAD_SHAPE;
+}
+
+extern "C" vqb_status vqb_moe_combine(const void* expert_out, const float* weights, void* out, int32_t n_tokens,
+                                      int32_t top_k, int32_t hidden, vqb_dtype dtype, vqb_stream_t stream) {
+  if (n_tokens < 0 || top_k < 1 || hidden < 1) return VQB_BAD_SHAPE;
+  if (n_tokens == 0) return VQB_OK;
+  if (!expert_out || !weights || !out) return VQB_NULL_POINTER;
+  vqb_status st = ensure_sms();
+  if (st != VQB_OK) return st;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  if (dtype == VQB_BF16) return launch_combine<__nv_bfloat16>(expert_out, weights, out, n_tokens, top_k, hidden, s);
+  if (dtype == VQB_F16) return launch_combine<__half>(expert_out, weights, out, n_tokens, top_k, hidden, s);
+  if (dtype == VQB_F32) return launch_combine<float>(expert_out, weights, out, n_tokens, top_k, hidden, s);
+  return VQB_BAD_SHAPE;
+}

@@ -238,32 +238,23 @@ __device__ __forceinline__ int pass_slice(int npass, int tile_local, int pass) {
 
 // ------------------------------------------------------------ decode side
 
-// Look one code up in the shared-memory codebook slice.  With several passes
-// a code outside the resident slice yields a zero weight; with one pass the
-// index is clamped to the table so a corrupt code cannot read past it.
+// Look one code up in the shared-memory codebook slice.  The slice holds
+// entries [h * KP, h * KP + KP) at [0, KP) and a zero entry at index `lim`
+// (KP, or K with one pass): `c ^ sel` is below KP exactly when the code lies
+// in the resident slice (sel = h * KP, KP a power of two), so min(c ^ sel, lim)
+// reads either the code's entry or the zero entry -- one unconditional
+// shared-memory load per code, and out-of-range codes read zeros too.
 template <int D>
-__device__ __forceinline__ void lookup(const uint16_t* cb_s, uint32_t c, bool masked, int kp_log2, int h,
-                                      uint32_t kmax, uint32_t* out) {
-  bool hit = true;
-  uint32_t li;
-  if (masked) {
-    hit = static_cast<int>(c >> kp_log2) == h;
-    li = c & ((1u << kp_log2) - 1u);
-  } else {
-    li = min(c, kmax);
-  }
+__device__ __forceinline__ void lookup(const uint16_t* cb_s, uint32_t c, uint32_t sel, uint32_t lim, uint32_t* out) {
+  const uint32_t li = min(c ^ sel, lim);
   if constexpr (D == 8) {
-    uint4 v = make_uint4(0, 0, 0, 0);
-    if (hit) v = reinterpret_cast<const uint4*>(cb_s)[li];
+    const uint4 v = reinterpret_cast<const uint4*>(cb_s)[li];
     out[0] = v.x; out[1] = v.y; out[2] = v.z; out[3] = v.w;
   } else if constexpr (D == 4) {
-    uint2 v = make_uint2(0, 0);
-    if (hit) v = reinterpret_cast<const uint2*>(cb_s)[li];
+    const uint2 v = reinterpret_cast<const uint2*>(cb_s)[li];
     out[0] = v.x; out[1] = v.y;
   } else {
-    uint32_t v = 0;
-    if (hit) v = reinterpret_cast<const uint32_t*>(cb_s)[li];
-    out[0] = v;
+    out[0] = reinterpret_cast<const uint32_t*>(cb_s)[li];
   }
 }
 
@@ -279,8 +270,8 @@ __device__ __forceinline__ void decode_chunk(const TParams& prm, const uint16_t*
                                              __half2 s2, int h, uint32_t* out) {
   constexpr int CPC = kChunkK / D;   // codes per chunk
   constexpr int WPC = D / 2;         // output words per code
-  const bool masked = prm.npass > 1;
-  const uint32_t kmax = static_cast<uint32_t>(prm.K - 1);
+  const uint32_t sel = prm.npass > 1 ? static_cast<uint32_t>(h) << prm.kp_log2 : 0u;
+  const uint32_t lim = prm.npass > 1 ? static_cast<uint32_t>(prm.kp) : static_cast<uint32_t>(prm.K);
   if constexpr (BITS > 0) {
     constexpr uint32_t MASK = (1u << BITS) - 1u;
     constexpr int NB = CPC * BITS;             // bits of the chunk
@@ -310,7 +301,7 @@ __device__ __forceinline__ void decode_chunk(const TParams& prm, const uint16_t*
       (void)dummy;
       const int bit = i * BITS, wi = bit >> 5, bs = bit & 31;
       const uint32_t v = (bs + BITS <= 32) ? (n[wi] >> bs) : __funnelshift_r(n[wi], n[wi + 1], bs);
-      lookup<D>(cb_s, v & MASK, masked, prm.kp_log2, h, kmax, out + WPC * i);
+      lookup<D>(cb_s, v & MASK, sel, lim, out + WPC * i);
     }
   } else {
     const int bits = prm.bits;
@@ -327,7 +318,7 @@ __device__ __forceinline__ void decode_chunk(const TParams& prm, const uint16_t*
       const uint32_t c = static_cast<uint32_t>(buf) & mask;
       buf >>= bits;
       nb -= bits;
-      lookup<D>(cb_s, c, masked, prm.kp_log2, h, kmax, out + WPC * i);
+      lookup<D>(cb_s, c, sel, lim, out + WPC * i);
     }
   }
 #pragma unroll
@@ -386,6 +377,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int i = 0; i < kIssuers; ++i) { mbar_init(&acc_full[i], 1); mbar_init(&mma_done[i], 1); }
     mbar_init(acc_empty, kDecodeWarps);
     *abort_flag = 0;
+    // the zero entry after the resident slice (never written by the slice copies)
+    uint16_t* zero = cb_s + static_cast<size_t>(prm.npass > 1 ? prm.kp : prm.K) * D;
+    for (int i = 0; i < D; ++i) zero[i] = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   if (warp == 0) {
@@ -815,18 +809,18 @@ vqb_status launch_prefill_tc(const LinearGeometry& geo, const void* x, int x_dty
   if (static_cast<size_t>(g_smem_optin) <= fixed + 1024) return VQB_UNSUPPORTED_GEOMETRY;
   const size_t avail = static_cast<size_t>(g_smem_optin) - fixed;
   const size_t entry = static_cast<size_t>(geo.D) * 2;
-  if (static_cast<size_t>(geo.K) * entry <= avail) {
+  if (static_cast<size_t>(geo.K + 1) * entry <= avail) {
     prm.kp = geo.K;
     prm.kp_log2 = 0;
     prm.npass = 1;
   } else {
     int l = 0;
-    while ((static_cast<size_t>(2) << l) * entry <= avail) ++l;
+    while (((static_cast<size_t>(2) << l) + 1) * entry <= avail) ++l;
     prm.kp_log2 = l;
     prm.kp = 1 << l;
     prm.npass = (geo.K + prm.kp - 1) / prm.kp;
   }
-  const size_t cb_bytes = (static_cast<size_t>(prm.kp) * entry + 15) & ~size_t(15);
+  const size_t cb_bytes = (static_cast<size_t>(prm.kp + 1) * entry + 15) & ~size_t(15);  // + the zero entry
   prm.off_win = kBStages * kBStageBytes;
   prm.off_cb = prm.off_win + kWStages * prm.win_stage_bytes;
   prm.off_bar = static_cast<int>(prm.off_cb + cb_bytes);

@@ -32,7 +32,7 @@ from typing import Callable, Optional
 import torch
 import torch.distributed as dist
 
-from .moe import route
+from .moe import combine, route, swiglu
 
 
 @dataclass
@@ -96,8 +96,7 @@ class EPMoEBlock(torch.nn.Module):
         xe = xp.reshape(R, 1, 1, H)
         g = self.gate_proj(xe, ids)
         u = self.up_proj(xe, ids)
-        h = (torch.nn.functional.silu(g.float()) * u.float()).to(xp.dtype)
-        return self.down_proj(h, ids).reshape(R, -1)
+        return self.down_proj(swiglu(g, u), ids).reshape(R, -1)
 
     def forward(self, x: torch.Tensor, router_logits: torch.Tensor) -> torch.Tensor:
         """x [T, H], router_logits [T, E] (this rank's tokens) -> y [T, H] in x's dtype."""
@@ -123,8 +122,10 @@ class EPMoEBlock(torch.nn.Module):
             back = y_recv
         y_pairs = torch.empty_like(back)
         y_pairs.index_copy_(0, plan.order, back)
-        y = (y_pairs.reshape(T, k, y_pairs.shape[1]).float() * w.unsqueeze(-1)).sum(dim=1)
-        return y.to(x.dtype)
+        y_pairs = y_pairs.reshape(T, k, y_pairs.shape[1])
+        if y_pairs.is_cuda and T > 0:
+            return combine(y_pairs, w)
+        return (y_pairs.float() * w.unsqueeze(-1)).sum(dim=1).to(x.dtype)
 
 
 def shard_experts(codes: torch.Tensor, scales: torch.Tensor, rank: int, world: int):

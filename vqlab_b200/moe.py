@@ -6,14 +6,43 @@ SwitchGLU / the Qwen3.5-MoE block, restated by the reference as the numpy
 of family/qwen3_5.py:110-118): fp32 softmax over the router logits, top-k,
 weights always renormalised, gate and up projections of each (token, slot)
 pair, h = silu(gate) * up, the down projection, and the weighted sum over
-the k slots.  Only the three projections are VQ kernels; the rest is small
-elementwise work on [T, k, ...] tensors.
+the k slots.  The three projections are the VQ kernels; SwiGLU and the slot
+combine are one fused library kernel each (vqb_swiglu, vqb_moe_combine).
 """
 from __future__ import annotations
 
+import ctypes
+
 import torch
 
-from .vq_switch import VQSwitchLinear
+from . import _lib
+from .vq_switch import VQSwitchLinear, _DTYPES, _stream_ptr
+
+
+def swiglu(g: torch.Tensor, u: torch.Tensor) -> torch.Tensor:
+    """dtype(silu(f32 g) * f32 u) in one pass (vqb_swiglu)."""
+    if g.shape != u.shape or g.dtype != u.dtype or not g.is_cuda or g.dtype not in _DTYPES:
+        raise ValueError("swiglu: gate and up must be CUDA tensors of one shape and a 16/32-bit float dtype")
+    g, u = g.contiguous(), u.contiguous()
+    h = torch.empty_like(g)
+    _lib.check(_lib.lib().vqb_swiglu(ctypes.c_void_p(g.data_ptr()), ctypes.c_void_p(u.data_ptr()),
+                                     ctypes.c_void_p(h.data_ptr()), g.numel(), _DTYPES[g.dtype], _stream_ptr(g.device)),
+               "vqb_swiglu")
+    return h
+
+
+def combine(d: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
+    """y[t] = dtype(sum_j w[t, j] * f32 d[t, j]) for expert outputs d [T, k, H] (vqb_moe_combine)."""
+    if d.dim() != 3 or w.shape != d.shape[:2] or not d.is_cuda or d.dtype not in _DTYPES:
+        raise ValueError("combine: expects d [T, k, H] on CUDA and weights [T, k]")
+    T, k, H = d.shape
+    d = d.contiguous()
+    w = w.to(torch.float32).contiguous()
+    y = torch.empty((T, H), dtype=d.dtype, device=d.device)
+    _lib.check(_lib.lib().vqb_moe_combine(ctypes.c_void_p(d.data_ptr()), ctypes.c_void_p(w.data_ptr()),
+                                          ctypes.c_void_p(y.data_ptr()), T, k, H, _DTYPES[d.dtype],
+                                          _stream_ptr(d.device)), "vqb_moe_combine")
+    return y
 
 
 def route(router_logits: torch.Tensor, top_k: int):
@@ -40,7 +69,6 @@ class VQMoEBlock(torch.nn.Module):
         xe = x.reshape(T, 1, 1, H)
         g = self.gate_proj(xe, idx)                       # [T, k, 1, I]
         u = self.up_proj(xe, idx)
-        h = (torch.nn.functional.silu(g.float()) * u.float()).to(x.dtype)
+        h = swiglu(g, u)
         d = self.down_proj(h, idx)                        # [T, k, 1, H]
-        y = (d.float().squeeze(2) * w.unsqueeze(-1)).sum(dim=1)
-        return y.to(x.dtype)
+        return combine(d.reshape(T, self.top_k, -1), w)
