@@ -55,7 +55,7 @@ constexpr int kBoxRows = 32;                         // x rows per TMA box
 constexpr int kBStageBytes = kMaxN * kChunkK * 2;    // 16 KB
 constexpr int kBStages = 4;                          // position g -> B stage g % 4
 constexpr int kAStages = 8;                          // position g -> A stage g % 8 (two per decode set)
-constexpr int kWStages = 2;                          // code/scale windows
+constexpr int kWStages = 3;                          // code/scale windows
 constexpr int kSets = 4;                             // window = kSets chunks, one per set
 constexpr int kIssuers = 2;                          // MMA issuing threads, one accumulator each
 constexpr int kDecodeWarps = 4 * kSets;              // 4 TMEM lane quarters per set
@@ -85,7 +85,8 @@ struct TParams {
   int y_dtype;
   int round_f16_first;
   int b_bf16;              // B (x) and A are bf16 (dense bf16 arm)
-  int W;                   // code window pitch in words (W / 4 odd: conflict-free 16-byte reads)
+  int W;                   // code window pitch in words
+  int wswz;                // window layout: 0 plain (W / 4 odd), 1 64-byte swizzle (W 16), 2 128-byte swizzle (W 32)
   int wpw;                 // code words per window of the packed row
   int code_stage_bytes;
   int win_stage_bytes;
@@ -259,15 +260,18 @@ __device__ __forceinline__ void lookup(const uint16_t* cb_s, uint32_t c, uint32_
 }
 
 // One row's 64 weights of one chunk -> 32 fp16x2 (or bf16x2) words.
-// crow: the row in the staged code window (16-byte aligned, pitch W words);
-// b0: bit offset of the chunk's first code in it (the same for every row).
+// crow: the row in the staged code window (16-byte aligned, pitch W words),
+// whose 16-byte units sit at index ^ xr (the TMA swizzle of this row; 0 for the
+// plain layout) -- either way 16-byte reads by 32 consecutive rows hit 32
+// different bank groups; b0: bit offset of the chunk's first code in the row
+// (the same for every row).
 // BITS > 0: the code width is a compile-time constant -- the chunk's bits are
 // read with conflict-free 16-byte loads, aligned to bit 0 with a funnel
 // shift, and every code sits at a fixed bit position.  BITS == 0: any width,
 // a sequential bit walk.
 template <int D, int BITS>
-__device__ __forceinline__ void decode_chunk(const TParams& prm, const uint16_t* cb_s, const uint32_t* crow, int b0,
-                                             __half2 s2, int h, uint32_t* out) {
+__device__ __forceinline__ void decode_chunk(const TParams& prm, const uint16_t* cb_s, const uint32_t* crow, int xr,
+                                             int b0, __half2 s2, int h, uint32_t* out) {
   constexpr int CPC = kChunkK / D;   // codes per chunk
   constexpr int WPC = D / 2;         // output words per code
   const uint32_t sel = prm.npass > 1 ? static_cast<uint32_t>(h) << prm.kp_log2 : 0u;
@@ -278,11 +282,11 @@ __device__ __forceinline__ void decode_chunk(const TParams& prm, const uint16_t*
     constexpr int NW = (NB + 31) / 32 + 1;     // words holding them after word alignment (+ straddle)
     constexpr int NQ = (NW + 3 + 3) / 4;       // 16-byte loads that cover a start anywhere in a 16-byte unit
     const int w0 = b0 >> 5, sh = b0 & 31, dw = w0 & 3;
-    const uint4* src = reinterpret_cast<const uint4*>(crow) + (w0 >> 2);
+    const uint4* row4 = reinterpret_cast<const uint4*>(crow);
     uint32_t q[4 * NQ];
 #pragma unroll
     for (int i = 0; i < NQ; ++i) {
-      const uint4 v = src[i];
+      const uint4 v = row4[((w0 >> 2) + i) ^ xr];
       q[4 * i] = v.x; q[4 * i + 1] = v.y; q[4 * i + 2] = v.z; q[4 * i + 3] = v.w;
     }
     // drop the dw leading words (dw is the same for the whole warp)
@@ -306,13 +310,14 @@ __device__ __forceinline__ void decode_chunk(const TParams& prm, const uint16_t*
   } else {
     const int bits = prm.bits;
     const uint32_t mask = (1u << bits) - 1u;
-    const uint32_t* p = crow + (b0 >> 5);
-    uint64_t buf = static_cast<uint64_t>(*p++) >> (b0 & 31);
+    auto word = [&](int wi) { return crow[(((wi >> 2) ^ xr) << 2) | (wi & 3)]; };
+    int wi = b0 >> 5;
+    uint64_t buf = static_cast<uint64_t>(word(wi++)) >> (b0 & 31);
     int nb = 32 - (b0 & 31);
 #pragma unroll 8
     for (int i = 0; i < CPC; ++i) {
       if (nb < bits) {
-        buf |= static_cast<uint64_t>(*p++) << nb;
+        buf |= static_cast<uint64_t>(word(wi++)) << nb;
         nb += 32;
       }
       const uint32_t c = static_cast<uint32_t>(buf) & mask;
@@ -540,6 +545,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int q = warp & 3;
     const uint32_t lane_off = static_cast<uint32_t>(q * 32) << 16;
     const int lrow = q * 32 + lane;                 // row inside the tile
+    const int xr = prm.wswz == 1 ? ((lrow >> 1) & 3) : (prm.wswz == 2 ? (lrow & 7) : 0);
     uint32_t ws = 0, wp = 0;
     uint32_t g = 0;                                 // position sequence number
     int cur = -1;
@@ -582,7 +588,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             const __half sh = __ushort_as_half(sc);
             const int wstart = w * prm.wpw;
             const int b0 = (wstart & 3) * 32 + s * (kChunkK / D) * prm.bits;
-            decode_chunk<D, BITS>(prm, cb_s, reinterpret_cast<const uint32_t*>(wst) + lrow * prm.W, b0,
+            decode_chunk<D, BITS>(prm, cb_s, reinterpret_cast<const uint32_t*>(wst) + lrow * prm.W, xr, b0,
                                   __halves2half2(sh, sh), h, out);
           } else {
 #pragma unroll
@@ -788,11 +794,21 @@ vqb_status launch_prefill_tc(const LinearGeometry& geo, const void* x, int x_dty
   prm.round_f16_first = round_f16_first ? 1 : 0;
   prm.b_bf16 = bf16_operands ? 1 : 0;
 
-  // code window: kSets chunks = 256 k = (256 / D) codes of every row
+  // code window: kSets chunks = 256 k = (256 / D) codes of every row, read
+  // from an aligned-down 16-byte boundary (up to o_max extra words); rows of
+  // 64 or 128 bytes take the matching TMA swizzle, longer rows an odd number
+  // of 16-byte units -- either way conflict-free 16-byte reads across rows
   prm.wpw = (kSets * kChunkK / geo.D) * geo.bits / 32;
   const int o_max = prm.wpw % 4 == 0 ? 0 : (prm.wpw % 2 == 0 ? 2 : 3);
-  int W = (o_max + prm.wpw + 3) & ~3;
-  if ((W / 4) % 2 == 0) W += 4;
+  const int need = o_max + prm.wpw;
+  int W;
+  if (need <= 16) { W = 16; prm.wswz = 1; }
+  else if (need <= 32) { W = 32; prm.wswz = 2; }
+  else {
+    W = (need + 3) & ~3;
+    if ((W / 4) % 2 == 0) W += 4;
+    prm.wswz = 0;
+  }
   prm.W = W;
   prm.code_stage_bytes = kTileM * W * 4;
   const bool g_pow2 = (geo.G & (geo.G - 1)) == 0;
@@ -848,8 +864,10 @@ vqb_status launch_prefill_tc(const LinearGeometry& geo, const void* x, int x_dty
       return VQB_CUDA_ERROR;
   }
   const uint64_t rows = static_cast<uint64_t>(geo.E) * geo.OUT;
+  const CUtensorMapSwizzle cswz = prm.wswz == 1 ? CU_TENSOR_MAP_SWIZZLE_64B
+                                  : (prm.wswz == 2 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE);
   if (!encode_2d(enc, &cmap, CU_TENSOR_MAP_DATA_TYPE_UINT32, 4, geo.codes, static_cast<uint64_t>(geo.row_words), rows,
-                 static_cast<uint32_t>(W), kTileM, CU_TENSOR_MAP_SWIZZLE_NONE))
+                 static_cast<uint32_t>(W), kTileM, cswz))
     return VQB_CUDA_ERROR;
   if (prm.scale_tma) {
     if (!encode_2d(enc, &smap, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, geo.scales, static_cast<uint64_t>(prm.NGRP), rows, 8,
