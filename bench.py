@@ -220,10 +220,11 @@ def kernel_seconds(torch, stream, call, reps):
     return statistics.mean(a.elapsed_time(b) for a, b in pairs) / 1e3
 
 
-def profiled_traffic(kernel):
-    """DRAM bytes per launch of `kernel` from the committed ncu summary
-    (profiles/*.txt lines `traffic_bytes_per_launch <kernel> <bytes>`), else None."""
-    for f in sorted((ROOT / "profiles").glob("*.txt")):
+def profiled_traffic(kernel, workload):
+    """DRAM bytes per launch of `kernel` on `workload` ("c2" / "c3") from the
+    committed ncu summaries (profiles/<kernel>_<workload>*.txt, line
+    `traffic_bytes_per_launch <kernel> <bytes>`), else None."""
+    for f in sorted((ROOT / "profiles").glob(f"{kernel}_{workload}*.txt")):
         for line in f.read_text().splitlines():
             parts = line.split()
             if len(parts) == 3 and parts[0] == "traffic_bytes_per_launch" and parts[1] == kernel:
@@ -289,7 +290,7 @@ def prefill_leg(torch, dev, args, peak_tf, peak_kind, rank, world):
             "flops_per_layer": flops, "clocks": clk.summary(),
             "roofline": {"bound": "tensor", "achieved": round(ach, 1), "peak": peak_tf, "unit": "TFLOP/s",
                          "frac": round(ach / peak_tf, 4),
-                         "traffic": profiled_traffic("vq_prefill_tc_kernel") if world == 1 else None,
+                         "traffic": profiled_traffic("vq_prefill_tc_kernel", "c3") if world == 1 else None,
                          "kernel": "vq_prefill_tc_kernel (gate projection, %d pairs on this rank), timed alone" % int(gidx.numel()),
                          "us_per_launch": round(dur * 1e6, 1), "peak_kind": f"{peak_kind} burst bf16 GEMM"}}
 
@@ -362,12 +363,12 @@ def gpu_arm(args, rank, world, dev):
     dur = kernel_seconds(torch, s, lambda i: projs[i % n_layers](x, idx), max(3, args.steps))
     alg = nd * EXPERT_BYTES["gate"] + CODEBOOK_BYTES + x.shape[0] * HIDDEN * 2 + npairs * INTER * 2
     achieved = alg / dur / 1e9
-    traffic = profiled_traffic("vq_decode_mma_kernel") if world == 1 else None
+    kname = ("vq_decode_mma_kernel" if npairs <= 512 or npairs * HIDDEN <= 4608 * projs[0].num_experts
+             else "vq_prefill_tc_kernel")
+    traffic = profiled_traffic(kname, "c2") if world == 1 else None
     roof = {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak_gbs, "unit": "GB/s",
             "frac": round(achieved / peak_gbs, 4), "traffic": traffic,
-            "kernel": "%s (gate projection, %d pairs, %d distinct experts), timed alone" % (
-                "vq_decode_mma_kernel" if npairs <= 512 or npairs <= 3 * projs[0].num_experts else "vq_prefill_tc_kernel",
-                npairs, nd),
+            "kernel": "%s (gate projection, %d pairs, %d distinct experts), timed alone" % (kname, npairs, nd),
             "algorithmic_bytes_per_launch": alg, "us_per_launch": round(dur * 1e6, 2),
             "peak_kind": f"{peak_kind} burst copy bandwidth"}
 
@@ -507,8 +508,8 @@ def main(argv=None) -> int:
     ap.add_argument("--skip-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--skip-prefill", action="store_true")
-    ap.add_argument("--cpu-tokens", type=int, default=1024,
-                    help="tokens of the CPU baseline sample (~10 s of oracle work on 16 host threads)")
+    ap.add_argument("--cpu-tokens", type=int, default=2048,
+                    help="tokens of the CPU baseline sample (~12 s of oracle work on 16 host threads)")
     args = ap.parse_args(argv)
     args.warmup = max(3, args.warmup)
 

@@ -56,10 +56,10 @@ typedef enum vqb_dtype { VQB_F16 = 0, VQB_BF16 = 1, VQB_F32 = 2 } vqb_dtype;
 
 /* Kernel path selection.  AUTO for vqb_switch_forward: the fused small-N
  * kernel up to VQ_FUSED_MAX_N = 512 pairs as in the reference
- * (vq_switch.py:45, :5313), the grouped prefill GEMM above it only when the
- * experts also average more than 3 pairs each (below that density the
- * expert-grouped decode kernel is faster on a B200).  AUTO for
- * vqb_dense_forward follows the reference's dense cutoffs. */
+ * (vq_switch.py:45, :5313); above it the grouped prefill GEMM once also
+ * pairs * in_features > 4608 * num_experts (its fixed cost per expert tile
+ * needs that much work to pay on a B200), else still the decode kernel.  AUTO
+ * for vqb_dense_forward follows the reference's dense cutoffs. */
 typedef enum vqb_path { VQB_PATH_AUTO = 0, VQB_PATH_DECODE = 1, VQB_PATH_PREFILL = 2 } vqb_path;
 
 /* One VQ-coded projection: a VQSwitchLinear (E experts) or a VQLinear (E = 1).

@@ -205,17 +205,19 @@ vqb_status vqb_switch_forward(const vqb_linear_desc* desc, const void* x, vqb_dt
   if (workspace_bytes < vqb_switch_workspace_size(desc, n_tokens, top_k, opts)) return VQB_WORKSPACE_TOO_SMALL;
   if (!workspace) return VQB_NULL_POINTER;
   // Path: the reference runs the fused small-N kernel up to VQ_FUSED_MAX_N =
-  // 512 pairs and the grouped GEMM above it (vq_switch.py:45, :5313-5315).
-  // The grouped GEMM decodes every routed expert's full weight tile, so on a
-  // B200 it only pays once experts average more than kGemmPairsPerExpert
-  // pairs (measured crossover on the 512-expert, 1024 x 4096 gate: the decode
-  // kernel is faster at <= 2.5 pairs per expert, the GEMM at >= 5); AUTO takes
-  // the GEMM when both cutoffs are passed.
-  constexpr int64_t kGemmPairsPerExpert = 3;
+  // 512 pairs and the grouped GEMM above it (vq_switch.py:45, :5313-5315).  The
+  // grouped GEMM decodes every routed expert's tile with a fixed cost per tile
+  // (codebook reload, epilogue) that the K extent amortises, so on a B200 it
+  // pays once pairs * IN exceed ~4608 per expert as well.  Measured (512
+  // experts, uniform routing): 1024 x 4096 gate at 1.25 pairs/expert 0.72 ms
+  // both kernels, 2.5 pairs 0.92 GEMM vs 1.06 decode; 4096 x 1024 down at 2.5
+  // pairs 1.20 GEMM vs 0.88 decode, at 5 pairs 1.31 vs 1.38.
+  constexpr int64_t kGemmPairInPerExpert = 4608;
   const int path = opts ? opts->path : VQB_PATH_AUTO;
   const int max_fused = (opts && opts->max_fused_pairs > 0) ? opts->max_fused_pairs : 512;
   const bool large = path == VQB_PATH_PREFILL ||
-                     (path == VQB_PATH_AUTO && N > max_fused && N > kGemmPairsPerExpert * geo.E);
+                     (path == VQB_PATH_AUTO && N > max_fused &&
+                      static_cast<int64_t>(N) * geo.IN > kGemmPairInPerExpert * geo.E);
   // MoE numerics: x narrowed to fp16, fp32 accumulation, fp16 output rounding
   // then the caller's dtype (vq_switch.py:5301-5308, :5423).
   return run_linear(geo, x, x_dtype, n_tokens, indices, top_k, N, y, y_dtype, workspace, opts,
