@@ -67,7 +67,7 @@ constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kTmemA = kIssuers * kMaxN;        // columns: [0,128) D0, [128,256) D1, then 8 A stages of 32
 constexpr uint32_t kSpinLimit = 1u << 26;
 constexpr int kScaleRowBytes = 16;                   // 8 fp16 scales per row per window
-constexpr int kNumBars = 2 * kBStages + 2 * kAStages + 2 * kWStages + 2 + kIssuers + 1 + kIssuers;
+constexpr int kNumBars = 2 * kBStages + 2 + kAStages + 2 * kWStages + 2 + kIssuers + 1 + kIssuers;
 
 struct TParams {
   const uint32_t* codes;
@@ -359,8 +359,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* bars = reinterpret_cast<uint64_t*>(base + prm.off_bar);
   uint64_t* b_full = bars;                         // [kBStages] x slot landed
   uint64_t* b_empty = b_full + kBStages;           // [kBStages] MMAs done with the slot
-  uint64_t* a_full = b_empty + kBStages;           // [kAStages] the 4 warps of a set stored it
-  uint64_t* st_free = a_full + kAStages;           // [kAStages] MMAs of position g done: A stage g % 8 free
+  uint64_t* a_full = b_empty + kBStages;           // [2] all 16 decode warps stored their window's A stages
+                                                   //     (window w -> a_full[w & 1]; one wait per window)
+  uint64_t* st_free = a_full + 2;                  // [kAStages] MMAs of position g done: A stage g % 8 free
   uint64_t* w_full = st_free + kAStages;           // [kWStages] code/scale window landed
   uint64_t* w_empty = w_full + kWStages;           // [kWStages] all 16 decode warps read it
   uint64_t* cb_full = w_empty + kWStages;          // [1] codebook slice landed
@@ -375,7 +376,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < kBStages; ++i) { mbar_init(&b_full[i], 1); mbar_init(&b_empty[i], 1); }
-    for (int i = 0; i < kAStages; ++i) { mbar_init(&a_full[i], 4); mbar_init(&st_free[i], 1); }
+    for (int i = 0; i < 2; ++i) mbar_init(&a_full[i], kDecodeWarps);
+    for (int i = 0; i < kAStages; ++i) mbar_init(&st_free[i], 1);
     for (int i = 0; i < kWStages; ++i) { mbar_init(&w_full[i], 1); mbar_init(&w_empty[i], kDecodeWarps); }
     mbar_init(cb_full, 1);
     mbar_init(cb_empty, kDecodeWarps);
@@ -440,6 +442,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       // descriptor of B stage 0; later stages / positions start further on (the start-address field counts 16-byte units)
       const uint64_t bdesc0 = sw128_desc(smem_u32(b_base));
       uint32_t g = 0, gs = 0;
+      uint32_t waited = 0xFFFFFFFFu;  // last window whose A stages this issuer has seen complete
       bool ok = true;
       int j = 0;
       for (int64_t it = blockIdx.x; it < nitems && ok; it += gridDim.x, ++j) {
@@ -459,8 +462,12 @@ __global__ void __launch_bounds__(kThreads, 1)
             for (int q = 0; q < pp; ++q) {
               const uint32_t gp = g + static_cast<uint32_t>(p0 + q);
               const uint32_t ast = gp % kAStages;
-              if (!(ok = mbar_wait(&a_full[ast], (gp / kAStages) & 1u, abort_flag))) break;
-              tc_fence_after();
+              const uint32_t win = gp >> 2;
+              if (win != waited) {
+                if (!(ok = mbar_wait(&a_full[win & 1u], (win >> 1) & 1u, abort_flag))) break;
+                tc_fence_after();
+                waited = win;
+              }
               const uint32_t a_tmem = tmem_base + kTmemA + ast * 32;
               const uint64_t bd = bdesc0 + static_cast<uint64_t>((bs * kBStageBytes + q * rows * kChunkK * 2) >> 4);
               tc_mma_ts(d_tmem, a_tmem, bd, idesc, acc);
@@ -607,7 +614,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           tc_wait_st();
           tc_fence_before();
           __syncwarp();
-          if (lane == 0) mbar_arrive(&a_full[ast]);
+          if (lane == 0) mbar_arrive(&a_full[(gp >> 2) & 1u]);
         }
         g += static_cast<uint32_t>(prm.n_pos);
       }
