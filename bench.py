@@ -232,6 +232,68 @@ def profiled_traffic(kernel, workload):
     return None
 
 
+DH, DI, DKV = 5120, 17408, 1024   # hidden, MLP intermediate, kv width
+
+
+def make_dense_layer(torch, dev, seed):
+    """One BASELINE config-4 layer as VQLinear projections: attention q/k/v/o
+    with d2/K256 (8-bit codes), MLP gate/up/down with d8/K16384 (14-bit)."""
+    from vqlab_b200 import VQLinear
+    g = torch.Generator(device=dev)
+    g.manual_seed(seed)
+
+    def lin(out, inn, d, k, bits):
+        wpr = (inn // d + 31) // 32 * bits
+        codes = torch.randint(-2 ** 31, 2 ** 31 - 1, (out, wpr), dtype=torch.int32, device=dev, generator=g)
+        cb = (torch.randn((k, d), device=dev, generator=g) * 0.02).to(torch.float16)
+        sc = (torch.rand((out, inn // G), device=dev, generator=g) + 0.5).to(torch.float16)
+        return VQLinear(codes, cb, sc, group_size=G, pack_bits=bits, in_features=inn)
+
+    attn = [lin(DH, DH, 2, 256, 8), lin(DKV, DH, 2, 256, 8), lin(DKV, DH, 2, 256, 8), lin(DH, DH, 2, 256, 8)]
+    mlp = [lin(DI, DH, 8, K, BITS), lin(DI, DH, 8, K, BITS), lin(DH, DI, 8, K, BITS)]
+    return attn, mlp
+
+
+def dense_step(layer, x):
+    """The seven projections of one dense layer (the attention kernel itself is
+    outside the VQ runtime: o is applied to q as its stand-in input)."""
+    from vqlab_b200.moe import swiglu
+    (wq, wk, wv, wo), (wg, wu, wd) = layer
+    q = wq(x)
+    wk(x)
+    wv(x)
+    h = x + wo(q)
+    return h + wd(swiglu(wg(h), wu(h)))
+
+
+def dense_leg(torch, dev, args):
+    """a 64-layer dense stack at batch 1 and 32 decode
+    tokens, timed per layer (4 seeded layers rotated: ~90 MB of packed weights
+    each, 360 MB per cycle > 126 MB L2) and scaled to 64 layers."""
+    layers = [make_dense_layer(torch, dev, 7000 + l) for l in range(4)]
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(23)
+    out = {}
+    for B in (1, 32):
+        xs = [torch.randn((B, DH), device=dev, generator=gen).to(torch.bfloat16) for _ in layers]
+        for l, L in enumerate(layers):
+            dense_step(L, xs[l])
+        torch.cuda.synchronize()
+        graphs = []
+        for l, L in enumerate(layers):
+            gr = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(gr):
+                dense_step(L, xs[l])
+            graphs.append(gr)
+        steps = max(20, args.steps)
+        secs = time_graph_steps(torch, graphs, steps, args.warmup)
+        ms = secs * 1e3 / steps
+        out[str(B)] = {"ms_per_layer": round(ms, 4), "tokens_per_s_64_layers": round(B / (64 * ms / 1e3), 2)}
+        del graphs
+    return {"metric": "dense VQ decode, BASELINE config 4 (64 x [q,k,v,o d2/K256 + gate,up,down d8/K16384])",
+            "unit": "tokens/s", "batches": out}
+
+
 def zipf_logits(torch, dev, gen, T, alpha=1.1):
     """Router logits whose top-10 is a draw without replacement from Zipf(alpha)
     expert popularity: log(popularity) + Gumbel noise (the Gumbel-top-k trick)."""
@@ -508,6 +570,7 @@ def main(argv=None) -> int:
     ap.add_argument("--skip-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--skip-prefill", action="store_true")
+    ap.add_argument("--skip-dense", action="store_true")
     ap.add_argument("--cpu-tokens", type=int, default=2048,
                     help="tokens of the CPU baseline sample (~12 s of oracle work on 16 host threads)")
     args = ap.parse_args(argv)
@@ -530,6 +593,9 @@ def main(argv=None) -> int:
     from vqlab_b200 import _lib
     _lib.lib()
     results, roof, e2e, launches = gpu_arm(args, rank, world, dev)
+    dense = None
+    if not args.skip_dense and world == 1:
+        dense = dense_leg(torch, dev, args)
     prefill = None
     if not args.skip_prefill:
         _, peak_tf, peak_kind = _peaks()
@@ -551,6 +617,8 @@ def main(argv=None) -> int:
                 "gpu_launches_per_step": launches}
         if prefill is not None:
             line["prefill"] = prefill
+        if dense is not None:
+            line["dense"] = dense
         if not args.no_cpu_baseline and world == 1:
             line["cpu_baseline"] = cpu_baseline_block(args.cpu_tokens)
         print(json.dumps(line), flush=True)
