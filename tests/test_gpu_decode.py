@@ -297,3 +297,17 @@ def test_dense_unpacked_cutoff_12():
         y = lin(x.cuda()).float().cpu().numpy()
         ref = orc.round_bf16(_dense_oracle(L, x.float().numpy(), torch.bfloat16, _dense_path_is_fused(2, False, n)))
         assert np.array_equal(y.view(np.uint32), ref.view(np.uint32)), n
+
+
+@pytest.mark.parametrize("IN,OUT,n", [(5120, 17408, 1), (5120, 17408, 32), (17408, 5120, 1)])
+def test_dense_c4_mlp_shapes(IN, OUT, n):
+    """BASELINE config 4 MLP projections at full size (d8/K16384, 14-bit):
+    10 and 34 windows of 512 k split over K-slices unevenly (the batch-1
+    decode kernel), and the 32-row grouped GEMM."""
+    L = make_layer(E=1, OUT=OUT, IN=IN, D=8, K=16384, G=64, seed=IN + n)
+    lin = _dense(L)
+    rng = np.random.default_rng(n + 5)
+    xb = torch.from_numpy(rng.standard_normal((n, IN)).astype(np.float32)).to(torch.bfloat16)
+    y = lin(xb.cuda()).float().cpu().numpy()
+    ref = _dense_oracle(L, xb.float().numpy(), torch.bfloat16, fused=False)
+    assert within_tol_bf16(orc.round_bf16(ref), y)
