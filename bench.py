@@ -571,6 +571,7 @@ def main(argv=None) -> int:
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--skip-prefill", action="store_true")
     ap.add_argument("--skip-dense", action="store_true")
+    ap.add_argument("--prefill-only", action="store_true", help="run only the C3 prefill leg (for profiling)")
     ap.add_argument("--cpu-tokens", type=int, default=2048,
                     help="tokens of the CPU baseline sample (~12 s of oracle work on 16 host threads)")
     args = ap.parse_args(argv)
@@ -592,6 +593,16 @@ def main(argv=None) -> int:
                                              device_id=dev)
     from vqlab_b200 import _lib
     _lib.lib()
+    if args.prefill_only:
+        # the C3 leg alone (profiling runs): its own JSON line
+        _, peak_tf, peak_kind = _peaks()
+        p = prefill_leg(torch, dev, args, peak_tf, peak_kind, rank, world)
+        if rank == 0:
+            print(json.dumps(p), flush=True)
+        if world > 1:
+            torch.distributed.barrier()
+            torch.distributed.destroy_process_group()
+        return 0
     results, roof, e2e, launches = gpu_arm(args, rank, world, dev)
     dense = None
     if not args.skip_dense and world == 1:
