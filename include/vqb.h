@@ -78,7 +78,11 @@ typedef struct vqb_linear_desc {
   const void* codes;
   const void* codebook;
   const void* scales;
-  const int32_t* row_table;   /* SKIPZERO row table; must be NULL (not supported yet) */
+  const int32_t* row_table;   /* SKIPZERO (vq_switch.py:5205-5216): int32 [E, OUT] mapping (expert, out
+                                 row) to a compact row of codes / scales, -1 = dead; NULL = the plain
+                                 [E, OUT, ...] layout.  Dead rows read no bytes and write +0. */
+  int32_t num_rows;           /* with row_table: rows of the compact codes [num_rows, WPR] and scales
+                                 [num_rows, IN/G]; entries >= num_rows are treated as dead */
 } vqb_linear_desc;
 
 /* Optional knobs; pass NULL for defaults. */

@@ -63,7 +63,7 @@ def _switch(d, n_tokens=1, top_k=2):
     (dict(group_size=60, in_features=480, codes_last_dim=0), _lib.VQB_BAD_SHAPE),
     (dict(pack_bits=10), _lib.VQB_BAD_SHAPE),        # 2^10 < K
     (dict(codes=None), _lib.VQB_NULL_POINTER),
-    (dict(row_table=0x8000), _lib.VQB_UNSUPPORTED_GEOMETRY),
+    (dict(row_table=0x8000, num_rows=-1), _lib.VQB_BAD_SHAPE),
     (dict(codebook=0x2008), _lib.VQB_BAD_ALIGNMENT),
     (dict(pack_bits=0, code_bytes=1, num_codes=4096), _lib.VQB_BAD_SHAPE),
     (dict(pack_bits=0, code_bytes=3), _lib.VQB_UNSUPPORTED_GEOMETRY),
@@ -109,9 +109,25 @@ def test_module_properties_and_from_weights():
     assert m2.pack_bits == 8 and m2.input_dims == 128
     with pytest.raises(ValueError):
         VQSwitchLinear(m.codes, m.codebook, m.vq_scales, pack_bits=8)  # no in_features
-    with pytest.raises(NotImplementedError):
+    with pytest.raises(ValueError, match="compact"):  # SKIPZERO needs compact 2-D codes / scales
         VQSwitchLinear(m.codes, m.codebook, m.vq_scales, pack_bits=8, in_features=128,
                        row_table=torch.zeros((2, 16), dtype=torch.int32))
+
+
+def test_skipzero_module_properties():
+    """SKIPZERO modules take E and OUT from the row table (vq_switch.py:5272-5282)."""
+    m = _module()
+    tbl = torch.full((2, 16), -1, dtype=torch.int32)
+    tbl[0, :5] = torch.arange(5, dtype=torch.int32)
+    sz = VQSwitchLinear(m.codes[0, :5].contiguous(), m.codebook, m.vq_scales[0, :5].contiguous(), pack_bits=8,
+                        in_features=128, row_table=tbl)
+    assert sz.skipzero and not m.skipzero
+    assert (sz.input_dims, sz.output_dims, sz.num_experts) == (128, 16, 2)
+    d = sz.desc()
+    assert d.num_rows == 5 and d.row_table == tbl.data_ptr()
+    with pytest.raises(ValueError, match="int32"):
+        VQSwitchLinear(m.codes[0, :5].contiguous(), m.codebook, m.vq_scales[0, :5].contiguous(), pack_bits=8,
+                       in_features=128, row_table=tbl.long())
 
 
 def test_module_refuses_cpu_tensors():
@@ -144,3 +160,26 @@ def test_measurement_aids_host_side():
     assert L.vqb_time_next_kernel(ctypes.c_void_p(16), None) == 10  # VQB_NULL_POINTER
     assert L.vqb_time_next_kernel(None, ctypes.c_void_p(16)) == 10
     assert L.vqb_time_next_kernel(None, None) == 0
+
+
+def test_dense_refuses_row_table():
+    """SKIPZERO is a switch-layer format; a dense call with a row table is refused before any launch."""
+    L = _lib.lib()
+    d = _desc(num_experts=1, row_table=0x8000, num_rows=10)
+    st = L.vqb_dense_forward(ctypes.byref(d), ctypes.c_void_p(0x4000), _lib.VQB_BF16, 1, ctypes.c_void_p(0x6000),
+                             _lib.VQB_BF16, ctypes.c_void_p(0x7000), 1 << 20, None, None)
+    assert st == _lib.VQB_UNSUPPORTED_GEOMETRY
+
+
+def test_skipzero_row_table_from_mask():
+    """Bit-packed live mask (little bit order) -> compact row per (expert, row), -1 dead."""
+    from vqlab_b200.vq_switch import skipzero_row_table
+    E, OUT = 3, 13
+    rng = np.random.default_rng(0)
+    live = rng.random((E, OUT)) < 0.6
+    live[1] = False
+    packed = np.packbits(np.pad(live, ((0, 0), (0, 16 - OUT))), axis=1, bitorder="little")
+    tbl = skipzero_row_table(torch.from_numpy(packed), E, OUT).numpy()
+    want = np.full((E, OUT), -1, np.int32)
+    want[live] = np.arange(int(live.sum()), dtype=np.int32)
+    assert tbl.dtype == np.int32 and np.array_equal(tbl, want)

@@ -49,6 +49,7 @@ class LinearDesc(ctypes.Structure):
         ("codebook", ctypes.c_void_p),
         ("scales", ctypes.c_void_p),
         ("row_table", ctypes.c_void_p),
+        ("num_rows", ctypes.c_int32),
     ]
 
 

@@ -33,6 +33,8 @@ struct DecodeParams {
   void* y;                   // [N, OUT]
   int* err;                  // device error word (bad expert index), may be nullptr
   int64_t expert_words;      // OUT * row_words
+  const int32_t* row_table;  // SKIPZERO [E, OUT] -> compact row (-1 dead), nullptr = plain layout
+  int64_t nrows;             // rows of codes / scales
   int row_words;             // words per code row
   int N, krep, E;
   int OUT, IN, G, NGRP, NSUB;
@@ -145,10 +147,15 @@ __global__ void __launch_bounds__(256) vq_decode_kernel(const DecodeParams prm) 
 
     const int r = blockIdx.x * rows_per_cta + rsub * 32 + lane;
     float acc = 0.0f;
-    if (r < prm.OUT && jb < je) {
-      const uint32_t* row = prm.codes + static_cast<int64_t>(e) * prm.expert_words +
-                            static_cast<int64_t>(r) * prm.row_words;
-      const uint16_t* srow = prm.scales + (static_cast<int64_t>(e) * prm.OUT + r) * prm.NGRP;
+    // the row's place in codes / scales: (e, r), or its compact row (dead -> -1: +0 out, nothing read)
+    int64_t crow = static_cast<int64_t>(e) * prm.OUT + r;
+    if (prm.row_table && r < prm.OUT) {
+      crow = prm.row_table[crow];
+      if (crow >= prm.nrows) crow = -1;
+    }
+    if (r < prm.OUT && jb < je && crow >= 0) {
+      const uint32_t* row = prm.codes + crow * prm.row_words;
+      const uint16_t* srow = prm.scales + crow * prm.NGRP;
       BitWalker<VEC> wk;
       wk.init(row, static_cast<int64_t>(jb) * prm.bits);
       int g = jb / SPG;
@@ -215,6 +222,10 @@ __global__ void __launch_bounds__(256) vq_decode_kernel(const DecodeParams prm) 
         if (rr < prm.OUT) {
           float s = red[ri];
           for (int q = 1; q < ks; ++q) s = s + red[q * rows_per_cta + ri];
+          if (prm.row_table) {
+            const int64_t cr = prm.row_table[static_cast<int64_t>(e) * prm.OUT + rr];
+            if (cr < 0 || cr >= prm.nrows) s = 0.0f;  // dead row: exact +0
+          }
           store_y(prm.y, static_cast<int64_t>(p) * prm.OUT + rr, s, prm.y_dtype, prm.round_f16_first != 0);
         }
       }
@@ -237,6 +248,8 @@ vqb_status launch_decode(const LinearGeometry& geo, const void* x, int x_dtype, 
   prm.err = err;
   prm.row_words = geo.row_words;
   prm.expert_words = static_cast<int64_t>(geo.OUT) * geo.row_words;
+  prm.row_table = geo.row_table;
+  prm.nrows = geo.nrows;
   prm.N = N;
   prm.krep = krep;
   prm.E = geo.E;

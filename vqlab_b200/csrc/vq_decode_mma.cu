@@ -54,6 +54,8 @@ struct MParams {
   const int* meta;
   void* y;
   int64_t expert_words;
+  const int32_t* row_table;  // SKIPZERO [E, OUT] -> compact row (-1 dead), nullptr = plain layout
+  int64_t nrows;             // rows of codes / scales
   int row_words;
   int OUT, IN, G, NGRP, NSUB, bits, krep;
   int ks, mt, tiles, ns;
@@ -188,6 +190,15 @@ __device__ __forceinline__ void st_cluster_f32(uint32_t addr, float v) {
   asm volatile("st.shared::cluster.f32 [%0], %1;" :: "r"(addr), "f"(v) : "memory");
 }
 
+// Place of (expert e, output row) in codes / scales: the plain [E, OUT, ...]
+// layout, or its SKIPZERO compact row; -1 = dead (reads nothing, writes +0).
+__device__ __forceinline__ int64_t code_row(const MParams& prm, int e, int row) {
+  const int64_t er = static_cast<int64_t>(e) * prm.OUT + row;
+  if (!prm.row_table) return er;
+  const int64_t c = prm.row_table[er];
+  return c < prm.nrows ? c : -1;
+}
+
 template <int D, int WR, int NT, bool SPLIT>
 __global__ void __launch_bounds__(kThreads, 1) vq_decode_mma_kernel(const MParams prm) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
@@ -282,8 +293,7 @@ __global__ void __launch_bounds__(kThreads, 1) vq_decode_mma_kernel(const MParam
 #pragma unroll
     for (int n = 0; n < NT; ++n) tok[n] = min(g + 8 * n, P - 1);
 
-    const uint32_t* ebase = prm.codes + static_cast<int64_t>(e) * prm.expert_words;
-    const uint16_t* sbase = prm.scales + static_cast<int64_t>(e) * prm.OUT * prm.NGRP;
+
     float part[NT][4];
 #pragma unroll
     for (int n = 0; n < NT; ++n) part[n][0] = part[n][1] = part[n][2] = part[n][3] = 0.0f;
@@ -294,19 +304,20 @@ __global__ void __launch_bounds__(kThreads, 1) vq_decode_mma_kernel(const MParam
       __syncwarp();
       const int g0 = (w * prm.win_k) / gk;
       if (l_chunk_ok) {
-        const uint32_t* src = ebase + static_cast<int64_t>(w) * prm.win_words + l_chunk * 4;
+        const uint32_t* src = prm.codes + static_cast<int64_t>(w) * prm.win_words + l_chunk * 4;
 #pragma unroll 4
         for (int rr = l_row; rr < 16; rr += rows_per_pass) {
-          const int row = min(r0 + rr, prm.OUT - 1);
-          *reinterpret_cast<uint4*>(c_s + rr * prm.cs_stride + l_chunk * 4) =
-              ldg_stream_v4(src + static_cast<int64_t>(row) * prm.row_words);
+          const int64_t cr = code_row(prm, e, min(r0 + rr, prm.OUT - 1));
+          uint4 v = make_uint4(0, 0, 0, 0);
+          if (cr >= 0) v = ldg_stream_v4(src + cr * prm.row_words);
+          *reinterpret_cast<uint4*>(c_s + rr * prm.cs_stride + l_chunk * 4) = v;
         }
       }
       if (s_ok) {
 #pragma unroll
         for (int rr = s_row; rr < 16; rr += 4) {
-          const int row = min(r0 + rr, prm.OUT - 1);
-          s_s[rr * prm.sc_stride + s_gi] = __ldg(sbase + static_cast<int64_t>(row) * prm.NGRP + g0 + s_gi);
+          const int64_t cr = code_row(prm, e, min(r0 + rr, prm.OUT - 1));
+          s_s[rr * prm.sc_stride + s_gi] = cr >= 0 ? __ldg(prm.scales + cr * prm.NGRP + g0 + s_gi) : uint16_t(0);
         }
       }
       __syncwarp();
@@ -380,8 +391,10 @@ __global__ void __launch_bounds__(kThreads, 1) vq_decode_mma_kernel(const MParam
       // a group cut by the slice end is closed here with its own scale
       if ((static_cast<int64_t>(we) * prm.win_k) % gk != 0 && wb < we) {
         const int grp = (we * prm.win_k - 1) / gk;
-        const float sa = h2f(sbase[static_cast<int64_t>(min(r0 + g, prm.OUT - 1)) * prm.NGRP + grp]);
-        const float sb = h2f(sbase[static_cast<int64_t>(min(r0 + g + 8, prm.OUT - 1)) * prm.NGRP + grp]);
+        const int64_t ca = code_row(prm, e, min(r0 + g, prm.OUT - 1));
+        const int64_t cb = code_row(prm, e, min(r0 + g + 8, prm.OUT - 1));
+        const float sa = ca >= 0 ? h2f(prm.scales[ca * prm.NGRP + grp]) : 0.0f;
+        const float sb = cb >= 0 ? h2f(prm.scales[cb * prm.NGRP + grp]) : 0.0f;
 #pragma unroll
         for (int n = 0; n < NT; ++n) {
           acc[n][0] = fmaf(sa, part[n][0], acc[n][0]);
@@ -419,6 +432,7 @@ __global__ void __launch_bounds__(kThreads, 1) vq_decode_mma_kernel(const MParam
                 v = (rk == 0 && sl == 0) ? red[rl * ntok + tk]
                                          : v + red[rk * plane + (static_cast<size_t>(sl) * rows_per_item + rl) * ntok + tk];
             const int pair = prm.sorted[ch.y + tk];
+            if (prm.row_table && code_row(prm, e, row) < 0) v = 0.0f;  // dead row: exact +0
             store_y(prm.y, static_cast<int64_t>(pair) * prm.OUT + row, v, prm.y_dtype, prm.round_f16_first != 0);
           }
         }
@@ -433,8 +447,8 @@ __global__ void __launch_bounds__(kThreads, 1) vq_decode_mma_kernel(const MParam
           const int row = r0 + g + 8 * (i >> 1);
           if (tk < P && row < prm.OUT) {
             const int pair = prm.sorted[ch.y + tk];
-            store_y(prm.y, static_cast<int64_t>(pair) * prm.OUT + row, acc[n][i], prm.y_dtype,
-                    prm.round_f16_first != 0);
+            const float v = (prm.row_table && code_row(prm, e, row) < 0) ? 0.0f : acc[n][i];  // dead: +0
+            store_y(prm.y, static_cast<int64_t>(pair) * prm.OUT + row, v, prm.y_dtype, prm.round_f16_first != 0);
           }
         }
     } else {
@@ -455,6 +469,7 @@ __global__ void __launch_bounds__(kThreads, 1) vq_decode_mma_kernel(const MParam
         if (row < prm.OUT) {
           float v = red[rl * ntok + tk];
           for (int sl = 1; sl < ks; ++sl) v = v + red[(sl * rows_per_item + rl) * ntok + tk];
+          if (prm.row_table && code_row(prm, e, row) < 0) v = 0.0f;  // dead row: exact +0
           const int pair = prm.sorted[ch.y + tk];
           store_y(prm.y, static_cast<int64_t>(pair) * prm.OUT + row, v, prm.y_dtype, prm.round_f16_first != 0);
         }
@@ -533,6 +548,8 @@ vqb_status launch_decode_mma(const LinearGeometry& geo, const GroupedDecodeArgs&
   prm.y = a.y;
   prm.row_words = geo.row_words;
   prm.expert_words = static_cast<int64_t>(geo.OUT) * geo.row_words;
+  prm.row_table = geo.row_table;
+  prm.nrows = geo.nrows;
   prm.OUT = geo.OUT;
   prm.IN = geo.IN;
   prm.G = geo.G;

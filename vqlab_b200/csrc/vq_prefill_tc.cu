@@ -96,6 +96,9 @@ struct TParams {
   int kp;
   int npass;
   int off_win, off_cb, off_bar;
+  const int32_t* row_table;  // SKIPZERO [E, OUT] -> compact row (-1 dead), nullptr = plain layout
+  const int* tile_base;      // SKIPZERO: first compact row of each (expert, 128-row tile), -1 = all dead
+  int64_t nrows;             // rows of codes / scales
 };
 
 // ------------------------------------------------------------ PTX helpers
@@ -501,7 +504,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int chunk = static_cast<int>(it / prm.row_tiles);
         const int rt = static_cast<int>(it - static_cast<int64_t>(chunk) * prm.row_tiles);
         const int4 ch = prm.chunks[chunk];
-        const int yrow = ch.x * prm.OUT + rt * kTileM;
+        // the tile's rows in codes / scales: (e, rt*128 ...), or from its first live compact row
+        const int yrow = prm.row_table ? max(prm.tile_base[ch.x * prm.row_tiles + rt], 0) : ch.x * prm.OUT + rt * kTileM;
         for (int pass = 0; pass < prm.npass && ok; ++pass) {
           for (int w = 0; w < nwin; ++w) {
             if (!mbar_wait(&w_empty[ws], wp ^ 1u, abort_flag)) { ok = false; break; }
@@ -552,7 +556,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int q = warp & 3;
     const uint32_t lane_off = static_cast<uint32_t>(q * 32) << 16;
     const int lrow = q * 32 + lane;                 // row inside the tile
-    const int xr = prm.wswz == 1 ? ((lrow >> 1) & 3) : (prm.wswz == 2 ? (lrow & 7) : 0);
     uint32_t ws = 0, wp = 0;
     uint32_t g = 0;                                 // position sequence number
     int cur = -1;
@@ -565,7 +568,21 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int4 ch = prm.chunks[chunk];
       const int r = rt * kTileM + lrow;
       const int rr = min(r, prm.OUT - 1);
-      const uint16_t* srow = prm.scales + (static_cast<int64_t>(ch.x) * prm.OUT + rr) * prm.NGRP;
+      // the row inside the staged windows (woff) and in codes / scales (crow);
+      // with a row table dead rows decode nothing and store +0, and a row whose
+      // compact index falls outside its tile's window counts as dead
+      int64_t crow = static_cast<int64_t>(ch.x) * prm.OUT + rr;
+      int woff = lrow;
+      bool live = true;
+      if (prm.row_table) {
+        const int tb = prm.tile_base[ch.x * prm.row_tiles + rt];
+        crow = r < prm.OUT ? static_cast<int64_t>(prm.row_table[static_cast<int64_t>(ch.x) * prm.OUT + r]) : -1;
+        const int64_t o = crow - tb;
+        live = crow >= 0 && crow < prm.nrows && tb >= 0 && o >= 0 && o < kTileM;
+        woff = live ? static_cast<int>(o) : 0;
+      }
+      const int xr = prm.wswz == 1 ? ((woff >> 1) & 3) : (prm.wswz == 2 ? (woff & 7) : 0);
+      const uint16_t* srow = prm.scales + (live ? crow : 0) * prm.NGRP;
       for (int pass = 0; pass < prm.npass && ok; ++pass) {
         const int h = pass_slice(prm.npass, j, pass);
         if (h != cur) {
@@ -582,10 +599,10 @@ __global__ void __launch_bounds__(kThreads, 1)
           const unsigned char* wst = w_base + ws * prm.win_stage_bytes;
           const int p = w * kSets + s;
           uint32_t out[32];
-          if (p < prm.n_k) {
+          if (p < prm.n_k && live) {
             uint16_t sc;
             if (prm.scale_tma) {
-              const uint4 sv = reinterpret_cast<const uint4*>(wst + prm.code_stage_bytes)[lrow];
+              const uint4 sv = reinterpret_cast<const uint4*>(wst + prm.code_stage_bytes)[woff];
               const int gi = ((p * kChunkK) >> prm.log2g) - (((w * kSets * kChunkK) >> prm.log2g) & ~7);
               const uint32_t sw = (gi & 4) ? ((gi & 2) ? sv.w : sv.z) : ((gi & 2) ? sv.y : sv.x);
               sc = static_cast<uint16_t>((gi & 1) ? (sw >> 16) : (sw & 0xFFFFu));
@@ -595,11 +612,11 @@ __global__ void __launch_bounds__(kThreads, 1)
             const __half sh = __ushort_as_half(sc);
             const int wstart = w * prm.wpw;
             const int b0 = (wstart & 3) * 32 + s * (kChunkK / D) * prm.bits;
-            decode_chunk<D, BITS>(prm, cb_s, reinterpret_cast<const uint32_t*>(wst) + lrow * prm.W, xr, b0,
+            decode_chunk<D, BITS>(prm, cb_s, reinterpret_cast<const uint32_t*>(wst) + woff * prm.W, xr, b0,
                                   __halves2half2(sh, sh), h, out);
           } else {
 #pragma unroll
-            for (int i = 0; i < 32; ++i) out[i] = 0u;  // K padding up to a whole window
+            for (int i = 0; i < 32; ++i) out[i] = 0u;  // K padding up to a whole window, or a dead row
           }
           __syncwarp();
           if (lane == 0) mbar_arrive(&w_empty[ws]);
@@ -637,7 +654,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int jj = 0; jj < 16; ++jj) {
             if (c0 + jj < ntok) {
               const int pair = prm.sorted[ch.y + c0 + jj];
-              const float acc = two ? __uint_as_float(v0[jj]) + __uint_as_float(v1[jj]) : __uint_as_float(v0[jj]);
+              float acc = two ? __uint_as_float(v0[jj]) + __uint_as_float(v1[jj]) : __uint_as_float(v0[jj]);
+              if (!live) acc = 0.0f;  // dead row (row table): exact +0
               store_y(prm.y, static_cast<int64_t>(pair) * prm.OUT + r, acc, prm.y_dtype, prm.round_f16_first != 0);
             }
           }
@@ -655,6 +673,27 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_after();
   if (*abort_flag && threadIdx.x == 0) atomicExch(prm.status + 1, static_cast<int>(VQB_TIMEOUT));
   if (warp == 0) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" :: "r"(tmem_base), "r"(kTmemCols) : "memory");
+}
+
+// SKIPZERO: the first live compact row of every (expert, 128-row tile), or -1
+// when the tile has none (a warp per tile; compact rows run in (expert, row)
+// order, so a tile's live rows are the next consecutive compact rows).
+__global__ void tile_base_kernel(const int32_t* __restrict__ rt, int E, int OUT, int row_tiles, int64_t nrows,
+                                 int* __restrict__ tb) {
+  const int lane = threadIdx.x & 31;
+  const int64_t t = (blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x) >> 5;
+  if (t >= static_cast<int64_t>(E) * row_tiles) return;
+  const int e = static_cast<int>(t / row_tiles), ti = static_cast<int>(t - static_cast<int64_t>(e) * row_tiles);
+  int m = 0x7FFFFFFF;
+  for (int i = lane; i < kTileM; i += 32) {
+    const int r = ti * kTileM + i;
+    if (r < OUT) {
+      const int v = rt[static_cast<int64_t>(e) * OUT + r];
+      if (v >= 0 && v < nrows) m = min(m, v);
+    }
+  }
+  for (int o = 16; o > 0; o >>= 1) m = min(m, __shfl_xor_sync(0xffffffffu, m, o));
+  if (lane == 0) tb[t] = m == 0x7FFFFFFF ? -1 : m;
 }
 
 // x rows gathered into expert-sorted order as 16-bit B rows: xs[s] = x[sorted[s] / krep].
@@ -800,6 +839,9 @@ vqb_status launch_prefill_tc(const LinearGeometry& geo, const void* x, int x_dty
   prm.y_dtype = y_dtype;
   prm.round_f16_first = round_f16_first ? 1 : 0;
   prm.b_bf16 = bf16_operands ? 1 : 0;
+  prm.row_table = geo.row_table;
+  prm.tile_base = rw.tile_base;
+  prm.nrows = geo.nrows;
 
   // code window: kSets chunks = 256 k = (256 / D) codes of every row, read
   // from an aligned-down 16-byte boundary (up to o_max extra words); rows of
@@ -861,6 +903,14 @@ vqb_status launch_prefill_tc(const LinearGeometry& geo, const void* x, int x_dty
     if (cudaGetLastError() != cudaSuccess) return VQB_CUDA_ERROR;
     note_launch();
   }
+  // 1b. SKIPZERO tile bases
+  if (geo.row_table) {
+    const int64_t warps = static_cast<int64_t>(geo.E) * prm.row_tiles;
+    tile_base_kernel<<<static_cast<unsigned>((warps * 32 + 255) / 256), 256, 0, stream>>>(
+        geo.row_table, geo.E, geo.OUT, prm.row_tiles, geo.nrows, rw.tile_base);
+    if (cudaGetLastError() != cudaSuccess) return VQB_CUDA_ERROR;
+    note_launch();
+  }
   // 2. TMA maps: xs [N, IN] 16-bit seen as [chunk][token][64 k] (boxes of
   //    32 x 4, 64 x 2 and 128 x 1 tokens x chunks, 128-byte swizzle); codes
   //    [E*OUT, row_words] u32 (box W x 128); scales [E*OUT, NGRP] fp16 (box 8 x 128)
@@ -870,7 +920,7 @@ vqb_status launch_prefill_tc(const LinearGeometry& geo, const void* x, int x_dty
     if (!encode_x3d(enc, &xmaps[i], bf16_operands, xs, geo.IN, N, rows, static_cast<uint32_t>(slot_positions(rows))))
       return VQB_CUDA_ERROR;
   }
-  const uint64_t rows = static_cast<uint64_t>(geo.E) * geo.OUT;
+  const uint64_t rows = static_cast<uint64_t>(geo.nrows > 0 ? geo.nrows : 1);
   const CUtensorMapSwizzle cswz = prm.wswz == 1 ? CU_TENSOR_MAP_SWIZZLE_64B
                                   : (prm.wswz == 2 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE);
   if (!encode_2d(enc, &cmap, CU_TENSOR_MAP_DATA_TYPE_UINT32, 4, geo.codes, static_cast<uint64_t>(geo.row_words), rows,

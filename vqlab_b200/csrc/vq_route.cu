@@ -144,7 +144,7 @@ __global__ void __launch_bounds__(kRouteThreads) route_small_kernel(const uint32
   }
 }
 
-size_t route_workspace_bytes(int N, int E, int max_pairs) {
+size_t route_workspace_bytes(int N, int E, int max_pairs, int row_tiles) {
   (void)max_pairs;
   size_t b = 0;
   auto add = [&](size_t n) { b += (n + 255) & ~size_t(255); };
@@ -153,10 +153,11 @@ size_t route_workspace_bytes(int N, int E, int max_pairs) {
   add(sizeof(int) * (E + 1));       // offsets
   add(sizeof(int) * (N > 0 ? N : 1));  // sorted
   add(sizeof(int4) * (N + E + 1));  // chunks (<= N + E)
+  add(sizeof(int) * static_cast<size_t>(E) * (row_tiles > 0 ? row_tiles : 1));  // tile bases
   return b;
 }
 
-RouteWorkspace carve_route_workspace(void* base, int N, int E) {
+RouteWorkspace carve_route_workspace(void* base, int N, int E, int row_tiles) {
   RouteWorkspace w;
   char* p = static_cast<char*>(base);
   auto take = [&](size_t n) { char* r = p; p += (n + 255) & ~size_t(255); return r; };
@@ -165,6 +166,7 @@ RouteWorkspace carve_route_workspace(void* base, int N, int E) {
   w.offsets = reinterpret_cast<int*>(take(sizeof(int) * (E + 1)));
   w.sorted = reinterpret_cast<int*>(take(sizeof(int) * (N > 0 ? N : 1)));
   w.chunks = reinterpret_cast<int4*>(take(sizeof(int4) * (N + E + 1)));
+  w.tile_base = reinterpret_cast<int*>(take(sizeof(int) * static_cast<size_t>(E) * (row_tiles > 0 ? row_tiles : 1)));
   return w;
 }
 

@@ -14,7 +14,7 @@ namespace vqb {
 // vq_pack/fit_moe), the codebook sharding guard (:5285-5296).
 vqb_status validate(const vqb_linear_desc* d, LinearGeometry* g) {
   if (!d || !d->codes || !d->codebook || !d->scales) return VQB_NULL_POINTER;
-  if (d->row_table) return VQB_UNSUPPORTED_GEOMETRY;
+  if (d->row_table && d->num_rows < 0) return VQB_BAD_SHAPE;
   if (d->expected_num_codes > 0 && d->num_codes != d->expected_num_codes) return VQB_CODEBOOK_SHARDED;
   if (d->dim != 2 && d->dim != 4 && d->dim != 8) return VQB_UNSUPPORTED_GEOMETRY;
   if (d->num_experts < 1 || d->out_features < 1 || d->in_features < 1 || d->group_size < 1 || d->num_codes < 1)
@@ -53,6 +53,8 @@ vqb_status validate(const vqb_linear_desc* d, LinearGeometry* g) {
   g->codes = d->codes;
   g->codebook = d->codebook;
   g->scales = d->scales;
+  g->row_table = d->row_table;
+  g->nrows = d->row_table ? static_cast<int64_t>(d->num_rows) : static_cast<int64_t>(g->E) * g->OUT;
   return VQB_OK;
 }
 
@@ -82,8 +84,8 @@ size_t x_region_bytes(int N, int64_t T, int IN) {
   const size_t a = mma_x16_bytes(T, IN), b = tc_prefill_x_bytes(N, IN);
   return a > b ? a : b;
 }
-size_t linear_workspace_bytes(int N, int E, int64_t T, int IN) {
-  return route_workspace_bytes(N, E, kDecodeMaxPairs) + x_region_bytes(N, T, IN);
+size_t linear_workspace_bytes(int N, int E, int64_t T, int IN, int OUT) {
+  return route_workspace_bytes(N, E, kDecodeMaxPairs, row_tiles_128(OUT)) + x_region_bytes(N, T, IN);
 }
 
 // Shared body of the switch and dense entry points once shapes are valid.
@@ -91,12 +93,13 @@ vqb_status run_linear(const LinearGeometry& geo, const void* x, int x_dtype, int
                              const uint32_t* indices, int krep, int N, void* y, int y_dtype, void* workspace,
                              const vqb_options* opts, bool narrow_x_f16, bool round_f16_first, int wround,
                              bool large, cudaStream_t stream) {
-  RouteWorkspace rw = carve_route_workspace(workspace, N, geo.E);
+  RouteWorkspace rw = carve_route_workspace(workspace, N, geo.E, row_tiles_128(geo.OUT));
   if (cudaMemsetAsync(rw.meta, 0, sizeof(int) * 4, stream) != cudaSuccess) return VQB_CUDA_ERROR;
   const int ks = opts ? opts->k_split : 0;
   const int variant = opts ? opts->decode_variant : 0;
   uint16_t* xbuf = reinterpret_cast<uint16_t*>(static_cast<char*>(workspace) +
-                                               route_workspace_bytes(N, geo.E, kDecodeMaxPairs));
+                                               route_workspace_bytes(N, geo.E, kDecodeMaxPairs,
+                                                                     row_tiles_128(geo.OUT)));
   if (large && variant == 0 && tc_prefill_supported(geo) && x_dtype != VQB_F32 &&
       (reinterpret_cast<uintptr_t>(x) & 15) == 0) {
     // grouped tcgen05 GEMM: tiles of up to 128 of one expert's tokens
@@ -186,7 +189,8 @@ size_t vqb_switch_workspace_size(const vqb_linear_desc* desc, int32_t n_tokens, 
   const int64_t N = T * (top_k > 0 ? top_k : 1);
   const int E = desc ? (desc->num_experts > 0 ? desc->num_experts : 1) : 1;
   const int IN = desc ? (desc->in_features > 0 ? desc->in_features : 0) : 0;
-  return linear_workspace_bytes(static_cast<int>(N), E, T, IN);
+  const int OUT = desc ? (desc->out_features > 0 ? desc->out_features : 0) : 0;
+  return linear_workspace_bytes(static_cast<int>(N), E, T, IN, OUT);
 }
 
 vqb_status vqb_switch_forward(const vqb_linear_desc* desc, const void* x, vqb_dtype x_dtype, int32_t n_tokens,
@@ -229,7 +233,8 @@ size_t vqb_dense_workspace_size(const vqb_linear_desc* desc, int64_t n_rows, con
   (void)opts;
   const int n = static_cast<int>(n_rows > 0 ? (n_rows > 0x7fffffff ? 0x7fffffff : n_rows) : 0);
   const int IN = desc ? (desc->in_features > 0 ? desc->in_features : 0) : 0;
-  return linear_workspace_bytes(n, 1, n, IN);
+  const int OUT = desc ? (desc->out_features > 0 ? desc->out_features : 0) : 0;
+  return linear_workspace_bytes(n, 1, n, IN, OUT);
 }
 
 vqb_status vqb_dense_forward(const vqb_linear_desc* desc, const void* x, vqb_dtype x_dtype, int64_t n_rows, void* y,
@@ -239,6 +244,7 @@ vqb_status vqb_dense_forward(const vqb_linear_desc* desc, const void* x, vqb_dty
   vqb_status st = validate(desc, &geo);
   if (st != VQB_OK) return st;
   if (geo.E != 1) return VQB_BAD_SHAPE;
+  if (geo.row_table) return VQB_UNSUPPORTED_GEOMETRY;  // SKIPZERO is a switch-layer format (vq_switch.py:5205)
   if (!dtype_ok(x_dtype) || !dtype_ok(y_dtype)) return VQB_BAD_SHAPE;
   if (n_rows < 0 || n_rows > 0x7fffffff) return VQB_BAD_SHAPE;
   if (n_rows == 0) return VQB_OK;

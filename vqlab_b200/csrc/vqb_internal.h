@@ -15,6 +15,8 @@ struct LinearGeometry {
   const void* codes;
   const void* codebook;
   const void* scales;
+  const int32_t* row_table;  // SKIPZERO [E, OUT] -> compact row, -1 dead; nullptr = plain layout
+  int64_t nrows;             // rows of codes / scales (E * OUT, or the compact live-row count)
 };
 
 vqb_status validate(const vqb_linear_desc* d, LinearGeometry* out);
@@ -26,10 +28,13 @@ struct RouteWorkspace {
   int* offsets;   // [E+1]
   int* sorted;    // [N] pair ids grouped by expert
   int4* chunks;   // (expert, first sorted slot, pairs, 0)
+  int* tile_base; // [E][row tiles of 128]: first compact row of each tile (SKIPZERO grouped GEMM)
 };
 
-size_t route_workspace_bytes(int N, int E, int max_pairs);
-RouteWorkspace carve_route_workspace(void* base, int N, int E);
+// row_tiles: 128-row tiles per expert (room for the SKIPZERO tile bases)
+size_t route_workspace_bytes(int N, int E, int max_pairs, int row_tiles);
+RouteWorkspace carve_route_workspace(void* base, int N, int E, int row_tiles);
+inline int row_tiles_128(int OUT) { return (OUT + 127) / 128; }
 vqb_status launch_route_small(const uint32_t* idx, int N, int E, int max_pairs, const RouteWorkspace& ws,
                               cudaStream_t stream);
 
@@ -81,7 +86,7 @@ void timer_before(cudaStream_t stream);
 void timer_after(cudaStream_t stream);
 
 // Workspace layout and the shared body of the switch / dense entry points (vqb_api.cu).
-size_t linear_workspace_bytes(int N, int E, int64_t T, int IN);
+size_t linear_workspace_bytes(int N, int E, int64_t T, int IN, int OUT);
 vqb_status run_linear(const LinearGeometry& geo, const void* x, int x_dtype, int n_tokens, const uint32_t* indices,
                       int krep, int N, void* y, int y_dtype, void* workspace, const vqb_options* opts,
                       bool narrow_x_f16, bool round_f16_first, int wround, bool large, cudaStream_t stream);

@@ -46,6 +46,21 @@ def make_options(path: int = 0, k_split: int = 0, max_fused_pairs: int = 0, deco
     return o
 
 
+def skipzero_row_table(rowmask: torch.Tensor, num_experts: int, out_features: int) -> torch.Tensor:
+    """SKIPZERO on-disk live mask -> row table (vq_switch.py:4958-4976).
+
+    rowmask: uint8 [E, ceil(OUT/8)], bit i of byte b = row 8*b + i (little bit
+    order).  Returns int32 [E, OUT]: the compact row of each live (expert, row)
+    in (expert, row) order, -1 for dead rows.  Integer work only; runs on the
+    mask's device."""
+    E, OUT = int(num_experts), int(out_features)
+    rm = rowmask.to(torch.int32).reshape(E, -1)
+    bits = (rm[..., None] >> torch.arange(8, device=rm.device, dtype=torch.int32)) & 1
+    live = bits.reshape(E, -1)[:, :OUT].reshape(-1)
+    pos = torch.cumsum(live, 0, dtype=torch.int32) - 1
+    return torch.where(live > 0, pos, torch.full_like(pos, -1)).to(torch.int32).reshape(E, OUT)
+
+
 class VQSwitchLinear(torch.nn.Module):
     """Routed VQ experts (bias-free), reading vq_pack codes in place."""
 
@@ -53,10 +68,15 @@ class VQSwitchLinear(torch.nn.Module):
                  in_features: int | None = None, row_table=None):
         super().__init__()
         if row_table is not None:
-            # SKIPZERO compact rows (vq_switch.py:5205-5216) are not served by
-            # this build yet; refusing is the reference's rule for any kernel
-            # that lacks the switch (vq_switch.py:3111-3123).
-            raise NotImplementedError("SKIPZERO row tables are not supported by the B200 runtime yet")
+            # SKIPZERO (vq_switch.py:5205-5216): codes / vq_scales hold live rows
+            # only ([NLIVE, W] / [NLIVE, NGRP]) and row_table [E, OUT] int32 maps
+            # (expert, out row) -> compact row, -1 = dead; dead rows read no
+            # bytes and produce +0.
+            if codes.dim() != 2 or vq_scales.dim() != 2:
+                raise ValueError("skipzero codes/vq_scales must be compact 2-D")
+            if row_table.dim() != 2 or row_table.dtype != torch.int32:
+                raise ValueError("row_table must be int32 [num_experts, out_features]")
+            self.register_buffer("row_table", row_table, persistent=True)
         if pack_bits and in_features is None:
             raise ValueError("packed codes need explicit in_features: a packed row is WPR words wide, so "
                              "its shape no longer implies the input dimension")
@@ -83,7 +103,7 @@ class VQSwitchLinear(torch.nn.Module):
 
     @property
     def skipzero(self) -> bool:
-        return False
+        return getattr(self, "row_table", None) is not None
 
     @property
     def input_dims(self) -> int:
@@ -94,10 +114,14 @@ class VQSwitchLinear(torch.nn.Module):
 
     @property
     def output_dims(self) -> int:
+        if self.skipzero:
+            return int(self.row_table.shape[1])
         return int(self.codes.shape[1])
 
     @property
     def num_experts(self) -> int:
+        if self.skipzero:
+            return int(self.row_table.shape[0])
         return int(self.codes.shape[0])
 
     def desc(self) -> _lib.LinearDesc:
@@ -115,7 +139,12 @@ class VQSwitchLinear(torch.nn.Module):
         d.codes = self.codes.data_ptr()
         d.codebook = self.codebook.data_ptr()
         d.scales = self.vq_scales.data_ptr()
-        d.row_table = None
+        if self.skipzero:
+            d.row_table = self.row_table.data_ptr()
+            d.num_rows = int(self.codes.shape[0])
+        else:
+            d.row_table = None
+            d.num_rows = 0
         return d
 
     def _check_tensors(self):
@@ -124,7 +153,7 @@ class VQSwitchLinear(torch.nn.Module):
             raise RuntimeError(
                 f"VQ codebook was sharded: K={k_now}, expected {self._k_expect}. The codebook is a SHARED "
                 f"lookup table and must be replicated across tensor-parallel ranks, not sliced.")
-        for name in ("codes", "codebook", "vq_scales"):
+        for name in ("codes", "codebook", "vq_scales") + (("row_table",) if self.skipzero else ()):
             t = getattr(self, name)
             if not t.is_cuda:
                 raise ValueError(f"{name} must be a CUDA tensor (the B200 runtime has no CPU path)")
