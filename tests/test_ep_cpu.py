@@ -104,3 +104,5 @@ def test_dispatch_plan_single_rank_orders_stably():
     p = dispatch_plan(idx, experts_per_rank=4, world=1)
     assert p.order.tolist() == [0, 1, 2, 3, 4, 5]
     assert p.send_counts == [6] and p.recv_counts == [6]
+    # one row per (token, destination): three tokens, each pair points at its token's row
+    assert p.row_send == [3] and p.row_tok.tolist() == [0, 1, 2] and p.pair_row.tolist() == [0, 0, 1, 1, 2, 2]

@@ -12,8 +12,10 @@ rank that holds the pair's expert:
   rank r holds experts [r * E_local, (r + 1) * E_local)   (E_local = E / world)
   1. route locally: idx [T, k] global expert ids, weights [T, k]
   2. order the T*k pairs by destination rank (stable), exchange the per-rank
-     pair counts (an all-to-all of `world` integers), then one all-to-all of
-     the pairs' token rows and one of their local expert ids
+     pair and row counts (an all-to-all of 2 * `world` integers), then one
+     all-to-all of token rows -- each token's row once per destination rank,
+     however many of its slots that rank serves -- and one of the pairs'
+     (row, local expert id) records; the receiver expands rows to pairs
   3. gate / up / SwiGLU / down on the received pairs (x given per pair)
   4. the reverse all-to-all returns each pair's output row to the rank that
      owns the token, which restores pair order and sums over the k slots.
@@ -41,21 +43,41 @@ class DispatchPlan:
     dest_counts: torch.Tensor  # [world] pairs this rank sends to each rank
     send_counts: list          # host copy of dest_counts
     recv_counts: list          # pairs this rank receives from each rank
+    row_tok: torch.Tensor      # [Rs] token of each sent row (rows grouped by destination, tokens ascending)
+    pair_row: torch.Tensor     # [P] row (within its destination's rows) of each sorted pair
+    row_send: list             # rows this rank sends to each rank
+    row_recv: list             # rows this rank receives from each rank
 
 
 def dispatch_plan(idx: torch.Tensor, experts_per_rank: int, world: int, group=None) -> DispatchPlan:
-    """Stable order of the flat (token, slot) pairs by owning rank, and the
-    split sizes of both all-to-alls (one small all-to-all of counts, read on
-    the host: the data all-to-alls need them as lists)."""
+    """Stable order of the flat (token, slot) pairs by owning rank, the
+    deduplicated rows (one per (token, destination)), and the split sizes of
+    the all-to-alls (one small all-to-all of counts, read on the host: the
+    data all-to-alls need them as lists)."""
+    T, k = idx.shape
     dest = idx.reshape(-1).long() // experts_per_rank
     order = torch.sort(dest, stable=True).indices
     counts = torch.bincount(dest, minlength=world)
-    recv = torch.empty_like(counts)
+    # rows: unique (destination, token), in (destination, token) order
+    key = dest * T + torch.arange(T * k, device=idx.device) // k
+    uniq, inv = torch.unique(key, sorted=True, return_inverse=True)
+    row_dest = uniq // T
+    row_counts = torch.bincount(row_dest, minlength=world)
+    row_start = torch.cumsum(row_counts, 0) - row_counts
+    # a sorted pair's row, numbered inside its destination's block
+    pair_row = inv.index_select(0, order) - row_start.index_select(0, dest.index_select(0, order))
     if world > 1:
-        dist.all_to_all_single(recv, counts, group=group)
+        # counts and row counts travel as one [world, 2] exchange
+        send2 = torch.stack([counts, row_counts], dim=1).contiguous()
+        recv2 = torch.empty_like(send2)
+        dist.all_to_all_single(recv2, send2, group=group)
+        rc, rr = recv2[:, 0], recv2[:, 1]
     else:
-        recv.copy_(counts)
-    return DispatchPlan(order=order, dest_counts=counts, send_counts=counts.tolist(), recv_counts=recv.tolist())
+        rc, rr = counts, row_counts
+    host = torch.cat([counts, row_counts, rc, rr]).tolist()
+    return DispatchPlan(order=order, dest_counts=counts, send_counts=host[:world], recv_counts=host[2 * world:3 * world],
+                        row_tok=uniq % T, pair_row=pair_row, row_send=host[world:2 * world],
+                        row_recv=host[3 * world:])
 
 
 def _a2a(t: torch.Tensor, out_rows: int, out_split, in_split, group) -> torch.Tensor:
@@ -105,15 +127,22 @@ class EPMoEBlock(torch.nn.Module):
         idx, w = route(router_logits, k)
         plan = dispatch_plan(idx, self.experts_per_rank, self.world, self.group)
         flat = idx.reshape(-1).long()
-        tok = plan.order // k                                   # token of each sorted pair
-        send_x = x.index_select(0, tok)
-        send_e = (flat.index_select(0, plan.order) % self.experts_per_rank).to(torch.int32)
+        send_rows = x.index_select(0, plan.row_tok)            # one row per (token, destination)
+        # per sorted pair: its row inside the destination's block, and its local expert
+        send_meta = torch.stack([plan.pair_row, flat.index_select(0, plan.order) % self.experts_per_rank],
+                                dim=1).to(torch.int32)
         n_recv = sum(plan.recv_counts)
         if self.world > 1:
-            recv_x = _a2a(send_x, n_recv, plan.recv_counts, plan.send_counts, self.group)
-            recv_e = _a2a(send_e, n_recv, plan.recv_counts, plan.send_counts, self.group)
+            recv_rows = _a2a(send_rows, sum(plan.row_recv), plan.row_recv, plan.row_send, self.group)
+            recv_meta = _a2a(send_meta, n_recv, plan.recv_counts, plan.send_counts, self.group)
         else:
-            recv_x, recv_e = send_x, send_e
+            recv_rows, recv_meta = send_rows, send_meta
+        # received pairs refer to rows of their source's block: offset by the block starts
+        src_row0 = torch.tensor([0] + plan.row_recv[:-1], device=x.device).cumsum(0)
+        src_of_pair = torch.repeat_interleave(torch.arange(self.world, device=x.device),
+                                              torch.tensor(plan.recv_counts, device=x.device), output_size=n_recv)
+        recv_x = recv_rows.index_select(0, recv_meta[:, 0].long() + src_row0.index_select(0, src_of_pair))
+        recv_e = recv_meta[:, 1].contiguous()
         self.last_recv = (recv_x, recv_e)  # the pairs this rank computed (kept for measurement)
         y_recv = self._experts(recv_x, recv_e)
         if self.world > 1:
