@@ -88,6 +88,41 @@ def test_grouped_gemm_skewed_routing(D, K, IN, OUT, G):
     assert rms(y32) <= 1.01 * rms(pre) + 1e-12
 
 
+DSPLIT_GEOMS = [  # (K, IN, OUT, G): d8 codebooks over the shared-memory budget
+    (16384, 1536, 200, 64),    # dimension split: ragged OUT, 3 windows per pass, two groups per position
+    (16384, 512, 128, 128),    # dimension split: one group per position, scales from global (NGRP < 8)
+    (12000, 1024, 128, 64),    # dimension split with K between the one-pass limit and 2^14
+    (16384, 1536, 128, 192),   # dimension split, G not a power of two
+    (16384, 576, 136, 64),     # IN not a multiple of 512: entry-slice passes instead
+]
+
+
+@pytest.mark.parametrize("K,IN,OUT,G", DSPLIT_GEOMS)
+def test_large_codebook_passes(K, IN, OUT, G):
+    """d8 codebooks larger than shared memory: each pass keeps half of every
+    entry's dims (or, where the split does not apply, a slice of the entries)
+    resident; the sum over passes must equal the one-pass product."""
+    E = 6
+    L = make_layer(E=E, OUT=OUT, IN=IN, D=8, K=K, G=G, seed=K + IN + G)
+    T, k = 90, 6  # 540 pairs
+    idx = skewed_routing(T, k, E, seed=11)
+    rng = np.random.default_rng(12)
+    x = torch.from_numpy(rng.standard_normal((T, 1, 1, IN)).astype(np.float32)).to(torch.bfloat16)
+    m = _switch(L, path=2)
+    ii = torch.from_numpy(idx.astype(np.int32)).cuda()
+    y = m(x.cuda(), ii).float().cpu().numpy().reshape(T * k, OUT)
+    ref32 = _check(L, x, idx.reshape(-1), k, y)
+    y32 = m(x.float().cuda(), ii).cpu().numpy().reshape(T * k, OUT)
+    assert max_rel(orc.round_f16(ref32), y32) <= 2e-3
+    xv = x.float().numpy().reshape(T, IN)
+    ex = orc.exact_f64(L.codes, L.cb_bits, L.sc_bits, orc.f16_vals(orc.f16_bits(xv)), idx=idx.reshape(-1), krep=k)
+    pre = orc.round_f16(_prescaled_oracle(L, xv, idx.reshape(-1), k))
+    rms = lambda a: float(np.sqrt(np.mean((np.asarray(a, np.float64) - ex) ** 2)))
+    assert rms(y32) <= 1.01 * rms(pre) + 1e-12
+    # deterministic: the same call gives the same bytes
+    assert np.array_equal(y32, m(x.float().cuda(), ii).cpu().numpy().reshape(T * k, OUT))
+
+
 def test_hot_expert_spans_several_tiles():
     """One expert with > 256 tokens: several 256-token tiles of the same rows."""
     E = 4

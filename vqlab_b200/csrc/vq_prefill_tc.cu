@@ -55,7 +55,7 @@ constexpr int kBoxRows = 32;                         // x rows per TMA box
 constexpr int kBStageBytes = kMaxN * kChunkK * 2;    // 16 KB
 constexpr int kBStages = 4;                          // position g -> B stage g % 4
 constexpr int kAStages = 8;                          // position g -> A stage g % 8 (two per decode set)
-constexpr int kWStages = 3;                          // code/scale windows
+constexpr int kWStages = 3;                          // code/scale windows (the dimension-split layout uses 2)
 constexpr int kSets = 4;                             // window = kSets chunks, one per set
 constexpr int kIssuers = 2;                          // MMA issuing threads, one accumulator each
 constexpr int kDecodeWarps = 4 * kSets;              // 4 TMEM lane quarters per set
@@ -79,8 +79,9 @@ struct TParams {
   int* status;             // [1] <- VQB_TIMEOUT on a bounded-wait expiry
   void* y;
   int OUT, IN, G, NGRP, bits, K;
-  int n_k;                 // real K chunks (IN / 64)
+  int n_k;                 // real K positions per pass (IN / 64; IN / 128 with the dimension split)
   int n_pos;               // A stages per tile per pass (n_k rounded up to whole windows)
+  int wst;                 // code/scale window stages in use (<= kWStages)
   int row_tiles;
   int y_dtype;
   int round_f16_first;
@@ -95,6 +96,7 @@ struct TParams {
   int kp_log2;             // codebook entries per pass = 1 << kp_log2 (npass > 1)
   int kp;
   int npass;
+  int kpos_log2;           // log2 of the original k a position covers (6; 7 with the dimension split)
   int off_win, off_cb, off_bar;
   const int32_t* row_table;  // SKIPZERO [E, OUT] -> compact row (-1 dead), nullptr = plain layout
   const int* tile_base;      // SKIPZERO: first compact row of each (expert, 128-row tile), -1 = all dead
@@ -262,16 +264,66 @@ __device__ __forceinline__ void lookup(const uint16_t* cb_s, uint32_t c, uint32_
   }
 }
 
+// The NC consecutive codes starting at bit b0 of a staged window row, for a
+// compile-time width BITS: the bits are read with conflict-free 16-byte loads,
+// aligned to bit 0 with a funnel shift, and every code then sits at a fixed
+// bit position.  crow: the row in the staged code window (16-byte aligned,
+// pitch W words), whose 16-byte units sit at index ^ xr (the TMA swizzle of
+// this row; 0 for the plain layout) -- either way 16-byte reads by 32
+// consecutive rows hit 32 different bank groups; b0 is the same for every row.
+template <int BITS, int NC>
+__device__ __forceinline__ void extract_codes(const uint32_t* crow, int xr, int b0, uint32_t* c) {
+  constexpr uint32_t MASK = (1u << BITS) - 1u;
+  constexpr int NB = NC * BITS;              // bits of the codes
+  constexpr int NW = (NB + 31) / 32 + 1;     // words holding them after word alignment (+ straddle)
+  constexpr int NQ = (NW + 3 + 3) / 4;       // 16-byte loads that cover a start anywhere in a 16-byte unit
+  const int w0 = b0 >> 5, sh = b0 & 31, dw = w0 & 3;
+  const uint4* row4 = reinterpret_cast<const uint4*>(crow);
+  uint32_t q[4 * NQ];
+#pragma unroll
+  for (int i = 0; i < NQ; ++i) {
+    const uint4 v = row4[((w0 >> 2) + i) ^ xr];
+    q[4 * i] = v.x; q[4 * i + 1] = v.y; q[4 * i + 2] = v.z; q[4 * i + 3] = v.w;
+  }
+  // drop the dw leading words (dw is the same for the whole warp)
+  uint32_t t[4 * NQ - 2];
+#pragma unroll
+  for (int i = 0; i < 4 * NQ - 2; ++i) t[i] = (dw & 2) ? q[i + 2] : q[i];
+  uint32_t r[NW];
+#pragma unroll
+  for (int i = 0; i < NW; ++i) r[i] = (dw & 1) ? t[i + 1] : t[i];
+  uint32_t n[NW - 1];
+#pragma unroll
+  for (int i = 0; i < NW - 1; ++i) n[i] = __funnelshift_r(r[i], r[i + 1], sh);
+#pragma unroll
+  for (int i = 0; i < NC; ++i) {
+    const int bit = i * BITS, wi = bit >> 5, bs = bit & 31;
+    const uint32_t v = (bs + BITS <= 32) ? (n[wi] >> bs) : __funnelshift_r(n[wi], n[wi + 1], bs);
+    c[i] = v & MASK;
+  }
+}
+
+// W = fp16(cb * s) in place over 32 fp16x2 words (words [0, 16) take s_lo,
+// [16, 32) s_hi), then bf16 for the bf16 operand arm.
+__device__ __forceinline__ void scale_words(uint32_t* out, __half2 s_lo, __half2 s_hi, bool to_bf16) {
+#pragma unroll
+  for (int i = 0; i < 32; ++i) {
+    __half2 v = __hmul2(*reinterpret_cast<__half2*>(&out[i]), i < 16 ? s_lo : s_hi);
+    out[i] = *reinterpret_cast<uint32_t*>(&v);
+  }
+  if (to_bf16) {
+#pragma unroll
+    for (int i = 0; i < 32; ++i) {
+      const float2 f = h2x2f(out[i]);
+      __nv_bfloat162 b = __floats2bfloat162_rn(f.x, f.y);
+      out[i] = *reinterpret_cast<uint32_t*>(&b);
+    }
+  }
+}
+
 // One row's 64 weights of one chunk -> 32 fp16x2 (or bf16x2) words.
-// crow: the row in the staged code window (16-byte aligned, pitch W words),
-// whose 16-byte units sit at index ^ xr (the TMA swizzle of this row; 0 for the
-// plain layout) -- either way 16-byte reads by 32 consecutive rows hit 32
-// different bank groups; b0: bit offset of the chunk's first code in the row
-// (the same for every row).
-// BITS > 0: the code width is a compile-time constant -- the chunk's bits are
-// read with conflict-free 16-byte loads, aligned to bit 0 with a funnel
-// shift, and every code sits at a fixed bit position.  BITS == 0: any width,
-// a sequential bit walk.
+// b0: bit offset of the chunk's first code in the staged row.  BITS > 0: the
+// fixed-position extraction above; BITS == 0: any width, a sequential bit walk.
 template <int D, int BITS>
 __device__ __forceinline__ void decode_chunk(const TParams& prm, const uint16_t* cb_s, const uint32_t* crow, int xr,
                                              int b0, __half2 s2, int h, uint32_t* out) {
@@ -280,36 +332,10 @@ __device__ __forceinline__ void decode_chunk(const TParams& prm, const uint16_t*
   const uint32_t sel = prm.npass > 1 ? static_cast<uint32_t>(h) << prm.kp_log2 : 0u;
   const uint32_t lim = prm.npass > 1 ? static_cast<uint32_t>(prm.kp) : static_cast<uint32_t>(prm.K);
   if constexpr (BITS > 0) {
-    constexpr uint32_t MASK = (1u << BITS) - 1u;
-    constexpr int NB = CPC * BITS;             // bits of the chunk
-    constexpr int NW = (NB + 31) / 32 + 1;     // words holding them after word alignment (+ straddle)
-    constexpr int NQ = (NW + 3 + 3) / 4;       // 16-byte loads that cover a start anywhere in a 16-byte unit
-    const int w0 = b0 >> 5, sh = b0 & 31, dw = w0 & 3;
-    const uint4* row4 = reinterpret_cast<const uint4*>(crow);
-    uint32_t q[4 * NQ];
+    uint32_t c[CPC];
+    extract_codes<BITS, CPC>(crow, xr, b0, c);
 #pragma unroll
-    for (int i = 0; i < NQ; ++i) {
-      const uint4 v = row4[((w0 >> 2) + i) ^ xr];
-      q[4 * i] = v.x; q[4 * i + 1] = v.y; q[4 * i + 2] = v.z; q[4 * i + 3] = v.w;
-    }
-    // drop the dw leading words (dw is the same for the whole warp)
-    uint32_t t[4 * NQ - 2];
-#pragma unroll
-    for (int i = 0; i < 4 * NQ - 2; ++i) t[i] = (dw & 2) ? q[i + 2] : q[i];
-    uint32_t r[NW];
-#pragma unroll
-    for (int i = 0; i < NW; ++i) r[i] = (dw & 1) ? t[i + 1] : t[i];
-    uint32_t n[NW - 1];
-#pragma unroll
-    for (int i = 0; i < NW - 1; ++i) n[i] = __funnelshift_r(r[i], r[i + 1], sh);
-#pragma unroll
-    for (int i = 0; i < CPC; ++i) {
-      constexpr int dummy = 0;
-      (void)dummy;
-      const int bit = i * BITS, wi = bit >> 5, bs = bit & 31;
-      const uint32_t v = (bs + BITS <= 32) ? (n[wi] >> bs) : __funnelshift_r(n[wi], n[wi + 1], bs);
-      lookup<D>(cb_s, v & MASK, sel, lim, out + WPC * i);
-    }
+    for (int i = 0; i < CPC; ++i) lookup<D>(cb_s, c[i], sel, lim, out + WPC * i);
   } else {
     const int bits = prm.bits;
     const uint32_t mask = (1u << bits) - 1u;
@@ -329,24 +355,33 @@ __device__ __forceinline__ void decode_chunk(const TParams& prm, const uint16_t*
       lookup<D>(cb_s, c, sel, lim, out + WPC * i);
     }
   }
+  scale_words(out, s2, s2, prm.b_bf16 != 0);
+}
+
+// Dimension split (d8 codebooks larger than shared memory): pass h keeps dims
+// [4h, 4h + 4) of every entry resident (8 bytes per entry, a zero entry at
+// index K), and a position covers 16 codes x 4 dims = 64 A columns.  Column
+// 4i + d of position p holds W[row, 8 (16p + i) + 4h + d]; x was gathered in
+// the same permuted order, so every weight is decoded once and enters one MMA.
+// Codes 0-7 and 8-15 of a position may sit in different scale groups (G = 64).
+template <int BITS>
+__device__ __forceinline__ void decode_pos_dsplit(const TParams& prm, const uint16_t* cb_s, const uint32_t* crow,
+                                                  int xr, int b0, __half2 s_lo, __half2 s_hi, uint32_t* out) {
+  uint32_t c[16];
+  extract_codes<BITS, 16>(crow, xr, b0, c);
+  const uint32_t lim = static_cast<uint32_t>(prm.K);
 #pragma unroll
-  for (int i = 0; i < 32; ++i) {
-    __half2 v = __hmul2(*reinterpret_cast<__half2*>(&out[i]), s2);
-    out[i] = *reinterpret_cast<uint32_t*>(&v);
+  for (int i = 0; i < 16; ++i) {
+    const uint2 v = reinterpret_cast<const uint2*>(cb_s)[min(c[i], lim)];
+    out[2 * i] = v.x;
+    out[2 * i + 1] = v.y;
   }
-  if (prm.b_bf16) {
-#pragma unroll
-    for (int i = 0; i < 32; ++i) {
-      const float2 f = h2x2f(out[i]);
-      __nv_bfloat162 b = __floats2bfloat162_rn(f.x, f.y);
-      out[i] = *reinterpret_cast<uint32_t*>(&b);
-    }
-  }
+  scale_words(out, s_lo, s_hi, prm.b_bf16 != 0);
 }
 
 // -------------------------------------------------------------- the kernel
 
-template <int D, int BITS>
+template <int D, int BITS, bool DS>
 __global__ void __launch_bounds__(kThreads, 1)
     vq_prefill_tc_kernel(const __grid_constant__ CUtensorMap xmap32, const __grid_constant__ CUtensorMap xmap64,
                          const __grid_constant__ CUtensorMap xmap128, const __grid_constant__ CUtensorMap cmap,
@@ -388,8 +423,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     mbar_init(acc_empty, kDecodeWarps);
     *abort_flag = 0;
     // the zero entry after the resident slice (never written by the slice copies)
-    uint16_t* zero = cb_s + static_cast<size_t>(prm.npass > 1 ? prm.kp : prm.K) * D;
-    for (int i = 0; i < D; ++i) zero[i] = 0;
+    constexpr int kEntryHalves = DS ? 4 : D;
+    uint16_t* zero = cb_s + static_cast<size_t>(DS ? prm.K : (prm.npass > 1 ? prm.kp : prm.K)) * kEntryHalves;
+    for (int i = 0; i < kEntryHalves; ++i) zero[i] = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   if (warp == 0) {
@@ -414,7 +450,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       asm volatile("prefetch.tensormap [%0];" :: "l"(reinterpret_cast<uint64_t>(&xmap128)) : "memory");
       uint32_t gs = 0;  // slot sequence number
       bool ok = true;
-      for (int64_t it = blockIdx.x; it < nitems && ok; it += gridDim.x) {
+      int j = 0;
+      for (int64_t it = blockIdx.x; it < nitems && ok; it += gridDim.x, ++j) {
         const int4 ch = prm.chunks[static_cast<int>(it / prm.row_tiles)];
         const int rows = slot_rows(ch.z);
         const int pp = slot_positions(rows);
@@ -422,12 +459,14 @@ __global__ void __launch_bounds__(kThreads, 1)
         const CUtensorMap* map = rows == 32 ? &xmap32 : (rows == 64 ? &xmap64 : &xmap128);
         const uint32_t bytes = static_cast<uint32_t>(pp * rows * kChunkK * 2);
         for (int pass = 0; pass < prm.npass && ok; ++pass) {
+          // the dimension split reads x's permuted half of the resident codebook dims
+          const int cbase = DS ? pass_slice(prm.npass, j, pass) * prm.n_pos : 0;
           for (int p0 = 0; p0 < prm.n_pos; p0 += pp, ++gs) {
             const uint32_t bs = gs % kBStages;
             if (!mbar_wait(&b_empty[bs], ((gs / kBStages) & 1u) ^ 1u, abort_flag)) { ok = false; break; }
             mbar_expect_tx(&b_full[bs], bytes);
             unsigned char* dst = b_base + bs * kBStageBytes;
-            tma_load_3d(map, &b_full[bs], dst, 0, ch.y, p0);
+            tma_load_3d(map, &b_full[bs], dst, 0, ch.y, cbase + p0);
           }
         }
       }
@@ -513,16 +552,16 @@ __global__ void __launch_bounds__(kThreads, 1)
             unsigned char* dst = w_base + ws * prm.win_stage_bytes;
             tma_load_2d(&cmap, &w_full[ws], dst, (w * prm.wpw) & ~3, yrow);
             if (prm.scale_tma) {
-              const int g_first = (w * kSets * kChunkK) >> prm.log2g;
+              const int g_first = ((w * kSets) << prm.kpos_log2) >> prm.log2g;
               tma_load_2d(&smap, &w_full[ws], dst + prm.code_stage_bytes, g_first & ~7, yrow);
             }
             filled[ws] = 1;
             fill_phase[ws] = wp;
-            if (++ws == kWStages) { ws = 0; wp ^= 1u; }
+            if (++ws == prm.wst) { ws = 0; wp ^= 1u; }
           }
         }
       }
-      for (int s = 0; s < kWStages; ++s)
+      for (int s = 0; s < prm.wst; ++s)
         if (filled[s]) mbar_drain(&w_full[s], fill_phase[s]);
     }
   } else if (warp == kWarpCbLoad) {
@@ -537,11 +576,15 @@ __global__ void __launch_bounds__(kThreads, 1)
           const int h = pass_slice(prm.npass, j, pass);
           if (h == resident) continue;
           if (loads > 0 && !mbar_wait(cb_empty, (loads - 1) & 1u, abort_flag)) { ok = false; break; }
-          const int64_t first = static_cast<int64_t>(h) * prm.kp;
-          const int64_t cnt = min(static_cast<int64_t>(prm.kp), static_cast<int64_t>(prm.K) - first);
-          const uint32_t bytes = static_cast<uint32_t>(cnt * D * 2);
+          // a slice of entries, or (dimension split) dims [4h, 4h + 4) of all
+          // entries from the [2][K][4] copy of the codebook
+          const int64_t first = DS ? 0 : static_cast<int64_t>(h) * prm.kp;
+          const int64_t cnt = DS ? static_cast<int64_t>(prm.K)
+                                 : min(static_cast<int64_t>(prm.kp), static_cast<int64_t>(prm.K) - first);
+          const uint32_t bytes = static_cast<uint32_t>(cnt * (DS ? 8 : D * 2));
           mbar_expect_tx(cb_full, bytes);
-          const unsigned char* src = reinterpret_cast<const unsigned char*>(prm.codebook) + first * D * 2;
+          const unsigned char* src = reinterpret_cast<const unsigned char*>(prm.codebook) +
+                                     (DS ? static_cast<int64_t>(h) * prm.K * 8 : first * D * 2);
           for (uint32_t off = 0; off < bytes; off += 32768u)
             bulk_load(reinterpret_cast<unsigned char*>(cb_s) + off, src + off, min(32768u, bytes - off), cb_full);
           resident = h;
@@ -600,27 +643,36 @@ __global__ void __launch_bounds__(kThreads, 1)
           const int p = w * kSets + s;
           uint32_t out[32];
           if (p < prm.n_k && live) {
-            uint16_t sc;
-            if (prm.scale_tma) {
-              const uint4 sv = reinterpret_cast<const uint4*>(wst + prm.code_stage_bytes)[woff];
-              const int gi = ((p * kChunkK) >> prm.log2g) - (((w * kSets * kChunkK) >> prm.log2g) & ~7);
-              const uint32_t sw = (gi & 4) ? ((gi & 2) ? sv.w : sv.z) : ((gi & 2) ? sv.y : sv.x);
-              sc = static_cast<uint16_t>((gi & 1) ? (sw >> 16) : (sw & 0xFFFFu));
-            } else {
-              sc = __ldg(srow + (p * kChunkK) / prm.G);
-            }
-            const __half sh = __ushort_as_half(sc);
+            // scale of the group holding original k = kk (staged with the window, or from global)
+            auto scale_at = [&](int kk) -> uint16_t {
+              if (prm.scale_tma) {
+                const uint4 sv = reinterpret_cast<const uint4*>(wst + prm.code_stage_bytes)[woff];
+                const int gi = (kk >> prm.log2g) - ((((w * kSets) << prm.kpos_log2) >> prm.log2g) & ~7);
+                const uint32_t sw = (gi & 4) ? ((gi & 2) ? sv.w : sv.z) : ((gi & 2) ? sv.y : sv.x);
+                return static_cast<uint16_t>((gi & 1) ? (sw >> 16) : (sw & 0xFFFFu));
+              }
+              return __ldg(srow + kk / prm.G);
+            };
             const int wstart = w * prm.wpw;
-            const int b0 = (wstart & 3) * 32 + s * (kChunkK / D) * prm.bits;
-            decode_chunk<D, BITS>(prm, cb_s, reinterpret_cast<const uint32_t*>(wst) + woff * prm.W, xr, b0,
-                                  __halves2half2(sh, sh), h, out);
+            const uint32_t* crow_s = reinterpret_cast<const uint32_t*>(wst) + woff * prm.W;
+            if constexpr (DS) {
+              const __half slo = __ushort_as_half(scale_at(p << 7));
+              const __half shi = __ushort_as_half(scale_at((p << 7) + 64));
+              const int b0 = (wstart & 3) * 32 + s * 16 * BITS;
+              decode_pos_dsplit<BITS>(prm, cb_s, crow_s, xr, b0, __halves2half2(slo, slo), __halves2half2(shi, shi),
+                                      out);
+            } else {
+              const __half sh = __ushort_as_half(scale_at(p * kChunkK));
+              const int b0 = (wstart & 3) * 32 + s * (kChunkK / D) * prm.bits;
+              decode_chunk<D, BITS>(prm, cb_s, crow_s, xr, b0, __halves2half2(sh, sh), h, out);
+            }
           } else {
 #pragma unroll
             for (int i = 0; i < 32; ++i) out[i] = 0u;  // K padding up to a whole window, or a dead row
           }
           __syncwarp();
           if (lane == 0) mbar_arrive(&w_empty[ws]);
-          if (++ws == kWStages) { ws = 0; wp ^= 1u; }
+          if (++ws == prm.wst) { ws = 0; wp ^= 1u; }
           // position p of this tile-pass has sequence number g + p; its A stage
           // was last read by position g + p - 8
           const uint32_t gp = g + static_cast<uint32_t>(p);
@@ -699,8 +751,11 @@ __global__ void tile_base_kernel(const int32_t* __restrict__ rt, int E, int OUT,
 // x rows gathered into expert-sorted order as 16-bit B rows: xs[s] = x[sorted[s] / krep].
 // One warp per row, 16 bytes (8 elements) per lane and step; x is fp16 or
 // bf16 with 16-byte aligned rows (IN % 64 == 0 and an aligned base).
+// dsplit: the dimension-split order -- elements 8j .. 8j+3 go to columns
+// 4j .. 4j+3 and elements 8j+4 .. 8j+7 to IN/2 + 4j .. (the x side of
+// decode_pos_dsplit's column order).
 __global__ void gather_sorted_kernel(const void* __restrict__ x, int x_dtype, const int* __restrict__ sorted, int N,
-                                     int krep, int IN, int to_bf16, uint16_t* __restrict__ xs) {
+                                     int krep, int IN, int to_bf16, int dsplit, uint16_t* __restrict__ xs) {
   const int lane = threadIdx.x & 31;
   const int vec = IN / 8;
   const bool convert = (x_dtype == VQB_BF16) != (to_bf16 != 0);
@@ -725,9 +780,25 @@ __global__ void gather_sorted_kernel(const void* __restrict__ x, int x_dtype, co
           }
         }
       }
-      dst[i] = v;
+      if (dsplit) {
+        uint2* d2 = reinterpret_cast<uint2*>(xs + static_cast<int64_t>(s) * IN);
+        d2[i] = make_uint2(v.x, v.y);
+        d2[vec + i] = make_uint2(v.z, v.w);
+      } else {
+        dst[i] = v;
+      }
     }
   }
+}
+
+// The d8 codebook [K][8] as two dimension halves [2][K][4] for the
+// dimension-split passes (one thread per entry).
+__global__ void split_codebook_kernel(const uint16_t* __restrict__ cb, int K, uint16_t* __restrict__ out) {
+  const int c = blockIdx.x * blockDim.x + threadIdx.x;
+  if (c >= K) return;
+  const uint4 v = __ldg(reinterpret_cast<const uint4*>(cb) + c);
+  reinterpret_cast<uint2*>(out)[c] = make_uint2(v.x, v.y);
+  reinterpret_cast<uint2*>(out)[K + c] = make_uint2(v.z, v.w);
 }
 
 using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
@@ -776,20 +847,24 @@ template <int D>
 void* pick_kernel(int bits) {
   // code widths of the shipped geometries get the fixed-position extraction
   if constexpr (D == 8) {
-    if (bits == 12) return reinterpret_cast<void*>(vq_prefill_tc_kernel<8, 12>);
-    if (bits == 14) return reinterpret_cast<void*>(vq_prefill_tc_kernel<8, 14>);
-    if (bits == 16) return reinterpret_cast<void*>(vq_prefill_tc_kernel<8, 16>);
-    return reinterpret_cast<void*>(vq_prefill_tc_kernel<8, 0>);
+    if (bits == 12) return reinterpret_cast<void*>(vq_prefill_tc_kernel<8, 12, false>);
+    if (bits == 14) return reinterpret_cast<void*>(vq_prefill_tc_kernel<8, 14, false>);
+    if (bits == 16) return reinterpret_cast<void*>(vq_prefill_tc_kernel<8, 16, false>);
+    return reinterpret_cast<void*>(vq_prefill_tc_kernel<8, 0, false>);
   } else if constexpr (D == 4) {
-    if (bits == 12) return reinterpret_cast<void*>(vq_prefill_tc_kernel<4, 12>);
-    if (bits == 13) return reinterpret_cast<void*>(vq_prefill_tc_kernel<4, 13>);
-    return reinterpret_cast<void*>(vq_prefill_tc_kernel<4, 0>);
+    if (bits == 12) return reinterpret_cast<void*>(vq_prefill_tc_kernel<4, 12, false>);
+    if (bits == 13) return reinterpret_cast<void*>(vq_prefill_tc_kernel<4, 13, false>);
+    return reinterpret_cast<void*>(vq_prefill_tc_kernel<4, 0, false>);
   } else {
-    if (bits == 8) return reinterpret_cast<void*>(vq_prefill_tc_kernel<2, 8>);
-    if (bits == 9) return reinterpret_cast<void*>(vq_prefill_tc_kernel<2, 9>);
-    return reinterpret_cast<void*>(vq_prefill_tc_kernel<2, 0>);
+    if (bits == 8) return reinterpret_cast<void*>(vq_prefill_tc_kernel<2, 8, false>);
+    if (bits == 9) return reinterpret_cast<void*>(vq_prefill_tc_kernel<2, 9, false>);
+    return reinterpret_cast<void*>(vq_prefill_tc_kernel<2, 0, false>);
   }
 }
+
+// Code widths with a dimension-split kernel (d8 codebooks over the shared-memory budget).
+bool dsplit_bits(int bits) { return bits == 14; }
+
 
 }  // namespace
 
@@ -802,7 +877,12 @@ bool tc_prefill_supported(const LinearGeometry& geo) {
   return true;
 }
 
-size_t tc_prefill_x_bytes(int64_t N, int IN) { return (static_cast<size_t>(N) * IN * 2 + 1023) & ~size_t(1023); }
+size_t tc_prefill_x_bytes(int64_t N, int IN, int K, int D) {
+  const size_t xs = (static_cast<size_t>(N) * IN * 2 + 1023) & ~size_t(1023);
+  // + the [2][K][4] dimension halves of a d8 codebook (dimension-split passes)
+  const size_t split = D == 8 && K > 0 ? (static_cast<size_t>(K) * 16 + 1023) & ~size_t(1023) : 0;
+  return IN > 0 ? xs + split : 0;
+}
 
 vqb_status launch_prefill_tc(const LinearGeometry& geo, const void* x, int x_dtype, int krep, const RouteWorkspace& rw,
                              int N, uint16_t* xs, void* y, int y_dtype, bool round_f16_first, bool bf16_operands,
@@ -833,8 +913,6 @@ vqb_status launch_prefill_tc(const LinearGeometry& geo, const void* x, int x_dty
   prm.NGRP = geo.IN / geo.G;
   prm.bits = geo.bits;
   prm.K = geo.K;
-  prm.n_k = geo.IN / kChunkK;
-  prm.n_pos = (prm.n_k + kSets - 1) / kSets * kSets;
   prm.row_tiles = (geo.OUT + kTileM - 1) / kTileM;
   prm.y_dtype = y_dtype;
   prm.round_f16_first = round_f16_first ? 1 : 0;
@@ -842,55 +920,83 @@ vqb_status launch_prefill_tc(const LinearGeometry& geo, const void* x, int x_dty
   prm.row_table = geo.row_table;
   prm.tile_base = rw.tile_base;
   prm.nrows = geo.nrows;
-
-  // code window: kSets chunks = 256 k = (256 / D) codes of every row, read
-  // from an aligned-down 16-byte boundary (up to o_max extra words); rows of
-  // 64 or 128 bytes take the matching TMA swizzle, longer rows an odd number
-  // of 16-byte units -- either way conflict-free 16-byte reads across rows
-  prm.wpw = (kSets * kChunkK / geo.D) * geo.bits / 32;
-  const int o_max = prm.wpw % 4 == 0 ? 0 : (prm.wpw % 2 == 0 ? 2 : 3);
-  const int need = o_max + prm.wpw;
-  int W;
-  if (need <= 16) { W = 16; prm.wswz = 1; }
-  else if (need <= 32) { W = 32; prm.wswz = 2; }
-  else {
-    W = (need + 3) & ~3;
-    if ((W / 4) % 2 == 0) W += 4;
-    prm.wswz = 0;
-  }
-  prm.W = W;
-  prm.code_stage_bytes = kTileM * W * 4;
   const bool g_pow2 = (geo.G & (geo.G - 1)) == 0;
   prm.scale_tma = (prm.NGRP % 8 == 0 && g_pow2 && (reinterpret_cast<uintptr_t>(geo.scales) & 15) == 0) ? 1 : 0;
   int log2g = 0;
   while ((1 << (log2g + 1)) <= geo.G) ++log2g;
   prm.log2g = log2g;
-  prm.win_stage_bytes = prm.code_stage_bytes + (prm.scale_tma ? kTileM * kScaleRowBytes : 0);
-
-  // shared memory: B stages, windows, then the largest power-of-two codebook slice that fits
   const size_t tail = static_cast<size_t>(kNumBars) * 8 + 16;
-  const size_t fixed = 1024 + static_cast<size_t>(kBStages) * kBStageBytes +
-                       static_cast<size_t>(kWStages) * prm.win_stage_bytes + tail + 16;
-  if (static_cast<size_t>(g_smem_optin) <= fixed + 1024) return VQB_UNSUPPORTED_GEOMETRY;
-  const size_t avail = static_cast<size_t>(g_smem_optin) - fixed;
-  const size_t entry = static_cast<size_t>(geo.D) * 2;
-  if (static_cast<size_t>(geo.K + 1) * entry <= avail) {
-    prm.kp = geo.K;
-    prm.kp_log2 = 0;
-    prm.npass = 1;
-  } else {
-    int l = 0;
-    while (((static_cast<size_t>(2) << l) + 1) * entry <= avail) ++l;
-    prm.kp_log2 = l;
-    prm.kp = 1 << l;
-    prm.npass = (geo.K + prm.kp - 1) / prm.kp;
+
+  // Shared-memory layout for one mode: [B stages][wst code/scale windows]
+  // [codebook slice + zero entry][barriers]; returns the total, or 0 when the
+  // slice does not fit.  ds: dimension split (all K entries, 4 dims, 2 window
+  // stages); else the largest power-of-two slice of whole entries that fits.
+  auto plan = [&](bool ds) -> size_t {
+    prm.kpos_log2 = ds ? 7 : 6;
+    prm.n_k = geo.IN >> prm.kpos_log2;
+    prm.n_pos = (prm.n_k + kSets - 1) / kSets * kSets;
+    prm.wst = ds ? 2 : kWStages;
+    // code window: kSets positions of every row, read from an aligned-down
+    // 16-byte boundary (up to o_max extra words); rows of 64 or 128 bytes take
+    // the matching TMA swizzle, others an odd number of 16-byte units -- either
+    // way conflict-free 16-byte reads across rows
+    prm.wpw = ((kSets << prm.kpos_log2) / geo.D) * geo.bits / 32;
+    const int o_max = prm.wpw % 4 == 0 ? 0 : (prm.wpw % 2 == 0 ? 2 : 3);
+    const int need = o_max + prm.wpw;
+    int W;
+    if (need <= 16) { W = 16; prm.wswz = 1; }
+    else if (need <= 32 && !(need % 4 == 0 && (need / 4) % 2 == 1)) { W = 32; prm.wswz = 2; }
+    else {
+      W = (need + 3) & ~3;
+      if ((W / 4) % 2 == 0) W += 4;
+      prm.wswz = 0;
+    }
+    prm.W = W;
+    prm.code_stage_bytes = kTileM * W * 4;
+    prm.win_stage_bytes = prm.code_stage_bytes + (prm.scale_tma ? kTileM * kScaleRowBytes : 0);
+    const size_t fixed = 1024 + static_cast<size_t>(kBStages) * kBStageBytes +
+                         static_cast<size_t>(prm.wst) * prm.win_stage_bytes + tail + 16;
+    if (static_cast<size_t>(g_smem_optin) <= fixed + 1024) return 0;
+    const size_t avail = static_cast<size_t>(g_smem_optin) - fixed;
+    size_t entry = static_cast<size_t>(geo.D) * 2;
+    if (ds) {
+      entry = 8;
+      if (static_cast<size_t>(geo.K + 1) * entry > avail) return 0;
+      prm.kp = geo.K;
+      prm.kp_log2 = 0;
+      prm.npass = 2;
+    } else if (static_cast<size_t>(geo.K + 1) * entry <= avail) {
+      prm.kp = geo.K;
+      prm.kp_log2 = 0;
+      prm.npass = 1;
+    } else {
+      int l = 0;
+      while (((static_cast<size_t>(2) << l) + 1) * entry <= avail) ++l;
+      prm.kp_log2 = l;
+      prm.kp = 1 << l;
+      prm.npass = (geo.K + prm.kp - 1) / prm.kp;
+    }
+    const size_t cb_bytes = (static_cast<size_t>(prm.kp + 1) * entry + 15) & ~size_t(15);  // + the zero entry
+    prm.off_win = kBStages * kBStageBytes;
+    prm.off_cb = prm.off_win + prm.wst * prm.win_stage_bytes;
+    prm.off_bar = static_cast<int>(prm.off_cb + cb_bytes);
+    const size_t smem = 1024 + static_cast<size_t>(prm.off_bar) + tail;
+    return smem <= static_cast<size_t>(g_smem_optin) ? smem : 0;
+  };
+  size_t smem = plan(false);
+  bool ds = false;
+  if (geo.D == 8 && prm.npass > 1 && dsplit_bits(geo.bits) && geo.IN % (kSets * 128) == 0 && geo.K % 2 == 0) {
+    const size_t s2 = plan(true);
+    if (s2 > 0) {
+      smem = s2;
+      ds = true;
+    } else {
+      smem = plan(false);
+    }
   }
-  const size_t cb_bytes = (static_cast<size_t>(prm.kp + 1) * entry + 15) & ~size_t(15);  // + the zero entry
-  prm.off_win = kBStages * kBStageBytes;
-  prm.off_cb = prm.off_win + kWStages * prm.win_stage_bytes;
-  prm.off_bar = static_cast<int>(prm.off_cb + cb_bytes);
-  const size_t smem = 1024 + static_cast<size_t>(prm.off_bar) + tail;
-  if (smem > static_cast<size_t>(g_smem_optin)) return VQB_UNSUPPORTED_GEOMETRY;
+  if (smem == 0) return VQB_UNSUPPORTED_GEOMETRY;
+  uint16_t* cb_split = ds ? reinterpret_cast<uint16_t*>(reinterpret_cast<char*>(xs) + tc_prefill_x_bytes(N, geo.IN, 0, 0))
+                          : nullptr;
 
   // 1. gather x into expert-sorted 16-bit rows
   {
@@ -899,9 +1005,17 @@ vqb_status launch_prefill_tc(const LinearGeometry& geo, const void* x, int x_dty
     int64_t blocks = (static_cast<int64_t>(N) + 7) / 8;
     if (blocks > 16 * g_sms_tc) blocks = 16 * g_sms_tc;
     gather_sorted_kernel<<<static_cast<unsigned>(blocks), 256, 0, stream>>>(x, x_dtype, rw.sorted, N, krep, geo.IN,
-                                                                            bf16_operands ? 1 : 0, xs);
+                                                                            bf16_operands ? 1 : 0, ds ? 1 : 0, xs);
     if (cudaGetLastError() != cudaSuccess) return VQB_CUDA_ERROR;
     note_launch();
+  }
+  // 1a. dimension halves of the codebook
+  if (ds) {
+    split_codebook_kernel<<<static_cast<unsigned>((geo.K + 255) / 256), 256, 0, stream>>>(prm.codebook, geo.K,
+                                                                                          cb_split);
+    if (cudaGetLastError() != cudaSuccess) return VQB_CUDA_ERROR;
+    note_launch();
+    prm.codebook = cb_split;
   }
   // 1b. SKIPZERO tile bases
   if (geo.row_table) {
@@ -924,7 +1038,7 @@ vqb_status launch_prefill_tc(const LinearGeometry& geo, const void* x, int x_dty
   const CUtensorMapSwizzle cswz = prm.wswz == 1 ? CU_TENSOR_MAP_SWIZZLE_64B
                                   : (prm.wswz == 2 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE);
   if (!encode_2d(enc, &cmap, CU_TENSOR_MAP_DATA_TYPE_UINT32, 4, geo.codes, static_cast<uint64_t>(geo.row_words), rows,
-                 static_cast<uint32_t>(W), kTileM, cswz))
+                 static_cast<uint32_t>(prm.W), kTileM, cswz))
     return VQB_CUDA_ERROR;
   if (prm.scale_tma) {
     if (!encode_2d(enc, &smap, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, geo.scales, static_cast<uint64_t>(prm.NGRP), rows, 8,
@@ -934,7 +1048,8 @@ vqb_status launch_prefill_tc(const LinearGeometry& geo, const void* x, int x_dty
     smap = cmap;  // unused
   }
 
-  void* kern = geo.D == 8 ? pick_kernel<8>(geo.bits) : (geo.D == 4 ? pick_kernel<4>(geo.bits) : pick_kernel<2>(geo.bits));
+  void* kern = ds ? reinterpret_cast<void*>(vq_prefill_tc_kernel<8, 14, true>)
+                  : (geo.D == 8 ? pick_kernel<8>(geo.bits) : (geo.D == 4 ? pick_kernel<4>(geo.bits) : pick_kernel<2>(geo.bits)));
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)) != cudaSuccess)
     return VQB_CUDA_ERROR;
   void* args[] = {&xmaps[0], &xmaps[1], &xmaps[2], &cmap, &smap, &prm};

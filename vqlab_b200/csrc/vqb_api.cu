@@ -80,12 +80,12 @@ static bool dtype_ok(int t) { return t == VQB_F16 || t == VQB_BF16 || t == VQB_F
 // Workspace: [routing (status block first)][x as 16-bit rows: the token rows
 // for the decode kernel's B operand, or all pairs' rows in expert order for
 // the grouped GEMM -- whichever is larger]
-size_t x_region_bytes(int N, int64_t T, int IN) {
-  const size_t a = mma_x16_bytes(T, IN), b = tc_prefill_x_bytes(N, IN);
+size_t x_region_bytes(int N, int64_t T, int IN, int K, int D) {
+  const size_t a = mma_x16_bytes(T, IN), b = tc_prefill_x_bytes(N, IN, K, D);
   return a > b ? a : b;
 }
-size_t linear_workspace_bytes(int N, int E, int64_t T, int IN, int OUT) {
-  return route_workspace_bytes(N, E, kDecodeMaxPairs, row_tiles_128(OUT)) + x_region_bytes(N, T, IN);
+size_t linear_workspace_bytes(int N, int E, int64_t T, int IN, int OUT, int K, int D) {
+  return route_workspace_bytes(N, E, kDecodeMaxPairs, row_tiles_128(OUT)) + x_region_bytes(N, T, IN, K, D);
 }
 
 // Shared body of the switch and dense entry points once shapes are valid.
@@ -190,7 +190,9 @@ size_t vqb_switch_workspace_size(const vqb_linear_desc* desc, int32_t n_tokens, 
   const int E = desc ? (desc->num_experts > 0 ? desc->num_experts : 1) : 1;
   const int IN = desc ? (desc->in_features > 0 ? desc->in_features : 0) : 0;
   const int OUT = desc ? (desc->out_features > 0 ? desc->out_features : 0) : 0;
-  return linear_workspace_bytes(static_cast<int>(N), E, T, IN, OUT);
+  const int K = desc ? (desc->num_codes > 0 ? desc->num_codes : 0) : 0;
+  const int D = desc ? desc->dim : 0;
+  return linear_workspace_bytes(static_cast<int>(N), E, T, IN, OUT, K, D);
 }
 
 vqb_status vqb_switch_forward(const vqb_linear_desc* desc, const void* x, vqb_dtype x_dtype, int32_t n_tokens,
@@ -234,7 +236,9 @@ size_t vqb_dense_workspace_size(const vqb_linear_desc* desc, int64_t n_rows, con
   const int n = static_cast<int>(n_rows > 0 ? (n_rows > 0x7fffffff ? 0x7fffffff : n_rows) : 0);
   const int IN = desc ? (desc->in_features > 0 ? desc->in_features : 0) : 0;
   const int OUT = desc ? (desc->out_features > 0 ? desc->out_features : 0) : 0;
-  return linear_workspace_bytes(n, 1, n, IN, OUT);
+  const int K = desc ? (desc->num_codes > 0 ? desc->num_codes : 0) : 0;
+  const int D = desc ? desc->dim : 0;
+  return linear_workspace_bytes(n, 1, n, IN, OUT, K, D);
 }
 
 vqb_status vqb_dense_forward(const vqb_linear_desc* desc, const void* x, vqb_dtype x_dtype, int64_t n_rows, void* y,

@@ -71,7 +71,7 @@ vqb_status launch_decode_mma(const LinearGeometry& geo, const GroupedDecodeArgs&
 
 // Grouped tcgen05 GEMM for large token counts (vq_prefill_tc.cu).
 bool tc_prefill_supported(const LinearGeometry& geo);
-size_t tc_prefill_x_bytes(int64_t N, int IN);
+size_t tc_prefill_x_bytes(int64_t N, int IN, int K, int D);  // gathered x (+ d8 codebook halves)
 vqb_status launch_prefill_tc(const LinearGeometry& geo, const void* x, int x_dtype, int krep, const RouteWorkspace& rw,
                              int N, uint16_t* xs, void* y, int y_dtype, bool round_f16_first, bool bf16_operands,
                              int* status, cudaStream_t stream);
@@ -86,7 +86,7 @@ void timer_before(cudaStream_t stream);
 void timer_after(cudaStream_t stream);
 
 // Workspace layout and the shared body of the switch / dense entry points (vqb_api.cu).
-size_t linear_workspace_bytes(int N, int E, int64_t T, int IN, int OUT);
+size_t linear_workspace_bytes(int N, int E, int64_t T, int IN, int OUT, int K, int D);
 vqb_status run_linear(const LinearGeometry& geo, const void* x, int x_dtype, int n_tokens, const uint32_t* indices,
                       int krep, int N, void* y, int y_dtype, void* workspace, const vqb_options* opts,
                       bool narrow_x_f16, bool round_f16_first, int wround, bool large, cudaStream_t stream);

@@ -74,7 +74,7 @@ extern "C" vqb_status vqb_switch_forward_static(const vqb_linear_desc* desc, con
   if (N == 0) return VQB_OK;
   if (!x || !indices || !y) return VQB_NULL_POINTER;
   // routing tables + x as 16-bit rows, the decode path's scratch
-  const size_t need = linear_workspace_bytes(N, geo.E, n_tokens, 0, geo.OUT) + mma_x16_bytes(n_tokens, geo.IN);
+  const size_t need = linear_workspace_bytes(N, geo.E, n_tokens, 0, geo.OUT, 0, 0) + mma_x16_bytes(n_tokens, geo.IN);
   if (need > kStaticScratchBytes) return VQB_WORKSPACE_TOO_SMALL;
   void* scratch = nullptr;
   st = scratch_address(&scratch);
