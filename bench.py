@@ -71,33 +71,76 @@ CODEBOOK_BYTES = K * D * 2
 # ---------------------------------------------------------------- clocks
 
 class ClockSampler:
-    """nvidia-smi clocks + throttle reasons sampled every 200 ms during the timed region."""
+    """SM clocks and clock-event (throttle) reasons sampled every 10 ms during
+    the timed region, read-only through NVML (the same counters nvidia-smi's
+    clocks.sm / clocks_event_reasons.* report); nvidia-smi at its 100 ms
+    minimum when NVML is not importable.  The GPU is found by PCI bus id so a
+    CUDA_VISIBLE_DEVICES remap cannot point it at another device."""
 
+    REASONS = {"hw_slowdown": 0x8, "hw_thermal_slowdown": 0x40, "sw_thermal_slowdown": 0x20, "sw_power_cap": 0x4}
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
-    def __init__(self, gpu_index: int):
+    def __init__(self, gpu_index: int, period_s: float = 0.01):
         self.gpu = gpu_index
-        self.proc = None
-        self.f = None
+        self.period = period_s
+        self.sm, self.mx, self.reasons, self.err = [], None, set(), None
+        self.proc = self.f = self.thread = None
+
+    def _nvml_handle(self):
+        import pynvml
+        import torch
+        pynvml.nvmlInit()
+        try:
+            p = torch.cuda.get_device_properties(self.gpu)
+            bus = f"{p.pci_domain_id:08x}:{p.pci_bus_id:02x}:{p.pci_device_id:02x}.0"
+            return pynvml, pynvml.nvmlDeviceGetHandleByPciBusId(bus.encode())
+        except Exception:
+            return pynvml, pynvml.nvmlDeviceGetHandleByIndex(self.gpu)
 
     def __enter__(self):
+        import threading
+        try:
+            nv, h = self._nvml_handle()
+            self.mx = float(nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM))
+            self.stop = threading.Event()
+
+            def run():
+                while True:
+                    try:
+                        self.sm.append(float(nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM)))
+                        bits = nv.nvmlDeviceGetCurrentClocksEventReasons(h)
+                        self.reasons.update(n for n, b in self.REASONS.items() if bits & b)
+                    except Exception as e:  # noqa: BLE001 - reported in the summary
+                        self.err = str(e)
+                    if self.stop.wait(self.period):
+                        return
+
+            self.thread = threading.Thread(target=run, daemon=True)
+            self.thread.start()
+        except Exception:
+            self.thread = None
+            self._start_smi()
+        return self
+
+    def _start_smi(self):
         try:
             self.f = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
                  "-lms", "100"], stdout=self.f, stderr=subprocess.DEVNULL)
-            # the timed region starts once the sampler is producing rows
             t0 = time.time()
             while time.time() - t0 < 3.0 and pathlib.Path(self.f.name).stat().st_size == 0:
                 time.sleep(0.02)
             self.skip = len(pathlib.Path(self.f.name).read_text().splitlines())
         except Exception:
             self.proc = None
-        return self
 
     def __exit__(self, *a):
+        if self.thread is not None:
+            self.stop.set()
+            self.thread.join(timeout=5)
         if self.proc is not None:
             self.proc.terminate()
             try:
@@ -106,27 +149,31 @@ class ClockSampler:
                 self.proc.kill()
 
     def summary(self):
-        if self.proc is None or self.f is None:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
-        self.f.flush()
-        rows = [r.split(",") for r in pathlib.Path(self.f.name).read_text().splitlines()[getattr(self, "skip", 0):]
-                if r.strip()]
-        sm, mx, reasons = [], None, set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for r in rows:
-            r = [c.strip() for c in r]
-            if len(r) < 9:
-                continue
-            try:
-                sm.append(float(r[1]))
-                mx = float(r[2])
-            except ValueError:
-                continue
-            for n, v in zip(names, r[5:9]):
-                if v.lower() == "active":
-                    reasons.add(n)
-        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx, "reasons": sorted(reasons),
-                "samples": len(sm)}
+        if self.thread is None:
+            if self.proc is None or self.f is None:
+                return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["clock sampling unavailable"]}
+            self.f.flush()
+            rows = [r.split(",") for r in pathlib.Path(self.f.name).read_text().splitlines()[getattr(self, "skip", 0):]
+                    if r.strip()]
+            names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+            for r in rows:
+                r = [c.strip() for c in r]
+                if len(r) < 9:
+                    continue
+                try:
+                    self.sm.append(float(r[1]))
+                    self.mx = float(r[2])
+                except ValueError:
+                    continue
+                for n, v in zip(names, r[5:9]):
+                    if v.lower() == "active":
+                        self.reasons.add(n)
+        out = {"sm_mhz": statistics.median(self.sm) if self.sm else None, "sm_max_mhz": self.mx,
+               "reasons": sorted(self.reasons), "samples": len(self.sm),
+               "source": "nvml 10 ms" if self.thread is not None else "nvidia-smi 100 ms"}
+        if self.err:
+            out["sampling_error"] = self.err
+        return out
 
 
 # ------------------------------------------------------------------ GPU arm

@@ -48,7 +48,10 @@ struct MParams {
   const uint32_t* codes;
   const uint16_t* codebook;
   const uint16_t* scales;
-  const uint16_t* x16;      // [T, IN] 16-bit x (fp16 or bf16 per WR)
+  const uint16_t* x16;      // [T, IN] 16-bit x (fp16 or bf16 per WR), x_mode 0
+  const void* xraw;         // the caller's x [T, IN] (16-byte aligned rows), x_mode 1 / 2
+  int x_dtype;              // its vqb_dtype
+  int x_mode;               // 0: x16; 1: xraw is already the 16-bit B type; 2: convert xraw while staging
   const int* sorted;
   const int4* chunks;
   const int* meta;
@@ -190,6 +193,41 @@ __device__ __forceinline__ void st_cluster_f32(uint32_t addr, float v) {
   asm volatile("st.shared::cluster.f32 [%0], %1;" :: "r"(addr), "f"(v) : "memory");
 }
 
+// Eight consecutive x elements from element i (16-byte aligned) as the B
+// operand's 16-bit type: fp16 by RNE (the narrowing x_to_16bit_kernel
+// applies), or bf16.
+__device__ __forceinline__ uint4 x8_to_16bit(const void* x, int dtype, int64_t i, bool to_bf16) {
+  float f[8];
+  if (dtype == VQB_F32) {
+    const float4 a = __ldg(reinterpret_cast<const float4*>(static_cast<const float*>(x) + i));
+    const float4 b = __ldg(reinterpret_cast<const float4*>(static_cast<const float*>(x) + i) + 1);
+    f[0] = a.x; f[1] = a.y; f[2] = a.z; f[3] = a.w; f[4] = b.x; f[5] = b.y; f[6] = b.z; f[7] = b.w;
+  } else {
+    const uint4 v = __ldg(reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(x) + i));
+    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      float2 t;
+      if (dtype == VQB_BF16) t = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w[j]));
+      else t = __half22float2(*reinterpret_cast<const __half2*>(&w[j]));
+      f[2 * j] = t.x;
+      f[2 * j + 1] = t.y;
+    }
+  }
+  uint32_t o[4];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    if (to_bf16) {
+      __nv_bfloat162 b = __floats2bfloat162_rn(f[2 * j], f[2 * j + 1]);
+      o[j] = *reinterpret_cast<uint32_t*>(&b);
+    } else {
+      __half2 h = __floats2half2_rn(f[2 * j], f[2 * j + 1]);
+      o[j] = *reinterpret_cast<uint32_t*>(&h);
+    }
+  }
+  return make_uint4(o[0], o[1], o[2], o[3]);
+}
+
 // Place of (expert e, output row) in codes / scales: the plain [E, OUT, ...]
 // layout, or its SKIPZERO compact row; -1 = dead (reads nothing, writes +0).
 __device__ __forceinline__ int64_t code_row(const MParams& prm, int e, int row) {
@@ -277,7 +315,11 @@ __global__ void __launch_bounds__(kThreads, 1) vq_decode_mma_kernel(const MParam
       for (int q = threadIdx.x; q < ch.z * nv; q += kThreads) {
         const int p = q / nv, v = q - p * nv;
         const int pair = prm.sorted[ch.y + p];
-        const uint4 val = __ldg(reinterpret_cast<const uint4*>(prm.x16 + static_cast<int64_t>(pair / prm.krep) * prm.IN) + v);
+        const int64_t xrow = static_cast<int64_t>(pair / prm.krep) * prm.IN;
+        uint4 val;
+        if (prm.x_mode == 0) val = __ldg(reinterpret_cast<const uint4*>(prm.x16 + xrow) + v);
+        else if (prm.x_mode == 1) val = __ldg(reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(prm.xraw) + xrow) + v);
+        else val = x8_to_16bit(prm.xraw, prm.x_dtype, xrow + v * 8, WR == 1);
         *reinterpret_cast<uint4*>(x_s + p * prm.x_stride + v * 8) = val;
       }
       cur_chunk = chunk;
@@ -359,6 +401,7 @@ __global__ void __launch_bounds__(kThreads, 1) vq_decode_mma_kernel(const MParam
         }
 #pragma unroll
         for (int n = 0; n < NT; ++n) {
+          if (n > 0 && 8 * n >= P) break;  // token tile beyond this chunk's pairs: no x reads, no MMAs
           const uint4 xv0 = *reinterpret_cast<const uint4*>(xrow[n] + kg / 2);
           const uint4 xv1 = *reinterpret_cast<const uint4*>(xrow[n] + kg / 2 + 4);
           const uint32_t xb[8] = {xv0.x, xv0.y, xv0.z, xv0.w, xv1.x, xv1.y, xv1.z, xv1.w};
@@ -480,7 +523,7 @@ __global__ void __launch_bounds__(kThreads, 1) vq_decode_mma_kernel(const MParam
 }
 
 // x -> 16-bit rows for the B operand: fp16 (narrowed, WR 0/2) or the raw
-// bf16 (WR 1).
+// bf16 (WR 1), for x whose rows the kernel cannot read in place.
 __global__ void x_to_16bit_kernel(const void* __restrict__ x, int x_dtype, int64_t n, int to_bf16,
                                   uint16_t* __restrict__ out) {
   for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n;
@@ -528,8 +571,12 @@ vqb_status launch_decode_mma(const LinearGeometry& geo, const GroupedDecodeArgs&
   }
   const int nsm = g_num_sms_mma;
   const int WR = a.wround;
-  // x -> 16-bit B-operand rows (the reference's host cast for the MoE path)
-  {
+  // x -> 16-bit B-operand rows (the reference's host cast for the MoE path):
+  // converted while the kernel stages x when its rows are 16-byte aligned
+  // (IN is a multiple of 512 here), else by a conversion pass
+  const bool x_direct = (reinterpret_cast<uintptr_t>(a.x) & 15) == 0;
+  const int x_target = WR == 1 ? VQB_BF16 : VQB_F16;
+  if (!x_direct) {
     const int64_t n = static_cast<int64_t>(T) * geo.IN;
     int64_t blocks = (n + 255) / 256;
     if (blocks > 4 * nsm) blocks = 4 * nsm;
@@ -542,6 +589,9 @@ vqb_status launch_decode_mma(const LinearGeometry& geo, const GroupedDecodeArgs&
   prm.codebook = static_cast<const uint16_t*>(geo.codebook);
   prm.scales = static_cast<const uint16_t*>(geo.scales);
   prm.x16 = x16;
+  prm.xraw = a.x;
+  prm.x_dtype = a.x_dtype;
+  prm.x_mode = !x_direct ? 0 : (a.x_dtype == x_target ? 1 : 2);
   prm.sorted = a.route->sorted;
   prm.chunks = a.route->chunks;
   prm.meta = a.route->meta;

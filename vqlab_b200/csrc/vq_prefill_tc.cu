@@ -866,7 +866,94 @@ void* pick_kernel(int bits) {
 bool dsplit_bits(int bits) { return bits == 14; }
 
 
+// Shared-memory layout for one mode: [B stages][wst code/scale windows]
+// [codebook slice + zero entry][barriers]; returns the total, or 0 when the
+// slice does not fit.  ds: dimension split (all K entries, 4 dims, 2 window
+// stages); else the largest power-of-two slice of whole entries that fits.
+size_t plan_smem(const LinearGeometry& geo, TParams& prm, bool ds) {
+  prm.kpos_log2 = ds ? 7 : 6;
+  prm.n_k = geo.IN >> prm.kpos_log2;
+  prm.n_pos = (prm.n_k + kSets - 1) / kSets * kSets;
+  prm.wst = ds ? 2 : kWStages;
+  // code window: kSets positions of every row, read from an aligned-down
+  // 16-byte boundary (up to o_max extra words); rows of 64 or 128 bytes take
+  // the matching TMA swizzle, others an odd number of 16-byte units -- either
+  // way conflict-free 16-byte reads across rows
+  prm.wpw = ((kSets << prm.kpos_log2) / geo.D) * geo.bits / 32;
+  const int o_max = prm.wpw % 4 == 0 ? 0 : (prm.wpw % 2 == 0 ? 2 : 3);
+  const int need = o_max + prm.wpw;
+  int W;
+  if (need <= 16) { W = 16; prm.wswz = 1; }
+  else if (need <= 32 && !(need % 4 == 0 && (need / 4) % 2 == 1)) { W = 32; prm.wswz = 2; }
+  else {
+    W = (need + 3) & ~3;
+    if ((W / 4) % 2 == 0) W += 4;
+    prm.wswz = 0;
+  }
+  prm.W = W;
+  prm.code_stage_bytes = kTileM * W * 4;
+  prm.win_stage_bytes = prm.code_stage_bytes + (prm.scale_tma ? kTileM * kScaleRowBytes : 0);
+  const size_t tail = static_cast<size_t>(kNumBars) * 8 + 16;
+  const size_t fixed = 1024 + static_cast<size_t>(kBStages) * kBStageBytes +
+                       static_cast<size_t>(prm.wst) * prm.win_stage_bytes + tail + 16;
+  if (static_cast<size_t>(g_smem_optin) <= fixed + 1024) return 0;
+  const size_t avail = static_cast<size_t>(g_smem_optin) - fixed;
+  size_t entry = static_cast<size_t>(geo.D) * 2;
+  if (ds) {
+    entry = 8;
+    if (static_cast<size_t>(geo.K + 1) * entry > avail) return 0;
+    prm.kp = geo.K;
+    prm.kp_log2 = 0;
+    prm.npass = 2;
+  } else if (static_cast<size_t>(geo.K + 1) * entry <= avail) {
+    prm.kp = geo.K;
+    prm.kp_log2 = 0;
+    prm.npass = 1;
+  } else {
+    int l = 0;
+    while (((static_cast<size_t>(2) << l) + 1) * entry <= avail) ++l;
+    prm.kp_log2 = l;
+    prm.kp = 1 << l;
+    prm.npass = (geo.K + prm.kp - 1) / prm.kp;
+  }
+  const size_t cb_bytes = (static_cast<size_t>(prm.kp + 1) * entry + 15) & ~size_t(15);  // + the zero entry
+  prm.off_win = kBStages * kBStageBytes;
+  prm.off_cb = prm.off_win + prm.wst * prm.win_stage_bytes;
+  prm.off_bar = static_cast<int>(prm.off_cb + cb_bytes);
+  const size_t smem = 1024 + static_cast<size_t>(prm.off_bar) + tail;
+  return smem <= static_cast<size_t>(g_smem_optin) ? smem : 0;
+}
+
+// The dimension split applies to d8 codebooks too large for one pass, with a
+// compiled code width and whole windows of 512 k.
+bool dsplit_eligible(const LinearGeometry& geo, const TParams& one_pass_plan) {
+  return geo.D == 8 && one_pass_plan.npass > 1 && dsplit_bits(geo.bits) && geo.IN % (kSets * 128) == 0 &&
+         geo.K % 2 == 0;
+}
+
+vqb_status ensure_device_attrs() {
+  if (g_sms_tc == 0) {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return VQB_CUDA_ERROR;
+    if (cudaDeviceGetAttribute(&g_sms_tc, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return VQB_CUDA_ERROR;
+    if (cudaDeviceGetAttribute(&g_smem_optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev) != cudaSuccess)
+      return VQB_CUDA_ERROR;
+  }
+  return VQB_OK;
+}
+
 }  // namespace
+
+bool tc_prefill_dsplit(const LinearGeometry& geo) {
+  if (!tc_prefill_supported(geo) || ensure_device_attrs() != VQB_OK) return false;
+  TParams prm{};
+  prm.IN = geo.IN;
+  prm.K = geo.K;
+  prm.NGRP = geo.G > 0 ? geo.IN / geo.G : 0;
+  prm.scale_tma = 1;
+  plan_smem(geo, prm, false);
+  return dsplit_eligible(geo, prm) && plan_smem(geo, prm, true) != 0;
+}
 
 bool tc_prefill_supported(const LinearGeometry& geo) {
   if (geo.IN % kChunkK != 0) return false;
@@ -888,13 +975,7 @@ vqb_status launch_prefill_tc(const LinearGeometry& geo, const void* x, int x_dty
                              int N, uint16_t* xs, void* y, int y_dtype, bool round_f16_first, bool bf16_operands,
                              int* status, cudaStream_t stream) {
   if (N <= 0) return VQB_OK;
-  if (g_sms_tc == 0) {
-    int dev = 0;
-    if (cudaGetDevice(&dev) != cudaSuccess) return VQB_CUDA_ERROR;
-    if (cudaDeviceGetAttribute(&g_sms_tc, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return VQB_CUDA_ERROR;
-    if (cudaDeviceGetAttribute(&g_smem_optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev) != cudaSuccess)
-      return VQB_CUDA_ERROR;
-  }
+  if (ensure_device_attrs() != VQB_OK) return VQB_CUDA_ERROR;
   EncodeTiledFn enc = encode_fn();
   if (!enc) return VQB_CUDA_ERROR;
 
@@ -926,72 +1007,15 @@ vqb_status launch_prefill_tc(const LinearGeometry& geo, const void* x, int x_dty
   while ((1 << (log2g + 1)) <= geo.G) ++log2g;
   prm.log2g = log2g;
   const size_t tail = static_cast<size_t>(kNumBars) * 8 + 16;
-
-  // Shared-memory layout for one mode: [B stages][wst code/scale windows]
-  // [codebook slice + zero entry][barriers]; returns the total, or 0 when the
-  // slice does not fit.  ds: dimension split (all K entries, 4 dims, 2 window
-  // stages); else the largest power-of-two slice of whole entries that fits.
-  auto plan = [&](bool ds) -> size_t {
-    prm.kpos_log2 = ds ? 7 : 6;
-    prm.n_k = geo.IN >> prm.kpos_log2;
-    prm.n_pos = (prm.n_k + kSets - 1) / kSets * kSets;
-    prm.wst = ds ? 2 : kWStages;
-    // code window: kSets positions of every row, read from an aligned-down
-    // 16-byte boundary (up to o_max extra words); rows of 64 or 128 bytes take
-    // the matching TMA swizzle, others an odd number of 16-byte units -- either
-    // way conflict-free 16-byte reads across rows
-    prm.wpw = ((kSets << prm.kpos_log2) / geo.D) * geo.bits / 32;
-    const int o_max = prm.wpw % 4 == 0 ? 0 : (prm.wpw % 2 == 0 ? 2 : 3);
-    const int need = o_max + prm.wpw;
-    int W;
-    if (need <= 16) { W = 16; prm.wswz = 1; }
-    else if (need <= 32 && !(need % 4 == 0 && (need / 4) % 2 == 1)) { W = 32; prm.wswz = 2; }
-    else {
-      W = (need + 3) & ~3;
-      if ((W / 4) % 2 == 0) W += 4;
-      prm.wswz = 0;
-    }
-    prm.W = W;
-    prm.code_stage_bytes = kTileM * W * 4;
-    prm.win_stage_bytes = prm.code_stage_bytes + (prm.scale_tma ? kTileM * kScaleRowBytes : 0);
-    const size_t fixed = 1024 + static_cast<size_t>(kBStages) * kBStageBytes +
-                         static_cast<size_t>(prm.wst) * prm.win_stage_bytes + tail + 16;
-    if (static_cast<size_t>(g_smem_optin) <= fixed + 1024) return 0;
-    const size_t avail = static_cast<size_t>(g_smem_optin) - fixed;
-    size_t entry = static_cast<size_t>(geo.D) * 2;
-    if (ds) {
-      entry = 8;
-      if (static_cast<size_t>(geo.K + 1) * entry > avail) return 0;
-      prm.kp = geo.K;
-      prm.kp_log2 = 0;
-      prm.npass = 2;
-    } else if (static_cast<size_t>(geo.K + 1) * entry <= avail) {
-      prm.kp = geo.K;
-      prm.kp_log2 = 0;
-      prm.npass = 1;
-    } else {
-      int l = 0;
-      while (((static_cast<size_t>(2) << l) + 1) * entry <= avail) ++l;
-      prm.kp_log2 = l;
-      prm.kp = 1 << l;
-      prm.npass = (geo.K + prm.kp - 1) / prm.kp;
-    }
-    const size_t cb_bytes = (static_cast<size_t>(prm.kp + 1) * entry + 15) & ~size_t(15);  // + the zero entry
-    prm.off_win = kBStages * kBStageBytes;
-    prm.off_cb = prm.off_win + prm.wst * prm.win_stage_bytes;
-    prm.off_bar = static_cast<int>(prm.off_cb + cb_bytes);
-    const size_t smem = 1024 + static_cast<size_t>(prm.off_bar) + tail;
-    return smem <= static_cast<size_t>(g_smem_optin) ? smem : 0;
-  };
-  size_t smem = plan(false);
+  size_t smem = plan_smem(geo, prm, false);
   bool ds = false;
-  if (geo.D == 8 && prm.npass > 1 && dsplit_bits(geo.bits) && geo.IN % (kSets * 128) == 0 && geo.K % 2 == 0) {
-    const size_t s2 = plan(true);
+  if (dsplit_eligible(geo, prm)) {
+    const size_t s2 = plan_smem(geo, prm, true);
     if (s2 > 0) {
       smem = s2;
       ds = true;
     } else {
-      smem = plan(false);
+      smem = plan_smem(geo, prm, false);
     }
   }
   if (smem == 0) return VQB_UNSUPPORTED_GEOMETRY;

@@ -11,7 +11,8 @@
 //                      argsort), so tile contents -- and with them the
 //                      GEMM's summation order -- are the same on every call
 //   chunks[*]          (expert, first sorted slot, pair count <= max_pairs)
-//   meta[0]            number of chunks; meta[1] error flag (expert id >= E)
+//   meta[0]            number of chunks; meta[1] error flag (expert id >= E);
+//                      the kernel clears meta[0..3] first
 // One CTA handles the whole batch.  Warp w owns the contiguous pair range
 // [w*per, (w+1)*per): it counts its pairs per expert into its own row of a
 // [32][E] shared table (lanes of a warp that share an expert are grouped with
@@ -25,8 +26,7 @@ namespace vqb {
 
 namespace {
 
-constexpr int kRouteThreads = 1024;
-constexpr int kRouteWarps = kRouteThreads / 32;
+constexpr int kRouteWarpsMax = 32;   // 1024 threads; small batches use 8 warps (less table to clear)
 
 __device__ __forceinline__ uint32_t expert_of(const uint32_t* idx, int p, int E, int* meta) {
   uint32_t e = idx ? idx[p] : 0u;
@@ -39,8 +39,9 @@ __device__ __forceinline__ uint32_t expert_of(const uint32_t* idx, int p, int E,
 
 }  // namespace
 
-__global__ void __launch_bounds__(kRouteThreads) route_small_kernel(const uint32_t* __restrict__ idx, int N, int E,
-                                                                     int max_pairs, RouteWorkspace ws) {
+template <int kRouteWarps>
+__global__ void __launch_bounds__(kRouteWarps * 32) route_small_kernel(const uint32_t* __restrict__ idx, int N, int E,
+                                                                        int max_pairs, RouteWorkspace ws) {
   extern __shared__ int sh[];
   int* cnt = sh;                 // [E]
   int* nch = sh + E;             // [E] chunk-count prefix
@@ -50,6 +51,7 @@ __global__ void __launch_bounds__(kRouteThreads) route_small_kernel(const uint32
   const int lo = min(N, wid * per), hi = min(N, lo + per);
   const uint32_t lt = (1u << lane) - 1u;
 
+  if (threadIdx.x < 4) ws.meta[threadIdx.x] = 0;  // status block, before any thread can report into it
   for (int i = threadIdx.x; i < kRouteWarps * E; i += blockDim.x) tab[i] = 0;
   __syncthreads();
   // 1. per-warp counts
@@ -170,19 +172,26 @@ RouteWorkspace carve_route_workspace(void* base, int N, int E, int row_tiles) {
   return w;
 }
 
-vqb_status launch_route_small(const uint32_t* idx, int N, int E, int max_pairs, const RouteWorkspace& ws,
-                              cudaStream_t stream) {
-  const size_t smem = sizeof(int) * (2 + kRouteWarps) * static_cast<size_t>(E);
+template <int W>
+static vqb_status launch_route_w(const uint32_t* idx, int N, int E, int max_pairs, const RouteWorkspace& ws,
+                                 cudaStream_t stream) {
+  const size_t smem = sizeof(int) * (2 + W) * static_cast<size_t>(E);
   if (smem > 200 * 1024) return VQB_UNSUPPORTED_GEOMETRY;
   cudaError_t ce = cudaSuccess;
   if (smem > 48 * 1024)
-    ce = cudaFuncSetAttribute(route_small_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    ce = cudaFuncSetAttribute(route_small_kernel<W>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                               static_cast<int>(smem));
   if (ce != cudaSuccess) return VQB_CUDA_ERROR;
-  route_small_kernel<<<1, kRouteThreads, smem, stream>>>(idx, N, E, max_pairs, ws);
+  route_small_kernel<W><<<1, W * 32, smem, stream>>>(idx, N, E, max_pairs, ws);
   if (cudaGetLastError() != cudaSuccess) return VQB_CUDA_ERROR;
   note_launch();
   return VQB_OK;
+}
+
+vqb_status launch_route_small(const uint32_t* idx, int N, int E, int max_pairs, const RouteWorkspace& ws,
+                              cudaStream_t stream) {
+  if (N <= 256) return launch_route_w<8>(idx, N, E, max_pairs, ws, stream);
+  return launch_route_w<kRouteWarpsMax>(idx, N, E, max_pairs, ws, stream);
 }
 
 }  // namespace vqb

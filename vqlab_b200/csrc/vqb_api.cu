@@ -93,8 +93,8 @@ vqb_status run_linear(const LinearGeometry& geo, const void* x, int x_dtype, int
                              const uint32_t* indices, int krep, int N, void* y, int y_dtype, void* workspace,
                              const vqb_options* opts, bool narrow_x_f16, bool round_f16_first, int wround,
                              bool large, cudaStream_t stream) {
+  // the routing kernel clears the status block itself; the per-pair paths, which route nothing, clear it here
   RouteWorkspace rw = carve_route_workspace(workspace, N, geo.E, row_tiles_128(geo.OUT));
-  if (cudaMemsetAsync(rw.meta, 0, sizeof(int) * 4, stream) != cudaSuccess) return VQB_CUDA_ERROR;
   const int ks = opts ? opts->k_split : 0;
   const int variant = opts ? opts->decode_variant : 0;
   uint16_t* xbuf = reinterpret_cast<uint16_t*>(static_cast<char*>(workspace) +
@@ -107,6 +107,9 @@ vqb_status run_linear(const LinearGeometry& geo, const void* x, int x_dtype, int
     if (st != VQB_OK) return st;
     return launch_prefill_tc(geo, x, x_dtype, krep, rw, N, xbuf, y, y_dtype, round_f16_first,
                              /*bf16_operands=*/wround == 1, rw.meta, stream);
+  }
+  if (variant == 1 || !mma_decode_supported(geo, wround, x_dtype)) {
+    if (cudaMemsetAsync(rw.meta, 0, sizeof(int) * 4, stream) != cudaSuccess) return VQB_CUDA_ERROR;
   }
   if (variant == 1) {
     // one pair per CTA, the reference walk order (kept for exact-order checks)
@@ -214,16 +217,23 @@ vqb_status vqb_switch_forward(const vqb_linear_desc* desc, const void* x, vqb_dt
   // 512 pairs and the grouped GEMM above it (vq_switch.py:45, :5313-5315).  The
   // grouped GEMM decodes every routed expert's tile with a fixed cost per tile
   // (codebook reload, epilogue) that the K extent amortises, so on a B200 it
-  // pays once pairs * IN exceed ~4608 per expert as well.  Measured (512
-  // experts, uniform routing): 1024 x 4096 gate at 1.25 pairs/expert 0.72 ms
-  // both kernels, 2.5 pairs 0.92 GEMM vs 1.06 decode; 4096 x 1024 down at 2.5
-  // pairs 1.20 GEMM vs 0.88 decode, at 5 pairs 1.31 vs 1.38.
-  constexpr int64_t kGemmPairInPerExpert = 4608;
+  // pays once pairs * IN exceed a few thousand per expert as well.  A d8
+  // codebook too large for shared memory changes the balance: the decode
+  // kernel then reads part of the codebook through L1/L2, while the GEMM keeps
+  // half of every entry resident per pass, so with IN >= 2048 the GEMM wins
+  // from a few dozen pairs on.  Measured (512 experts, d8/K16384, uniform
+  // routing, ms per call):
+  //   1024 x 4096 gate:  10 pairs: 0.069 GEMM vs 0.060 decode; 20: 0.076 vs 0.072;
+  //                      40: 0.103 vs 0.113;  1.0 pairs/expert: 0.48 vs 0.72;  2.5: 0.68 vs 1.11
+  //   4096 x 1024 down:  0.3: 0.31 vs 0.27;  1.0: 0.70 vs 0.63;  1.9: 0.92 vs 0.94;
+  //                      2.5: 0.98 vs 1.06;  5.0: 1.08 vs 1.64
+  const int64_t pair_in_per_expert = tc_prefill_dsplit(geo) ? 2048 : 4608;
   const int path = opts ? opts->path : VQB_PATH_AUTO;
   const int max_fused = (opts && opts->max_fused_pairs > 0) ? opts->max_fused_pairs : 512;
+  const bool wide_dsplit = N > 32 && geo.IN >= 2048 && !(opts && opts->max_fused_pairs > 0) && tc_prefill_dsplit(geo);
   const bool large = path == VQB_PATH_PREFILL ||
-                     (path == VQB_PATH_AUTO && N > max_fused &&
-                      static_cast<int64_t>(N) * geo.IN > kGemmPairInPerExpert * geo.E);
+                     (path == VQB_PATH_AUTO &&
+                      (wide_dsplit || (N > max_fused && static_cast<int64_t>(N) * geo.IN > pair_in_per_expert * geo.E)));
   // MoE numerics: x narrowed to fp16, fp32 accumulation, fp16 output rounding
   // then the caller's dtype (vq_switch.py:5301-5308, :5423).
   return run_linear(geo, x, x_dtype, n_tokens, indices, top_k, N, y, y_dtype, workspace, opts,
