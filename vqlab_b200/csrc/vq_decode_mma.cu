@@ -33,6 +33,9 @@
 // vq_dense.py:267-312): A = fp16(cb * s) (one RNE rounding, the fp16 multiply
 // of vq_dense.py:136), re-rounded to bf16 for bf16 x (WR == 1), B = x in its
 // own dtype, fp32 accumulation over all k.
+#include <algorithm>
+#include <cmath>
+
 #include "vqb_common.cuh"
 #include "vqb_internal.h"
 
@@ -60,7 +63,7 @@ struct MParams {
   const int32_t* row_table;  // SKIPZERO [E, OUT] -> compact row (-1 dead), nullptr = plain layout
   int64_t nrows;             // rows of codes / scales
   int row_words;
-  int OUT, IN, G, NGRP, NSUB, bits, krep;
+  int OUT, IN, G, NGRP, NSUB, bits, krep, K;
   int ks, mt, tiles, ns;
   int win_k;                // k values per window (kWinK, or 1024 when 512 does not give 16-byte rows)
   int win_words;            // code words of one row per window
@@ -108,6 +111,17 @@ __device__ __forceinline__ void fetch_codes(const uint32_t* row_words, int bit0,
     for (int i = 0; i < CPT; ++i) c[i] = (v >> (i * bits)) & mask;
     return;
   }
+  if (CPT * bits <= 64) {
+    // inside one 64-bit window of three words (d2/8-bit, d4/12-bit); the
+    // staged rows carry spare words for the read past the last code
+    const int wi = bit0 >> 5, sh = bit0 & 31;
+    const uint32_t lo = __funnelshift_r(row_words[wi], row_words[wi + 1], sh);
+    const uint32_t hi = __funnelshift_r(row_words[wi + 1], row_words[wi + 2], sh);
+    const uint64_t v = (static_cast<uint64_t>(hi) << 32) | lo;
+#pragma unroll
+    for (int i = 0; i < CPT; ++i) c[i] = static_cast<uint32_t>(v >> (i * bits)) & mask;
+    return;
+  }
   int wi = bit0 >> 5;
   const int sh = bit0 & 31;
   uint64_t buf = row_words[wi++] >> sh;
@@ -150,28 +164,50 @@ __device__ __forceinline__ void lookup_split(const uint16_t* cb_s, uint32_t base
   }
 }
 
-template <int D>
-__device__ __forceinline__ void lookup(const uint16_t* cb_s, const uint16_t* __restrict__ cb_g, int ns,
+// Codebook lookups.  CB == kCbFull: shared memory holds all K entries and a
+// zero entry at index K, so min(c, K) is one unconditional shared-memory read
+// (a code >= K, which no valid stream holds, reads zeros).  CB == kCbPrefix:
+// the first ns entries are in shared memory, the rest are read through L1 at
+// min(c, K - 1), so no code reads outside the codebook.
+constexpr int kCbPrefix = 0, kCbFull = 1, kCbSplit = 2;
+
+template <int D, int CB>
+__device__ __forceinline__ void lookup(const uint16_t* cb_s, const uint16_t* __restrict__ cb_g, int ns, int K,
                                        const uint32_t* c, uint32_t* w) {
-  if constexpr (D == 8) {
+  constexpr int CPT = 16 / D;
 #pragma unroll
-    for (int i = 0; i < 2; ++i) {
-      const uint4 v = c[i] < static_cast<uint32_t>(ns) ? reinterpret_cast<const uint4*>(cb_s)[c[i]]
-                                                       : __ldg(reinterpret_cast<const uint4*>(cb_g) + c[i]);
+  for (int i = 0; i < CPT; ++i) {
+    if constexpr (D == 8) {
+      uint4 v;
+      if constexpr (CB == kCbFull) {
+        v = reinterpret_cast<const uint4*>(cb_s)[min(c[i], static_cast<uint32_t>(K))];
+      } else {
+        v = c[i] < static_cast<uint32_t>(ns)
+                ? reinterpret_cast<const uint4*>(cb_s)[c[i]]
+                : __ldg(reinterpret_cast<const uint4*>(cb_g) + min(c[i], static_cast<uint32_t>(K - 1)));
+      }
       w[4 * i] = v.x; w[4 * i + 1] = v.y; w[4 * i + 2] = v.z; w[4 * i + 3] = v.w;
-    }
-  } else if constexpr (D == 4) {
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const uint2 v = c[i] < static_cast<uint32_t>(ns) ? reinterpret_cast<const uint2*>(cb_s)[c[i]]
-                                                       : __ldg(reinterpret_cast<const uint2*>(cb_g) + c[i]);
+    } else if constexpr (D == 4) {
+      uint2 v;
+      if constexpr (CB == kCbFull) {
+        v = reinterpret_cast<const uint2*>(cb_s)[min(c[i], static_cast<uint32_t>(K))];
+      } else {
+        v = c[i] < static_cast<uint32_t>(ns)
+                ? reinterpret_cast<const uint2*>(cb_s)[c[i]]
+                : __ldg(reinterpret_cast<const uint2*>(cb_g) + min(c[i], static_cast<uint32_t>(K - 1)));
+      }
       w[2 * i] = v.x; w[2 * i + 1] = v.y;
+    } else {
+      uint32_t v;
+      if constexpr (CB == kCbFull) {
+        v = reinterpret_cast<const uint32_t*>(cb_s)[min(c[i], static_cast<uint32_t>(K))];
+      } else {
+        v = c[i] < static_cast<uint32_t>(ns)
+                ? reinterpret_cast<const uint32_t*>(cb_s)[c[i]]
+                : __ldg(reinterpret_cast<const uint32_t*>(cb_g) + min(c[i], static_cast<uint32_t>(K - 1)));
+      }
+      w[i] = v;
     }
-  } else {
-#pragma unroll
-    for (int i = 0; i < 8; ++i)
-      w[i] = c[i] < static_cast<uint32_t>(ns) ? reinterpret_cast<const uint32_t*>(cb_s)[c[i]]
-                                              : __ldg(reinterpret_cast<const uint32_t*>(cb_g) + c[i]);
   }
 }
 
@@ -237,8 +273,9 @@ __device__ __forceinline__ int64_t code_row(const MParams& prm, int e, int row) 
   return c < prm.nrows ? c : -1;
 }
 
-template <int D, int WR, int NT, bool SPLIT>
+template <int D, int WR, int NT, int CB>
 __global__ void __launch_bounds__(kThreads, 1) vq_decode_mma_kernel(const MParams prm) {
+  constexpr bool SPLIT = CB == kCbSplit;
   extern __shared__ __align__(16) unsigned char smem_raw[];
   // layout: [cb prefix][x rows][per-warp code+scale windows][slice partials]
   uint16_t* cb_s = reinterpret_cast<uint16_t*>(smem_raw);
@@ -269,6 +306,9 @@ __global__ void __launch_bounds__(kThreads, 1) vq_decode_mma_kernel(const MParam
       for (int u = 0; u < 8; ++u) dst[i + u * kThreads] = v[u];
     }
     for (; i < n16; i += kThreads) dst[i] = __ldg(src + i);
+    if (CB == kCbFull && threadIdx.x == 0) {
+      for (int j = 0; j < D; ++j) cb_s[static_cast<size_t>(prm.K) * D + j] = 0;  // the zero entry at index K
+    }
   }
 
   // the partner CTA must be running before its shared memory is written
@@ -380,8 +420,8 @@ __global__ void __launch_bounds__(kThreads, 1) vq_decode_mma_kernel(const MParam
           lookup_split<D>(cb_s, cb_base, static_cast<uint32_t>(prm.cb_half), ca, wa);
           lookup_split<D>(cb_s, cb_base, static_cast<uint32_t>(prm.cb_half), cb2, wb8);
         } else {
-          lookup<D>(cb_s, prm.codebook, prm.ns, ca, wa);
-          lookup<D>(cb_s, prm.codebook, prm.ns, cb2, wb8);
+          lookup<D, CB>(cb_s, prm.codebook, prm.ns, prm.K, ca, wa);
+          lookup<D, CB>(cb_s, prm.codebook, prm.ns, prm.K, cb2, wb8);
         }
         if constexpr (WR != 0) {
           const __half sa = __ushort_as_half(s_s[g * prm.sc_stride + gslot]);
@@ -606,6 +646,7 @@ vqb_status launch_decode_mma(const LinearGeometry& geo, const GroupedDecodeArgs&
   prm.NGRP = geo.IN / geo.G;
   prm.NSUB = geo.IN / geo.D;
   prm.bits = geo.bits;
+  prm.K = geo.K;
   prm.krep = a.krep;
   prm.y_dtype = a.y_dtype;
   prm.round_f16_first = a.round_f16_first ? 1 : 0;
@@ -628,10 +669,28 @@ vqb_status launch_decode_mma(const LinearGeometry& geo, const GroupedDecodeArgs&
   int ks = a.ks;
   const int n_win = geo.IN / win_k;
   if (ks <= 0) {
-    const int64_t chunks_est = (a.N + a.pmax - 1) / a.pmax;
-    const int64_t mtiles = chunks_est * ((geo.OUT + 15) / 16);
+    // K-slices per item.  With eight or more 16-row units per warp at one
+    // slice, one slice (no partial reduction, the most shared memory left for
+    // the codebook); otherwise the most slices among those that minimise
+    // (items per CTA, rounded up) x (windows of the longest slice).  Chunks
+    // are estimated as the distinct experts uniform routing would give, or
+    // pairs / chunk size if more.  Measured on B200 (us): d8/K16384 switch
+    // 1024 x 4096 at 80 pairs: 229 / 200 / 187 / 197 for 1 / 2 / 4 / 8 slices,
+    // at 640 pairs 821 / 859 / 895 / 1001; dense d8 17408 x 5120 at N = 1
+    // 107 / 65 / 72 / 90; dense d2 5120 x 5120 at N = 1: 89 / 52 / 44 / 44.
+    const double de = static_cast<double>(geo.E) * (1.0 - std::exp(-static_cast<double>(a.N) / geo.E));
+    const int64_t chunks_est =
+        std::max<int64_t>((a.N + a.pmax - 1) / a.pmax, std::max<int64_t>(1, static_cast<int64_t>(de + 0.5)));
+    const int64_t units = chunks_est * ((geo.OUT + 15) / 16);
     ks = 1;
-    while (ks < 16 && ks * 2 <= n_win && mtiles * ks < static_cast<int64_t>(nsm) * kWarps * 2) ks *= 2;
+    if (units < 8 * static_cast<int64_t>(nsm) * kWarps) {
+      int64_t best = -1;
+      for (int k = 1; k <= 16 && k <= n_win; k *= 2) {
+        const int64_t items = chunks_est * ((geo.OUT + 16 * (kWarps / k) - 1) / (16 * (kWarps / k)));
+        const int64_t cost = ((items + nsm - 1) / nsm) * ((n_win + k - 1) / k);
+        if (best < 0 || cost <= best) { best = cost; ks = k; }
+      }
+    }
   }
   if (ks > n_win) ks = n_win;
   if (ks != 1 && ks != 2 && ks != 4 && ks != 8 && ks != 16) return VQB_BAD_SHAPE;
@@ -672,8 +731,11 @@ vqb_status launch_decode_mma(const LinearGeometry& geo, const GroupedDecodeArgs&
     if (a.stage_codebook == 0) ns = 0;
     prm.cb_half = 0;
   }
+  // the whole codebook plus its zero entry in shared memory: one unconditional read per code
+  const bool full = !split && ns == static_cast<size_t>(geo.K) &&
+                    fixed + ((static_cast<size_t>(geo.K + 1) * entry + 15) & ~size_t(15)) <= budget;
   prm.ns = static_cast<int>(ns);
-  const size_t smem = ((ns * entry + 15) & ~size_t(15)) + fixed;
+  const size_t smem = (((full ? ns + 1 : ns) * entry + 15) & ~size_t(15)) + fixed;
   const int grid = split ? (nsm & ~1) : nsm;
 
   cudaError_t ce = cudaSuccess;
@@ -699,8 +761,9 @@ vqb_status launch_decode_mma(const LinearGeometry& geo, const GroupedDecodeArgs&
   };
 #define VQB_M1(DD, WW, NN)                                                               \
   do {                                                                                   \
-    if (split) launch(vq_decode_mma_kernel<DD, WW, NN, true>, true);                      \
-    else launch(vq_decode_mma_kernel<DD, WW, NN, false>, false);                          \
+    if (split) launch(vq_decode_mma_kernel<DD, WW, NN, kCbSplit>, true);                  \
+    else if (full) launch(vq_decode_mma_kernel<DD, WW, NN, kCbFull>, false);              \
+    else launch(vq_decode_mma_kernel<DD, WW, NN, kCbPrefix>, false);                      \
   } while (0)
 #define VQB_M2(DD, WW) do { if (NT == 1) VQB_M1(DD, WW, 1); else VQB_M1(DD, WW, 2); } while (0)
 #define VQB_M3(DD) do { if (WR == 1) VQB_M2(DD, 1); else if (WR == 2) VQB_M2(DD, 2); else VQB_M2(DD, 0); } while (0)
