@@ -379,6 +379,65 @@ __device__ __forceinline__ void decode_pos_dsplit(const TParams& prm, const uint
   scale_words(out, s_lo, s_hi, prm.b_bf16 != 0);
 }
 
+// Tiles run in groups: up to 8 consecutive tiles of this CTA whose
+// accumulators (two per tile, n16 columns each, n16 = tokens rounded up to 16)
+// fit the 256 accumulator columns together.  Every pass of a group runs over
+// all its tiles before the next pass, so one codebook reload and one
+// accumulator drain serve the whole group -- the small-token tiles of decode
+// batches are short, and a reload per tile would cost as much as the tile.
+struct TileGroup {
+  int count;
+  int n16;
+};
+constexpr int kAccCols = kIssuers * kMaxN;  // TMEM columns [0, 256)
+constexpr int kMaxGroup = 8;
+
+__device__ __forceinline__ int tile_n16(const TParams& prm, int64_t it) {
+  return (prm.chunks[static_cast<int>(it / prm.row_tiles)].z + 15) & ~15;
+}
+__device__ __forceinline__ TileGroup form_group(const TParams& prm, int64_t it0, int64_t nitems) {
+  TileGroup grp{1, tile_n16(prm, it0)};
+  while (grp.count < kMaxGroup) {
+    const int64_t it = it0 + static_cast<int64_t>(grp.count) * gridDim.x;
+    if (it >= nitems) break;
+    const int n16 = max(grp.n16, tile_n16(prm, it));
+    if ((grp.count + 1) * 2 * n16 > kAccCols) break;
+    grp.n16 = n16;
+    ++grp.count;
+  }
+  return grp;
+}
+
+// A decode thread's row of tile `it`: r (output row), whether it is live, its
+// row in codes / scales (crow) and in the staged windows (woff).  With a row
+// table dead rows decode nothing and store +0, and a row whose compact index
+// falls outside its tile's window counts as dead.
+struct TileRow {
+  int r;
+  bool live;
+  int64_t crow;
+  int woff;
+};
+__device__ __forceinline__ TileRow tile_row(const TParams& prm, int64_t it, int lrow) {
+  const int chunk = static_cast<int>(it / prm.row_tiles);
+  const int rt = static_cast<int>(it - static_cast<int64_t>(chunk) * prm.row_tiles);
+  const int e = prm.chunks[chunk].x;
+  TileRow tr;
+  tr.r = rt * kTileM + lrow;
+  const int rr = min(tr.r, prm.OUT - 1);
+  tr.crow = static_cast<int64_t>(e) * prm.OUT + rr;
+  tr.woff = lrow;
+  tr.live = true;
+  if (prm.row_table) {
+    const int tb = prm.tile_base[e * prm.row_tiles + rt];
+    tr.crow = tr.r < prm.OUT ? static_cast<int64_t>(prm.row_table[static_cast<int64_t>(e) * prm.OUT + tr.r]) : -1;
+    const int64_t o = tr.crow - tb;
+    tr.live = tr.crow >= 0 && tr.crow < prm.nrows && tb >= 0 && o >= 0 && o < kTileM;
+    tr.woff = tr.live ? static_cast<int>(o) : 0;
+  }
+  return tr;
+}
+
 // -------------------------------------------------------------- the kernel
 
 template <int D, int BITS, bool DS>
@@ -450,81 +509,90 @@ __global__ void __launch_bounds__(kThreads, 1)
       asm volatile("prefetch.tensormap [%0];" :: "l"(reinterpret_cast<uint64_t>(&xmap128)) : "memory");
       uint32_t gs = 0;  // slot sequence number
       bool ok = true;
-      int j = 0;
-      for (int64_t it = blockIdx.x; it < nitems && ok; it += gridDim.x, ++j) {
-        const int4 ch = prm.chunks[static_cast<int>(it / prm.row_tiles)];
-        const int rows = slot_rows(ch.z);
-        const int pp = slot_positions(rows);
-        // one box per slot: 64 k x rows tokens x pp chunks, laid out [chunk][token][k]
-        const CUtensorMap* map = rows == 32 ? &xmap32 : (rows == 64 ? &xmap64 : &xmap128);
-        const uint32_t bytes = static_cast<uint32_t>(pp * rows * kChunkK * 2);
+      int jg = 0;
+      for (int64_t it0 = blockIdx.x; it0 < nitems && ok; ++jg) {
+        const TileGroup grp = form_group(prm, it0, nitems);
         for (int pass = 0; pass < prm.npass && ok; ++pass) {
           // the dimension split reads x's permuted half of the resident codebook dims
-          const int cbase = DS ? pass_slice(prm.npass, j, pass) * prm.n_pos : 0;
-          for (int p0 = 0; p0 < prm.n_pos; p0 += pp, ++gs) {
-            const uint32_t bs = gs % kBStages;
-            if (!mbar_wait(&b_empty[bs], ((gs / kBStages) & 1u) ^ 1u, abort_flag)) { ok = false; break; }
-            mbar_expect_tx(&b_full[bs], bytes);
-            unsigned char* dst = b_base + bs * kBStageBytes;
-            tma_load_3d(map, &b_full[bs], dst, 0, ch.y, cbase + p0);
+          const int cbase = DS ? pass_slice(prm.npass, jg, pass) * prm.n_pos : 0;
+          for (int t = 0; t < grp.count && ok; ++t) {
+            const int4 ch = prm.chunks[static_cast<int>((it0 + static_cast<int64_t>(t) * gridDim.x) / prm.row_tiles)];
+            const int rows = slot_rows(ch.z);
+            const int pp = slot_positions(rows);
+            // one box per slot: 64 k x rows tokens x pp chunks, laid out [chunk][token][k]
+            const CUtensorMap* map = rows == 32 ? &xmap32 : (rows == 64 ? &xmap64 : &xmap128);
+            const uint32_t bytes = static_cast<uint32_t>(pp * rows * kChunkK * 2);
+            for (int p0 = 0; p0 < prm.n_pos; p0 += pp, ++gs) {
+              const uint32_t bs = gs % kBStages;
+              if (!mbar_wait(&b_empty[bs], ((gs / kBStages) & 1u) ^ 1u, abort_flag)) { ok = false; break; }
+              mbar_expect_tx(&b_full[bs], bytes);
+              unsigned char* dst = b_base + bs * kBStageBytes;
+              tma_load_3d(map, &b_full[bs], dst, 0, ch.y, cbase + p0);
+            }
           }
         }
+        it0 += static_cast<int64_t>(grp.count) * gridDim.x;
       }
       // no copy may still be writing shared memory when the CTA exits
       for (uint32_t k = 1; k <= kBStages && k <= gs; ++k) mbar_drain(&b_full[(gs - k) % kBStages], ((gs - k) / kBStages) & 1u);
     }
   } else if (warp == kWarpMma0 || warp == kWarpMma1) {
     // ---------------- MMA issuers.  A tile's K positions come in slots of pp
-    // positions sharing one B stage (pp > 1 for tiles of <= 64 tokens); the
-    // slots alternate between the two issuers, each accumulating into its own
-    // D_i, and the epilogue adds D_0 + D_1.
+    // positions sharing one B stage (pp > 1 for tiles of <= 64 tokens); a
+    // tile's slots alternate between the two issuers, each accumulating into
+    // its own D_i of that tile, and the epilogue adds D_0 + D_1.  Tile t of a
+    // group owns accumulator columns [2 t n16, 2 t n16 + 2 n16).
     if (lane == 0) {
       const int iss = warp == kWarpMma0 ? 0 : 1;
-      const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(iss * kMaxN);
       // descriptor of B stage 0; later stages / positions start further on (the start-address field counts 16-byte units)
       const uint64_t bdesc0 = sw128_desc(smem_u32(b_base));
       uint32_t g = 0, gs = 0;
       uint32_t waited = 0xFFFFFFFFu;  // last window whose A stages this issuer has seen complete
       bool ok = true;
-      int j = 0;
-      for (int64_t it = blockIdx.x; it < nitems && ok; it += gridDim.x, ++j) {
-        const int4 ch = prm.chunks[static_cast<int>(it / prm.row_tiles)];
-        if (j >= 1 && !mbar_wait(acc_empty, static_cast<uint32_t>((j - 1) & 1), abort_flag)) break;
+      int jg = 0;
+      for (int64_t it0 = blockIdx.x; it0 < nitems && ok; ++jg) {
+        const TileGroup grp = form_group(prm, it0, nitems);
+        if (jg >= 1 && !mbar_wait(acc_empty, static_cast<uint32_t>((jg - 1) & 1), abort_flag)) break;
         tc_fence_after();
-        const uint32_t idesc = make_idesc((ch.z + 15) & ~15, prm.b_bf16 != 0);
-        const int rows = slot_rows(ch.z);
-        const int pp = slot_positions(rows);
-        uint32_t acc = 0;
-        int k = 0;  // slot index inside the tile
+        uint32_t started = 0;  // tiles whose accumulator this issuer has written in this group
         for (int pass = 0; pass < prm.npass && ok; ++pass) {
-          for (int p0 = 0; p0 < prm.n_pos; p0 += pp, ++gs, ++k) {
-            if ((k & 1) != iss) continue;
-            const uint32_t bs = gs % kBStages;
-            if (!(ok = mbar_wait(&b_full[bs], (gs / kBStages) & 1u, abort_flag))) break;
-            for (int q = 0; q < pp; ++q) {
-              const uint32_t gp = g + static_cast<uint32_t>(p0 + q);
-              const uint32_t ast = gp % kAStages;
-              const uint32_t win = gp >> 2;
-              if (win != waited) {
-                if (!(ok = mbar_wait(&a_full[win & 1u], (win >> 1) & 1u, abort_flag))) break;
-                tc_fence_after();
-                waited = win;
+          for (int t = 0; t < grp.count && ok; ++t) {
+            const int4 ch = prm.chunks[static_cast<int>((it0 + static_cast<int64_t>(t) * gridDim.x) / prm.row_tiles)];
+            const uint32_t idesc = make_idesc((ch.z + 15) & ~15, prm.b_bf16 != 0);
+            const int rows = slot_rows(ch.z);
+            const int pp = slot_positions(rows);
+            const uint32_t d_tmem = tmem_base + static_cast<uint32_t>((2 * t + iss) * grp.n16);
+            int k = pass * (prm.n_pos / pp);  // slot index inside the tile
+            for (int p0 = 0; p0 < prm.n_pos; p0 += pp, ++gs, ++k) {
+              if ((k & 1) != iss) continue;
+              const uint32_t bs = gs % kBStages;
+              if (!(ok = mbar_wait(&b_full[bs], (gs / kBStages) & 1u, abort_flag))) break;
+              for (int q = 0; q < pp; ++q) {
+                const uint32_t gp = g + static_cast<uint32_t>(p0 + q);
+                const uint32_t ast = gp % kAStages;
+                const uint32_t win = gp >> 2;
+                if (win != waited) {
+                  if (!(ok = mbar_wait(&a_full[win & 1u], (win >> 1) & 1u, abort_flag))) break;
+                  tc_fence_after();
+                  waited = win;
+                }
+                const uint32_t a_tmem = tmem_base + kTmemA + ast * 32;
+                const uint64_t bd = bdesc0 + static_cast<uint64_t>((bs * kBStageBytes + q * rows * kChunkK * 2) >> 4);
+                tc_mma_ts(d_tmem, a_tmem, bd, idesc, (started >> t) & 1u);
+                tc_mma_ts(d_tmem, a_tmem + 8, bd + 2, idesc, 1u);    // +32 bytes: next 16 k of the swizzle row
+                tc_mma_ts(d_tmem, a_tmem + 16, bd + 4, idesc, 1u);
+                tc_mma_ts(d_tmem, a_tmem + 24, bd + 6, idesc, 1u);
+                started |= 1u << t;
+                tc_commit(&st_free[ast]);
               }
-              const uint32_t a_tmem = tmem_base + kTmemA + ast * 32;
-              const uint64_t bd = bdesc0 + static_cast<uint64_t>((bs * kBStageBytes + q * rows * kChunkK * 2) >> 4);
-              tc_mma_ts(d_tmem, a_tmem, bd, idesc, acc);
-              tc_mma_ts(d_tmem, a_tmem + 8, bd + 2, idesc, 1u);    // +32 bytes: next 16 k of the swizzle row
-              tc_mma_ts(d_tmem, a_tmem + 16, bd + 4, idesc, 1u);
-              tc_mma_ts(d_tmem, a_tmem + 24, bd + 6, idesc, 1u);
-              acc = 1u;
-              tc_commit(&st_free[ast]);
+              if (!ok) break;
+              tc_commit(&b_empty[bs]);
             }
-            if (!ok) break;
-            tc_commit(&b_empty[bs]);
+            g += static_cast<uint32_t>(prm.n_pos);
           }
-          g += static_cast<uint32_t>(prm.n_pos);
         }
         if (ok) tc_commit(&acc_full[iss]);
+        it0 += static_cast<int64_t>(grp.count) * gridDim.x;
       }
       // every MMA this thread issued has completed before TMEM is freed
       tc_commit(&mma_done[iss]);
@@ -539,27 +607,32 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint32_t fill_phase[kWStages] = {};
       const uint32_t bytes = static_cast<uint32_t>(prm.code_stage_bytes + (prm.scale_tma ? kTileM * kScaleRowBytes : 0));
       bool ok = true;
-      for (int64_t it = blockIdx.x; it < nitems && ok; it += gridDim.x) {
-        const int chunk = static_cast<int>(it / prm.row_tiles);
-        const int rt = static_cast<int>(it - static_cast<int64_t>(chunk) * prm.row_tiles);
-        const int4 ch = prm.chunks[chunk];
-        // the tile's rows in codes / scales: (e, rt*128 ...), or from its first live compact row
-        const int yrow = prm.row_table ? max(prm.tile_base[ch.x * prm.row_tiles + rt], 0) : ch.x * prm.OUT + rt * kTileM;
+      for (int64_t it0 = blockIdx.x; it0 < nitems && ok;) {
+        const TileGroup grp = form_group(prm, it0, nitems);
         for (int pass = 0; pass < prm.npass && ok; ++pass) {
-          for (int w = 0; w < nwin; ++w) {
-            if (!mbar_wait(&w_empty[ws], wp ^ 1u, abort_flag)) { ok = false; break; }
-            mbar_expect_tx(&w_full[ws], bytes);
-            unsigned char* dst = w_base + ws * prm.win_stage_bytes;
-            tma_load_2d(&cmap, &w_full[ws], dst, (w * prm.wpw) & ~3, yrow);
-            if (prm.scale_tma) {
-              const int g_first = ((w * kSets) << prm.kpos_log2) >> prm.log2g;
-              tma_load_2d(&smap, &w_full[ws], dst + prm.code_stage_bytes, g_first & ~7, yrow);
+          for (int t = 0; t < grp.count && ok; ++t) {
+            const int64_t it = it0 + static_cast<int64_t>(t) * gridDim.x;
+            const int chunk = static_cast<int>(it / prm.row_tiles);
+            const int rt = static_cast<int>(it - static_cast<int64_t>(chunk) * prm.row_tiles);
+            const int4 ch = prm.chunks[chunk];
+            // the tile's rows in codes / scales: (e, rt*128 ...), or from its first live compact row
+            const int yrow = prm.row_table ? max(prm.tile_base[ch.x * prm.row_tiles + rt], 0) : ch.x * prm.OUT + rt * kTileM;
+            for (int w = 0; w < nwin; ++w) {
+              if (!mbar_wait(&w_empty[ws], wp ^ 1u, abort_flag)) { ok = false; break; }
+              mbar_expect_tx(&w_full[ws], bytes);
+              unsigned char* dst = w_base + ws * prm.win_stage_bytes;
+              tma_load_2d(&cmap, &w_full[ws], dst, (w * prm.wpw) & ~3, yrow);
+              if (prm.scale_tma) {
+                const int g_first = ((w * kSets) << prm.kpos_log2) >> prm.log2g;
+                tma_load_2d(&smap, &w_full[ws], dst + prm.code_stage_bytes, g_first & ~7, yrow);
+              }
+              filled[ws] = 1;
+              fill_phase[ws] = wp;
+              if (++ws == prm.wst) { ws = 0; wp ^= 1u; }
             }
-            filled[ws] = 1;
-            fill_phase[ws] = wp;
-            if (++ws == prm.wst) { ws = 0; wp ^= 1u; }
           }
         }
+        it0 += static_cast<int64_t>(grp.count) * gridDim.x;
       }
       for (int s = 0; s < prm.wst; ++s)
         if (filled[s]) mbar_drain(&w_full[s], fill_phase[s]);
@@ -570,10 +643,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       int resident = -1;
       uint32_t loads = 0;
       bool ok = true;
-      int j = 0;
-      for (int64_t it = blockIdx.x; it < nitems && ok; it += gridDim.x, ++j) {
+      int jg = 0;
+      for (int64_t it0 = blockIdx.x; it0 < nitems && ok; ++jg) {
+        const TileGroup grp = form_group(prm, it0, nitems);
         for (int pass = 0; pass < prm.npass; ++pass) {
-          const int h = pass_slice(prm.npass, j, pass);
+          const int h = pass_slice(prm.npass, jg, pass);
           if (h == resident) continue;
           if (loads > 0 && !mbar_wait(cb_empty, (loads - 1) & 1u, abort_flag)) { ok = false; break; }
           // a slice of entries, or (dimension split) dims [4h, 4h + 4) of all
@@ -590,6 +664,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           resident = h;
           ++loads;
         }
+        it0 += static_cast<int64_t>(grp.count) * gridDim.x;
       }
       if (loads > 0) mbar_drain(cb_full, (loads - 1) & 1u);
     }
@@ -604,30 +679,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     int cur = -1;
     uint32_t cb_loads = 0;
     bool ok = true;
-    int j = 0;
-    for (int64_t it = blockIdx.x; it < nitems && ok; it += gridDim.x, ++j) {
-      const int chunk = static_cast<int>(it / prm.row_tiles);
-      const int rt = static_cast<int>(it - static_cast<int64_t>(chunk) * prm.row_tiles);
-      const int4 ch = prm.chunks[chunk];
-      const int r = rt * kTileM + lrow;
-      const int rr = min(r, prm.OUT - 1);
-      // the row inside the staged windows (woff) and in codes / scales (crow);
-      // with a row table dead rows decode nothing and store +0, and a row whose
-      // compact index falls outside its tile's window counts as dead
-      int64_t crow = static_cast<int64_t>(ch.x) * prm.OUT + rr;
-      int woff = lrow;
-      bool live = true;
-      if (prm.row_table) {
-        const int tb = prm.tile_base[ch.x * prm.row_tiles + rt];
-        crow = r < prm.OUT ? static_cast<int64_t>(prm.row_table[static_cast<int64_t>(ch.x) * prm.OUT + r]) : -1;
-        const int64_t o = crow - tb;
-        live = crow >= 0 && crow < prm.nrows && tb >= 0 && o >= 0 && o < kTileM;
-        woff = live ? static_cast<int>(o) : 0;
-      }
-      const int xr = prm.wswz == 1 ? ((woff >> 1) & 3) : (prm.wswz == 2 ? (woff & 7) : 0);
-      const uint16_t* srow = prm.scales + (live ? crow : 0) * prm.NGRP;
+    int jg = 0;
+    for (int64_t it0 = blockIdx.x; it0 < nitems && ok; ++jg) {
+      const TileGroup grp = form_group(prm, it0, nitems);
       for (int pass = 0; pass < prm.npass && ok; ++pass) {
-        const int h = pass_slice(prm.npass, j, pass);
+        const int h = pass_slice(prm.npass, jg, pass);
         if (h != cur) {
           if (cur >= 0) {
             __syncwarp();
@@ -637,78 +693,92 @@ __global__ void __launch_bounds__(kThreads, 1)
           ++cb_loads;
           cur = h;
         }
-        for (int w = 0; w < nwin; ++w) {
-          if (!warp_wait(&w_full[ws], wp, abort_flag)) { ok = false; break; }
-          const unsigned char* wst = w_base + ws * prm.win_stage_bytes;
-          const int p = w * kSets + s;
-          uint32_t out[32];
-          if (p < prm.n_k && live) {
-            // scale of the group holding original k = kk (staged with the window, or from global)
-            auto scale_at = [&](int kk) -> uint16_t {
-              if (prm.scale_tma) {
-                const uint4 sv = reinterpret_cast<const uint4*>(wst + prm.code_stage_bytes)[woff];
-                const int gi = (kk >> prm.log2g) - ((((w * kSets) << prm.kpos_log2) >> prm.log2g) & ~7);
-                const uint32_t sw = (gi & 4) ? ((gi & 2) ? sv.w : sv.z) : ((gi & 2) ? sv.y : sv.x);
-                return static_cast<uint16_t>((gi & 1) ? (sw >> 16) : (sw & 0xFFFFu));
+        for (int t = 0; t < grp.count && ok; ++t) {
+          const TileRow tr = tile_row(prm, it0 + static_cast<int64_t>(t) * gridDim.x, lrow);
+          const int xr = prm.wswz == 1 ? ((tr.woff >> 1) & 3) : (prm.wswz == 2 ? (tr.woff & 7) : 0);
+          const uint16_t* srow = prm.scales + (tr.live ? tr.crow : 0) * prm.NGRP;
+          for (int w = 0; w < nwin; ++w) {
+            if (!warp_wait(&w_full[ws], wp, abort_flag)) { ok = false; break; }
+            const unsigned char* wst = w_base + ws * prm.win_stage_bytes;
+            const int p = w * kSets + s;
+            uint32_t out[32];
+            if (p < prm.n_k && tr.live) {
+              // scale of the group holding original k = kk (staged with the window, or from global)
+              auto scale_at = [&](int kk) -> uint16_t {
+                if (prm.scale_tma) {
+                  const uint4 sv = reinterpret_cast<const uint4*>(wst + prm.code_stage_bytes)[tr.woff];
+                  const int gi = (kk >> prm.log2g) - ((((w * kSets) << prm.kpos_log2) >> prm.log2g) & ~7);
+                  const uint32_t sw = (gi & 4) ? ((gi & 2) ? sv.w : sv.z) : ((gi & 2) ? sv.y : sv.x);
+                  return static_cast<uint16_t>((gi & 1) ? (sw >> 16) : (sw & 0xFFFFu));
+                }
+                return __ldg(srow + kk / prm.G);
+              };
+              const int wstart = w * prm.wpw;
+              const uint32_t* crow_s = reinterpret_cast<const uint32_t*>(wst) + tr.woff * prm.W;
+              if constexpr (DS) {
+                const __half slo = __ushort_as_half(scale_at(p << 7));
+                const __half shi = __ushort_as_half(scale_at((p << 7) + 64));
+                const int b0 = (wstart & 3) * 32 + s * 16 * BITS;
+                decode_pos_dsplit<BITS>(prm, cb_s, crow_s, xr, b0, __halves2half2(slo, slo), __halves2half2(shi, shi),
+                                        out);
+              } else {
+                const __half sh = __ushort_as_half(scale_at(p * kChunkK));
+                const int b0 = (wstart & 3) * 32 + s * (kChunkK / D) * prm.bits;
+                decode_chunk<D, BITS>(prm, cb_s, crow_s, xr, b0, __halves2half2(sh, sh), h, out);
               }
-              return __ldg(srow + kk / prm.G);
-            };
-            const int wstart = w * prm.wpw;
-            const uint32_t* crow_s = reinterpret_cast<const uint32_t*>(wst) + woff * prm.W;
-            if constexpr (DS) {
-              const __half slo = __ushort_as_half(scale_at(p << 7));
-              const __half shi = __ushort_as_half(scale_at((p << 7) + 64));
-              const int b0 = (wstart & 3) * 32 + s * 16 * BITS;
-              decode_pos_dsplit<BITS>(prm, cb_s, crow_s, xr, b0, __halves2half2(slo, slo), __halves2half2(shi, shi),
-                                      out);
             } else {
-              const __half sh = __ushort_as_half(scale_at(p * kChunkK));
-              const int b0 = (wstart & 3) * 32 + s * (kChunkK / D) * prm.bits;
-              decode_chunk<D, BITS>(prm, cb_s, crow_s, xr, b0, __halves2half2(sh, sh), h, out);
-            }
-          } else {
 #pragma unroll
-            for (int i = 0; i < 32; ++i) out[i] = 0u;  // K padding up to a whole window, or a dead row
+              for (int i = 0; i < 32; ++i) out[i] = 0u;  // K padding up to a whole window, or a dead row
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&w_empty[ws]);
+            if (++ws == prm.wst) { ws = 0; wp ^= 1u; }
+            // position p of this tile-pass has sequence number g + p; its A stage
+            // was last read by position g + p - 8
+            const uint32_t gp = g + static_cast<uint32_t>(p);
+            const uint32_t ast = gp % kAStages;
+            if (!warp_wait(&st_free[ast], ((gp / kAStages) & 1u) ^ 1u, abort_flag)) { ok = false; break; }
+            tc_fence_after();
+            tc_st_x32(tmem_base + lane_off + kTmemA + ast * 32, out);
+            tc_wait_st();
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&a_full[(gp >> 2) & 1u]);
           }
-          __syncwarp();
-          if (lane == 0) mbar_arrive(&w_empty[ws]);
-          if (++ws == prm.wst) { ws = 0; wp ^= 1u; }
-          // position p of this tile-pass has sequence number g + p; its A stage
-          // was last read by position g + p - 8
-          const uint32_t gp = g + static_cast<uint32_t>(p);
-          const uint32_t ast = gp % kAStages;
-          if (!warp_wait(&st_free[ast], ((gp / kAStages) & 1u) ^ 1u, abort_flag)) { ok = false; break; }
-          tc_fence_after();
-          tc_st_x32(tmem_base + lane_off + kTmemA + ast * 32, out);
-          tc_wait_st();
-          tc_fence_before();
-          __syncwarp();
-          if (lane == 0) mbar_arrive(&a_full[(gp >> 2) & 1u]);
+          g += static_cast<uint32_t>(prm.n_pos);
         }
-        g += static_cast<uint32_t>(prm.n_pos);
       }
       if (!ok) break;
-      // epilogue: y = D_0 (+ D_1 when both issuers took part), column blocks of 16 split over the 4 sets
-      if (!warp_wait(&acc_full[0], static_cast<uint32_t>(j & 1), abort_flag) ||
-          !warp_wait(&acc_full[1], static_cast<uint32_t>(j & 1), abort_flag))
+      // epilogue: y = D_0 (+ D_1 when both issuers took part) for every tile of
+      // the group; (tile, 16-column block) pairs dealt round-robin to the 4 sets
+      if (!warp_wait(&acc_full[0], static_cast<uint32_t>(jg & 1), abort_flag) ||
+          !warp_wait(&acc_full[1], static_cast<uint32_t>(jg & 1), abort_flag))
         break;
       tc_fence_after();
-      const int ntok = ch.z;
-      const int n = (ntok + 15) & ~15;
-      const bool two = prm.npass * prm.n_pos / slot_positions(slot_rows(ntok)) > 1;
-      for (int c0 = s * 16; c0 < n; c0 += kSets * 16) {
-        uint32_t v0[16], v1[16];
-        tc_ld_x16(tmem_base + lane_off + static_cast<uint32_t>(c0), v0);
-        tc_ld_x16(tmem_base + lane_off + static_cast<uint32_t>(kMaxN + c0), v1);
-        tc_wait_ld();
-        if (r < prm.OUT) {
+      int blk = 0;
+      for (int t = 0; t < grp.count; ++t) {
+        const int64_t it = it0 + static_cast<int64_t>(t) * gridDim.x;
+        const int4 ch = prm.chunks[static_cast<int>(it / prm.row_tiles)];
+        const TileRow tr = tile_row(prm, it, lrow);
+        const int ntok = ch.z;
+        const int n = (ntok + 15) & ~15;
+        const bool two = prm.npass * prm.n_pos / slot_positions(slot_rows(ntok)) > 1;
+        const uint32_t d0 = static_cast<uint32_t>(2 * t * grp.n16), d1 = d0 + static_cast<uint32_t>(grp.n16);
+        for (int c0 = 0; c0 < n; c0 += 16, ++blk) {
+          if ((blk & (kSets - 1)) != s) continue;
+          uint32_t v0[16], v1[16];
+          tc_ld_x16(tmem_base + lane_off + d0 + static_cast<uint32_t>(c0), v0);
+          tc_ld_x16(tmem_base + lane_off + d1 + static_cast<uint32_t>(c0), v1);
+          tc_wait_ld();
+          if (tr.r < prm.OUT) {
 #pragma unroll
-          for (int jj = 0; jj < 16; ++jj) {
-            if (c0 + jj < ntok) {
-              const int pair = prm.sorted[ch.y + c0 + jj];
-              float acc = two ? __uint_as_float(v0[jj]) + __uint_as_float(v1[jj]) : __uint_as_float(v0[jj]);
-              if (!live) acc = 0.0f;  // dead row (row table): exact +0
-              store_y(prm.y, static_cast<int64_t>(pair) * prm.OUT + r, acc, prm.y_dtype, prm.round_f16_first != 0);
+            for (int jj = 0; jj < 16; ++jj) {
+              if (c0 + jj < ntok) {
+                const int pair = prm.sorted[ch.y + c0 + jj];
+                float acc = two ? __uint_as_float(v0[jj]) + __uint_as_float(v1[jj]) : __uint_as_float(v0[jj]);
+                if (!tr.live) acc = 0.0f;  // dead row (row table): exact +0
+                store_y(prm.y, static_cast<int64_t>(pair) * prm.OUT + tr.r, acc, prm.y_dtype, prm.round_f16_first != 0);
+              }
             }
           }
         }
@@ -716,6 +786,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(acc_empty);
+      it0 += static_cast<int64_t>(grp.count) * gridDim.x;
     }
   }
 

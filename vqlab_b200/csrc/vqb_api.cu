@@ -215,25 +215,26 @@ vqb_status vqb_switch_forward(const vqb_linear_desc* desc, const void* x, vqb_dt
   if (!workspace) return VQB_NULL_POINTER;
   // Path: the reference runs the fused small-N kernel up to VQ_FUSED_MAX_N =
   // 512 pairs and the grouped GEMM above it (vq_switch.py:45, :5313-5315).  The
-  // grouped GEMM decodes every routed expert's tile with a fixed cost per tile
-  // (codebook reload, epilogue) that the K extent amortises, so on a B200 it
-  // pays once pairs * IN exceed a few thousand per expert as well.  A d8
-  // codebook too large for shared memory changes the balance: the decode
-  // kernel then reads part of the codebook through L1/L2, while the GEMM keeps
-  // half of every entry resident per pass, so with IN >= 2048 the GEMM wins
-  // from a few dozen pairs on.  Measured (512 experts, d8/K16384, uniform
-  // routing, ms per call):
-  //   1024 x 4096 gate:  10 pairs: 0.069 GEMM vs 0.060 decode; 20: 0.076 vs 0.072;
-  //                      40: 0.103 vs 0.113;  1.0 pairs/expert: 0.48 vs 0.72;  2.5: 0.68 vs 1.11
-  //   4096 x 1024 down:  0.3: 0.31 vs 0.27;  1.0: 0.70 vs 0.63;  1.9: 0.92 vs 0.94;
-  //                      2.5: 0.98 vs 1.06;  5.0: 1.08 vs 1.64
-  const int64_t pair_in_per_expert = tc_prefill_dsplit(geo) ? 2048 : 4608;
+  // grouped GEMM decodes every routed expert's tile with a fixed cost per
+  // tile group (codebook reload, accumulator drain) that the K extent
+  // amortises, so on a B200 it pays once pairs * IN exceed ~4608 per expert as
+  // well.  A d8 codebook too large for shared memory changes the balance: the
+  // decode kernel then reads part of the codebook through L1/L2 while the
+  // GEMM keeps half of every entry resident per pass, and the GEMM wins from a
+  // few dozen pairs on.  Measured (512 experts, d8/K16384, uniform routing,
+  // ms per call, GEMM vs decode):
+  //   1024 x 4096 gate:  10 pairs 0.068 vs 0.063;  40: 0.096 vs 0.115;
+  //                      1.25 pairs/expert 0.50 vs 0.79;  10: 0.68 vs 2.81
+  //   4096 x 1024 down:  10 pairs 0.067 vs 0.062;  40: 0.091 vs 0.107;
+  //                      1.25 pairs/expert 0.57 vs 0.71;  10: 0.82 vs 2.62
+  constexpr int64_t kGemmPairInPerExpert = 4608;
+  constexpr int kDsplitMinPairs = 32;
   const int path = opts ? opts->path : VQB_PATH_AUTO;
   const int max_fused = (opts && opts->max_fused_pairs > 0) ? opts->max_fused_pairs : 512;
-  const bool wide_dsplit = N > 32 && geo.IN >= 2048 && !(opts && opts->max_fused_pairs > 0) && tc_prefill_dsplit(geo);
+  const bool dsplit_gemm = N > kDsplitMinPairs && !(opts && opts->max_fused_pairs > 0) && tc_prefill_dsplit(geo);
   const bool large = path == VQB_PATH_PREFILL ||
                      (path == VQB_PATH_AUTO &&
-                      (wide_dsplit || (N > max_fused && static_cast<int64_t>(N) * geo.IN > pair_in_per_expert * geo.E)));
+                      (dsplit_gemm || (N > max_fused && static_cast<int64_t>(N) * geo.IN > kGemmPairInPerExpert * geo.E)));
   // MoE numerics: x narrowed to fp16, fp32 accumulation, fp16 output rounding
   // then the caller's dtype (vq_switch.py:5301-5308, :5423).
   return run_linear(geo, x, x_dtype, n_tokens, indices, top_k, N, y, y_dtype, workspace, opts,
