@@ -299,11 +299,11 @@ def test_dense_unpacked_cutoff_12():
         assert np.array_equal(y.view(np.uint32), ref.view(np.uint32)), n
 
 
-@pytest.mark.parametrize("IN,OUT,n", [(5120, 17408, 1), (5120, 17408, 32), (17408, 5120, 1)])
+@pytest.mark.parametrize("IN,OUT,n", [(5120, 17408, 1), (5120, 17408, 32), (17408, 5120, 1), (17408, 5120, 7)])
 def test_dense_c4_mlp_shapes(IN, OUT, n):
-    """BASELINE config 4 MLP projections at full size (d8/K16384, 14-bit):
-    10 and 34 windows of 512 k split over K-slices unevenly (the batch-1
-    decode kernel), and the 32-row grouped GEMM."""
+    """BASELINE config 4 MLP projections at full size (d8/K16384, 14-bit) on
+    the grouped GEMM's dimension-split passes: 136 row tiles of 5120 k, and
+    40 row tiles of 17408 k cut over three CTAs each (split-K)."""
     L = make_layer(E=1, OUT=OUT, IN=IN, D=8, K=16384, G=64, seed=IN + n)
     lin = _dense(L)
     rng = np.random.default_rng(n + 5)

@@ -193,3 +193,21 @@ def test_dense_large_n_decode_matmul_numerics(D, K, IN, OUT, G, n, xdt):
         ref = orc.dense_decode_matmul(L.codes[0], L.cb_bits, L.sc_bits[0], xv, wbf16=(xdt == torch.bfloat16))
     rounded = orc.round_bf16(ref) if xdt == torch.bfloat16 else orc.round_f16(ref)
     assert within_tol_bf16(rounded, y)
+
+
+@pytest.mark.parametrize("OUT,IN", [(384, 4096), (200, 2048)])
+@pytest.mark.parametrize("n,xdt", [(1, torch.bfloat16), (5, torch.float16), (130, torch.bfloat16)])
+def test_dense_split_k(OUT, IN, n, xdt):
+    """Dense d8/K16384 layers with few row tiles: the GEMM cuts each tile's K
+    windows over several CTAs and sums the fp32 partials in split order.
+    The result stays within the _decode_matmul tolerance and is deterministic."""
+    L = make_layer(E=1, OUT=OUT, IN=IN, D=8, K=16384, G=64, seed=n + OUT)
+    codes, cb, sc = to_torch(L)
+    lin = VQLinear(codes[0], cb, sc[0], group_size=64, pack_bits=L.bits, in_features=IN)
+    rng = np.random.default_rng(n + 1)
+    x = torch.from_numpy(rng.standard_normal((n, IN)).astype(np.float32)).to(xdt)
+    y = lin(x.cuda())
+    ref = orc.dense_decode_matmul(L.codes[0], L.cb_bits, L.sc_bits[0], x.float().numpy(), wbf16=(xdt == torch.bfloat16))
+    rounded = orc.round_bf16(ref) if xdt == torch.bfloat16 else orc.round_f16(ref)
+    assert within_tol_bf16(rounded, y.float().cpu().numpy())
+    assert torch.equal(y, lin(x.cuda()))

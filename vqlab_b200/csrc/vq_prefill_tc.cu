@@ -41,6 +41,8 @@
 // tensor memory and returns.
 #include <cuda.h>
 
+#include <algorithm>
+
 #include "vqb_common.cuh"
 #include "vqb_internal.h"
 
@@ -101,6 +103,8 @@ struct TParams {
   const int32_t* row_table;  // SKIPZERO [E, OUT] -> compact row (-1 dead), nullptr = plain layout
   const int* tile_base;      // SKIPZERO: first compact row of each (expert, 128-row tile), -1 = all dead
   int64_t nrows;             // rows of codes / scales
+  int ksplit;                // work items per tile: split-K over its windows (1 = whole tiles)
+  float* partial;            // ksplit > 1: fp32 partial tiles [item][128 columns][128 rows]
 };
 
 // ------------------------------------------------------------ PTX helpers
@@ -392,8 +396,33 @@ struct TileGroup {
 constexpr int kAccCols = kIssuers * kMaxN;  // TMEM columns [0, 256)
 constexpr int kMaxGroup = 8;
 
+// Work item it: tile it / ksplit (chunk-major over row tiles), split it % ksplit
+// of the tile's npass * nwin windows (contiguous, window-aligned ranges).
+__device__ __forceinline__ int item_chunk(const TParams& prm, int64_t it) {
+  return static_cast<int>((it / prm.ksplit) / prm.row_tiles);
+}
+__device__ __forceinline__ int item_row_tile(const TParams& prm, int64_t it) {
+  return static_cast<int>((it / prm.ksplit) % prm.row_tiles);
+}
+// the item's windows inside pass `pass`: [lo, hi) of that pass's nwin (empty when lo >= hi)
+__device__ __forceinline__ void item_pass_windows(const TParams& prm, int64_t it, int pass, int nwin, int& lo,
+                                                  int& hi) {
+  const int S = prm.ksplit, sp = static_cast<int>(it % S), nwt = prm.npass * nwin;
+  const int wlo = sp * nwt / S, whi = (sp + 1) * nwt / S;
+  lo = max(wlo - pass * nwin, 0);
+  hi = min(whi - pass * nwin, nwin);
+}
+__device__ __forceinline__ int item_windows(const TParams& prm, int64_t it, int nwin) {
+  const int S = prm.ksplit, sp = static_cast<int>(it % S), nwt = prm.npass * nwin;
+  return (sp + 1) * nwt / S - sp * nwt / S;
+}
+__device__ __forceinline__ int item_first_window(const TParams& prm, int64_t it, int nwin) {
+  const int S = prm.ksplit, sp = static_cast<int>(it % S);
+  return sp * (prm.npass * nwin) / S;
+}
+
 __device__ __forceinline__ int tile_n16(const TParams& prm, int64_t it) {
-  return (prm.chunks[static_cast<int>(it / prm.row_tiles)].z + 15) & ~15;
+  return (prm.chunks[item_chunk(prm, it)].z + 15) & ~15;
 }
 __device__ __forceinline__ TileGroup form_group(const TParams& prm, int64_t it0, int64_t nitems) {
   TileGroup grp{1, tile_n16(prm, it0)};
@@ -419,8 +448,8 @@ struct TileRow {
   int woff;
 };
 __device__ __forceinline__ TileRow tile_row(const TParams& prm, int64_t it, int lrow) {
-  const int chunk = static_cast<int>(it / prm.row_tiles);
-  const int rt = static_cast<int>(it - static_cast<int64_t>(chunk) * prm.row_tiles);
+  const int chunk = item_chunk(prm, it);
+  const int rt = item_row_tile(prm, it);
   const int e = prm.chunks[chunk].x;
   TileRow tr;
   tr.r = rt * kTileM + lrow;
@@ -498,7 +527,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t tmem_base = *tmem_slot;
 
   const int nchunks = prm.meta[0];
-  const int64_t nitems = static_cast<int64_t>(nchunks) * prm.row_tiles;
+  const int64_t nitems = static_cast<int64_t>(nchunks) * prm.row_tiles * prm.ksplit;
   const int nwin = prm.n_pos / kSets;
 
   if (warp == kWarpTmaX) {
@@ -516,13 +545,16 @@ __global__ void __launch_bounds__(kThreads, 1)
           // the dimension split reads x's permuted half of the resident codebook dims
           const int cbase = DS ? pass_slice(prm.npass, jg, pass) * prm.n_pos : 0;
           for (int t = 0; t < grp.count && ok; ++t) {
-            const int4 ch = prm.chunks[static_cast<int>((it0 + static_cast<int64_t>(t) * gridDim.x) / prm.row_tiles)];
+            const int64_t it = it0 + static_cast<int64_t>(t) * gridDim.x;
+            int lo, hi;
+            item_pass_windows(prm, it, pass, nwin, lo, hi);
+            const int4 ch = prm.chunks[item_chunk(prm, it)];
             const int rows = slot_rows(ch.z);
             const int pp = slot_positions(rows);
             // one box per slot: 64 k x rows tokens x pp chunks, laid out [chunk][token][k]
             const CUtensorMap* map = rows == 32 ? &xmap32 : (rows == 64 ? &xmap64 : &xmap128);
             const uint32_t bytes = static_cast<uint32_t>(pp * rows * kChunkK * 2);
-            for (int p0 = 0; p0 < prm.n_pos; p0 += pp, ++gs) {
+            for (int p0 = lo * kSets; p0 < hi * kSets; p0 += pp, ++gs) {
               const uint32_t bs = gs % kBStages;
               if (!mbar_wait(&b_empty[bs], ((gs / kBStages) & 1u) ^ 1u, abort_flag)) { ok = false; break; }
               mbar_expect_tx(&b_full[bs], bytes);
@@ -557,18 +589,23 @@ __global__ void __launch_bounds__(kThreads, 1)
         uint32_t started = 0;  // tiles whose accumulator this issuer has written in this group
         for (int pass = 0; pass < prm.npass && ok; ++pass) {
           for (int t = 0; t < grp.count && ok; ++t) {
-            const int4 ch = prm.chunks[static_cast<int>((it0 + static_cast<int64_t>(t) * gridDim.x) / prm.row_tiles)];
+            const int64_t it = it0 + static_cast<int64_t>(t) * gridDim.x;
+            int lo, hi;
+            item_pass_windows(prm, it, pass, nwin, lo, hi);
+            if (lo >= hi) continue;
+            const int4 ch = prm.chunks[item_chunk(prm, it)];
             const uint32_t idesc = make_idesc((ch.z + 15) & ~15, prm.b_bf16 != 0);
             const int rows = slot_rows(ch.z);
             const int pp = slot_positions(rows);
             const uint32_t d_tmem = tmem_base + static_cast<uint32_t>((2 * t + iss) * grp.n16);
-            int k = pass * (prm.n_pos / pp);  // slot index inside the tile
-            for (int p0 = 0; p0 < prm.n_pos; p0 += pp, ++gs, ++k) {
+            // slot index inside the work item
+            int k = ((pass * nwin + lo - item_first_window(prm, it, nwin)) * kSets) / pp;
+            for (int p0 = lo * kSets; p0 < hi * kSets; p0 += pp, ++gs, ++k) {
               if ((k & 1) != iss) continue;
               const uint32_t bs = gs % kBStages;
               if (!(ok = mbar_wait(&b_full[bs], (gs / kBStages) & 1u, abort_flag))) break;
               for (int q = 0; q < pp; ++q) {
-                const uint32_t gp = g + static_cast<uint32_t>(p0 + q);
+                const uint32_t gp = g + static_cast<uint32_t>(p0 - lo * kSets + q);
                 const uint32_t ast = gp % kAStages;
                 const uint32_t win = gp >> 2;
                 if (win != waited) {
@@ -588,7 +625,7 @@ __global__ void __launch_bounds__(kThreads, 1)
               if (!ok) break;
               tc_commit(&b_empty[bs]);
             }
-            g += static_cast<uint32_t>(prm.n_pos);
+            g += static_cast<uint32_t>((hi - lo) * kSets);
           }
         }
         if (ok) tc_commit(&acc_full[iss]);
@@ -612,12 +649,13 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int pass = 0; pass < prm.npass && ok; ++pass) {
           for (int t = 0; t < grp.count && ok; ++t) {
             const int64_t it = it0 + static_cast<int64_t>(t) * gridDim.x;
-            const int chunk = static_cast<int>(it / prm.row_tiles);
-            const int rt = static_cast<int>(it - static_cast<int64_t>(chunk) * prm.row_tiles);
-            const int4 ch = prm.chunks[chunk];
+            int lo, hi;
+            item_pass_windows(prm, it, pass, nwin, lo, hi);
+            const int rt = item_row_tile(prm, it);
+            const int4 ch = prm.chunks[item_chunk(prm, it)];
             // the tile's rows in codes / scales: (e, rt*128 ...), or from its first live compact row
             const int yrow = prm.row_table ? max(prm.tile_base[ch.x * prm.row_tiles + rt], 0) : ch.x * prm.OUT + rt * kTileM;
-            for (int w = 0; w < nwin; ++w) {
+            for (int w = lo; w < hi; ++w) {
               if (!mbar_wait(&w_empty[ws], wp ^ 1u, abort_flag)) { ok = false; break; }
               mbar_expect_tx(&w_full[ws], bytes);
               unsigned char* dst = w_base + ws * prm.win_stage_bytes;
@@ -694,10 +732,14 @@ __global__ void __launch_bounds__(kThreads, 1)
           cur = h;
         }
         for (int t = 0; t < grp.count && ok; ++t) {
-          const TileRow tr = tile_row(prm, it0 + static_cast<int64_t>(t) * gridDim.x, lrow);
+          const int64_t it = it0 + static_cast<int64_t>(t) * gridDim.x;
+          int lo, hi;
+          item_pass_windows(prm, it, pass, nwin, lo, hi);
+          if (lo >= hi) continue;
+          const TileRow tr = tile_row(prm, it, lrow);
           const int xr = prm.wswz == 1 ? ((tr.woff >> 1) & 3) : (prm.wswz == 2 ? (tr.woff & 7) : 0);
           const uint16_t* srow = prm.scales + (tr.live ? tr.crow : 0) * prm.NGRP;
-          for (int w = 0; w < nwin; ++w) {
+          for (int w = lo; w < hi; ++w) {
             if (!warp_wait(&w_full[ws], wp, abort_flag)) { ok = false; break; }
             const unsigned char* wst = w_base + ws * prm.win_stage_bytes;
             const int p = w * kSets + s;
@@ -733,9 +775,9 @@ __global__ void __launch_bounds__(kThreads, 1)
             __syncwarp();
             if (lane == 0) mbar_arrive(&w_empty[ws]);
             if (++ws == prm.wst) { ws = 0; wp ^= 1u; }
-            // position p of this tile-pass has sequence number g + p; its A stage
-            // was last read by position g + p - 8
-            const uint32_t gp = g + static_cast<uint32_t>(p);
+            // position p of this tile-pass has sequence number g + p - 4 lo; its
+            // A stage was last read by the position 8 before it
+            const uint32_t gp = g + static_cast<uint32_t>(p - lo * kSets);
             const uint32_t ast = gp % kAStages;
             if (!warp_wait(&st_free[ast], ((gp / kAStages) & 1u) ^ 1u, abort_flag)) { ok = false; break; }
             tc_fence_after();
@@ -745,7 +787,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             __syncwarp();
             if (lane == 0) mbar_arrive(&a_full[(gp >> 2) & 1u]);
           }
-          g += static_cast<uint32_t>(prm.n_pos);
+          g += static_cast<uint32_t>((hi - lo) * kSets);
         }
       }
       if (!ok) break;
@@ -758,11 +800,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       int blk = 0;
       for (int t = 0; t < grp.count; ++t) {
         const int64_t it = it0 + static_cast<int64_t>(t) * gridDim.x;
-        const int4 ch = prm.chunks[static_cast<int>(it / prm.row_tiles)];
+        const int4 ch = prm.chunks[item_chunk(prm, it)];
         const TileRow tr = tile_row(prm, it, lrow);
         const int ntok = ch.z;
         const int n = (ntok + 15) & ~15;
-        const bool two = prm.npass * prm.n_pos / slot_positions(slot_rows(ntok)) > 1;
+        const bool two = item_windows(prm, it, nwin) * kSets / slot_positions(slot_rows(ntok)) > 1;
+        float* part = prm.ksplit > 1 ? prm.partial + it * (kMaxN * kTileM) : nullptr;
         const uint32_t d0 = static_cast<uint32_t>(2 * t * grp.n16), d1 = d0 + static_cast<uint32_t>(grp.n16);
         for (int c0 = 0; c0 < n; c0 += 16, ++blk) {
           if ((blk & (kSets - 1)) != s) continue;
@@ -770,7 +813,14 @@ __global__ void __launch_bounds__(kThreads, 1)
           tc_ld_x16(tmem_base + lane_off + d0 + static_cast<uint32_t>(c0), v0);
           tc_ld_x16(tmem_base + lane_off + d1 + static_cast<uint32_t>(c0), v1);
           tc_wait_ld();
-          if (tr.r < prm.OUT) {
+          if (part) {
+            // split-K: this item's fp32 partial, column-major so a warp's 32 rows are one 128-byte line
+#pragma unroll
+            for (int jj = 0; jj < 16; ++jj) {
+              const float v = two ? __uint_as_float(v0[jj]) + __uint_as_float(v1[jj]) : __uint_as_float(v0[jj]);
+              if (c0 + jj < ntok) part[(c0 + jj) * kTileM + lrow] = v;
+            }
+          } else if (tr.r < prm.OUT) {
 #pragma unroll
             for (int jj = 0; jj < 16; ++jj) {
               if (c0 + jj < ntok) {
@@ -859,6 +909,32 @@ __global__ void gather_sorted_kernel(const void* __restrict__ x, int x_dtype, co
         dst[i] = v;
       }
     }
+  }
+}
+
+// Split-K: y[pair, row] = the sum of a tile's ksplit fp32 partials in split
+// order, with the output rounding (one thread per (tile, column, row), rows
+// fastest; cmax bounds the columns any chunk holds).
+__global__ void splitk_reduce_kernel(const float* __restrict__ partial, const int* __restrict__ meta,
+                                     const int4* __restrict__ chunks, const int* __restrict__ sorted, int row_tiles,
+                                     int S, int OUT, int cmax, void* y, int y_dtype, int round_f16_first) {
+  const int64_t ntiles = static_cast<int64_t>(meta[0]) * row_tiles;
+  const int64_t total = ntiles * cmax * kTileM;
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int lr = static_cast<int>(i % kTileM);
+    const int64_t rest = i / kTileM;
+    const int c = static_cast<int>(rest % cmax);
+    const int64_t ti = rest / cmax;
+    const int4 ch = chunks[static_cast<int>(ti / row_tiles)];
+    const int r = static_cast<int>(ti % row_tiles) * kTileM + lr;
+    if (c >= ch.z || r >= OUT) continue;
+    float v = 0.0f;
+    for (int sp = 0; sp < S; ++sp) {
+      const float pv = partial[((ti * S + sp) * kMaxN + c) * kTileM + lr];
+      v = sp == 0 ? pv : v + pv;
+    }
+    store_y(y, static_cast<int64_t>(sorted[ch.y + c]) * OUT + r, v, y_dtype, round_f16_first != 0);
   }
 }
 
@@ -1035,11 +1111,37 @@ bool tc_prefill_supported(const LinearGeometry& geo) {
   return true;
 }
 
-size_t tc_prefill_x_bytes(int64_t N, int IN, int K, int D) {
-  const size_t xs = (static_cast<size_t>(N) * IN * 2 + 1023) & ~size_t(1023);
-  // + the [2][K][4] dimension halves of a d8 codebook (dimension-split passes)
-  const size_t split = D == 8 && K > 0 ? (static_cast<size_t>(K) * 16 + 1023) & ~size_t(1023) : 0;
-  return IN > 0 ? xs + split : 0;
+// Split-K for dense layers (E = 1) whose tiles cannot fill the GPU: each
+// tile's windows are cut into ksplit contiguous ranges, one work item each,
+// when fewer tiles than half the SMs exist (at most 8 ranges, at least 4
+// windows of 256 k each).
+int tc_prefill_ksplit(int64_t N, int E, int OUT, int IN) {
+  if (E != 1 || N <= 0 || IN <= 0 || ensure_device_attrs() != VQB_OK) return 1;
+  const int64_t tiles = ((N + kMaxN - 1) / kMaxN) * ((OUT + kTileM - 1) / kTileM);
+  if (tiles * 2 > g_sms_tc) return 1;
+  int64_t S = g_sms_tc / tiles;
+  S = std::min<int64_t>(S, 8);
+  S = std::min<int64_t>(S, IN / 1024);
+  return static_cast<int>(std::max<int64_t>(S, 1));
+}
+
+// Workspace of one grouped-GEMM call after the routing tables: x gathered in
+// expert order [N, IN] 16-bit, the [2][K][4] dimension halves of a d8
+// codebook, and the split-K partial tiles.
+static size_t xs_bytes(int64_t N, int IN) { return (static_cast<size_t>(N) * IN * 2 + 1023) & ~size_t(1023); }
+static size_t split_cb_bytes(int K, int D) {
+  return D == 8 && K > 0 ? (static_cast<size_t>(K) * 16 + 1023) & ~size_t(1023) : 0;
+}
+static size_t partial_bytes(int64_t N, int E, int OUT, int IN) {
+  const int S = tc_prefill_ksplit(N, E, OUT, IN);
+  if (S <= 1) return 0;
+  const int64_t tiles = ((N + kMaxN - 1) / kMaxN) * ((OUT + kTileM - 1) / kTileM);
+  return static_cast<size_t>(tiles) * S * kMaxN * kTileM * sizeof(float);
+}
+
+size_t tc_prefill_x_bytes(int64_t N, int IN, int K, int D, int E, int OUT) {
+  if (IN <= 0) return 0;
+  return xs_bytes(N, IN) + split_cb_bytes(K, D) + partial_bytes(N, E, OUT, IN);
 }
 
 vqb_status launch_prefill_tc(const LinearGeometry& geo, const void* x, int x_dtype, int krep, const RouteWorkspace& rw,
@@ -1090,8 +1192,11 @@ vqb_status launch_prefill_tc(const LinearGeometry& geo, const void* x, int x_dty
     }
   }
   if (smem == 0) return VQB_UNSUPPORTED_GEOMETRY;
-  uint16_t* cb_split = ds ? reinterpret_cast<uint16_t*>(reinterpret_cast<char*>(xs) + tc_prefill_x_bytes(N, geo.IN, 0, 0))
-                          : nullptr;
+  uint16_t* cb_split = ds ? reinterpret_cast<uint16_t*>(reinterpret_cast<char*>(xs) + xs_bytes(N, geo.IN)) : nullptr;
+  prm.ksplit = tc_prefill_ksplit(N, geo.E, geo.OUT, geo.IN);
+  prm.partial = prm.ksplit > 1 ? reinterpret_cast<float*>(reinterpret_cast<char*>(xs) + xs_bytes(N, geo.IN) +
+                                                          split_cb_bytes(geo.K, geo.D))
+                               : nullptr;
 
   // 1. gather x into expert-sorted 16-bit rows
   {
@@ -1153,6 +1258,17 @@ vqb_status launch_prefill_tc(const LinearGeometry& geo, const void* x, int x_dty
   timer_after(stream);
   if (ce != cudaSuccess || cudaGetLastError() != cudaSuccess) return VQB_CUDA_ERROR;
   note_launch();
+  if (prm.ksplit > 1) {
+    const int cmax = static_cast<int>(std::min<int64_t>(kMaxN, (static_cast<int64_t>(N) + 15) & ~int64_t(15)));
+    const int64_t tiles = ((static_cast<int64_t>(N) + kMaxN - 1) / kMaxN) * prm.row_tiles;
+    int64_t blocks = (tiles * cmax * kTileM + 255) / 256;
+    if (blocks > 8 * g_sms_tc) blocks = 8 * g_sms_tc;
+    splitk_reduce_kernel<<<static_cast<unsigned>(blocks), 256, 0, stream>>>(
+        prm.partial, rw.meta, rw.chunks, rw.sorted, prm.row_tiles, prm.ksplit, geo.OUT, cmax, y, y_dtype,
+        round_f16_first ? 1 : 0);
+    if (cudaGetLastError() != cudaSuccess) return VQB_CUDA_ERROR;
+    note_launch();
+  }
   return VQB_OK;
 }
 

@@ -80,12 +80,12 @@ static bool dtype_ok(int t) { return t == VQB_F16 || t == VQB_BF16 || t == VQB_F
 // Workspace: [routing (status block first)][x as 16-bit rows: the token rows
 // for the decode kernel's B operand, or all pairs' rows in expert order for
 // the grouped GEMM -- whichever is larger]
-size_t x_region_bytes(int N, int64_t T, int IN, int K, int D) {
-  const size_t a = mma_x16_bytes(T, IN), b = tc_prefill_x_bytes(N, IN, K, D);
+size_t x_region_bytes(int N, int E, int64_t T, int IN, int OUT, int K, int D) {
+  const size_t a = mma_x16_bytes(T, IN), b = tc_prefill_x_bytes(N, IN, K, D, E, OUT);
   return a > b ? a : b;
 }
 size_t linear_workspace_bytes(int N, int E, int64_t T, int IN, int OUT, int K, int D) {
-  return route_workspace_bytes(N, E, kDecodeMaxPairs, row_tiles_128(OUT)) + x_region_bytes(N, T, IN, K, D);
+  return route_workspace_bytes(N, E, kDecodeMaxPairs, row_tiles_128(OUT)) + x_region_bytes(N, E, T, IN, OUT, K, D);
 }
 
 // Shared body of the switch and dense entry points once shapes are valid.
@@ -286,8 +286,16 @@ vqb_status vqb_dense_forward(const vqb_linear_desc* desc, const void* x, vqb_dty
   const int wround = fused ? 0 : (x_dtype == VQB_BF16 ? 1 : 2);
   const int n = static_cast<int>(n_rows);
   // the grouped GEMM once the decode kernel would need more than one pass of
-  // 16 tokens over the weights
-  const bool large = path == VQB_PATH_PREFILL || (!fused && n > 16);
+  // 16 tokens over the weights, and at every N for a d8 codebook too large for
+  // shared memory (dimension-split passes; split-K fills the GPU when the
+  // layer has few row tiles).  Measured on B200, d8/K16384, us, GEMM vs
+  // decode: 17408 x 5120 at N = 1 47 vs 57, N = 4 48 vs 59; 5120 x 17408 at
+  // N = 4 120 vs 221 before split-K.
+  // The fused arm's calls above 8 rows go to the GEMM too, with its fp16
+  // operands (x narrowed to fp16, W = fp16(cb*s), fp32 accumulation): d2/K256
+  // 5120 x 5120 at N = 16 30 vs 73 us, N = 32 31 vs 118 us.
+  const bool large = path == VQB_PATH_PREFILL || (!fused && (n > 16 || tc_prefill_dsplit(geo))) ||
+                     (fused && path == VQB_PATH_AUTO && n > 8);
   return run_linear(geo, x, x_dtype, n, nullptr, 1, n, y, y_dtype, workspace, opts, /*narrow_x_f16=*/fused,
                     /*round_f16_first=*/false, wround, large, reinterpret_cast<cudaStream_t>(stream));
 }
