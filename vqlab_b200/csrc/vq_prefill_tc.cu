@@ -36,7 +36,7 @@
 // fp32 group partials instead), x is fp16 (the MoE host cast) or bf16 with
 // bf16(fp16(cb*s)) weights (dense bf16, vq_dense.py:294), accumulation fp32.
 //
-// Every mbarrier wait is bounded: on expiry the CTA records VQB_TIMEOUT in
+// Every mbarrier wait is bounded (2 s of %globaltimer): on expiry the CTA records VQB_TIMEOUT in
 // the status word, stops issuing, waits for its copies in flight, frees its
 // tensor memory and returns.
 #include <cuda.h>
@@ -67,7 +67,7 @@ constexpr int kFirstDecodeWarp = 5;
 constexpr int kThreads = (kFirstDecodeWarp + kDecodeWarps) * 32;
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kTmemA = kIssuers * kMaxN;        // columns: [0,128) D0, [128,256) D1, then 8 A stages of 32
-constexpr uint32_t kSpinLimit = 1u << 26;
+constexpr uint64_t kWaitLimitNs = 2000000000ull;  // a bounded wait gives up after 2 s
 constexpr int kScaleRowBytes = 16;                   // 8 fp16 scales per row per window
 constexpr int kNumBars = 2 * kBStages + 2 + kAStages + 2 * kWStages + 2 + kIssuers + 1 + kIssuers;
 
@@ -123,17 +123,29 @@ __device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
   asm volatile("{\n\t.reg .b64 st;\n\tmbarrier.arrive.expect_tx.shared::cta.b64 st, [%0], %1;\n\t}"
                :: "r"(smem_u32(bar)), "r"(bytes) : "memory");
 }
+// One try (the hardware may suspend the thread briefly while the phase is
+// pending).  A suspend-time hint measured slower on the prefill pipeline.
 __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   uint32_t ok;
   asm volatile("{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\tselp.u32 %0, 1, 0, p;\n\t}"
                : "=r"(ok) : "r"(smem_u32(bar)), "r"(parity) : "memory");
   return ok != 0;
 }
-// bounded wait: false when the limit expired or another role aborted
+__device__ __forceinline__ uint64_t global_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+// bounded wait: false when the time limit expired or another role aborted
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag) {
-  for (uint32_t i = 0; i < kSpinLimit; ++i) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = global_ns();
+  for (uint32_t i = 1;; ++i) {
     if (mbar_try_wait(bar, parity)) return true;
-    if ((i & 1023u) == 1023u && *abort_flag) return false;
+    if ((i & 63u) == 0u) {
+      if (*abort_flag) return false;
+      if (global_ns() - t0 > kWaitLimitNs) break;
+    }
   }
   *abort_flag = 1;
   return false;
@@ -144,7 +156,8 @@ __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, volati
 }
 // bounded drain used at teardown (no abort check: a copy in flight must land)
 __device__ __forceinline__ void mbar_drain(uint64_t* bar, uint32_t parity) {
-  for (uint32_t i = 0; i < kSpinLimit && !mbar_try_wait(bar, parity); ++i) {
+  const uint64_t t0 = global_ns();
+  while (!mbar_try_wait(bar, parity) && global_ns() - t0 <= kWaitLimitNs) {
   }
 }
 
@@ -368,17 +381,62 @@ __device__ __forceinline__ void decode_chunk(const TParams& prm, const uint16_t*
 // 4i + d of position p holds W[row, 8 (16p + i) + 4h + d]; x was gathered in
 // the same permuted order, so every weight is decoded once and enters one MMA.
 // Codes 0-7 and 8-15 of a position may sit in different scale groups (G = 64).
+// 16 codes of BITS whose stream starts at bit 0 of word DW of q (twelve words
+// read from the 16-byte unit holding the first one): constant shifts only.
+template <int BITS, int DW>
+__device__ __forceinline__ void codes16_at_word(const uint32_t* q, uint32_t* c) {
+  constexpr uint32_t MASK = (1u << BITS) - 1u;
+#pragma unroll
+  for (int i = 0; i < 16; ++i) {
+    constexpr int dummy = 0;
+    (void)dummy;
+    const int bit = i * BITS, wi = DW + (bit >> 5), bs = bit & 31;
+    const uint32_t v = (bs + BITS <= 32) ? (q[wi] >> bs) : __funnelshift_r(q[wi], q[wi + 1], bs);
+    c[i] = v & MASK;
+  }
+}
+
 template <int BITS>
 __device__ __forceinline__ void decode_pos_dsplit(const TParams& prm, const uint16_t* cb_s, const uint32_t* crow,
                                                   int xr, int b0, __half2 s_lo, __half2 s_hi, uint32_t* out) {
   uint32_t c[16];
-  extract_codes<BITS, 16>(crow, xr, b0, c);
-  const uint32_t lim = static_cast<uint32_t>(prm.K);
+  if ((b0 & 31) == 0 && 16 * BITS <= 8 * 32) {
+    // the position starts on a word (d8/14-bit: 224 bits per position): the
+    // warp-uniform word offset inside the first 16-byte unit picks an
+    // unrolled extraction, no select tree or funnel alignment
+    const int w0 = b0 >> 5;
+    const uint4* row4 = reinterpret_cast<const uint4*>(crow);
+    uint32_t q[12];
 #pragma unroll
-  for (int i = 0; i < 16; ++i) {
-    const uint2 v = reinterpret_cast<const uint2*>(cb_s)[min(c[i], lim)];
-    out[2 * i] = v.x;
-    out[2 * i + 1] = v.y;
+    for (int i = 0; i < 3; ++i) {
+      const uint4 v = row4[((w0 >> 2) + i) ^ xr];
+      q[4 * i] = v.x; q[4 * i + 1] = v.y; q[4 * i + 2] = v.z; q[4 * i + 3] = v.w;
+    }
+    switch (w0 & 3) {
+      case 0: codes16_at_word<BITS, 0>(q, c); break;
+      case 1: codes16_at_word<BITS, 1>(q, c); break;
+      case 2: codes16_at_word<BITS, 2>(q, c); break;
+      default: codes16_at_word<BITS, 3>(q, c); break;
+    }
+  } else {
+    extract_codes<BITS, 16>(crow, xr, b0, c);
+  }
+  if (prm.K == (1 << BITS)) {
+    // every code of the width is a codebook entry: no clamp
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      const uint2 v = reinterpret_cast<const uint2*>(cb_s)[c[i]];
+      out[2 * i] = v.x;
+      out[2 * i + 1] = v.y;
+    }
+  } else {
+    const uint32_t lim = static_cast<uint32_t>(prm.K);
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      const uint2 v = reinterpret_cast<const uint2*>(cb_s)[min(c[i], lim)];
+      out[2 * i] = v.x;
+      out[2 * i + 1] = v.y;
+    }
   }
   scale_words(out, s_lo, s_hi, prm.b_bf16 != 0);
 }
@@ -758,8 +816,17 @@ __global__ void __launch_bounds__(kThreads, 1)
               const int wstart = w * prm.wpw;
               const uint32_t* crow_s = reinterpret_cast<const uint32_t*>(wst) + tr.woff * prm.W;
               if constexpr (DS) {
-                const __half slo = __ushort_as_half(scale_at(p << 7));
-                const __half shi = __ushort_as_half(scale_at((p << 7) + 64));
+                __half slo, shi;
+                if (prm.scale_tma && prm.log2g == 6) {
+                  // G = 64: the window's 8 staged scales are groups 8w .. 8w+7, this
+                  // position's pair (2s, 2s+1) is 32-bit word s of the row's 16 bytes
+                  const uint32_t sw = reinterpret_cast<const uint32_t*>(wst + prm.code_stage_bytes)[tr.woff * 4 + s];
+                  slo = __ushort_as_half(static_cast<uint16_t>(sw & 0xFFFFu));
+                  shi = __ushort_as_half(static_cast<uint16_t>(sw >> 16));
+                } else {
+                  slo = __ushort_as_half(scale_at(p << 7));
+                  shi = __ushort_as_half(scale_at((p << 7) + 64));
+                }
                 const int b0 = (wstart & 3) * 32 + s * 16 * BITS;
                 decode_pos_dsplit<BITS>(prm, cb_s, crow_s, xr, b0, __halves2half2(slo, slo), __halves2half2(shi, shi),
                                         out);
