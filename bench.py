@@ -472,8 +472,8 @@ def gpu_arm(args, rank, world, dev):
     dur = kernel_seconds(torch, s, lambda i: projs[i % n_layers](x, idx), max(3, args.steps))
     alg = nd * EXPERT_BYTES["gate"] + CODEBOOK_BYTES + x.shape[0] * HIDDEN * 2 + npairs * INTER * 2
     achieved = alg / dur / 1e9
-    kname = ("vq_decode_mma_kernel" if npairs <= 512 or npairs * HIDDEN <= 4608 * projs[0].num_experts
-             else "vq_prefill_tc_kernel")
+    kname = ("vq_prefill_tc_kernel" if projs[0].kernel_path(x.shape[0], idx.shape[-1]) == "gemm"
+             else "vq_decode_mma_kernel")
     traffic = profiled_traffic(kname, "c2") if world == 1 else None
     roof = {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak_gbs, "unit": "GB/s",
             "frac": round(achieved / peak_gbs, 4), "traffic": traffic,

@@ -125,6 +125,14 @@ vqb_status vqb_switch_forward(const vqb_linear_desc* desc, const void* x, vqb_dt
                               void* y, vqb_dtype y_dtype, void* workspace, size_t workspace_bytes,
                               const vqb_options* opts, vqb_stream_t stream);
 
+/* The kernel family vqb_switch_forward selects for this call shape:
+ * VQB_PATH_DECODE (fused decode kernel) or VQB_PATH_PREFILL (grouped GEMM),
+ * for 16-byte aligned fp16 / bf16 x (fp32 or unaligned x always decode); a
+ * negative value is -vqb_status for an invalid descriptor or shape.  No
+ * reference counterpart: the reference's dispatch is internal
+ * (vq_switch.py:5313-5315); measurement and tests use it to name the kernel. */
+int32_t vqb_switch_path(const vqb_linear_desc* desc, int32_t n_tokens, int32_t top_k, const vqb_options* opts);
+
 /* vqb_switch_forward without a workspace argument: the call allocates
  * nothing and takes its scratch from an 8 MiB array inside the library's
  * device image.  No counterpart in the reference (its runtime allocates

@@ -98,6 +98,8 @@ def _bind(L):
     L.vqb_launch_count.argtypes = []
     L.vqb_time_next_kernel.restype = i32
     L.vqb_time_next_kernel.argtypes = [P, P]
+    L.vqb_switch_path.restype = i32
+    L.vqb_switch_path.argtypes = [P, i32, i32, P]
     return L
 
 
@@ -142,7 +144,7 @@ def exported_symbols():
     """Names of every function include/vqb.h declares (for the load test)."""
     return ["vqb_version", "vqb_status_string", "vqb_unpack", "vqb_switch_workspace_size",
             "vqb_switch_forward", "vqb_dense_workspace_size", "vqb_dense_forward", "vqb_switch_forward_static",
-            "vqb_launch_count", "vqb_time_next_kernel", "vqb_swiglu", "vqb_moe_combine"]
+            "vqb_launch_count", "vqb_time_next_kernel", "vqb_swiglu", "vqb_moe_combine", "vqb_switch_path"]
 
 
 def launch_count() -> int:

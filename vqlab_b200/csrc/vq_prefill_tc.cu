@@ -103,6 +103,7 @@ struct TParams {
   const int32_t* row_table;  // SKIPZERO [E, OUT] -> compact row (-1 dead), nullptr = plain layout
   const int* tile_base;      // SKIPZERO: first compact row of each (expert, 128-row tile), -1 = all dead
   int64_t nrows;             // rows of codes / scales
+  int max_group;             // tiles per group allowed by the L2 budget for re-read code windows
   int ksplit;                // work items per tile: split-K over its windows (1 = whole tiles)
   float* partial;            // ksplit > 1: fp32 partial tiles [item][128 columns][128 rows]
 };
@@ -447,6 +448,8 @@ __device__ __forceinline__ void decode_pos_dsplit(const TParams& prm, const uint
 // all its tiles before the next pass, so one codebook reload and one
 // accumulator drain serve the whole group -- the small-token tiles of decode
 // batches are short, and a reload per tile would cost as much as the tile.
+// The second pass re-reads the group's code windows, so a group's packed
+// codes stay within an L2 budget per CTA (max_group) and come from L2.
 struct TileGroup {
   int count;
   int n16;
@@ -484,7 +487,7 @@ __device__ __forceinline__ int tile_n16(const TParams& prm, int64_t it) {
 }
 __device__ __forceinline__ TileGroup form_group(const TParams& prm, int64_t it0, int64_t nitems) {
   TileGroup grp{1, tile_n16(prm, it0)};
-  while (grp.count < kMaxGroup) {
+  while (grp.count < prm.max_group) {
     const int64_t it = it0 + static_cast<int64_t>(grp.count) * gridDim.x;
     if (it >= nitems) break;
     const int n16 = max(grp.n16, tile_n16(prm, it));
@@ -1261,6 +1264,13 @@ vqb_status launch_prefill_tc(const LinearGeometry& geo, const void* x, int x_dty
   if (smem == 0) return VQB_UNSUPPORTED_GEOMETRY;
   uint16_t* cb_split = ds ? reinterpret_cast<uint16_t*>(reinterpret_cast<char*>(xs) + xs_bytes(N, geo.IN)) : nullptr;
   prm.ksplit = tc_prefill_ksplit(N, geo.E, geo.OUT, geo.IN);
+  {
+    // the code bytes of a group read twice stay in L2: 256 KB per CTA (37 MB over 148 SMs)
+    constexpr int64_t kGroupCodeBudget = 256 * 1024;
+    const int64_t tile_bytes = static_cast<int64_t>(kTileM) * geo.row_words * 4;
+    const int64_t g = prm.npass > 1 ? kGroupCodeBudget / std::max<int64_t>(tile_bytes, 1) : kMaxGroup;
+    prm.max_group = static_cast<int>(std::min<int64_t>(kMaxGroup, std::max<int64_t>(1, g)));
+  }
   prm.partial = prm.ksplit > 1 ? reinterpret_cast<float*>(reinterpret_cast<char*>(xs) + xs_bytes(N, geo.IN) +
                                                           split_cb_bytes(geo.K, geo.D))
                                : nullptr;

@@ -198,21 +198,9 @@ size_t vqb_switch_workspace_size(const vqb_linear_desc* desc, int32_t n_tokens, 
   return linear_workspace_bytes(static_cast<int>(N), E, T, IN, OUT, K, D);
 }
 
-vqb_status vqb_switch_forward(const vqb_linear_desc* desc, const void* x, vqb_dtype x_dtype, int32_t n_tokens,
-                              const uint32_t* indices, int32_t top_k, void* y, vqb_dtype y_dtype, void* workspace,
-                              size_t workspace_bytes, const vqb_options* opts, vqb_stream_t stream) {
-  LinearGeometry geo;
-  vqb_status st = validate(desc, &geo);
-  if (st != VQB_OK) return st;
-  if (n_tokens < 0 || top_k < 1) return VQB_BAD_SHAPE;
-  if (!dtype_ok(x_dtype) || !dtype_ok(y_dtype)) return VQB_BAD_SHAPE;
-  const int64_t N64 = int64_t(n_tokens) * top_k;
-  if (N64 > 0x7fffffff) return VQB_BAD_SHAPE;
-  const int N = static_cast<int>(N64);
-  if (N == 0) return VQB_OK;
-  if (!x || !indices || !y) return VQB_NULL_POINTER;
-  if (workspace_bytes < vqb_switch_workspace_size(desc, n_tokens, top_k, opts)) return VQB_WORKSPACE_TOO_SMALL;
-  if (!workspace) return VQB_NULL_POINTER;
+// The switch entry's kernel family for N pairs (the GEMM or the decode
+// kernel), before the per-call fallbacks for fp32 or unaligned x.
+static bool switch_uses_gemm(const LinearGeometry& geo, int N, const vqb_options* opts) {
   // Path: the reference runs the fused small-N kernel up to VQ_FUSED_MAX_N =
   // 512 pairs and the grouped GEMM above it (vq_switch.py:45, :5313-5315).  The
   // grouped GEMM decodes every routed expert's tile with a fixed cost per
@@ -232,14 +220,41 @@ vqb_status vqb_switch_forward(const vqb_linear_desc* desc, const void* x, vqb_dt
   const int path = opts ? opts->path : VQB_PATH_AUTO;
   const int max_fused = (opts && opts->max_fused_pairs > 0) ? opts->max_fused_pairs : 512;
   const bool dsplit_gemm = N > kDsplitMinPairs && !(opts && opts->max_fused_pairs > 0) && tc_prefill_dsplit(geo);
-  const bool large = path == VQB_PATH_PREFILL ||
+  return path == VQB_PATH_PREFILL ||
                      (path == VQB_PATH_AUTO &&
                       (dsplit_gemm || (N > max_fused && static_cast<int64_t>(N) * geo.IN > kGemmPairInPerExpert * geo.E)));
+}
+
+vqb_status vqb_switch_forward(const vqb_linear_desc* desc, const void* x, vqb_dtype x_dtype, int32_t n_tokens,
+                              const uint32_t* indices, int32_t top_k, void* y, vqb_dtype y_dtype, void* workspace,
+                              size_t workspace_bytes, const vqb_options* opts, vqb_stream_t stream) {
+  LinearGeometry geo;
+  vqb_status st = validate(desc, &geo);
+  if (st != VQB_OK) return st;
+  if (n_tokens < 0 || top_k < 1) return VQB_BAD_SHAPE;
+  if (!dtype_ok(x_dtype) || !dtype_ok(y_dtype)) return VQB_BAD_SHAPE;
+  const int64_t N64 = int64_t(n_tokens) * top_k;
+  if (N64 > 0x7fffffff) return VQB_BAD_SHAPE;
+  const int N = static_cast<int>(N64);
+  if (N == 0) return VQB_OK;
+  if (!x || !indices || !y) return VQB_NULL_POINTER;
+  if (workspace_bytes < vqb_switch_workspace_size(desc, n_tokens, top_k, opts)) return VQB_WORKSPACE_TOO_SMALL;
+  if (!workspace) return VQB_NULL_POINTER;
+  const bool large = switch_uses_gemm(geo, N, opts);
   // MoE numerics: x narrowed to fp16, fp32 accumulation, fp16 output rounding
   // then the caller's dtype (vq_switch.py:5301-5308, :5423).
   return run_linear(geo, x, x_dtype, n_tokens, indices, top_k, N, y, y_dtype, workspace, opts,
                     /*narrow_x_f16=*/true, /*round_f16_first=*/true, /*wround=*/0, large,
                     reinterpret_cast<cudaStream_t>(stream));
+}
+
+int32_t vqb_switch_path(const vqb_linear_desc* desc, int32_t n_tokens, int32_t top_k, const vqb_options* opts) {
+  LinearGeometry geo;
+  const vqb_status st = validate(desc, &geo);
+  if (st != VQB_OK) return -static_cast<int32_t>(st);
+  if (n_tokens < 0 || top_k < 1 || int64_t(n_tokens) * top_k > 0x7fffffff) return -static_cast<int32_t>(VQB_BAD_SHAPE);
+  const int N = n_tokens * top_k;
+  return switch_uses_gemm(geo, N, opts) && tc_prefill_supported(geo) ? VQB_PATH_PREFILL : VQB_PATH_DECODE;
 }
 
 size_t vqb_dense_workspace_size(const vqb_linear_desc* desc, int64_t n_rows, const vqb_options* opts) {

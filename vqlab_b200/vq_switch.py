@@ -164,6 +164,18 @@ class VQSwitchLinear(torch.nn.Module):
         if int(self.vq_scales.shape[-1]) * self.group_size != self.input_dims:
             raise ValueError("vq_scales last axis must be in_features / group_size")
 
+    def kernel_path(self, n_tokens: int, top_k: int) -> str:
+        """Which kernel family a call of n_tokens x top_k pairs runs on: "decode"
+        (the fused small-N kernel) or "gemm" (the grouped tcgen05 GEMM), for
+        fp16 / bf16 x (the library's AUTO rule, or the forced path in options)."""
+        d = self.desc()
+        opts = self.options
+        r = _lib.lib().vqb_switch_path(ctypes.byref(d), int(n_tokens), int(top_k),
+                                       ctypes.byref(opts) if opts is not None else None)
+        if r < 0:
+            _lib.check(-r, "vqb_switch_path")
+        return "gemm" if r == 2 else "decode"
+
     def forward(self, x: torch.Tensor, indices: torch.Tensor, sorted_indices: bool = False,
                 out: torch.Tensor | None = None) -> torch.Tensor:
         self._check_tensors()
