@@ -60,7 +60,7 @@ typedef enum vqb_dtype { VQB_F16 = 0, VQB_BF16 = 1, VQB_F32 = 2 } vqb_dtype;
  * pairs * in_features > 4608 * num_experts (its fixed cost per expert tile
  * needs that much work to pay on a B200), else still the decode kernel.  A d8
  * codebook too large for shared memory (the GEMM's dimension-split passes)
- * sends every call of more than 32 pairs to the GEMM.  AUTO for
+ * sends every call to the GEMM.  AUTO for
  * vqb_dense_forward follows the reference's dense cutoffs. */
 typedef enum vqb_path { VQB_PATH_AUTO = 0, VQB_PATH_DECODE = 1, VQB_PATH_PREFILL = 2 } vqb_path;
 

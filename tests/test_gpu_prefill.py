@@ -211,3 +211,20 @@ def test_dense_split_k(OUT, IN, n, xdt):
     rounded = orc.round_bf16(ref) if xdt == torch.bfloat16 else orc.round_f16(ref)
     assert within_tol_bf16(rounded, y.float().cpu().numpy())
     assert torch.equal(y, lin(x.cuda()))
+
+
+@pytest.mark.parametrize("T", [1, 2])
+def test_switch_decode_batch_split_k(T):
+    """A decode batch over a few experts on the dimension-split GEMM: 10-20
+    pairs give 80-160 tiles, each cut over 2-3 CTAs, and most CTAs run two
+    work items, the second in the reversed codebook-slice order -- each
+    item must still cover its own K range."""
+    E, OUT, IN, k = 16, 1024, 4096, 10
+    L = make_layer(E=E, OUT=OUT, IN=IN, D=8, K=16384, G=64, seed=300 + T)
+    idx = np.stack([np.random.default_rng(T * 10 + t).permutation(E)[:k] for t in range(T)]).astype(np.uint32)
+    rng = np.random.default_rng(301)
+    x = torch.from_numpy(rng.standard_normal((T, 1, 1, IN)).astype(np.float32)).to(torch.bfloat16)
+    m = _switch(L)
+    assert m.kernel_path(T, k) == "gemm"
+    y = m(x.cuda(), torch.from_numpy(idx.astype(np.int32)).cuda()).float().cpu().numpy().reshape(T * k, OUT)
+    _check(L, x, idx.reshape(-1), k, y)

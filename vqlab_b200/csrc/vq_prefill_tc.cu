@@ -105,7 +105,8 @@ struct TParams {
   int64_t nrows;             // rows of codes / scales
   int max_group;             // tiles per group allowed by the L2 budget for re-read code windows
   int ksplit;                // work items per tile: split-K over its windows (1 = whole tiles)
-  float* partial;            // ksplit > 1: fp32 partial tiles [item][128 columns][128 rows]
+  float* partial;            // ksplit > 1: fp32 partial tiles [item][pcols columns][128 rows]
+  int pcols;                 // columns of a partial slot (tokens a chunk can hold, rounded to 16)
 };
 
 // ------------------------------------------------------------ PTX helpers
@@ -465,13 +466,14 @@ __device__ __forceinline__ int item_chunk(const TParams& prm, int64_t it) {
 __device__ __forceinline__ int item_row_tile(const TParams& prm, int64_t it) {
   return static_cast<int>((it / prm.ksplit) % prm.row_tiles);
 }
-// the item's windows inside pass `pass`: [lo, hi) of that pass's nwin (empty when lo >= hi)
-__device__ __forceinline__ void item_pass_windows(const TParams& prm, int64_t it, int pass, int nwin, int& lo,
-                                                  int& hi) {
+// The item's windows of codebook slice h (a pass runs slice pass_slice(...)):
+// [lo, hi) of that slice's nwin windows, empty when lo >= hi.  The item's
+// range is fixed in slice order, whatever order a group walks the slices in.
+__device__ __forceinline__ void item_pass_windows(const TParams& prm, int64_t it, int h, int nwin, int& lo, int& hi) {
   const int S = prm.ksplit, sp = static_cast<int>(it % S), nwt = prm.npass * nwin;
   const int wlo = sp * nwt / S, whi = (sp + 1) * nwt / S;
-  lo = max(wlo - pass * nwin, 0);
-  hi = min(whi - pass * nwin, nwin);
+  lo = max(wlo - h * nwin, 0);
+  hi = min(whi - h * nwin, nwin);
 }
 __device__ __forceinline__ int item_windows(const TParams& prm, int64_t it, int nwin) {
   const int S = prm.ksplit, sp = static_cast<int>(it % S), nwt = prm.npass * nwin;
@@ -608,7 +610,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int t = 0; t < grp.count && ok; ++t) {
             const int64_t it = it0 + static_cast<int64_t>(t) * gridDim.x;
             int lo, hi;
-            item_pass_windows(prm, it, pass, nwin, lo, hi);
+            item_pass_windows(prm, it, pass_slice(prm.npass, jg, pass), nwin, lo, hi);
             const int4 ch = prm.chunks[item_chunk(prm, it)];
             const int rows = slot_rows(ch.z);
             const int pp = slot_positions(rows);
@@ -652,7 +654,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int t = 0; t < grp.count && ok; ++t) {
             const int64_t it = it0 + static_cast<int64_t>(t) * gridDim.x;
             int lo, hi;
-            item_pass_windows(prm, it, pass, nwin, lo, hi);
+            item_pass_windows(prm, it, pass_slice(prm.npass, jg, pass), nwin, lo, hi);
             if (lo >= hi) continue;
             const int4 ch = prm.chunks[item_chunk(prm, it)];
             const uint32_t idesc = make_idesc((ch.z + 15) & ~15, prm.b_bf16 != 0);
@@ -660,7 +662,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             const int pp = slot_positions(rows);
             const uint32_t d_tmem = tmem_base + static_cast<uint32_t>((2 * t + iss) * grp.n16);
             // slot index inside the work item
-            int k = ((pass * nwin + lo - item_first_window(prm, it, nwin)) * kSets) / pp;
+            int k = ((pass_slice(prm.npass, jg, pass) * nwin + lo - item_first_window(prm, it, nwin)) * kSets) / pp;
             for (int p0 = lo * kSets; p0 < hi * kSets; p0 += pp, ++gs, ++k) {
               if ((k & 1) != iss) continue;
               const uint32_t bs = gs % kBStages;
@@ -705,13 +707,14 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint32_t fill_phase[kWStages] = {};
       const uint32_t bytes = static_cast<uint32_t>(prm.code_stage_bytes + (prm.scale_tma ? kTileM * kScaleRowBytes : 0));
       bool ok = true;
-      for (int64_t it0 = blockIdx.x; it0 < nitems && ok;) {
+      int jg = 0;
+      for (int64_t it0 = blockIdx.x; it0 < nitems && ok; ++jg) {
         const TileGroup grp = form_group(prm, it0, nitems);
         for (int pass = 0; pass < prm.npass && ok; ++pass) {
           for (int t = 0; t < grp.count && ok; ++t) {
             const int64_t it = it0 + static_cast<int64_t>(t) * gridDim.x;
             int lo, hi;
-            item_pass_windows(prm, it, pass, nwin, lo, hi);
+            item_pass_windows(prm, it, pass_slice(prm.npass, jg, pass), nwin, lo, hi);
             const int rt = item_row_tile(prm, it);
             const int4 ch = prm.chunks[item_chunk(prm, it)];
             // the tile's rows in codes / scales: (e, rt*128 ...), or from its first live compact row
@@ -795,7 +798,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int t = 0; t < grp.count && ok; ++t) {
           const int64_t it = it0 + static_cast<int64_t>(t) * gridDim.x;
           int lo, hi;
-          item_pass_windows(prm, it, pass, nwin, lo, hi);
+          item_pass_windows(prm, it, pass_slice(prm.npass, jg, pass), nwin, lo, hi);
           if (lo >= hi) continue;
           const TileRow tr = tile_row(prm, it, lrow);
           const int xr = prm.wswz == 1 ? ((tr.woff >> 1) & 3) : (prm.wswz == 2 ? (tr.woff & 7) : 0);
@@ -875,7 +878,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int ntok = ch.z;
         const int n = (ntok + 15) & ~15;
         const bool two = item_windows(prm, it, nwin) * kSets / slot_positions(slot_rows(ntok)) > 1;
-        float* part = prm.ksplit > 1 ? prm.partial + it * (kMaxN * kTileM) : nullptr;
+        float* part = prm.ksplit > 1 ? prm.partial + it * (static_cast<int64_t>(prm.pcols) * kTileM) : nullptr;
         const uint32_t d0 = static_cast<uint32_t>(2 * t * grp.n16), d1 = d0 + static_cast<uint32_t>(grp.n16);
         for (int c0 = 0; c0 < n; c0 += 16, ++blk) {
           if ((blk & (kSets - 1)) != s) continue;
@@ -940,54 +943,56 @@ __global__ void tile_base_kernel(const int32_t* __restrict__ rt, int E, int OUT,
 }
 
 // x rows gathered into expert-sorted order as 16-bit B rows: xs[s] = x[sorted[s] / krep].
-// One warp per row, 16 bytes (8 elements) per lane and step; x is fp16 or
-// bf16 with 16-byte aligned rows (IN % 64 == 0 and an aligned base).
-// dsplit: the dimension-split order -- elements 8j .. 8j+3 go to columns
-// 4j .. 4j+3 and elements 8j+4 .. 8j+7 to IN/2 + 4j .. (the x side of
-// decode_pos_dsplit's column order).
+// One thread per 16-byte vector (8 elements) of the output, so a few rows
+// still spread over many threads; x is fp16 or bf16 with 16-byte aligned rows
+// (IN % 64 == 0 and an aligned base).  dsplit: the dimension-split order --
+// elements 8j .. 8j+3 go to columns 4j .. 4j+3 and elements 8j+4 .. 8j+7 to
+// IN/2 + 4j .. (the x side of decode_pos_dsplit's column order).
 __global__ void gather_sorted_kernel(const void* __restrict__ x, int x_dtype, const int* __restrict__ sorted, int N,
                                      int krep, int IN, int to_bf16, int dsplit, uint16_t* __restrict__ xs) {
-  const int lane = threadIdx.x & 31;
   const int vec = IN / 8;
   const bool convert = (x_dtype == VQB_BF16) != (to_bf16 != 0);
-  for (int s = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); s < N; s += gridDim.x * (blockDim.x >> 5)) {
+  const int64_t total = static_cast<int64_t>(N) * vec;
+  for (int64_t q = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; q < total;
+       q += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int s = static_cast<int>(q / vec), i = static_cast<int>(q - static_cast<int64_t>(s) * vec);
     const int t = sorted[s] / krep;
-    const uint4* src = reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(x) + static_cast<int64_t>(t) * IN);
-    uint4* dst = reinterpret_cast<uint4*>(xs + static_cast<int64_t>(s) * IN);
-    for (int i = lane; i < vec; i += 32) {
-      uint4 v = __ldg(src + i);
-      if (convert) {
-        uint32_t* w = reinterpret_cast<uint32_t*>(&v);
+    uint4 v = __ldg(reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(x) + static_cast<int64_t>(t) * IN) + i);
+    if (convert) {
+      uint32_t* w = reinterpret_cast<uint32_t*>(&v);
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          if (to_bf16) {
-            const float2 f = __half22float2(*reinterpret_cast<__half2*>(&w[j]));
-            __nv_bfloat162 b = __floats2bfloat162_rn(f.x, f.y);
-            w[j] = *reinterpret_cast<uint32_t*>(&b);
-          } else {
-            const float2 f = __bfloat1622float2(*reinterpret_cast<__nv_bfloat162*>(&w[j]));
-            __half2 h = __floats2half2_rn(f.x, f.y);
-            w[j] = *reinterpret_cast<uint32_t*>(&h);
-          }
+      for (int j = 0; j < 4; ++j) {
+        if (to_bf16) {
+          const float2 f = __half22float2(*reinterpret_cast<__half2*>(&w[j]));
+          __nv_bfloat162 b = __floats2bfloat162_rn(f.x, f.y);
+          w[j] = *reinterpret_cast<uint32_t*>(&b);
+        } else {
+          const float2 f = __bfloat1622float2(*reinterpret_cast<__nv_bfloat162*>(&w[j]));
+          __half2 h = __floats2half2_rn(f.x, f.y);
+          w[j] = *reinterpret_cast<uint32_t*>(&h);
         }
       }
-      if (dsplit) {
-        uint2* d2 = reinterpret_cast<uint2*>(xs + static_cast<int64_t>(s) * IN);
-        d2[i] = make_uint2(v.x, v.y);
-        d2[vec + i] = make_uint2(v.z, v.w);
-      } else {
-        dst[i] = v;
-      }
+    }
+    if (dsplit) {
+      uint2* d2 = reinterpret_cast<uint2*>(xs + static_cast<int64_t>(s) * IN);
+      d2[i] = make_uint2(v.x, v.y);
+      d2[vec + i] = make_uint2(v.z, v.w);
+    } else {
+      reinterpret_cast<uint4*>(xs + static_cast<int64_t>(s) * IN)[i] = v;
     }
   }
 }
 
 // Split-K: y[pair, row] = the sum of a tile's ksplit fp32 partials in split
 // order, with the output rounding (one thread per (tile, column, row), rows
-// fastest; cmax bounds the columns any chunk holds).
+// fastest; cmax = the partial slot's columns, the most tokens a chunk holds).
+// With a row table a dead row stores +0 (the GEMM epilogue's rule: no compact
+// row, or one outside its tile's staged window).
 __global__ void splitk_reduce_kernel(const float* __restrict__ partial, const int* __restrict__ meta,
                                      const int4* __restrict__ chunks, const int* __restrict__ sorted, int row_tiles,
-                                     int S, int OUT, int cmax, void* y, int y_dtype, int round_f16_first) {
+                                     int S, int OUT, int cmax, void* y, int y_dtype, int round_f16_first,
+                                     const int32_t* __restrict__ row_table, const int* __restrict__ tile_base,
+                                     int64_t nrows) {
   const int64_t ntiles = static_cast<int64_t>(meta[0]) * row_tiles;
   const int64_t total = ntiles * cmax * kTileM;
   for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
@@ -1001,8 +1006,15 @@ __global__ void splitk_reduce_kernel(const float* __restrict__ partial, const in
     if (c >= ch.z || r >= OUT) continue;
     float v = 0.0f;
     for (int sp = 0; sp < S; ++sp) {
-      const float pv = partial[((ti * S + sp) * kMaxN + c) * kTileM + lr];
+      const float pv = partial[((ti * S + sp) * cmax + c) * kTileM + lr];
       v = sp == 0 ? pv : v + pv;
+    }
+    if (row_table) {
+      const int rt = static_cast<int>(ti % row_tiles);
+      const int tb = tile_base[ch.x * row_tiles + rt];
+      const int64_t crow = row_table[static_cast<int64_t>(ch.x) * OUT + r];
+      const int64_t o = crow - tb;
+      if (!(crow >= 0 && crow < nrows && tb >= 0 && o >= 0 && o < kTileM)) v = 0.0f;
     }
     store_y(y, static_cast<int64_t>(sorted[ch.y + c]) * OUT + r, v, y_dtype, round_f16_first != 0);
   }
@@ -1181,18 +1193,32 @@ bool tc_prefill_supported(const LinearGeometry& geo) {
   return true;
 }
 
-// Split-K for dense layers (E = 1) whose tiles cannot fill the GPU: each
-// tile's windows are cut into ksplit contiguous ranges, one work item each,
-// when fewer tiles than half the SMs exist (at most 8 ranges, at least 4
-// windows of 256 k each).
+// Upper bound on the tiles of a call: chunks of <= 128 tokens per expert
+// (at most the distinct experts plus N / 128 of them) times the row tiles.
+static int64_t tiles_bound(int64_t N, int E, int OUT) {
+  const int64_t chunks = E == 1 ? (N + kMaxN - 1) / kMaxN : std::min<int64_t>(N, E) + N / kMaxN;
+  return chunks * ((OUT + kTileM - 1) / kTileM);
+}
+// Columns of a split-K partial slot: the most tokens a chunk can hold.
+static int partial_cols(int64_t N) { return static_cast<int>(std::min<int64_t>(kMaxN, (N + 15) & ~int64_t(15))); }
+
+// Split-K for calls whose tiles cannot fill the GPU (a dense layer with few
+// row tiles, a decode batch over a few experts): each tile's IN / 256 windows
+// are cut into ksplit contiguous ranges, one work item each.  ksplit
+// minimises (items per SM, rounded up) x (windows per item + 2, the per-item
+// fixed cost), over 1..8 ranges of at least 2 windows, for the tile bound.
 int tc_prefill_ksplit(int64_t N, int E, int OUT, int IN) {
-  if (E != 1 || N <= 0 || IN <= 0 || ensure_device_attrs() != VQB_OK) return 1;
-  const int64_t tiles = ((N + kMaxN - 1) / kMaxN) * ((OUT + kTileM - 1) / kTileM);
-  if (tiles * 2 > g_sms_tc) return 1;
-  int64_t S = g_sms_tc / tiles;
-  S = std::min<int64_t>(S, 8);
-  S = std::min<int64_t>(S, IN / 1024);
-  return static_cast<int>(std::max<int64_t>(S, 1));
+  if (N <= 0 || IN <= 0 || ensure_device_attrs() != VQB_OK) return 1;
+  const int64_t tiles = tiles_bound(N, E, OUT);
+  if (tiles > 2 * static_cast<int64_t>(g_sms_tc)) return 1;
+  const int64_t nwt = IN / 256;
+  int best = 1;
+  int64_t best_cost = -1;
+  for (int S = 1; S <= 8 && nwt / S >= 2; ++S) {
+    const int64_t cost = ((tiles * S + g_sms_tc - 1) / g_sms_tc) * ((nwt + S - 1) / S + 2);
+    if (best_cost < 0 || cost < best_cost) { best_cost = cost; best = S; }
+  }
+  return best;
 }
 
 // Workspace of one grouped-GEMM call after the routing tables: x gathered in
@@ -1205,8 +1231,7 @@ static size_t split_cb_bytes(int K, int D) {
 static size_t partial_bytes(int64_t N, int E, int OUT, int IN) {
   const int S = tc_prefill_ksplit(N, E, OUT, IN);
   if (S <= 1) return 0;
-  const int64_t tiles = ((N + kMaxN - 1) / kMaxN) * ((OUT + kTileM - 1) / kTileM);
-  return static_cast<size_t>(tiles) * S * kMaxN * kTileM * sizeof(float);
+  return static_cast<size_t>(tiles_bound(N, E, OUT)) * S * partial_cols(N) * kTileM * sizeof(float);
 }
 
 size_t tc_prefill_x_bytes(int64_t N, int IN, int K, int D, int E, int OUT) {
@@ -1264,6 +1289,7 @@ vqb_status launch_prefill_tc(const LinearGeometry& geo, const void* x, int x_dty
   if (smem == 0) return VQB_UNSUPPORTED_GEOMETRY;
   uint16_t* cb_split = ds ? reinterpret_cast<uint16_t*>(reinterpret_cast<char*>(xs) + xs_bytes(N, geo.IN)) : nullptr;
   prm.ksplit = tc_prefill_ksplit(N, geo.E, geo.OUT, geo.IN);
+  prm.pcols = partial_cols(N);
   {
     // the code bytes of a group read twice stay in L2: 256 KB per CTA (37 MB over 148 SMs)
     constexpr int64_t kGroupCodeBudget = 256 * 1024;
@@ -1279,7 +1305,7 @@ vqb_status launch_prefill_tc(const LinearGeometry& geo, const void* x, int x_dty
   {
     if (x_dtype != VQB_F16 && x_dtype != VQB_BF16) return VQB_UNSUPPORTED_GEOMETRY;
     if ((reinterpret_cast<uintptr_t>(x) & 15) != 0) return VQB_BAD_ALIGNMENT;
-    int64_t blocks = (static_cast<int64_t>(N) + 7) / 8;
+    int64_t blocks = (static_cast<int64_t>(N) * (geo.IN / 8) + 255) / 256;
     if (blocks > 16 * g_sms_tc) blocks = 16 * g_sms_tc;
     gather_sorted_kernel<<<static_cast<unsigned>(blocks), 256, 0, stream>>>(x, x_dtype, rw.sorted, N, krep, geo.IN,
                                                                             bf16_operands ? 1 : 0, ds ? 1 : 0, xs);
@@ -1336,13 +1362,13 @@ vqb_status launch_prefill_tc(const LinearGeometry& geo, const void* x, int x_dty
   if (ce != cudaSuccess || cudaGetLastError() != cudaSuccess) return VQB_CUDA_ERROR;
   note_launch();
   if (prm.ksplit > 1) {
-    const int cmax = static_cast<int>(std::min<int64_t>(kMaxN, (static_cast<int64_t>(N) + 15) & ~int64_t(15)));
-    const int64_t tiles = ((static_cast<int64_t>(N) + kMaxN - 1) / kMaxN) * prm.row_tiles;
+    const int cmax = prm.pcols;
+    const int64_t tiles = tiles_bound(N, geo.E, geo.OUT);
     int64_t blocks = (tiles * cmax * kTileM + 255) / 256;
     if (blocks > 8 * g_sms_tc) blocks = 8 * g_sms_tc;
     splitk_reduce_kernel<<<static_cast<unsigned>(blocks), 256, 0, stream>>>(
         prm.partial, rw.meta, rw.chunks, rw.sorted, prm.row_tiles, prm.ksplit, geo.OUT, cmax, y, y_dtype,
-        round_f16_first ? 1 : 0);
+        round_f16_first ? 1 : 0, geo.row_table, rw.tile_base, geo.nrows);
     if (cudaGetLastError() != cudaSuccess) return VQB_CUDA_ERROR;
     note_launch();
   }

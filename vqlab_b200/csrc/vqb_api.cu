@@ -208,15 +208,16 @@ static bool switch_uses_gemm(const LinearGeometry& geo, int N, const vqb_options
   // amortises, so on a B200 it pays once pairs * IN exceed ~4608 per expert as
   // well.  A d8 codebook too large for shared memory changes the balance: the
   // decode kernel then reads part of the codebook through L1/L2 while the
-  // GEMM keeps half of every entry resident per pass, and the GEMM wins from a
-  // few dozen pairs on.  Measured (512 experts, d8/K16384, uniform routing,
-  // ms per call, GEMM vs decode):
-  //   1024 x 4096 gate:  10 pairs 0.068 vs 0.063;  40: 0.096 vs 0.115;
-  //                      1.25 pairs/expert 0.50 vs 0.79;  10: 0.68 vs 2.81
-  //   4096 x 1024 down:  10 pairs 0.067 vs 0.062;  40: 0.091 vs 0.107;
-  //                      1.25 pairs/expert 0.57 vs 0.71;  10: 0.82 vs 2.62
+  // GEMM keeps half of every entry resident per pass (and splits K over CTAs
+  // when a call has few tiles), and the GEMM wins at every batch.  Measured
+  // (512 experts, d8/K16384, uniform routing, device time per call, us,
+  // GEMM vs decode):
+  //   1024 x 4096 gate:  10 pairs 35.7 vs 40.1;  20: 58.7 vs 61.6;  30: 61.5 vs 84.3;
+  //                      1.25 pairs/expert 500 vs 790;  10: 680 vs 2810
+  //   4096 x 1024 down:  10 pairs 36.5 vs 38.0;  20: 52.6 vs 57.6;  30: 68.1 vs 78.4;
+  //                      1.25 pairs/expert 570 vs 710;  10: 820 vs 2620
   constexpr int64_t kGemmPairInPerExpert = 4608;
-  constexpr int kDsplitMinPairs = 32;
+  constexpr int kDsplitMinPairs = 0;
   const int path = opts ? opts->path : VQB_PATH_AUTO;
   const int max_fused = (opts && opts->max_fused_pairs > 0) ? opts->max_fused_pairs : 512;
   const bool dsplit_gemm = N > kDsplitMinPairs && !(opts && opts->max_fused_pairs > 0) && tc_prefill_dsplit(geo);
