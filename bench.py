@@ -201,7 +201,10 @@ def make_layer(torch, dev, seed, rank=0, world=1):
 
     if world == 1:
         return VQMoEBlock(proj(INTER, HIDDEN), proj(INTER, HIDDEN), proj(HIDDEN, INTER), TOPK)
-    return EPMoEBlock(proj(INTER, HIDDEN), proj(INTER, HIDDEN), proj(HIDDEN, INTER), TOPK, num_experts=E)
+    # decode batches take the fixed-shape path that CUDA graphs capture (gpu_arm sets
+    # static_tokens to the batch it runs; larger batches take the dynamic path)
+    return EPMoEBlock(proj(INTER, HIDDEN), proj(INTER, HIDDEN), proj(HIDDEN, INTER), TOPK, num_experts=E,
+                      static_tokens=64)
 
 
 def distinct_experts(torch, logits):
@@ -386,10 +389,9 @@ def prefill_leg(torch, dev, args, peak_tf, peak_kind, rank, world):
     if world == 1:
         xg, gidx = x[:, None, None, :], idx
     else:
-        xr, er = layer.last_recv
-        xg, gidx = xr.reshape(-1, 1, 1, HIDDEN), er.reshape(-1, 1)
+        xg, gidx = layer.last_pairs
     dur = kernel_seconds(torch, s, lambda i: layer.gate_proj(xg, gidx), 5)
-    kflops = 2 * INTER * HIDDEN * int(gidx.numel())
+    kflops = 2 * INTER * HIDDEN * int((gidx >= 0).sum())
     ach = kflops / dur / 1e12
     return {"metric": "VQ-MoE prefill TFLOP/s (one MoE layer, C3: 4096 tokens, Zipf(1.1) top-10)",
             "value": round(flops * steps * world / secs / 1e12, 2), "unit": "TFLOP/s", "steps": steps,
@@ -400,7 +402,7 @@ def prefill_leg(torch, dev, args, peak_tf, peak_kind, rank, world):
             "roofline": {"bound": "tensor", "achieved": round(ach, 1), "peak": peak_tf, "unit": "TFLOP/s",
                          "frac": round(ach / peak_tf, 4),
                          "traffic": profiled_traffic("vq_prefill_tc_kernel", "c3") if world == 1 else None,
-                         "kernel": "vq_prefill_tc_kernel (gate projection, %d pairs on this rank), timed alone" % int(gidx.numel()),
+                         "kernel": "vq_prefill_tc_kernel (gate projection, %d pairs on this rank), timed alone" % int((gidx >= 0).sum()),
                          "us_per_launch": round(dur * 1e6, 1), "peak_kind": f"{peak_kind} burst bf16 GEMM"}}
 
 
@@ -416,6 +418,9 @@ def gpu_arm(args, rank, world, dev):
     results = {}
     launches_per_step = None
     for B in batches:
+        if world > 1:
+            for L in layers:
+                L.static_tokens = B  # the fixed-shape expert-parallel path pads every rank to this batch
         xs = [torch.randn((B, HIDDEN), device=dev, generator=gen).to(torch.bfloat16) for _ in range(n_layers)]
         lg = [torch.randn((B, E), device=dev, generator=gen) for _ in range(n_layers)]
         outs = [None] * n_layers
@@ -424,15 +429,22 @@ def gpu_arm(args, rank, world, dev):
             outs[l] = layers[l](xs[l], lg[l])
         torch.cuda.synchronize()
         graphs = []
-        if world == 1:
+        graph_note = "cuda graphs"
+        try:
             for l in range(n_layers):
                 g = torch.cuda.CUDAGraph()
                 with torch.cuda.graph(g):
                     outs[l] = layers[l](xs[l], lg[l])
                 graphs.append(g)
+        except Exception as e:  # noqa: BLE001 - a capture the backend refuses: eager steps instead
+            graphs = []
+            graph_note = f"eager steps (graph capture failed: {type(e).__name__})"
+            torch.cuda.synchronize()
         torch.cuda.synchronize()
+        if world > 1:
+            torch.distributed.barrier()
         with ClockSampler(dev.index if dev.index is not None else 0) as clk:
-            if world == 1:
+            if graphs:
                 secs = time_graph_steps(torch, graphs, args.steps, args.warmup)
             else:
                 secs = time_eager_steps(torch, layers, xs, lg, args.steps, args.warmup)
@@ -446,7 +458,7 @@ def gpu_arm(args, rank, world, dev):
                       "tokens_per_s": B * args.steps * world / secs,
                       # packed weight bytes of the experts a step touches (one GPU holds them all)
                       "hbm_gbs": avg_bytes * args.steps / secs / 1e9 if world == 1 else None,
-                      "distinct_experts_mean": statistics.mean(nd), "clocks": clk.summary()}
+                      "distinct_experts_mean": statistics.mean(nd), "clocks": clk.summary(), "timing": graph_note}
         del graphs
         torch.cuda.synchronize()
         xs_last, lg_last = xs, lg
@@ -460,17 +472,17 @@ def gpu_arm(args, rank, world, dev):
         from vqlab_b200.moe import route
         idx, _ = route(lgt, TOPK)
     else:
-        # the pairs this rank's experts received in the last expert-parallel step
-        xr, er = layers[0].last_recv
-        x, idx = xr.reshape(-1, 1, 1, HIDDEN), er.reshape(-1, 1)
-    npairs = int(idx.numel())
-    nd = int(torch.unique(idx).numel())
+        # the pairs this rank's experts served in the last expert-parallel step (-1: another rank's)
+        x, idx = layers[0].last_pairs
+    npairs = int((idx >= 0).sum())
+    nd = int(torch.unique(idx[idx >= 0]).numel())
     for p in projs:
         p(x, idx)
     torch.cuda.synchronize()
     s = torch.cuda.current_stream()
     dur = kernel_seconds(torch, s, lambda i: projs[i % n_layers](x, idx), max(3, args.steps))
-    alg = nd * EXPERT_BYTES["gate"] + CODEBOOK_BYTES + x.shape[0] * HIDDEN * 2 + npairs * INTER * 2
+    rows = int((idx >= 0).reshape(x.shape[0], -1).any(dim=1).sum())  # token rows the served pairs read
+    alg = nd * EXPERT_BYTES["gate"] + CODEBOOK_BYTES + rows * HIDDEN * 2 + npairs * INTER * 2
     achieved = alg / dur / 1e9
     kname = ("vq_prefill_tc_kernel" if projs[0].kernel_path(x.shape[0], idx.shape[-1]) == "gemm"
              else "vq_decode_mma_kernel")
@@ -481,28 +493,60 @@ def gpu_arm(args, rank, world, dev):
             "algorithmic_bytes_per_launch": alg, "us_per_launch": round(dur * 1e6, 2),
             "peak_kind": f"{peak_kind} burst copy bandwidth"}
 
-    # ---- e2e through the public API with host buffers
+    # ---- e2e through the public API with host buffers: every step copies its
+    # inputs from pinned host memory into the layer's input buffers, runs the
+    # layer (replaying the graph captured from the same public calls, or
+    # eagerly when capture is refused) and reads the result back to the host
     e2e = None
     if not args.skip_e2e:
         xh = torch.randn((B, HIDDEN)).to(torch.bfloat16).pin_memory()
         lh = torch.randn((B, E)).pin_memory()
         yh = torch.empty((B, HIDDEN), dtype=torch.bfloat16).pin_memory()
+        xin = [torch.empty((B, HIDDEN), dtype=torch.bfloat16, device=dev) for _ in range(n_layers)]
+        lin = [torch.empty((B, E), device=dev) for _ in range(n_layers)]
+        for l in range(n_layers):
+            xin[l].copy_(xh)
+            lin[l].copy_(lh)
+        youts = [None] * n_layers
+        egraphs = []
+        try:
+            for l in range(n_layers):
+                youts[l] = layers[l](xin[l], lin[l])
+            torch.cuda.synchronize()
+            for l in range(n_layers):
+                g = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(g):
+                    youts[l] = layers[l](xin[l], lin[l])
+                egraphs.append(g)
+        except Exception:  # noqa: BLE001 - capture refused: eager layer calls
+            egraphs = []
+            torch.cuda.synchronize()
+
+        def e2e_step(i):
+            l = i % n_layers
+            xin[l].copy_(xh, non_blocking=True)
+            lin[l].copy_(lh, non_blocking=True)
+            if egraphs:
+                egraphs[l].replay()
+                y = youts[l]
+            else:
+                y = layers[l](xin[l], lin[l])
+            yh.copy_(y, non_blocking=True)
+            s.synchronize()
+
         for i in range(args.warmup):
-            layers[i % n_layers](xh.to(dev, non_blocking=True), lh.to(dev, non_blocking=True))
+            e2e_step(i)
         torch.cuda.synchronize()
         if world > 1:
             torch.distributed.barrier()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record(s)
         for i in range(args.steps):
-            xd = xh.to(dev, non_blocking=True)
-            ld = lh.to(dev, non_blocking=True)
-            yd = layers[i % n_layers](xd, ld)
-            yh.copy_(yd, non_blocking=True)
-            s.synchronize()
+            e2e_step(i)
         e1.record(s)
         torch.cuda.synchronize()
         secs = e0.elapsed_time(e1) / 1e3
+        del egraphs
         if world > 1:
             t = torch.tensor([secs], device=dev)
             torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)

@@ -109,10 +109,16 @@ const char* vqb_status_string(vqb_status status);
 vqb_status vqb_unpack(const uint32_t* packed, int64_t rows, int64_t wpr, int32_t nsub,
                       int32_t bits, uint16_t* out, vqb_stream_t stream);
 
+/* Expert index of a pair to leave out: vqb_switch_forward computes nothing
+ * for it and does not write its output row (expert parallelism marks the
+ * pairs another rank serves this way, with no host-side compaction). */
+#define VQB_SKIP_EXPERT 0xFFFFFFFFu
+
 /* Scratch bytes vqb_switch_forward needs for n_tokens x top_k pairs.  The
  * first 16 bytes of the workspace are a status block the call rewrites:
- * int32 [1] is set to VQB_BAD_ROUTING when an expert index >= E was seen
- * (such a pair is computed as expert 0, never read out of range). */
+ * int32 [1] is set to VQB_BAD_ROUTING when an expert index >= E (other than
+ * VQB_SKIP_EXPERT) was seen (such a pair is computed as expert 0, never read
+ * out of range). */
 size_t vqb_switch_workspace_size(const vqb_linear_desc* desc, int32_t n_tokens, int32_t top_k,
                                  const vqb_options* opts);
 
@@ -167,6 +173,15 @@ vqb_status vqb_switch_forward_static(const vqb_linear_desc* desc, const void* x,
 vqb_status vqb_swiglu(const void* gate, const void* up, void* out, int64_t n, vqb_dtype dtype, vqb_stream_t stream);
 vqb_status vqb_moe_combine(const void* expert_out, const float* weights, void* out, int32_t n_tokens,
                            int32_t top_k, int32_t hidden, vqb_dtype dtype, vqb_stream_t stream);
+
+/* Expert-parallel partial combine: out[t, :] = sum_j w[t, j] * expert_out[t, j, :]
+ * over the slots whose indices[t, j] != VQB_SKIP_EXPERT (indices may be NULL:
+ * every slot), slot order, fp32 out [n_tokens, hidden] with no rounding; a
+ * skipped slot's expert_out row is never read.  No reference counterpart
+ * (the reference runs every expert on one device). */
+vqb_status vqb_moe_combine_partial(const void* expert_out, const float* weights, const uint32_t* indices, float* out,
+                                   int32_t n_tokens, int32_t top_k, int32_t hidden, vqb_dtype dtype,
+                                   vqb_stream_t stream);
 
 /* Measurement aids; neither has a counterpart in the reference, whose Metal
  * runtime exposes no launch accounting or per-kernel timing.

@@ -54,7 +54,7 @@ def _inputs(rank, T, skew):
     return x, logits
 
 
-def _worker(rank, world, port, out_dir, sizes, skew):
+def _worker(rank, world, port, out_dir, sizes, skew, static=None):
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
     dist.init_process_group("gloo", rank=rank, world_size=world)
@@ -65,7 +65,7 @@ def _worker(rank, world, port, out_dir, sizes, skew):
         def experts(xp, local):
             return _expert_rows(xp, local.long() + rank * n, W)
 
-        blk = EPMoEBlock(None, None, None, top_k=K, num_experts=E, experts=experts)
+        blk = EPMoEBlock(None, None, None, top_k=K, num_experts=E, experts=experts, static_tokens=static)
         x, logits = _inputs(rank, sizes[rank], skew)
         y = blk(x, logits)
         ref = _reference(x, logits, W)
@@ -97,6 +97,21 @@ def test_ep_two_ranks_matches_single_process(tmp_path, sizes, skew):
         assert d["y"].shape == (sizes[r], H)
         assert torch.allclose(d["y"], d["ref"], rtol=1e-12, atol=1e-12)
         assert d["refused"]  # 7 experts do not split over 2 ranks
+
+
+@pytest.mark.parametrize("sizes,skew", [((5, 7), False), ((0, 4), False), ((6, 6), True)])
+def test_ep_static_path_matches_single_process(tmp_path, sizes, skew):
+    """The fixed-shape decode path (all-gather, pairs of other ranks skipped,
+    fp32 partial combine returned by one all-to-all): same pairs, the slot
+    sums grouped by rank, so agreement is to fp32 rounding."""
+    world = 2
+    mp.start_processes(_worker, args=(world, _free_port(), str(tmp_path), sizes, skew, 8), nprocs=world,
+                       join=True, start_method="spawn")
+    for r in range(world):
+        d = torch.load(tmp_path / f"r{r}.pt")
+        assert d["y"].shape == (sizes[r], H)
+        tol = 1e-5 * float(d["ref"].abs().max()) if sizes[r] else 0.0
+        assert torch.allclose(d["y"], d["ref"], rtol=1e-5, atol=tol)
 
 
 def test_dispatch_plan_single_rank_orders_stably():

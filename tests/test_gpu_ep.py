@@ -32,7 +32,7 @@ def _proj_np(rng, out, inn):
     return packed, cb, sc
 
 
-def _worker(rank, world, port, out_dir):
+def _worker(rank, world, port, out_dir, static=None):
     import datetime
     import torch.distributed as dist
     from vqlab_b200 import VQSwitchLinear
@@ -62,7 +62,7 @@ def _worker(rank, world, port, out_dir):
                                   in_features=inn)
 
         single = VQMoEBlock(full(P[0], H), full(P[1], H), full(P[2], I), K)
-        ep = EPMoEBlock(shard(P[0], H), shard(P[1], H), shard(P[2], I), K, num_experts=E)
+        ep = EPMoEBlock(shard(P[0], H), shard(P[1], H), shard(P[2], I), K, num_experts=E, static_tokens=static)
         g = torch.Generator().manual_seed(7 + rank)
         x = torch.randn((T + 3 * rank, H), generator=g).to(torch.bfloat16).to(dev)
         lg = torch.randn((T + 3 * rank, E), generator=g).to(dev)
@@ -70,15 +70,28 @@ def _worker(rank, world, port, out_dir):
         y_ep = ep(x, lg)
         y_ref = single(x, lg)
         torch.cuda.synchronize()
+        if static:
+            # the fixed-shape path has no host synchronisation: it replays from a CUDA graph
+            gr = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(gr):
+                y_g = ep(x, lg)
+            gr.replay()
+            torch.cuda.synchronize()
+            assert torch.equal(y_g, y_ep)
+            del gr
         torch.save({"ep": y_ep.float().cpu(), "ref": y_ref.float().cpu()}, os.path.join(out_dir, f"r{rank}.pt"))
     finally:
         dist.destroy_process_group()
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
-def test_ep_two_gpus_matches_single_gpu_block(tmp_path):
+@pytest.mark.parametrize("static", [None, 64])
+def test_ep_two_gpus_matches_single_gpu_block(tmp_path, static):
+    """Both dispatch paths: the dynamic one (exact split sizes read on the host)
+    and the fixed-shape decode path (all-gather, skipped pairs, fp32 partial
+    combine), which must also replay from a CUDA graph with its NCCL calls."""
     world = 2
-    mp.start_processes(_worker, args=(world, _free_port(), str(tmp_path)), nprocs=world, join=True,
+    mp.start_processes(_worker, args=(world, _free_port(), str(tmp_path), static), nprocs=world, join=True,
                        start_method="spawn")
     for r in range(world):
         d = torch.load(tmp_path / f"r{r}.pt")

@@ -100,6 +100,8 @@ def _bind(L):
     L.vqb_time_next_kernel.argtypes = [P, P]
     L.vqb_switch_path.restype = i32
     L.vqb_switch_path.argtypes = [P, i32, i32, P]
+    L.vqb_moe_combine_partial.restype = i32
+    L.vqb_moe_combine_partial.argtypes = [P, P, P, P, i32, i32, i32, i32, P]
     return L
 
 
@@ -144,7 +146,8 @@ def exported_symbols():
     """Names of every function include/vqb.h declares (for the load test)."""
     return ["vqb_version", "vqb_status_string", "vqb_unpack", "vqb_switch_workspace_size",
             "vqb_switch_forward", "vqb_dense_workspace_size", "vqb_dense_forward", "vqb_switch_forward_static",
-            "vqb_launch_count", "vqb_time_next_kernel", "vqb_swiglu", "vqb_moe_combine", "vqb_switch_path"]
+            "vqb_launch_count", "vqb_time_next_kernel", "vqb_swiglu", "vqb_moe_combine", "vqb_switch_path",
+            "vqb_moe_combine_partial"]
 
 
 def launch_count() -> int:

@@ -134,6 +134,7 @@ __global__ void __launch_bounds__(256) vq_decode_kernel(const DecodeParams prm) 
   for (int p = blockIdx.y; p < prm.N; p += gridDim.y) {
     const int t = p / prm.krep;
     uint32_t e = prm.idx ? prm.idx[p] : 0u;
+    if (e == kSkipExpert) continue;  // a pair left out: no output row (uniform over the CTA)
     if (e >= static_cast<uint32_t>(prm.E)) {
       // routing error: report once and treat the pair as expert 0 (no OOB read)
       if (prm.err && threadIdx.x == 0) atomicExch(prm.err, static_cast<int>(VQB_BAD_ROUTING));

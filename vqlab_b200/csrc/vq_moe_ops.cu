@@ -95,6 +95,43 @@ __global__ void combine_kernel(const T* __restrict__ d, const float* __restrict_
   }
 }
 
+// Partial combine for expert parallelism: out[t, :] = sum over this rank's
+// slots j (skip[t, j] != kSkipExpert) of w[t, j] * f32(d[t, j, :]), in slot
+// order, kept in fp32 (the owner of token t adds the ranks' partials).  A
+// skipped slot's d row is never read.
+template <typename T, int VEC>
+__global__ void combine_partial_kernel(const T* __restrict__ d, const float* __restrict__ w,
+                                       const uint32_t* __restrict__ skip, float* __restrict__ y, int Tn, int k,
+                                       int H) {
+  const int per_tok = H / VEC;
+  const int64_t total = static_cast<int64_t>(Tn) * per_tok;
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int t = static_cast<int>(i / per_tok);
+    const int c = static_cast<int>(i - static_cast<int64_t>(t) * per_tok);
+    float acc[VEC];
+#pragma unroll
+    for (int e = 0; e < VEC; ++e) acc[e] = 0.0f;
+    for (int j = 0; j < k; ++j) {
+      if (skip && __ldg(skip + static_cast<int64_t>(t) * k + j) == kSkipExpert) continue;
+      const float wj = __ldg(w + static_cast<int64_t>(t) * k + j);
+      const T* row = d + (static_cast<int64_t>(t) * k + j) * H + static_cast<int64_t>(c) * VEC;
+      T v[VEC];
+      if constexpr (VEC * sizeof(T) == 16) {
+        *reinterpret_cast<uint4*>(v) = __ldg(reinterpret_cast<const uint4*>(row));
+      } else {
+#pragma unroll
+        for (int e = 0; e < VEC; ++e) v[e] = row[e];
+      }
+#pragma unroll
+      for (int e = 0; e < VEC; ++e) acc[e] = __fadd_rn(acc[e], __fmul_rn(to_f(v[e]), wj));
+    }
+    float* out = y + static_cast<int64_t>(t) * H + static_cast<int64_t>(c) * VEC;
+#pragma unroll
+    for (int e = 0; e < VEC; ++e) out[e] = acc[e];
+  }
+}
+
 int g_sms_ops = 0;
 
 vqb_status ensure_sms() {
@@ -144,6 +181,22 @@ vqb_status launch_combine(const void* d, const float* w, void* y, int Tn, int k,
   return VQB_OK;
 }
 
+template <typename T>
+vqb_status launch_combine_partial(const void* d, const float* w, const uint32_t* skip, float* y, int Tn, int k, int H,
+                                  cudaStream_t s) {
+  constexpr int V = 16 / sizeof(T);
+  if (H % V == 0 && aligned16(d)) {
+    combine_partial_kernel<T, V><<<grid_for(static_cast<int64_t>(Tn) * (H / V)), 256, 0, s>>>(
+        static_cast<const T*>(d), w, skip, y, Tn, k, H);
+  } else {
+    combine_partial_kernel<T, 1><<<grid_for(static_cast<int64_t>(Tn) * H), 256, 0, s>>>(static_cast<const T*>(d), w,
+                                                                                       skip, y, Tn, k, H);
+  }
+  if (cudaGetLastError() != cudaSuccess) return VQB_CUDA_ERROR;
+  note_launch();
+  return VQB_OK;
+}
+
 }  // namespace
 
 }  // namespace vqb
@@ -175,5 +228,21 @@ extern "C" vqb_status vqb_moe_combine(const void* expert_out, const float* weigh
   if (dtype == VQB_BF16) return launch_combine<__nv_bfloat16>(expert_out, weights, out, n_tokens, top_k, hidden, s);
   if (dtype == VQB_F16) return launch_combine<__half>(expert_out, weights, out, n_tokens, top_k, hidden, s);
   if (dtype == VQB_F32) return launch_combine<float>(expert_out, weights, out, n_tokens, top_k, hidden, s);
+  return VQB_BAD_SHAPE;
+}
+
+extern "C" vqb_status vqb_moe_combine_partial(const void* expert_out, const float* weights, const uint32_t* indices,
+                                              float* out, int32_t n_tokens, int32_t top_k, int32_t hidden,
+                                              vqb_dtype dtype, vqb_stream_t stream) {
+  if (n_tokens < 0 || top_k < 1 || hidden < 1) return VQB_BAD_SHAPE;
+  if (n_tokens == 0) return VQB_OK;
+  if (!expert_out || !weights || !out) return VQB_NULL_POINTER;
+  vqb_status st = ensure_sms();
+  if (st != VQB_OK) return st;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  if (dtype == VQB_BF16)
+    return launch_combine_partial<__nv_bfloat16>(expert_out, weights, indices, out, n_tokens, top_k, hidden, s);
+  if (dtype == VQB_F16) return launch_combine_partial<__half>(expert_out, weights, indices, out, n_tokens, top_k, hidden, s);
+  if (dtype == VQB_F32) return launch_combine_partial<float>(expert_out, weights, indices, out, n_tokens, top_k, hidden, s);
   return VQB_BAD_SHAPE;
 }

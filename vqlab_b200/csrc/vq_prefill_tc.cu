@@ -948,11 +948,12 @@ __global__ void tile_base_kernel(const int32_t* __restrict__ rt, int E, int OUT,
 // (IN % 64 == 0 and an aligned base).  dsplit: the dimension-split order --
 // elements 8j .. 8j+3 go to columns 4j .. 4j+3 and elements 8j+4 .. 8j+7 to
 // IN/2 + 4j .. (the x side of decode_pos_dsplit's column order).
-__global__ void gather_sorted_kernel(const void* __restrict__ x, int x_dtype, const int* __restrict__ sorted, int N,
-                                     int krep, int IN, int to_bf16, int dsplit, uint16_t* __restrict__ xs) {
+__global__ void gather_sorted_kernel(const void* __restrict__ x, int x_dtype, const int* __restrict__ sorted,
+                                     const int* __restrict__ n_sorted, int krep, int IN, int to_bf16, int dsplit,
+                                     uint16_t* __restrict__ xs) {
   const int vec = IN / 8;
   const bool convert = (x_dtype == VQB_BF16) != (to_bf16 != 0);
-  const int64_t total = static_cast<int64_t>(N) * vec;
+  const int64_t total = static_cast<int64_t>(*n_sorted) * vec;  // pairs left out are not in sorted
   for (int64_t q = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; q < total;
        q += static_cast<int64_t>(gridDim.x) * blockDim.x) {
     const int s = static_cast<int>(q / vec), i = static_cast<int>(q - static_cast<int64_t>(s) * vec);
@@ -1307,7 +1308,8 @@ vqb_status launch_prefill_tc(const LinearGeometry& geo, const void* x, int x_dty
     if ((reinterpret_cast<uintptr_t>(x) & 15) != 0) return VQB_BAD_ALIGNMENT;
     int64_t blocks = (static_cast<int64_t>(N) * (geo.IN / 8) + 255) / 256;
     if (blocks > 16 * g_sms_tc) blocks = 16 * g_sms_tc;
-    gather_sorted_kernel<<<static_cast<unsigned>(blocks), 256, 0, stream>>>(x, x_dtype, rw.sorted, N, krep, geo.IN,
+    gather_sorted_kernel<<<static_cast<unsigned>(blocks), 256, 0, stream>>>(x, x_dtype, rw.sorted, rw.offsets + geo.E,
+                                                                            krep, geo.IN,
                                                                             bf16_operands ? 1 : 0, ds ? 1 : 0, xs);
     if (cudaGetLastError() != cudaSuccess) return VQB_CUDA_ERROR;
     note_launch();

@@ -11,7 +11,8 @@
 //                      argsort), so tile contents -- and with them the
 //                      GEMM's summation order -- are the same on every call
 //   chunks[*]          (expert, first sorted slot, pair count <= max_pairs)
-//   meta[0]            number of chunks; meta[1] error flag (expert id >= E);
+//   meta[0]            number of chunks; meta[1] error flag (expert id >= E,
+//                      other than kSkipExpert, which marks a pair to leave out);
 //                      the kernel clears meta[0..3] first
 // One CTA handles the whole batch.  Warp w owns the contiguous pair range
 // [w*per, (w+1)*per): it counts its pairs per expert into its own row of a
@@ -28,10 +29,14 @@ namespace {
 
 constexpr int kRouteWarpsMax = 32;   // 1024 threads; small batches use 8 warps (less table to clear)
 
+// The pair's expert, kSkipExpert for a pair to leave out (no chunk holds it,
+// its output row is not written), else an index >= E is reported and the
+// pair routed to expert 0 so no read goes out of range.
 __device__ __forceinline__ uint32_t expert_of(const uint32_t* idx, int p, int E, int* meta) {
   uint32_t e = idx ? idx[p] : 0u;
+  if (e == kSkipExpert) return e;
   if (e >= static_cast<uint32_t>(E)) {
-    meta[1] = VQB_BAD_ROUTING;  // reported; the pair is routed to expert 0 so no read goes out of range
+    meta[1] = VQB_BAD_ROUTING;
     e = 0;
   }
   return e;
@@ -58,8 +63,8 @@ __global__ void __launch_bounds__(kRouteWarps * 32) route_small_kernel(const uin
   int* row = tab + wid * E;
   for (int b = lo; b < hi; b += 32) {
     const int p = b + lane;
-    const bool valid = p < hi;
-    const uint32_t e = valid ? expert_of(idx, p, E, ws.meta) : 0xFFFFFFFFu;
+    uint32_t e = p < hi ? expert_of(idx, p, E, ws.meta) : kSkipExpert;
+    const bool valid = e != kSkipExpert;
     const uint32_t peers = __match_any_sync(0xFFFFFFFFu, e);
     if (valid && (peers & lt) == 0) row[e] += __popc(peers);
     __syncwarp();
@@ -132,12 +137,12 @@ __global__ void __launch_bounds__(kRouteWarps * 32) route_small_kernel(const uin
   // 3. stable placement: warp w walks its range again in order
   for (int b = lo; b < hi; b += 32) {
     const int p = b + lane;
-    const bool valid = p < hi;
-    uint32_t e = 0xFFFFFFFFu;
-    if (valid) {
+    uint32_t e = kSkipExpert;
+    if (p < hi) {
       e = idx ? idx[p] : 0u;
-      if (e >= static_cast<uint32_t>(E)) e = 0;
+      if (e != kSkipExpert && e >= static_cast<uint32_t>(E)) e = 0;
     }
+    const bool valid = e != kSkipExpert;
     const uint32_t peers = __match_any_sync(0xFFFFFFFFu, e);
     if (valid) ws.sorted[row[e] + __popc(peers & lt)] = p;
     __syncwarp();

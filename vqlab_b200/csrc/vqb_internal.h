@@ -46,6 +46,7 @@ vqb_status launch_decode(const LinearGeometry& geo, const void* x, int x_dtype, 
 vqb_status launch_unpack(const uint32_t* packed, int64_t rows, int64_t wpr, int nsub, int bits, uint16_t* out,
                          cudaStream_t stream);
 
+constexpr uint32_t kSkipExpert = 0xFFFFFFFFu;  // expert index of a pair to leave out (no output row)
 constexpr int kDecodeMaxPairs = 16;  // route workspace sizing bound (chunks <= N + E either way)
 
 // Expert-grouped decode on the tensor cores (vq_decode_mma.cu).

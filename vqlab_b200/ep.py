@@ -25,6 +25,24 @@ B200 ranks; gloo for the CPU tests).  The expert compute is pluggable so the
 dispatch/combine logic can be tested without a GPU: `experts(x_pairs [R, H],
 local_ids [R]) -> y_pairs [R, H]`; the default runs the three VQSwitchLinear
 projections of this rank.
+
+Decode batches (at most `static_tokens` tokens per rank) take a fixed-shape
+path with no host synchronisation, so a whole layer can be captured in a CUDA
+graph:
+
+  1. every rank pads its tokens to `static_tokens` rows and all-gathers the
+     token rows, expert ids and weights (padding rows route nowhere);
+  2. the pairs of this rank's experts keep their local id, every other pair
+     is marked VQB_SKIP_EXPERT (-1): the projections run on all gathered
+     pairs with no compaction and compute only this rank's;
+  3. each token's slots on this rank are summed in fp32 (slot order,
+     vqb_moe_combine_partial), an all-to-all of equal splits returns each
+     token's partial sum to its owner, and the owner adds the ranks'
+     partials in rank order and rounds once.
+
+The all-gathered rows are world x static_tokens x H; for a decode batch that
+is a few MB over NVLink.  The numerics differ from the single-GPU block only
+in the fp32 summation order over slots (grouped by rank).
 """
 from __future__ import annotations
 
@@ -94,8 +112,10 @@ class EPMoEBlock(torch.nn.Module):
     """
 
     def __init__(self, gate_proj, up_proj, down_proj, top_k: int, num_experts: int, group=None,
-                 experts: Optional[Callable[[torch.Tensor, torch.Tensor], torch.Tensor]] = None):
+                 experts: Optional[Callable[[torch.Tensor, torch.Tensor], torch.Tensor]] = None,
+                 static_tokens: Optional[int] = None):
         super().__init__()
+        self.static_tokens = int(static_tokens) if static_tokens else None
         self.gate_proj, self.up_proj, self.down_proj = gate_proj, up_proj, down_proj
         self.top_k = int(top_k)
         self.group = group
@@ -120,8 +140,56 @@ class EPMoEBlock(torch.nn.Module):
         u = self.up_proj(xe, ids)
         return self.down_proj(swiglu(g, u), ids).reshape(R, -1)
 
+    def _all_gather(self, t: torch.Tensor) -> torch.Tensor:
+        out = t.new_empty((self.world * t.shape[0],) + tuple(t.shape[1:]))
+        if self.world == 1:
+            out.copy_(t)
+        elif t.is_cuda:
+            dist.all_gather_into_tensor(out, t.contiguous(), group=self.group)
+        else:
+            dist.all_gather(list(out.chunk(self.world)), t.contiguous(), group=self.group)
+        return out
+
+    def forward_static(self, x: torch.Tensor, router_logits: torch.Tensor) -> torch.Tensor:
+        """The fixed-shape path (module docstring): T <= static_tokens on every rank."""
+        T, H = x.shape
+        C, k, W, el = self.static_tokens, self.top_k, self.world, self.experts_per_rank
+        if T > C:
+            raise ValueError(f"{T} tokens exceed static_tokens={C}")
+        idx, w = route(router_logits, k)
+        xp = x.new_zeros((C, H))
+        xp[:T] = x
+        ip = torch.full((C, k), -1, dtype=torch.int32, device=x.device)
+        ip[:T] = idx
+        wp = torch.zeros((C, k), dtype=torch.float32, device=x.device)
+        wp[:T] = w
+        X, I, Wt = self._all_gather(xp), self._all_gather(ip), self._all_gather(wp)
+        lo = self.rank * el
+        mine = (I >= lo) & (I < lo + el)
+        ids = torch.where(mine, I - lo, torch.full_like(I, -1))      # -1 = VQB_SKIP_EXPERT
+        self.last_pairs = (X.reshape(W * C, 1, 1, H), ids)          # this rank's pairs (kept for measurement)
+        if X.is_cuda and self._experts == self._vq_experts:
+            from .moe import combine_partial
+            g = self.gate_proj(X.reshape(W * C, 1, 1, H), ids)        # [W*C, k, 1, I]
+            u = self.up_proj(X.reshape(W * C, 1, 1, H), ids)
+            d = self.down_proj(swiglu(g, u), ids)                     # [W*C, k, 1, H]; skipped rows unwritten
+            part = combine_partial(d.reshape(W * C, k, -1), Wt, ids)  # fp32 [W*C, H]
+        else:
+            # pluggable experts (CPU tests): every gathered pair computed, other ranks' masked out
+            yp = self._experts(X.repeat_interleave(k, dim=0), ids.reshape(-1).clamp(min=0)).reshape(W * C, k, -1)
+            part = torch.where(mine.unsqueeze(-1), yp.float() * Wt.unsqueeze(-1),
+                               torch.zeros((), device=x.device)).sum(1)
+        if W > 1:
+            back = torch.empty_like(part)
+            dist.all_to_all_single(back, part.contiguous(), group=self.group)
+        else:
+            back = part
+        return back.reshape(W, C, -1).sum(0)[:T].to(x.dtype)
+
     def forward(self, x: torch.Tensor, router_logits: torch.Tensor) -> torch.Tensor:
         """x [T, H], router_logits [T, E] (this rank's tokens) -> y [T, H] in x's dtype."""
+        if self.static_tokens is not None and x.shape[0] <= self.static_tokens:
+            return self.forward_static(x, router_logits)
         T, H = x.shape
         k = self.top_k
         idx, w = route(router_logits, k)
@@ -143,7 +211,7 @@ class EPMoEBlock(torch.nn.Module):
                                               torch.tensor(plan.recv_counts, device=x.device), output_size=n_recv)
         recv_x = recv_rows.index_select(0, recv_meta[:, 0].long() + src_row0.index_select(0, src_of_pair))
         recv_e = recv_meta[:, 1].contiguous()
-        self.last_recv = (recv_x, recv_e)  # the pairs this rank computed (kept for measurement)
+        self.last_pairs = (recv_x.reshape(-1, 1, 1, H), recv_e.reshape(-1, 1))  # this rank's pairs (measurement)
         y_recv = self._experts(recv_x, recv_e)
         if self.world > 1:
             back = _a2a(y_recv, T * k, plan.send_counts, plan.recv_counts, self.group)

@@ -45,6 +45,28 @@ def combine(d: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
     return y
 
 
+def combine_partial(d: torch.Tensor, w: torch.Tensor, ids: torch.Tensor | None = None) -> torch.Tensor:
+    """fp32 partial combine for expert parallelism: out[t] = sum over the slots
+    j with ids[t, j] != -1 (VQB_SKIP_EXPERT) of w[t, j] * f32 d[t, j], in slot
+    order, no rounding (vqb_moe_combine_partial); a skipped slot's row of d is
+    never read."""
+    if d.dim() != 3 or w.shape != d.shape[:2] or not d.is_cuda or d.dtype not in _DTYPES:
+        raise ValueError("combine_partial: expects d [T, k, H] on CUDA and weights [T, k]")
+    T, k, H = d.shape
+    d = d.contiguous()
+    w = w.to(torch.float32).contiguous()
+    if ids is not None:
+        if ids.shape != (T, k):
+            raise ValueError("combine_partial: ids must be [T, k]")
+        ids = ids.to(torch.int32).contiguous()
+    y = torch.empty((T, H), dtype=torch.float32, device=d.device)
+    _lib.check(_lib.lib().vqb_moe_combine_partial(
+        ctypes.c_void_p(d.data_ptr()), ctypes.c_void_p(w.data_ptr()),
+        ctypes.c_void_p(ids.data_ptr()) if ids is not None else None, ctypes.c_void_p(y.data_ptr()), T, k, H,
+        _DTYPES[d.dtype], _stream_ptr(d.device)), "vqb_moe_combine_partial")
+    return y
+
+
 def route(router_logits: torch.Tensor, top_k: int):
     """fp32 softmax, top-k, renormalise.  Returns (indices int32 [T,k], weights fp32 [T,k])."""
     pr = torch.softmax(router_logits.float(), dim=-1)
