@@ -510,10 +510,8 @@ struct TileRow {
   int64_t crow;
   int woff;
 };
-__device__ __forceinline__ TileRow tile_row(const TParams& prm, int64_t it, int lrow) {
-  const int chunk = item_chunk(prm, it);
+__device__ __forceinline__ TileRow tile_row(const TParams& prm, int64_t it, int lrow, int e) {
   const int rt = item_row_tile(prm, it);
-  const int e = prm.chunks[chunk].x;
   TileRow tr;
   tr.r = rt * kTileM + lrow;
   const int rr = min(tr.r, prm.OUT - 1);
@@ -761,8 +759,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           mbar_expect_tx(cb_full, bytes);
           const unsigned char* src = reinterpret_cast<const unsigned char*>(prm.codebook) +
                                      (DS ? static_cast<int64_t>(h) * prm.K * 8 : first * D * 2);
-          for (uint32_t off = 0; off < bytes; off += 32768u)
-            bulk_load(reinterpret_cast<unsigned char*>(cb_s) + off, src + off, min(32768u, bytes - off), cb_full);
+          for (uint32_t off = 0; off < bytes; off += 8192u)
+            bulk_load(reinterpret_cast<unsigned char*>(cb_s) + off, src + off, min(8192u, bytes - off), cb_full);
           resident = h;
           ++loads;
         }
@@ -800,7 +798,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           int lo, hi;
           item_pass_windows(prm, it, pass_slice(prm.npass, jg, pass), nwin, lo, hi);
           if (lo >= hi) continue;
-          const TileRow tr = tile_row(prm, it, lrow);
+          const TileRow tr = tile_row(prm, it, lrow, prm.chunks[item_chunk(prm, it)].x);
           const int xr = prm.wswz == 1 ? ((tr.woff >> 1) & 3) : (prm.wswz == 2 ? (tr.woff & 7) : 0);
           const uint16_t* srow = prm.scales + (tr.live ? tr.crow : 0) * prm.NGRP;
           for (int w = lo; w < hi; ++w) {
@@ -865,23 +863,27 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       if (!ok) break;
       // epilogue: y = D_0 (+ D_1 when both issuers took part) for every tile of
-      // the group; (tile, 16-column block) pairs dealt round-robin to the 4 sets
+      // the group.  A group of one tile deals its 16-column blocks to the 4
+      // sets; a group of several gives tile t to set t % 4, so each set reads
+      // the routing records of its own tiles only (those global reads are the
+      // epilogue's latency)
       if (!warp_wait(&acc_full[0], static_cast<uint32_t>(jg & 1), abort_flag) ||
           !warp_wait(&acc_full[1], static_cast<uint32_t>(jg & 1), abort_flag))
         break;
       tc_fence_after();
       int blk = 0;
-      for (int t = 0; t < grp.count; ++t) {
+      const bool spread = grp.count == 1;
+      for (int t = spread ? 0 : s; t < grp.count; t += spread ? 1 : kSets) {
         const int64_t it = it0 + static_cast<int64_t>(t) * gridDim.x;
         const int4 ch = prm.chunks[item_chunk(prm, it)];
-        const TileRow tr = tile_row(prm, it, lrow);
+        const TileRow tr = tile_row(prm, it, lrow, ch.x);
         const int ntok = ch.z;
         const int n = (ntok + 15) & ~15;
         const bool two = item_windows(prm, it, nwin) * kSets / slot_positions(slot_rows(ntok)) > 1;
         float* part = prm.ksplit > 1 ? prm.partial + it * (static_cast<int64_t>(prm.pcols) * kTileM) : nullptr;
         const uint32_t d0 = static_cast<uint32_t>(2 * t * grp.n16), d1 = d0 + static_cast<uint32_t>(grp.n16);
         for (int c0 = 0; c0 < n; c0 += 16, ++blk) {
-          if ((blk & (kSets - 1)) != s) continue;
+          if (spread && (blk & (kSets - 1)) != s) continue;
           uint32_t v0[16], v1[16];
           tc_ld_x16(tmem_base + lane_off + d0 + static_cast<uint32_t>(c0), v0);
           tc_ld_x16(tmem_base + lane_off + d1 + static_cast<uint32_t>(c0), v1);
