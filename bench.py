@@ -1,6 +1,6 @@
 """Benchmark: VQ-MoE decode (and prefill) on B200 through the repo's own API.
 
-Workload ("one vq_switch MoE layer, decode"): hidden 4096,
+Workload (benchmark configuration C2, "one vq_switch MoE layer, decode"): hidden 4096,
 512 experts, expert intermediate 1024, top-10 softmax routing from router
 logits ~N(0,1), SwiGLU gate/up [1024 x 4096] and down [4096 x 1024], d=8,
 K=16384 (14-bit packed codes), one fp16 codebook per projection per layer,
@@ -9,17 +9,18 @@ bf16 activations.  Seeded synthetic weights (codes uniform over K, codebook
 
 A step is one MoE layer forward (router top-k, gate, up, SwiGLU, down,
 weighted combine) on the headline batch (64 tokens; 1 and 8 are reported
-beside it).  The prefill leg runs the same layer on 4096
+beside it).  The prefill leg (benchmark configuration C3) runs the same layer on 4096
 tokens with top-10 routing drawn from Zipf(1.1) expert popularity and
 reports TFLOP/s of the three expert projections.  Several independently seeded layers are rotated so the
 weights a step reads are not in L2 from the previous step (the bytes each
 step touches, times the rotation, exceed the 126 MB L2).
 
-Multi-GPU (torchrun, one rank per GPU): expert parallelism (BASELINE config
-5): rank r holds experts [r*E/N, (r+1)*E/N) of every projection, each rank
-brings its own batch of tokens (weak scaling), and every layer dispatches the
-(token, slot) pairs to the owning ranks and combines the outputs back with
-NCCL all-to-alls (vqlab_b200.ep).  `value` is all ranks' tokens over the
+Multi-GPU (torchrun, one rank per GPU): expert parallelism (benchmark configuration
+C5): rank r holds experts [r*E/N, (r+1)*E/N) of every projection, each rank
+brings its own batch of tokens (weak scaling), and every layer sends the
+(token, slot) pairs to the owning ranks and combines the outputs back over
+NCCL (vqlab_b200.ep: a graph-captured fixed-shape path for decode batches, a
+dynamic all-to-all path for prefill).  `value` is all ranks' tokens over the
 max-over-ranks time.  The dispatch reads its split sizes on the host, so
 multi-GPU steps run eagerly (single-GPU steps replay CUDA graphs).
 
@@ -282,11 +283,11 @@ def profiled_traffic(kernel, workload):
     return None
 
 
-DH, DI, DKV = 5120, 17408, 1024   # hidden, MLP intermediate, kv width
+DH, DI, DKV = 5120, 17408, 1024   # benchmark configuration C4: hidden, MLP intermediate, kv width
 
 
 def make_dense_layer(torch, dev, seed):
-    """One BASELINE config-4 layer as VQLinear projections: attention q/k/v/o
+    """One C4 benchmark layer as VQLinear projections: attention q/k/v/o
     with d2/K256 (8-bit codes), MLP gate/up/down with d8/K16384 (14-bit)."""
     from vqlab_b200 import VQLinear
     g = torch.Generator(device=dev)
@@ -317,7 +318,7 @@ def dense_step(layer, x):
 
 
 def dense_leg(torch, dev, args):
-    """a 64-layer dense stack at batch 1 and 32 decode
+    """benchmark configuration C4: a 64-layer dense stack at batch 1 and 32 decode
     tokens, timed per layer (4 seeded layers rotated: ~90 MB of packed weights
     each, 360 MB per cycle > 126 MB L2) and scaled to 64 layers."""
     layers = [make_dense_layer(torch, dev, 7000 + l) for l in range(4)]
@@ -340,7 +341,7 @@ def dense_leg(torch, dev, args):
         ms = secs * 1e3 / steps
         out[str(B)] = {"ms_per_layer": round(ms, 4), "tokens_per_s_64_layers": round(B / (64 * ms / 1e3), 2)}
         del graphs
-    return {"metric": "dense VQ decode, BASELINE config 4 (64 x [q,k,v,o d2/K256 + gate,up,down d8/K16384])",
+    return {"metric": "dense VQ decode, benchmark configuration C4 (64 x [q,k,v,o d2/K256 + gate,up,down d8/K16384])",
             "unit": "tokens/s", "batches": out}
 
 
@@ -355,7 +356,7 @@ def zipf_logits(torch, dev, gen, T, alpha=1.1):
 
 
 def prefill_leg(torch, dev, args, peak_tf, peak_kind, rank, world):
-    """one MoE layer on 4096 tokens, Zipf(1.1) routing."""
+    """benchmark configuration C3: one MoE layer on 4096 tokens, Zipf(1.1) routing."""
     T = 4096
     layer = make_layer(torch, dev, 5000, rank, world)
     gen = torch.Generator(device=dev)

@@ -9,7 +9,7 @@ reference is absent (the GPU boxes).
                          numpy writer/reader src/vqlab/runtime/vq_pack.py
                          (pack :48-76, unpack :79-97, words_per_row :41-45),
                          bit widths 1..16, aligned and ragged NSUB, and the
-                         BASELINE geometries (14-bit NSUB 512/128, 12-bit
+                         benchmark geometries (14-bit NSUB 512/128, 12-bit
                          NSUB 512, 8-bit NSUB 2560, ragged 14-bit NSUB 80).
   moe_block_golden.npz -- the reference's float64 numpy MoE block
                          `ref_moe` (tests/test_qwen3_5_parity.py:180-204) on a

@@ -9,7 +9,7 @@ Tolerances (written here, applied below):
     order: fp32-level max relative error (the reference's metric,
     max|a-b|/max|a|, tests/test_vq_prefill_paths.py:209-210) <= 2e-3, and a
     bf16 output within 2e-3*max|ref| + 1 bf16 ULP of the oracle's
-    (the BASELINE north-star bound; the ULP admits one output rounding step).
+    (the ULP admits one output rounding step).
 """
 import pathlib
 
@@ -212,7 +212,7 @@ def test_empty_and_single_pair():
 
 
 def test_c2_shapes_at_batch_1_and_8():
-    """BASELINE config 2 projection shapes (d8, K16384/14-bit, hidden 4096,
+    """benchmark configuration C2 projection shapes (d8, K16384/14-bit, hidden 4096,
     intermediate 1024, top-10) on 16 experts, with the default auto split."""
     rng = np.random.default_rng(18)
     for OUT, IN in ((1024, 4096), (4096, 1024)):
@@ -301,7 +301,7 @@ def test_dense_unpacked_cutoff_12():
 
 @pytest.mark.parametrize("IN,OUT,n", [(5120, 17408, 1), (5120, 17408, 32), (17408, 5120, 1), (17408, 5120, 7)])
 def test_dense_c4_mlp_shapes(IN, OUT, n):
-    """BASELINE config 4 MLP projections at full size (d8/K16384, 14-bit) on
+    """benchmark configuration C4 MLP projections at full size (d8/K16384, 14-bit) on
     the grouped GEMM's dimension-split passes: 136 row tiles of 5120 k, and
     40 row tiles of 17408 k cut over three CTAs each (split-K)."""
     L = make_layer(E=1, OUT=OUT, IN=IN, D=8, K=16384, G=64, seed=IN + n)

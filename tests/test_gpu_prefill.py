@@ -10,8 +10,8 @@ bf16 ULP, and accuracy against the float64 reconstruction no worse than the
 reference's own non-ACCS arm (the same one weight rounding) by more than 1%.
 The reference's gates use skewed routing on purpose (hot expert, one
 never-used and one single-row expert, a duplicated expert in a token,
-tests/test_vq_prefill_paths.py:32-43) and Zipf(1.1) popularity (BASELINE
-config 3).
+tests/test_vq_prefill_paths.py:32-43) and Zipf(1.1) popularity (benchmark
+configuration C3).
 """
 import numpy as np
 import pytest
@@ -149,7 +149,7 @@ def test_forced_gemm_on_tiny_batches(T, k):
 
 
 def test_zipf_prefill_small():
-    """BASELINE config 3 in miniature: Zipf(1.1) popularity, 10 distinct experts per token."""
+    """benchmark configuration C3 in miniature: Zipf(1.1) popularity, 10 distinct experts per token."""
     E, T, k = 64, 256, 10
     L = make_layer(E=E, OUT=256, IN=1024, D=8, K=16384, G=64, seed=77)
     idx = zipf_routing(T, k, E, seed=5)

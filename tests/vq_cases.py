@@ -1,6 +1,6 @@
 """Seeded synthetic VQ layers for the tests (numpy side) and their torch twins.
 
-Value distributions follow the reference tests and BASELINE configs: codes
+Value distributions follow the reference tests and benchmark configurations: codes
 uniform over [0, K), codebook fp16 ~N(0, sigma), scales fp16 ~U(0.5, 1.5)
 (or ~N(1, 0.1) like tests/test_vq_prefill_paths.py:26-27), x ~N(0, 1).
 """
@@ -73,7 +73,7 @@ def skewed_routing(T, k, E, seed=1):
 
 def zipf_routing(T, k, E, s=1.1, seed=2):
     """Zipf(s) expert popularity over a seeded permutation of the experts,
-    k distinct experts per token."""
+    k distinct experts per token (benchmark configuration C3)."""
     r = np.random.default_rng(seed)
     perm = r.permutation(E)
     w = 1.0 / np.arange(1, E + 1) ** s
