@@ -17,7 +17,7 @@
 // One CTA handles the whole batch.  Warp w owns the contiguous pair range
 // [w*per, (w+1)*per): it counts its pairs per expert into its own row of a
 // [32][E] shared table (lanes of a warp that share an expert are grouped with
-// __match_any_sync, the lowest lane adds the group's size), the table is
+// bit ballots, the lowest lane adds the group's size), the table is
 // scanned over warps per expert, and the warp walks its range again placing
 // each pair at its expert's running slot.
 #include "vqb_common.cuh"
@@ -42,6 +42,20 @@ __device__ __forceinline__ uint32_t expert_of(const uint32_t* idx, int p, int E,
   return e;
 }
 
+// Lanes of the warp holding the same key (key < 2^nbits): the AND over the
+// key's bits of each bit's ballot or its complement.  nbits ballots replace
+// __match_any_sync, which is slow when most lanes hold distinct keys (random
+// routing: ~30 distinct experts per 32 pairs).
+__device__ __forceinline__ uint32_t same_key_lanes(uint32_t key, int nbits) {
+  uint32_t peers = 0xFFFFFFFFu;
+  for (int b = 0; b < nbits; ++b) {
+    const bool bit = (key >> b) & 1u;
+    const uint32_t m = __ballot_sync(0xFFFFFFFFu, bit);
+    peers &= bit ? m : ~m;
+  }
+  return peers;
+}
+
 }  // namespace
 
 template <int kRouteWarps>
@@ -53,21 +67,34 @@ __global__ void __launch_bounds__(kRouteWarps * 32) route_small_kernel(const uin
   int* tab = sh + 2 * E;         // [kRouteWarps][E] per-warp counts, then per-warp running slots
   const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
   const int per = (N + kRouteWarps - 1) / kRouteWarps;
+  // keys: the expert, or E for a lane with no pair / a skipped pair
+  int nbits = 1;
+  while ((1 << nbits) <= E) ++nbits;
   const int lo = min(N, wid * per), hi = min(N, lo + per);
   const uint32_t lt = (1u << lane) - 1u;
 
   if (threadIdx.x < 4) ws.meta[threadIdx.x] = 0;  // status block, before any thread can report into it
   for (int i = threadIdx.x; i < kRouteWarps * E; i += blockDim.x) tab[i] = 0;
   __syncthreads();
-  // 1. per-warp counts
+  // 1. per-warp counts (the range's expert ids are read kBatch steps at a
+  // time, so the loads of a warp are in flight together)
   int* row = tab + wid * E;
-  for (int b = lo; b < hi; b += 32) {
-    const int p = b + lane;
-    uint32_t e = p < hi ? expert_of(idx, p, E, ws.meta) : kSkipExpert;
-    const bool valid = e != kSkipExpert;
-    const uint32_t peers = __match_any_sync(0xFFFFFFFFu, e);
-    if (valid && (peers & lt) == 0) row[e] += __popc(peers);
-    __syncwarp();
+  constexpr int kBatch = 4;
+  for (int b0 = lo; b0 < hi; b0 += 32 * kBatch) {
+    uint32_t eb[kBatch];
+#pragma unroll
+    for (int u = 0; u < kBatch; ++u) {
+      const int p = b0 + 32 * u + lane;
+      eb[u] = p < hi ? expert_of(idx, p, E, ws.meta) : kSkipExpert;
+    }
+#pragma unroll
+    for (int u = 0; u < kBatch; ++u) {
+      const uint32_t e = eb[u];
+      const bool valid = e != kSkipExpert;
+      const uint32_t peers = same_key_lanes(valid ? e : static_cast<uint32_t>(E), nbits);
+      if (valid && (peers & lt) == 0) row[e] += __popc(peers);
+      __syncwarp();
+    }
   }
   __syncthreads();
   // 2. per expert: total, and exclusive prefix over warps
@@ -135,19 +162,29 @@ __global__ void __launch_bounds__(kRouteWarps * 32) route_small_kernel(const uin
     }
   }
   // 3. stable placement: warp w walks its range again in order
-  for (int b = lo; b < hi; b += 32) {
-    const int p = b + lane;
-    uint32_t e = kSkipExpert;
-    if (p < hi) {
-      e = idx ? idx[p] : 0u;
-      if (e != kSkipExpert && e >= static_cast<uint32_t>(E)) e = 0;
+  for (int b0 = lo; b0 < hi; b0 += 32 * kBatch) {
+    uint32_t eb[kBatch];
+#pragma unroll
+    for (int u = 0; u < kBatch; ++u) {
+      const int p = b0 + 32 * u + lane;
+      uint32_t e = kSkipExpert;
+      if (p < hi) {
+        e = idx ? idx[p] : 0u;
+        if (e != kSkipExpert && e >= static_cast<uint32_t>(E)) e = 0;
+      }
+      eb[u] = e;
     }
-    const bool valid = e != kSkipExpert;
-    const uint32_t peers = __match_any_sync(0xFFFFFFFFu, e);
-    if (valid) ws.sorted[row[e] + __popc(peers & lt)] = p;
-    __syncwarp();
-    if (valid && (peers & lt) == 0) row[e] += __popc(peers);
-    __syncwarp();
+#pragma unroll
+    for (int u = 0; u < kBatch; ++u) {
+      const int p = b0 + 32 * u + lane;
+      const uint32_t e = eb[u];
+      const bool valid = e != kSkipExpert;
+      const uint32_t peers = same_key_lanes(valid ? e : static_cast<uint32_t>(E), nbits);
+      if (valid) ws.sorted[row[e] + __popc(peers & lt)] = p;
+      __syncwarp();
+      if (valid && (peers & lt) == 0) row[e] += __popc(peers);
+      __syncwarp();
+    }
   }
 }
 
