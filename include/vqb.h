@@ -96,8 +96,21 @@ typedef struct vqb_options {
   int32_t stage_codebook;     /* grouped kernel: 0 = auto, 1 = shared-memory prefix (no pair split),
                                  2 = none, 3 = split the codebook across a CTA pair */
   int32_t pairs_per_chunk;    /* grouped kernel: tokens sharing one lookup pass (0 = auto, else 1, 2 or 4) */
-  int32_t reserved[2];
+  int32_t reuse;              /* VQB_REUSE_* flags: the workspace already holds this call's routing tables
+                                 (and gathered x) from the previous call on the same stream; honoured on the
+                                 grouped-GEMM path only (the decode kernel chunks pairs differently) */
+  int32_t reserved;
 } vqb_options;
+
+/* vqb_options.reuse: an MoE block's gate, up and down projections share one
+ * routing (same indices, n_tokens, top_k and num_experts) and gate / up one
+ * x.  With one workspace for the three calls, the first call routes (and
+ * gathers x), the others skip that work:
+ *   VQB_REUSE_ROUTING  routing tables valid in the workspace (same indices)
+ *   VQB_REUSE_X        x gathered for the same x, in_features, codebook
+ *                      geometry and dtypes (implies VQB_REUSE_ROUTING) */
+#define VQB_REUSE_ROUTING 1
+#define VQB_REUSE_X 2
 
 /* Library identity and messages. */
 const char* vqb_version(void);

@@ -49,3 +49,26 @@ def test_moe_block_matches_oracle_composition(T):
     # bf16 outputs at every stage: 2e-3 of the output scale plus one bf16 ulp of each value
     tol = 2e-3 * np.abs(ref).max() + np.abs(ref) * 2.0 ** -7 + 1e-6
     assert np.all(np.abs(y - ref) <= 4 * tol), float(np.max(np.abs(y - ref) / tol))
+
+
+@pytest.mark.parametrize("T,K_", [(5, 16384), (64, 16384), (300, 4096)])
+def test_shared_workspace_is_identical_to_separate_calls(T, K_):
+    """gate / up / down on one workspace (routing from gate, x gathered once,
+    VQB_REUSE_*) give the same bytes as three independent calls."""
+    from vqlab_b200.moe import expert_mlp, swiglu
+    rng = np.random.default_rng(T + K_)
+    bits = int(K_ - 1).bit_length()
+
+    def proj(out, inn):
+        codes = rng.integers(0, K_, (E, out, inn // 8)).astype(np.uint16)
+        cb = (rng.standard_normal((K_, 8)) * 0.02).astype(np.float16)
+        sc = rng.uniform(0.5, 1.5, (E, out, inn // G)).astype(np.float16)
+        return VQSwitchLinear(torch.from_numpy(orc.pack(codes, bits).view(np.int32)).cuda(), torch.from_numpy(cb).cuda(),
+                              torch.from_numpy(sc).cuda(), group_size=G, pack_bits=bits, in_features=inn)
+
+    gp, up, dp = proj(I, H), proj(I, H), proj(H, I)
+    x = torch.from_numpy(rng.standard_normal((T, 1, 1, H)).astype(np.float32)).cuda().to(torch.bfloat16)
+    idx = torch.from_numpy(np.stack([rng.permutation(E)[:TOPK] for _ in range(T)]).astype(np.int32)).cuda()
+    shared = expert_mlp(gp, up, dp, x, idx)
+    separate = dp(swiglu(gp(x, idx), up(x, idx)), idx)
+    assert torch.equal(shared.view(torch.int16), separate.view(torch.int16))

@@ -61,7 +61,8 @@ class Options(ctypes.Structure):
         ("decode_variant", ctypes.c_int32),
         ("stage_codebook", ctypes.c_int32),
         ("pairs_per_chunk", ctypes.c_int32),
-        ("reserved", ctypes.c_int32 * 2),
+        ("reuse", ctypes.c_int32),
+        ("reserved", ctypes.c_int32),
     ]
 
 

@@ -1244,7 +1244,7 @@ size_t tc_prefill_x_bytes(int64_t N, int IN, int K, int D, int E, int OUT) {
 
 vqb_status launch_prefill_tc(const LinearGeometry& geo, const void* x, int x_dtype, int krep, const RouteWorkspace& rw,
                              int N, uint16_t* xs, void* y, int y_dtype, bool round_f16_first, bool bf16_operands,
-                             int* status, cudaStream_t stream) {
+                             bool gather_x, int* status, cudaStream_t stream) {
   if (N <= 0) return VQB_OK;
   if (ensure_device_attrs() != VQB_OK) return VQB_CUDA_ERROR;
   EncodeTiledFn enc = encode_fn();
@@ -1304,8 +1304,8 @@ vqb_status launch_prefill_tc(const LinearGeometry& geo, const void* x, int x_dty
                                                           split_cb_bytes(geo.K, geo.D))
                                : nullptr;
 
-  // 1. gather x into expert-sorted 16-bit rows
-  {
+  // 1. gather x into expert-sorted 16-bit rows (unless the caller's previous call did)
+  if (gather_x) {
     if (x_dtype != VQB_F16 && x_dtype != VQB_BF16) return VQB_UNSUPPORTED_GEOMETRY;
     if ((reinterpret_cast<uintptr_t>(x) & 15) != 0) return VQB_BAD_ALIGNMENT;
     int64_t blocks = (static_cast<int64_t>(N) * (geo.IN / 8) + 255) / 256;

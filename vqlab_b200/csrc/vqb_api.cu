@@ -102,11 +102,15 @@ vqb_status run_linear(const LinearGeometry& geo, const void* x, int x_dtype, int
                                                                      row_tiles_128(geo.OUT)));
   if (large && variant == 0 && tc_prefill_supported(geo) && x_dtype != VQB_F32 &&
       (reinterpret_cast<uintptr_t>(x) & 15) == 0) {
-    // grouped tcgen05 GEMM: tiles of up to 128 of one expert's tokens
-    vqb_status st = launch_route_small(indices, N, geo.E, kPrefillTileTokens, rw, stream);
-    if (st != VQB_OK) return st;
+    // grouped tcgen05 GEMM: tiles of up to 128 of one expert's tokens; routing
+    // tables and gathered x reused from the previous call when the caller says so
+    const int reuse = opts ? opts->reuse : 0;
+    if (!(reuse & (VQB_REUSE_ROUTING | VQB_REUSE_X))) {
+      vqb_status st = launch_route_small(indices, N, geo.E, kPrefillTileTokens, rw, stream);
+      if (st != VQB_OK) return st;
+    }
     return launch_prefill_tc(geo, x, x_dtype, krep, rw, N, xbuf, y, y_dtype, round_f16_first,
-                             /*bf16_operands=*/wround == 1, rw.meta, stream);
+                             /*bf16_operands=*/wround == 1, /*gather_x=*/!(reuse & VQB_REUSE_X), rw.meta, stream);
   }
   if (variant == 1 || !mma_decode_supported(geo, wround, x_dtype)) {
     if (cudaMemsetAsync(rw.meta, 0, sizeof(int) * 4, stream) != cudaSuccess) return VQB_CUDA_ERROR;

@@ -76,7 +76,7 @@ bool tc_prefill_dsplit(const LinearGeometry& geo);  // the GEMM would run dimens
 size_t tc_prefill_x_bytes(int64_t N, int IN, int K, int D, int E, int OUT);  // gathered x, d8 codebook halves, split-K partials
 int tc_prefill_ksplit(int64_t N, int E, int OUT, int IN);
 vqb_status launch_prefill_tc(const LinearGeometry& geo, const void* x, int x_dtype, int krep, const RouteWorkspace& rw,
-                             int N, uint16_t* xs, void* y, int y_dtype, bool round_f16_first, bool bf16_operands,
+                             int N, uint16_t* xs, void* y, int y_dtype, bool round_f16_first, bool bf16_operands, bool gather_x,
                              int* status, cudaStream_t stream);
 constexpr int kPrefillTileTokens = 128;
 

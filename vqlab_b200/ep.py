@@ -52,7 +52,7 @@ from typing import Callable, Optional
 import torch
 import torch.distributed as dist
 
-from .moe import combine, route, swiglu
+from .moe import combine, expert_mlp, route
 
 
 @dataclass
@@ -135,10 +135,7 @@ class EPMoEBlock(torch.nn.Module):
         if R == 0:
             return xp.new_empty((0, self.down_proj.output_dims))
         ids = local.to(torch.int32).reshape(R, 1)
-        xe = xp.reshape(R, 1, 1, H)
-        g = self.gate_proj(xe, ids)
-        u = self.up_proj(xe, ids)
-        return self.down_proj(swiglu(g, u), ids).reshape(R, -1)
+        return expert_mlp(self.gate_proj, self.up_proj, self.down_proj, xp.reshape(R, 1, 1, H), ids).reshape(R, -1)
 
     def _all_gather(self, t: torch.Tensor) -> torch.Tensor:
         out = t.new_empty((self.world * t.shape[0],) + tuple(t.shape[1:]))
@@ -170,9 +167,8 @@ class EPMoEBlock(torch.nn.Module):
         self.last_pairs = (X.reshape(W * C, 1, 1, H), ids)          # this rank's pairs (kept for measurement)
         if X.is_cuda and self._experts == self._vq_experts:
             from .moe import combine_partial
-            g = self.gate_proj(X.reshape(W * C, 1, 1, H), ids)        # [W*C, k, 1, I]
-            u = self.up_proj(X.reshape(W * C, 1, 1, H), ids)
-            d = self.down_proj(swiglu(g, u), ids)                     # [W*C, k, 1, H]; skipped rows unwritten
+            # [W*C, k, 1, H]; rows of skipped pairs are not written
+            d = expert_mlp(self.gate_proj, self.up_proj, self.down_proj, X.reshape(W * C, 1, 1, H), ids)
             part = combine_partial(d.reshape(W * C, k, -1), Wt, ids)  # fp32 [W*C, H]
         else:
             # pluggable experts (CPU tests): every gathered pair computed, other ranks' masked out

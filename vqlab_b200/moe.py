@@ -45,6 +45,29 @@ def combine(d: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
     return y
 
 
+# vqb_options.reuse flags (include/vqb.h)
+REUSE_ROUTING = 1
+REUSE_X = 2
+
+
+def expert_mlp(gate_proj: VQSwitchLinear, up_proj: VQSwitchLinear, down_proj: VQSwitchLinear, xe: torch.Tensor,
+               idx: torch.Tensor) -> torch.Tensor:
+    """down(swiglu(gate(x), up(x))) for the pairs of idx [R, k] (x per token,
+    xe [R, 1, 1, H]) -> [R, k, 1, H].  When the three projections run the
+    grouped GEMM they share one workspace: gate routes and gathers x, up reuses
+    both, down reuses the routing (VQB_REUSE_*)."""
+    R, k = idx.shape
+    if (gate_proj.kernel_path(R, k) == "gemm" and up_proj.kernel_path(R, k) == "gemm"
+            and down_proj.kernel_path(R * k, 1) == "gemm"):
+        nbytes = max(gate_proj.workspace_bytes(R, k), up_proj.workspace_bytes(R, k),
+                     down_proj.workspace_bytes(R * k, 1))
+        ws = torch.empty(nbytes, dtype=torch.uint8, device=xe.device)
+        g = gate_proj(xe, idx, workspace=ws)
+        u = up_proj(xe, idx, workspace=ws, reuse=REUSE_ROUTING | REUSE_X)
+        return down_proj(swiglu(g, u), idx, workspace=ws, reuse=REUSE_ROUTING)
+    return down_proj(swiglu(gate_proj(xe, idx), up_proj(xe, idx)), idx)
+
+
 def combine_partial(d: torch.Tensor, w: torch.Tensor, ids: torch.Tensor | None = None) -> torch.Tensor:
     """fp32 partial combine for expert parallelism: out[t] = sum over the slots
     j with ids[t, j] != -1 (VQB_SKIP_EXPERT) of w[t, j] * f32 d[t, j], in slot
@@ -88,9 +111,10 @@ class VQMoEBlock(torch.nn.Module):
         """x [T, H] (bf16), router_logits [T, E] -> y [T, H] in x's dtype."""
         T, H = x.shape
         idx, w = route(router_logits, self.top_k)
-        xe = x.reshape(T, 1, 1, H)
-        g = self.gate_proj(xe, idx)                       # [T, k, 1, I]
-        u = self.up_proj(xe, idx)
-        h = swiglu(g, u)
-        d = self.down_proj(h, idx)                        # [T, k, 1, H]
+        return self.project(x, idx, w)
+
+    def project(self, x: torch.Tensor, idx: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
+        """The three projections, SwiGLU and combine for given routing."""
+        T, H = x.shape
+        d = expert_mlp(self.gate_proj, self.up_proj, self.down_proj, x.reshape(T, 1, 1, H), idx)
         return combine(d.reshape(T, self.top_k, -1), w)

@@ -176,8 +176,21 @@ class VQSwitchLinear(torch.nn.Module):
             _lib.check(-r, "vqb_switch_path")
         return "gemm" if r == 2 else "decode"
 
+    def workspace_bytes(self, n_tokens: int, top_k: int) -> int:
+        """Scratch bytes a call of n_tokens rows x top_k pairs each needs (vqb_switch_workspace_size)."""
+        d = self.desc()
+        opts = self.options
+        return int(_lib.lib().vqb_switch_workspace_size(ctypes.byref(d), int(n_tokens), int(top_k),
+                                                         ctypes.byref(opts) if opts is not None else None))
+
     def forward(self, x: torch.Tensor, indices: torch.Tensor, sorted_indices: bool = False,
-                out: torch.Tensor | None = None) -> torch.Tensor:
+                out: torch.Tensor | None = None, workspace: torch.Tensor | None = None,
+                reuse: int = 0) -> torch.Tensor:
+        """The reference call (vq_switch.py:5284).  Extensions for a block that
+        runs several projections on one routing: `workspace` (a uint8 CUDA
+        tensor of at least workspace_bytes) is used instead of a fresh one, and
+        `reuse` (VQB_REUSE_* flags) tells the library that it already holds
+        this call's routing tables / gathered x from the previous call."""
         self._check_tensors()
         IN = self.input_dims
         OUT = self.output_dims
@@ -213,10 +226,21 @@ class VQSwitchLinear(torch.nn.Module):
                 raise ValueError("out must be a contiguous [N, OUT] tensor of x's dtype")
         d = self.desc()
         opts = self.options
+        if reuse:
+            base = opts if opts is not None else _lib.Options()
+            opts = _lib.Options.from_buffer_copy(base)
+            opts.reuse = int(reuse)
         optp = ctypes.byref(opts) if opts is not None else None
         L = _lib.lib()
         ws_bytes = L.vqb_switch_workspace_size(ctypes.byref(d), ntok, krep, optp)
-        ws = torch.empty(ws_bytes, dtype=torch.uint8, device=x.device)
+        if workspace is not None:
+            if workspace.dtype != torch.uint8 or workspace.device != x.device or workspace.numel() < ws_bytes:
+                raise ValueError(f"workspace must be a uint8 tensor of >= {ws_bytes} bytes on {x.device}")
+            ws = workspace
+        else:
+            if reuse:
+                raise ValueError("reuse needs the workspace of the call that routed")
+            ws = torch.empty(ws_bytes, dtype=torch.uint8, device=x.device)
         st = L.vqb_switch_forward(ctypes.byref(d), ctypes.c_void_p(x2.data_ptr()), _DTYPES[x.dtype], ntok,
                                   ctypes.c_void_p(idx.data_ptr()), krep, ctypes.c_void_p(y.data_ptr()),
                                   _DTYPES[x.dtype], ctypes.c_void_p(ws.data_ptr()), ws_bytes, optp,
