@@ -179,7 +179,7 @@ class ClockSampler:
 
 # ------------------------------------------------------------------ GPU arm
 
-def make_layer(torch, dev, seed, rank=0, world=1):
+def make_layer(torch, dev, seed, rank=0, world=1, exchange="p2p"):
     """One seeded MoE layer; with world > 1 this rank's expert shard of it
     wrapped in the expert-parallel block (codebooks are per layer, so every
     rank builds the same ones)."""
@@ -205,7 +205,7 @@ def make_layer(torch, dev, seed, rank=0, world=1):
     # decode batches take the fixed-shape path that CUDA graphs capture (gpu_arm sets
     # static_tokens to the batch it runs; larger batches take the dynamic path)
     return EPMoEBlock(proj(INTER, HIDDEN), proj(INTER, HIDDEN), proj(HIDDEN, INTER), TOPK, num_experts=E,
-                      static_tokens=64)
+                      static_tokens=64, exchange=exchange)
 
 
 def distinct_experts(torch, logits):
@@ -413,7 +413,7 @@ def gpu_arm(args, rank, world, dev):
     peak_gbs, peak_tf, peak_kind = _peaks()
     batches = sorted(set([args.batch] + [int(b) for b in args.extra_batches.split(",") if b]))
     n_layers = args.layers
-    layers = [make_layer(torch, dev, 1000 + l, rank, world) for l in range(n_layers)]
+    layers = [make_layer(torch, dev, 1000 + l, rank, world, args.exchange) for l in range(n_layers)]
     gen = torch.Generator(device=dev)
     gen.manual_seed(7 + rank)
     results = {}
@@ -561,6 +561,9 @@ def gpu_arm(args, rank, world, dev):
     layers[0](xs_last[0], lg_last[0])
     torch.cuda.synchronize()
     launches = _lib.launch_count() - c0
+    if world > 1:
+        for L in layers:
+            L.close()  # collective: peer regions are released together
     return results, roof, e2e, launches
 
 
@@ -646,7 +649,10 @@ def _config(args, world):
                         f"inter 1024, top-10, d8 K16384 14-bit, G64)",
             "global_batch": args.batch * world, "experts": E, "top_k": TOPK, "hidden": HIDDEN,
             "intermediate": INTER, "dim": D, "codebook": K, "pack_bits": BITS, "group": G,
-            "parallelism": f"ep{world} (experts sharded, NCCL all-to-all dispatch/combine)" if world > 1 else "single",
+            "parallelism": (f"ep{world} (experts sharded; decode batches exchanged " +
+                            ("by peer-memory kernels over NVLink, vqb_ep_dispatch/combine/reduce)"
+                             if args.exchange == "p2p" else "by NCCL all-gather / all-to-all)")) if world > 1
+                           else "single",
             "l2": f"{args.layers} independently seeded layers rotated per step (weights touched per cycle >> 126 MB L2)"}
 
 
@@ -660,6 +666,8 @@ def main(argv=None) -> int:
     ap.add_argument("--extra-batches", default="1,8")
     ap.add_argument("--layers", type=int, default=8)
     ap.add_argument("--skip-e2e", action="store_true")
+    ap.add_argument("--exchange", default="p2p", choices=["p2p", "nccl"],
+                    help="expert-parallel decode exchange (N > 1): peer-memory kernels or NCCL collectives")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--skip-prefill", action="store_true")
     ap.add_argument("--skip-dense", action="store_true")

@@ -196,6 +196,85 @@ vqb_status vqb_moe_combine_partial(const void* expert_out, const float* weights,
                                    int32_t n_tokens, int32_t top_k, int32_t hidden, vqb_dtype dtype,
                                    vqb_stream_t stream);
 
+/* ---- Expert-parallel exchange over peer memory (fixed-shape decode path) ----
+ *
+ * No reference counterpart: the reference runs every expert on one device
+ * (its multi-node path pipelines whole layers).  This replaces the NCCL
+ * all-gather / all-to-all pair around the expert projections when every rank
+ * holds at most `tokens` tokens: each rank WRITES its token rows straight into
+ * the other ranks' memory, and each rank's partial expert sums are written
+ * straight into the owning rank's memory.
+ *
+ * One process per GPU; the `world` GPUs must have peer access to one another
+ * (NVLink / NVSwitch on one node).  Each rank allocates one exchange region
+ * (vqb_ep_region_alloc) and maps every other rank's region through CUDA IPC
+ * (vqb_ep_ipc_handle, then vqb_ep_ipc_open of each peer's handle).  One layer
+ * step, all on one stream and with no host synchronisation (graph-capturable):
+ *   vqb_ep_dispatch   this rank's rows, expert slots and weights into every region
+ *   the rank's projections on its region's x_rows / slots (vqb_switch_forward)
+ *   vqb_ep_combine    fp32 slot sums of this rank's pairs into the owners' regions
+ *   vqb_ep_reduce     the owner sums the ranks' partials (rank order), rounds once
+ * Every rank makes the same calls in the same order.  Each dispatch and combine
+ * ends in a bounded wait for the other ranks' signals (opts->wait_limit_us,
+ * default 2 s): when it gives up, the int32 at VQB_EP_STATUS_OFFSET of the
+ * rank's region becomes VQB_TIMEOUT and the exchange is out of step -- free
+ * the regions and set them up again.
+ *
+ * Region layout (byte offsets from vqb_ep_region_bytes; W = world, C = tokens):
+ *   [0, 512)  control: signal words the ranks write, epoch, status
+ *   x_rows    16-bit [W * C, hidden]: block s = rank s's token rows (x dtype);
+ *             a row whose token has no pair on this rank is not sent
+ *   slots     int32 [W * C, top_k]: this rank's local expert of each pair,
+ *             VQB_SKIP_EXPERT (-1) for pairs of other ranks and padding rows
+ *   weights   fp32 [W * C, top_k]
+ *   partials  fp32 [W, C, hidden]: block s = rank s's slot sums for this rank's tokens */
+#define VQB_EP_MAX_WORLD 8
+#define VQB_EP_STATUS_OFFSET 272
+#define VQB_EP_IPC_HANDLE_BYTES 64
+
+typedef struct vqb_ep_layout {
+  int32_t world;             /* ranks, 1..VQB_EP_MAX_WORLD */
+  int32_t rank;              /* this rank */
+  int32_t tokens;            /* C: token rows per rank per step (the fixed shape) */
+  int32_t top_k;             /* 1..256 */
+  int32_t hidden;            /* a multiple of 8 */
+  int32_t experts_per_rank;  /* rank r serves global experts [r * E_local, (r + 1) * E_local) */
+} vqb_ep_layout;
+
+typedef struct vqb_ep_options {
+  int32_t phases;            /* 0 or 3 = both; 1 = write and signal only, 2 = wait only: ranks
+                                emulated in one process run every rank's phase 1 before any
+                                phase 2, so that no launch waits on a later launch */
+  int32_t wait_limit_us;     /* 0 = 2,000,000 */
+} vqb_ep_options;
+
+/* Region size; offsets (may be NULL) receives {x_rows, slots, weights, partials}. */
+size_t vqb_ep_region_bytes(const vqb_ep_layout* layout, size_t* offsets);
+/* cudaMalloc of the region on the current device, zeroed (synchronous; set-up only). */
+vqb_status vqb_ep_region_alloc(const vqb_ep_layout* layout, void** region);
+vqb_status vqb_ep_region_free(void* region);
+/* The region's CUDA IPC handle (VQB_EP_IPC_HANDLE_BYTES bytes) for the other ranks. */
+vqb_status vqb_ep_ipc_handle(void* region, void* handle);
+/* Map a peer's region into this process (peer access enabled); close with vqb_ep_ipc_close. */
+vqb_status vqb_ep_ipc_open(const void* handle, void** peer_region);
+vqb_status vqb_ep_ipc_close(void* peer_region);
+
+/* regions: host array of `world` device pointers, regions[rank] = this rank's
+ * own region, the others its mappings of the peers' regions.
+ * x [n_tokens, hidden] 16-bit (16-byte aligned rows), indices int32
+ * [n_tokens, top_k] GLOBAL expert ids, weights fp32 [n_tokens, top_k];
+ * n_tokens <= tokens (rows n_tokens..tokens-1 route nowhere). */
+vqb_status vqb_ep_dispatch(const vqb_ep_layout* layout, void* const* regions, const void* x, vqb_dtype x_dtype,
+                           int32_t n_tokens, const int32_t* indices, const float* weights,
+                           const vqb_ep_options* opts, vqb_stream_t stream);
+/* expert_out [world * tokens, top_k, hidden] (dtype): the projections' output
+ * for this region's x_rows / slots; rows of skipped pairs are never read. */
+vqb_status vqb_ep_combine(const vqb_ep_layout* layout, void* const* regions, const void* expert_out,
+                          vqb_dtype dtype, const vqb_ep_options* opts, vqb_stream_t stream);
+/* y[t, :] = y_dtype(sum over ranks r in order of partials[r, t, :]) for t < n_tokens. */
+vqb_status vqb_ep_reduce(const vqb_ep_layout* layout, void* region, void* y, vqb_dtype y_dtype, int32_t n_tokens,
+                         vqb_stream_t stream);
+
 /* Measurement aids; neither has a counterpart in the reference, whose Metal
  * runtime exposes no launch accounting or per-kernel timing.
  *

@@ -183,3 +183,71 @@ def test_skipzero_row_table_from_mask():
     want = np.full((E, OUT), -1, np.int32)
     want[live] = np.arange(int(live.sum()), dtype=np.int32)
     assert tbl.dtype == np.int32 and np.array_equal(tbl, want)
+
+
+def _ep_layout(**kw):
+    base = dict(world=4, rank=1, tokens=16, top_k=4, hidden=512, experts_per_rank=2)
+    base.update(kw)
+    return _lib.EpLayout(*(base[n] for n, _ in _lib.EpLayout._fields_))
+
+
+def test_peer_exchange_region_layout():
+    """Region = 512-byte control block, then x rows, slots, weights, partials,
+    each 256-byte aligned and sized for world * tokens rows."""
+    L = _lib.lib()
+    offs = (ctypes.c_size_t * 4)()
+    n = L.vqb_ep_region_bytes(ctypes.byref(_ep_layout()), offs)
+    R = 4 * 16
+    assert list(offs) == [512, 512 + R * 512 * 2, 512 + R * 512 * 2 + R * 4 * 4, 512 + R * 512 * 2 + 2 * R * 4 * 4]
+    assert n == offs[3] + R * 512 * 4
+    assert all(o % 256 == 0 for o in offs)
+    assert _lib.VQB_EP_STATUS_OFFSET + 4 <= 512
+
+
+@pytest.mark.parametrize("kw", [dict(world=0), dict(world=9), dict(rank=4), dict(rank=-1), dict(tokens=0),
+                                dict(top_k=0), dict(top_k=257), dict(hidden=12), dict(experts_per_rank=0)])
+def test_peer_exchange_rejects_bad_layouts(kw):
+    L = _lib.lib()
+    lay = _ep_layout(**kw)
+    assert L.vqb_ep_region_bytes(ctypes.byref(lay), None) == 0
+    regions = (ctypes.c_void_p * 8)(*([256] * 8))
+    st = L.vqb_ep_dispatch(ctypes.byref(lay), regions, ctypes.c_void_p(256), _lib.VQB_BF16, 1, ctypes.c_void_p(256),
+                           ctypes.c_void_p(256), None, None)
+    assert st == _lib.VQB_BAD_SHAPE
+    assert L.vqb_ep_combine(ctypes.byref(lay), regions, ctypes.c_void_p(256), _lib.VQB_BF16, None, None) == \
+        _lib.VQB_BAD_SHAPE
+    assert L.vqb_ep_reduce(ctypes.byref(lay), ctypes.c_void_p(256), ctypes.c_void_p(256), _lib.VQB_BF16, 1,
+                           None) == _lib.VQB_BAD_SHAPE
+
+
+def test_peer_exchange_host_validation():
+    """Null or unaligned regions, too many tokens and bad option phases are
+    refused before any launch."""
+    L = _lib.lib()
+    lay = _ep_layout()
+    null = (ctypes.c_void_p * 4)(256, None, 256, 256)
+    assert L.vqb_ep_dispatch(ctypes.byref(lay), null, ctypes.c_void_p(256), _lib.VQB_BF16, 1, ctypes.c_void_p(256),
+                             ctypes.c_void_p(256), None, None) == _lib.VQB_NULL_POINTER
+    odd = (ctypes.c_void_p * 4)(256, 256 + 16, 256, 256)
+    assert L.vqb_ep_combine(ctypes.byref(lay), odd, ctypes.c_void_p(256), _lib.VQB_BF16, None, None) == \
+        _lib.VQB_BAD_ALIGNMENT
+    bad_phase = _lib.EpOptions(7, 0)
+    ok = (ctypes.c_void_p * 4)(256, 512, 768, 1024)
+    assert L.vqb_ep_combine(ctypes.byref(lay), ok, ctypes.c_void_p(256), _lib.VQB_BF16, ctypes.byref(bad_phase),
+                            None) == _lib.VQB_BAD_SHAPE
+    assert L.vqb_ep_reduce(ctypes.byref(lay), ctypes.c_void_p(256), ctypes.c_void_p(256), _lib.VQB_BF16, 17,
+                           None) == _lib.VQB_BAD_SHAPE
+    assert L.vqb_ep_reduce(ctypes.byref(lay), ctypes.c_void_p(256), ctypes.c_void_p(256), _lib.VQB_BF16, 0,
+                           None) == _lib.VQB_OK
+    assert L.vqb_ep_region_alloc(ctypes.byref(lay), None) == _lib.VQB_NULL_POINTER
+    assert L.vqb_ep_ipc_handle(None, None) == _lib.VQB_NULL_POINTER
+    assert L.vqb_ep_ipc_close(None) == _lib.VQB_OK
+    assert L.vqb_ep_region_free(None) == _lib.VQB_OK
+
+
+def test_ep_block_exchange_argument():
+    from vqlab_b200.ep import EPMoEBlock
+    with pytest.raises(ValueError):
+        EPMoEBlock(None, None, None, 2, num_experts=4, exchange="nvshmem")
+    with pytest.raises(ValueError):
+        EPMoEBlock(None, None, None, 2, num_experts=4, exchange="p2p")  # needs static_tokens

@@ -32,7 +32,7 @@ def _proj_np(rng, out, inn):
     return packed, cb, sc
 
 
-def _worker(rank, world, port, out_dir, static=None):
+def _worker(rank, world, port, out_dir, static=None, exchange="nccl"):
     import datetime
     import torch.distributed as dist
     from vqlab_b200 import VQSwitchLinear
@@ -62,7 +62,8 @@ def _worker(rank, world, port, out_dir, static=None):
                                   in_features=inn)
 
         single = VQMoEBlock(full(P[0], H), full(P[1], H), full(P[2], I), K)
-        ep = EPMoEBlock(shard(P[0], H), shard(P[1], H), shard(P[2], I), K, num_experts=E, static_tokens=static)
+        ep = EPMoEBlock(shard(P[0], H), shard(P[1], H), shard(P[2], I), K, num_experts=E, static_tokens=static,
+                        exchange=exchange)
         g = torch.Generator().manual_seed(7 + rank)
         x = torch.randn((T + 3 * rank, H), generator=g).to(torch.bfloat16).to(dev)
         lg = torch.randn((T + 3 * rank, E), generator=g).to(dev)
@@ -79,19 +80,24 @@ def _worker(rank, world, port, out_dir, static=None):
             torch.cuda.synchronize()
             assert torch.equal(y_g, y_ep)
             del gr
+        if exchange == "p2p":
+            ep._peer.check()  # no wait gave up
+            ep.close()
         torch.save({"ep": y_ep.float().cpu(), "ref": y_ref.float().cpu()}, os.path.join(out_dir, f"r{rank}.pt"))
     finally:
         dist.destroy_process_group()
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
-@pytest.mark.parametrize("static", [None, 64])
-def test_ep_two_gpus_matches_single_gpu_block(tmp_path, static):
-    """Both dispatch paths: the dynamic one (exact split sizes read on the host)
-    and the fixed-shape decode path (all-gather, skipped pairs, fp32 partial
-    combine), which must also replay from a CUDA graph with its NCCL calls."""
+@pytest.mark.parametrize("static,exchange", [(None, "nccl"), (64, "nccl"), (64, "p2p")])
+def test_ep_two_gpus_matches_single_gpu_block(tmp_path, static, exchange):
+    """Every dispatch path: the dynamic one (exact split sizes read on the
+    host), the fixed-shape decode path (all-gather, skipped pairs, fp32
+    partial combine), which must also replay from a CUDA graph with its NCCL
+    calls, and the same fixed-shape step over peer memory (IPC-mapped
+    regions, no NCCL on the data path), also replayed from a graph."""
     world = 2
-    mp.start_processes(_worker, args=(world, _free_port(), str(tmp_path), static), nprocs=world, join=True,
+    mp.start_processes(_worker, args=(world, _free_port(), str(tmp_path), static, exchange), nprocs=world, join=True,
                        start_method="spawn")
     for r in range(world):
         d = torch.load(tmp_path / f"r{r}.pt")

@@ -66,6 +66,19 @@ class Options(ctypes.Structure):
     ]
 
 
+class EpLayout(ctypes.Structure):
+    _fields_ = [(n, ctypes.c_int32) for n in ("world", "rank", "tokens", "top_k", "hidden", "experts_per_rank")]
+
+
+class EpOptions(ctypes.Structure):
+    _fields_ = [("phases", ctypes.c_int32), ("wait_limit_us", ctypes.c_int32)]
+
+
+VQB_EP_MAX_WORLD = 8
+VQB_EP_STATUS_OFFSET = 272
+VQB_EP_IPC_HANDLE_BYTES = 64
+
+
 class VQBError(RuntimeError):
     """A non-OK status that maps to no narrower Python exception."""
 
@@ -103,6 +116,24 @@ def _bind(L):
     L.vqb_switch_path.argtypes = [P, i32, i32, P]
     L.vqb_moe_combine_partial.restype = i32
     L.vqb_moe_combine_partial.argtypes = [P, P, P, P, i32, i32, i32, i32, P]
+    L.vqb_ep_region_bytes.restype = sz
+    L.vqb_ep_region_bytes.argtypes = [P, P]
+    L.vqb_ep_region_alloc.restype = i32
+    L.vqb_ep_region_alloc.argtypes = [P, P]
+    L.vqb_ep_region_free.restype = i32
+    L.vqb_ep_region_free.argtypes = [P]
+    L.vqb_ep_ipc_handle.restype = i32
+    L.vqb_ep_ipc_handle.argtypes = [P, P]
+    L.vqb_ep_ipc_open.restype = i32
+    L.vqb_ep_ipc_open.argtypes = [P, P]
+    L.vqb_ep_ipc_close.restype = i32
+    L.vqb_ep_ipc_close.argtypes = [P]
+    L.vqb_ep_dispatch.restype = i32
+    L.vqb_ep_dispatch.argtypes = [P, P, P, i32, i32, P, P, P, P]
+    L.vqb_ep_combine.restype = i32
+    L.vqb_ep_combine.argtypes = [P, P, P, i32, P, P]
+    L.vqb_ep_reduce.restype = i32
+    L.vqb_ep_reduce.argtypes = [P, P, P, i32, i32, P]
     return L
 
 
@@ -148,7 +179,9 @@ def exported_symbols():
     return ["vqb_version", "vqb_status_string", "vqb_unpack", "vqb_switch_workspace_size",
             "vqb_switch_forward", "vqb_dense_workspace_size", "vqb_dense_forward", "vqb_switch_forward_static",
             "vqb_launch_count", "vqb_time_next_kernel", "vqb_swiglu", "vqb_moe_combine", "vqb_switch_path",
-            "vqb_moe_combine_partial"]
+            "vqb_moe_combine_partial", "vqb_ep_region_bytes", "vqb_ep_region_alloc", "vqb_ep_region_free",
+            "vqb_ep_ipc_handle", "vqb_ep_ipc_open", "vqb_ep_ipc_close", "vqb_ep_dispatch", "vqb_ep_combine",
+            "vqb_ep_reduce"]
 
 
 def launch_count() -> int:

@@ -43,16 +43,26 @@ graph:
 The all-gathered rows are world x static_tokens x H; for a decode batch that
 is a few MB over NVLink.  The numerics differ from the single-GPU block only
 in the fp32 summation order over slots (grouped by rank).
+
+With exchange="p2p" the fixed-shape path moves the same data without NCCL
+(PeerExchange, vqb_ep_* in include/vqb.h): every rank writes its rows, expert
+slots and weights straight into the other ranks' exchange regions (CUDA IPC
+mappings over NVLink), and writes each token's partial sum straight into the
+owner's region, three library kernels per layer with the waits inside them.
+The arithmetic is the NCCL path's (same slot sums, same rank-order sum).
 """
 from __future__ import annotations
 
+import ctypes
 from dataclasses import dataclass
 from typing import Callable, Optional
 
 import torch
 import torch.distributed as dist
 
+from . import _lib
 from .moe import combine, expert_mlp, route
+from .vq_switch import _DTYPES, _stream_ptr
 
 
 @dataclass
@@ -104,6 +114,161 @@ def _a2a(t: torch.Tensor, out_rows: int, out_split, in_split, group) -> torch.Te
     return out
 
 
+class _DeviceBytes:
+    """A raw device allocation seen by torch through __cuda_array_interface__
+    (zero-copy; the owner keeps the memory alive)."""
+
+    def __init__(self, ptr: int, nbytes: int):
+        self.__cuda_array_interface__ = {"shape": (nbytes,), "typestr": "|u1", "data": (ptr, False),
+                                         "version": 2, "strides": None}
+
+
+class PeerExchange:
+    """The exchange regions of one rank for the peer-memory fixed-shape path
+    (vqb_ep_region_alloc / vqb_ep_ipc_* / vqb_ep_dispatch / _combine / _reduce).
+
+    Set-up is collective over `group` (an all-gather of the 64-byte IPC
+    handles and a barrier): every rank constructs its exchange at the same
+    point, outside any CUDA graph capture.  `emulated(...)` builds `world`
+    exchanges over regions of ONE GPU for single-GPU tests; each step then
+    runs every rank's phase 1 before any rank's phase 2 (phases=1 / 2), so
+    that no launch waits on a later one.
+    """
+
+    def __init__(self, tokens: int, top_k: int, hidden: int, experts_per_rank: int, dtype=torch.bfloat16,
+                 device=None, group=None, wait_limit_us: int = 2_000_000, _regions=None, _rank=None, _world=None):
+        L = _lib.lib()
+        dev = torch.device(device) if device is not None else torch.device("cuda")
+        self.device = dev if dev.index is not None else torch.device("cuda", torch.cuda.current_device())
+        emulated = _regions is not None
+        self.world = _world if emulated else (dist.get_world_size(group) if dist.is_initialized() else 1)
+        self.rank = _rank if emulated else (dist.get_rank(group) if dist.is_initialized() else 0)
+        if self.world > _lib.VQB_EP_MAX_WORLD:
+            raise ValueError(f"peer exchange spans at most {_lib.VQB_EP_MAX_WORLD} ranks, got {self.world}")
+        if dtype not in (torch.bfloat16, torch.float16):
+            raise ValueError("peer exchange rows are bf16 or fp16")
+        self.tokens, self.top_k, self.hidden, self.dtype = int(tokens), int(top_k), int(hidden), dtype
+        self.group = group
+        self.layout = _lib.EpLayout(self.world, self.rank, self.tokens, self.top_k, self.hidden, int(experts_per_rank))
+        offs = (ctypes.c_size_t * 4)()
+        self.nbytes = int(L.vqb_ep_region_bytes(ctypes.byref(self.layout), offs))
+        if self.nbytes == 0:
+            raise ValueError("peer exchange: invalid layout (world, tokens, top_k, hidden % 8, experts)")
+        self._opened = []
+        self._own = None
+        if emulated:
+            ptrs = list(_regions)
+        else:
+            own = ctypes.c_void_p()
+            _lib.check(L.vqb_ep_region_alloc(ctypes.byref(self.layout), ctypes.byref(own)), "vqb_ep_region_alloc")
+            self._own = own.value
+            ptrs = [None] * self.world
+            ptrs[self.rank] = self._own
+            if self.world > 1:
+                h = (ctypes.c_ubyte * _lib.VQB_EP_IPC_HANDLE_BYTES)()
+                _lib.check(L.vqb_ep_ipc_handle(ctypes.c_void_p(self._own), h), "vqb_ep_ipc_handle")
+                mine = torch.tensor(list(h), dtype=torch.uint8, device=self.device)
+                every = torch.empty(self.world * mine.numel(), dtype=torch.uint8, device=self.device)
+                dist.all_gather_into_tensor(every, mine, group=group)
+                every = every.cpu().reshape(self.world, -1).tolist()
+                for r in range(self.world):
+                    if r == self.rank:
+                        continue
+                    hr = (ctypes.c_ubyte * _lib.VQB_EP_IPC_HANDLE_BYTES)(*every[r])
+                    pr = ctypes.c_void_p()
+                    _lib.check(L.vqb_ep_ipc_open(hr, ctypes.byref(pr)), "vqb_ep_ipc_open")
+                    self._opened.append(pr.value)
+                    ptrs[r] = pr.value
+                dist.barrier(group=group)
+        self._regions = (ctypes.c_void_p * self.world)(*ptrs)
+        self._opts = {ph: _lib.EpOptions(ph, int(wait_limit_us)) for ph in (0, 1, 2, 3)}
+        base = torch.as_tensor(_DeviceBytes(ptrs[self.rank], self.nbytes), device=self.device)
+        R, k, H = self.world * self.tokens, self.top_k, self.hidden
+        self.x_rows = base[offs[0]:offs[0] + R * H * 2].view(dtype).view(R, H)
+        self.slots = base[offs[1]:offs[1] + R * k * 4].view(torch.int32).view(R, k)
+        self.weights = base[offs[2]:offs[2] + R * k * 4].view(torch.float32).view(R, k)
+        self.partials = base[offs[3]:offs[3] + R * H * 4].view(torch.float32).view(self.world, self.tokens, H)
+        off = _lib.VQB_EP_STATUS_OFFSET
+        self._status = base[off:off + 4].view(torch.int32)
+
+    @classmethod
+    def emulated(cls, world: int, tokens: int, top_k: int, hidden: int, experts_per_rank: int, dtype=torch.bfloat16,
+                 wait_limit_us: int = 2_000_000):
+        """`world` exchanges over regions on the current GPU (tests without peers)."""
+        L = _lib.lib()
+        lay = _lib.EpLayout(world, 0, tokens, top_k, hidden, experts_per_rank)
+        regions = []
+        for _ in range(world):
+            p = ctypes.c_void_p()
+            _lib.check(L.vqb_ep_region_alloc(ctypes.byref(lay), ctypes.byref(p)), "vqb_ep_region_alloc")
+            regions.append(p.value)
+        ex = [cls(tokens, top_k, hidden, experts_per_rank, dtype, device="cuda", wait_limit_us=wait_limit_us,
+                  _regions=regions, _rank=r, _world=world) for r in range(world)]
+        ex[0]._emulated_regions = regions
+        return ex
+
+    def dispatch(self, x: torch.Tensor, idx: torch.Tensor, w: torch.Tensor, phases: int = 0) -> None:
+        """x [T, H] (T <= tokens), idx [T, k] global expert ids, w [T, k] -> every rank's region."""
+        T, H = x.shape
+        if H != self.hidden or x.dtype != self.dtype or T > self.tokens or idx.shape != (T, self.top_k):
+            raise ValueError(f"dispatch: x {tuple(x.shape)} {x.dtype}, idx {tuple(idx.shape)} do not fit the exchange "
+                             f"(tokens {self.tokens}, hidden {self.hidden}, top_k {self.top_k}, {self.dtype})")
+        x = x.contiguous()
+        idx = idx.to(torch.int32).contiguous()
+        w = w.to(torch.float32).contiguous()
+        _lib.check(_lib.lib().vqb_ep_dispatch(ctypes.byref(self.layout), self._regions, ctypes.c_void_p(x.data_ptr()),
+                                              _DTYPES[x.dtype], T, ctypes.c_void_p(idx.data_ptr()),
+                                              ctypes.c_void_p(w.data_ptr()), ctypes.byref(self._opts[phases]),
+                                              _stream_ptr(x.device)), "vqb_ep_dispatch")
+
+    def combine(self, d: torch.Tensor, phases: int = 0) -> None:
+        """d [world * tokens, top_k, hidden]: the projections' output for x_rows / slots."""
+        if d.shape != (self.world * self.tokens, self.top_k, self.hidden) or d.dtype not in (torch.bfloat16,
+                                                                                              torch.float16):
+            raise ValueError(f"combine: expects [{self.world * self.tokens}, {self.top_k}, {self.hidden}] bf16/fp16")
+        d = d.contiguous()
+        _lib.check(_lib.lib().vqb_ep_combine(ctypes.byref(self.layout), self._regions, ctypes.c_void_p(d.data_ptr()),
+                                             _DTYPES[d.dtype], ctypes.byref(self._opts[phases]),
+                                             _stream_ptr(d.device)), "vqb_ep_combine")
+
+    def reduce(self, n_tokens: int, dtype=None) -> torch.Tensor:
+        """y [n_tokens, hidden]: this rank's tokens, the ranks' partials summed in rank order."""
+        dtype = dtype or self.dtype
+        y = torch.empty((n_tokens, self.hidden), dtype=dtype, device=self.device)
+        _lib.check(_lib.lib().vqb_ep_reduce(ctypes.byref(self.layout), ctypes.c_void_p(self._regions[self.rank]),
+                                            ctypes.c_void_p(y.data_ptr()), _DTYPES[dtype], n_tokens,
+                                            _stream_ptr(self.device)), "vqb_ep_reduce")
+        return y
+
+    def status(self) -> int:
+        """VQB_OK, or VQB_TIMEOUT once a wait in this rank's kernels gave up (synchronises)."""
+        return int(self._status.item())
+
+    def check(self) -> None:
+        _lib.check(self.status(), "peer exchange")
+
+    def close(self) -> None:
+        """Collective: every rank stops using the peers' regions before any region is freed."""
+        if self._regions is None:
+            return
+        torch.cuda.synchronize(self.device)
+        L = _lib.lib()
+        if self._own is not None and self.world > 1:
+            dist.barrier(group=self.group)
+        for p in self._opened:
+            L.vqb_ep_ipc_close(ctypes.c_void_p(p))
+        self._opened = []
+        if self._own is not None:
+            if self.world > 1:
+                dist.barrier(group=self.group)
+            L.vqb_ep_region_free(ctypes.c_void_p(self._own))
+            self._own = None
+        for p in getattr(self, "_emulated_regions", []):
+            L.vqb_ep_region_free(ctypes.c_void_p(p))
+        self._emulated_regions = []
+        self._regions = None
+
+
 class EPMoEBlock(torch.nn.Module):
     """One MoE layer with its experts sharded over the ranks of `group`.
 
@@ -113,9 +278,15 @@ class EPMoEBlock(torch.nn.Module):
 
     def __init__(self, gate_proj, up_proj, down_proj, top_k: int, num_experts: int, group=None,
                  experts: Optional[Callable[[torch.Tensor, torch.Tensor], torch.Tensor]] = None,
-                 static_tokens: Optional[int] = None):
+                 static_tokens: Optional[int] = None, exchange: str = "nccl"):
         super().__init__()
         self.static_tokens = int(static_tokens) if static_tokens else None
+        if exchange not in ("nccl", "p2p"):
+            raise ValueError(f"exchange must be 'nccl' or 'p2p', not {exchange!r}")
+        if exchange == "p2p" and not self.static_tokens:
+            raise ValueError("exchange='p2p' serves the fixed-shape path: give static_tokens")
+        self.exchange = exchange
+        self._peer: Optional[PeerExchange] = None
         self.gate_proj, self.up_proj, self.down_proj = gate_proj, up_proj, down_proj
         self.top_k = int(top_k)
         self.group = group
@@ -147,6 +318,35 @@ class EPMoEBlock(torch.nn.Module):
             dist.all_gather(list(out.chunk(self.world)), t.contiguous(), group=self.group)
         return out
 
+    def peer_exchange(self, hidden: int, dtype, device) -> PeerExchange:
+        """This rank's PeerExchange (collective on first use, and again when
+        static_tokens, the hidden size or the dtype changed: every rank makes
+        it together)."""
+        p = self._peer
+        if p is not None and (p.tokens, p.hidden, p.dtype) != (self.static_tokens, hidden, dtype):
+            self.close()
+        if self._peer is None:
+            self._peer = PeerExchange(self.static_tokens, self.top_k, hidden, self.experts_per_rank, dtype=dtype,
+                                      device=device, group=self.group)
+        return self._peer
+
+    def close(self) -> None:
+        """Release the peer exchange (collective); the NCCL path holds nothing."""
+        if self._peer is not None:
+            self._peer.close()
+            self._peer = None
+
+    def _forward_p2p(self, x: torch.Tensor, idx: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
+        T, H = x.shape
+        C, k, W = self.static_tokens, self.top_k, self.world
+        ex = self.peer_exchange(H, x.dtype, x.device)
+        ex.dispatch(x, idx, w)
+        X = ex.x_rows.reshape(W * C, 1, 1, H)
+        self.last_pairs = (X, ex.slots)
+        d = expert_mlp(self.gate_proj, self.up_proj, self.down_proj, X, ex.slots)
+        ex.combine(d.reshape(W * C, k, -1))
+        return ex.reduce(T, x.dtype)
+
     def forward_static(self, x: torch.Tensor, router_logits: torch.Tensor) -> torch.Tensor:
         """The fixed-shape path (module docstring): T <= static_tokens on every rank."""
         T, H = x.shape
@@ -154,6 +354,8 @@ class EPMoEBlock(torch.nn.Module):
         if T > C:
             raise ValueError(f"{T} tokens exceed static_tokens={C}")
         idx, w = route(router_logits, k)
+        if self.exchange == "p2p" and x.is_cuda and self._experts == self._vq_experts:
+            return self._forward_p2p(x, idx, w)
         xp = x.new_zeros((C, H))
         xp[:T] = x
         ip = torch.full((C, k), -1, dtype=torch.int32, device=x.device)
