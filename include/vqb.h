@@ -85,6 +85,9 @@ typedef struct vqb_linear_desc {
                                  [E, OUT, ...] layout.  Dead rows read no bytes and write +0. */
   int32_t num_rows;           /* with row_table: rows of the compact codes [num_rows, WPR] and scales
                                  [num_rows, IN/G]; entries >= num_rows are treated as dead */
+  const void* codebook_halves; /* optional, D = 8 only: the codebook's two dimension halves, fp16
+                                 [2][K][4] (vqb_codebook_halves), 16-byte aligned; NULL = a call on
+                                 the grouped GEMM derives them itself (one more kernel per call) */
 } vqb_linear_desc;
 
 /* Optional knobs; pass NULL for defaults. */
@@ -121,6 +124,14 @@ const char* vqb_status_string(vqb_status status);
  * reader _unpack_rows (src/vqlab/runtime/vq_dense.py:140-184). */
 vqb_status vqb_unpack(const uint32_t* packed, int64_t rows, int64_t wpr, int32_t nsub,
                       int32_t bits, uint16_t* out, vqb_stream_t stream);
+
+/* The two dimension halves of a d8 codebook: out fp16 [2][K][4] = dims 0-3 of
+ * every entry, then dims 4-7 (codebook fp16 [K][8], both 16-byte aligned).
+ * The grouped GEMM keeps one half of a d8/K16384 codebook in shared memory per
+ * pass and reads it in this layout; a caller that builds it once per codebook
+ * and passes it as vqb_linear_desc.codebook_halves saves that kernel on every
+ * call.  No reference counterpart (the reference's kernels read [K][D]). */
+vqb_status vqb_codebook_halves(const void* codebook, int32_t num_codes, void* out, vqb_stream_t stream);
 
 /* Expert index of a pair to leave out: vqb_switch_forward computes nothing
  * for it and does not write its output row (expert parallelism marks the

@@ -251,3 +251,20 @@ def test_ep_block_exchange_argument():
         EPMoEBlock(None, None, None, 2, num_experts=4, exchange="nvshmem")
     with pytest.raises(ValueError):
         EPMoEBlock(None, None, None, 2, num_experts=4, exchange="p2p")  # needs static_tokens
+
+
+def test_codebook_halves_validation():
+    """vqb_codebook_halves and the desc's codebook_halves field are checked on
+    the host: D must be 8, pointers 16-byte aligned and non-null."""
+    L = _lib.lib()
+    assert L.vqb_codebook_halves(ctypes.c_void_p(256), 0, ctypes.c_void_p(256), None) == _lib.VQB_BAD_SHAPE
+    assert L.vqb_codebook_halves(None, 16, ctypes.c_void_p(256), None) == _lib.VQB_NULL_POINTER
+    assert L.vqb_codebook_halves(ctypes.c_void_p(264), 16, ctypes.c_void_p(256), None) == _lib.VQB_BAD_ALIGNMENT
+    d = _lib.LinearDesc(num_experts=2, out_features=16, in_features=64, dim=4, num_codes=256, group_size=64,
+                        pack_bits=8, codes=256, codebook=256, scales=256, codebook_halves=256)
+    y = ctypes.c_void_p(256)
+    st = L.vqb_switch_forward(ctypes.byref(d), y, _lib.VQB_BF16, 1, y, 1, y, _lib.VQB_BF16, y, 1 << 20, None, None)
+    assert st == _lib.VQB_BAD_SHAPE  # halves given for a d4 codebook
+    d.dim, d.num_codes, d.codebook_halves = 8, 256, 264
+    st = L.vqb_switch_forward(ctypes.byref(d), y, _lib.VQB_BF16, 1, y, 1, y, _lib.VQB_BF16, y, 1 << 20, None, None)
+    assert st == _lib.VQB_BAD_ALIGNMENT

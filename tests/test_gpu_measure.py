@@ -64,8 +64,8 @@ def test_switch_path_query_names_the_kernel():
     assert m.kernel_path(4, 2) == "gemm"  # forced
     m.options = None
     assert m.kernel_path(4, 2) == "decode"  # K4096 fits shared memory: decode up to 512 pairs
-    # the count of launches of one call matches the family: GEMM = route + gather + codebook halves + GEMM
-    # (+ the split-K reduction when the call has few tiles)
+    # the count of launches of one call matches the family: GEMM = route + gather + GEMM (+ the split-K
+    # reduction when the call has few tiles); the d8 codebook's halves were built once by the first call
     x = torch.zeros((8, 1, 1, 512), dtype=torch.bfloat16, device="cuda")
     idx = torch.arange(80, device="cuda", dtype=torch.int32).reshape(8, 10) % 4
     mb(x, idx)
@@ -73,4 +73,4 @@ def test_switch_path_query_names_the_kernel():
     c0 = _lib.launch_count()
     mb(x, idx)
     torch.cuda.synchronize()
-    assert _lib.launch_count() - c0 in (4, 5)
+    assert _lib.launch_count() - c0 in (3, 4)

@@ -228,3 +228,38 @@ def test_switch_decode_batch_split_k(T):
     assert m.kernel_path(T, k) == "gemm"
     y = m(x.cuda(), torch.from_numpy(idx.astype(np.int32)).cuda()).float().cpu().numpy().reshape(T * k, OUT)
     _check(L, x, idx.reshape(-1), k, y)
+
+
+class _NoHalves:
+    """Stands in for a module's CodebookHalves: always NULL, so every call
+    derives the dimension halves itself."""
+
+    def pointer(self, codebook):
+        return None
+
+
+def test_codebook_halves_built_once_give_the_same_bytes():
+    """A module passes its d8 codebook's dimension halves, built once
+    (vqb_codebook_halves), to every call; the result must be byte-equal to a
+    call that derives them inside, for the switch and the dense entry point,
+    and the halves must follow an in-place change of the codebook."""
+    L = make_layer(E=5, OUT=256, IN=1024, D=8, K=16384, G=64, seed=77)
+    T, k = 40, 3
+    idx = torch.from_numpy(skewed_routing(T, k, 5, seed=3).astype(np.int32)).cuda()
+    x = torch.randn((T, 1, 1, 1024), generator=torch.Generator().manual_seed(5)).to(torch.bfloat16).cuda()
+    a, b = _switch(L, path=2), _switch(L, path=2)
+    b._halves = _NoHalves()
+    ya = a(x, idx)
+    assert a._halves.pointer(a.codebook) is not None
+    assert torch.equal(ya.view(torch.int16), b(x, idx).view(torch.int16))
+    # in place: the cached halves are rebuilt (the tensor's version counter moved)
+    a.codebook.mul_(0.5)
+    b.codebook.mul_(0.5)
+    assert torch.equal(a(x, idx).view(torch.int16), b(x, idx).view(torch.int16))
+    assert not torch.equal(a(x, idx).view(torch.int16), ya.view(torch.int16))
+    codes, cb, sc = to_torch(L)
+    da = VQLinear(codes[0], cb, sc[0], group_size=64, pack_bits=L.bits, in_features=1024)
+    db = VQLinear(codes[0], cb.clone(), sc[0], group_size=64, pack_bits=L.bits, in_features=1024)
+    db._halves = _NoHalves()
+    xd = x.reshape(T, 1024)
+    assert torch.equal(da(xd).view(torch.int16), db(xd).view(torch.int16))

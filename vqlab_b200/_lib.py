@@ -50,6 +50,7 @@ class LinearDesc(ctypes.Structure):
         ("scales", ctypes.c_void_p),
         ("row_table", ctypes.c_void_p),
         ("num_rows", ctypes.c_int32),
+        ("codebook_halves", ctypes.c_void_p),
     ]
 
 
@@ -116,6 +117,8 @@ def _bind(L):
     L.vqb_switch_path.argtypes = [P, i32, i32, P]
     L.vqb_moe_combine_partial.restype = i32
     L.vqb_moe_combine_partial.argtypes = [P, P, P, P, i32, i32, i32, i32, P]
+    L.vqb_codebook_halves.restype = i32
+    L.vqb_codebook_halves.argtypes = [P, i32, P, P]
     L.vqb_ep_region_bytes.restype = sz
     L.vqb_ep_region_bytes.argtypes = [P, P]
     L.vqb_ep_region_alloc.restype = i32
@@ -179,7 +182,7 @@ def exported_symbols():
     return ["vqb_version", "vqb_status_string", "vqb_unpack", "vqb_switch_workspace_size",
             "vqb_switch_forward", "vqb_dense_workspace_size", "vqb_dense_forward", "vqb_switch_forward_static",
             "vqb_launch_count", "vqb_time_next_kernel", "vqb_swiglu", "vqb_moe_combine", "vqb_switch_path",
-            "vqb_moe_combine_partial", "vqb_ep_region_bytes", "vqb_ep_region_alloc", "vqb_ep_region_free",
+            "vqb_moe_combine_partial", "vqb_codebook_halves", "vqb_ep_region_bytes", "vqb_ep_region_alloc", "vqb_ep_region_free",
             "vqb_ep_ipc_handle", "vqb_ep_ipc_open", "vqb_ep_ipc_close", "vqb_ep_dispatch", "vqb_ep_combine",
             "vqb_ep_reduce"]
 
@@ -194,3 +197,32 @@ def time_next_kernel(start_event, stop_event) -> None:
     thread's next projection call (on the call's stream), then disarm."""
     check(lib().vqb_time_next_kernel(ctypes.c_void_p(start_event.cuda_event), ctypes.c_void_p(stop_event.cuda_event)),
           "vqb_time_next_kernel")
+
+
+class CodebookHalves:
+    """The [2][K][4] dimension halves of a d8 codebook (vqb_codebook_halves),
+    built once and rebuilt only when the codebook tensor is replaced or
+    modified in place (its data pointer, shape or version counter changes).
+    Never built while a CUDA graph is being captured: the call then passes
+    NULL and the library derives the halves inside the call."""
+
+    def __init__(self):
+        self._key = None
+        self._t = None
+
+    def pointer(self, codebook):
+        import torch
+        if codebook.dim() != 2 or int(codebook.shape[1]) != 8 or not codebook.is_cuda \
+                or codebook.dtype != torch.float16 or not codebook.is_contiguous():
+            return None
+        key = (codebook.data_ptr(), tuple(codebook.shape), codebook._version, codebook.device)
+        if key != self._key:
+            if torch.cuda.is_current_stream_capturing():
+                return None
+            K = int(codebook.shape[0])
+            t = torch.empty((2, K, 4), dtype=torch.float16, device=codebook.device)
+            stream = ctypes.c_void_p(torch.cuda.current_stream(codebook.device).cuda_stream)
+            check(lib().vqb_codebook_halves(ctypes.c_void_p(codebook.data_ptr()), K, ctypes.c_void_p(t.data_ptr()),
+                                            stream), "vqb_codebook_halves")
+            self._t, self._key = t, key
+        return self._t.data_ptr()

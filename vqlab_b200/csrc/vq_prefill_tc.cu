@@ -1316,8 +1316,10 @@ vqb_status launch_prefill_tc(const LinearGeometry& geo, const void* x, int x_dty
     if (cudaGetLastError() != cudaSuccess) return VQB_CUDA_ERROR;
     note_launch();
   }
-  // 1a. dimension halves of the codebook
-  if (ds) {
+  // 1a. dimension halves of the codebook (the caller's, when it built them once)
+  if (ds && geo.codebook_halves) {
+    prm.codebook = static_cast<const uint16_t*>(geo.codebook_halves);
+  } else if (ds) {
     split_codebook_kernel<<<static_cast<unsigned>((geo.K + 255) / 256), 256, 0, stream>>>(prm.codebook, geo.K,
                                                                                           cb_split);
     if (cudaGetLastError() != cudaSuccess) return VQB_CUDA_ERROR;
@@ -1380,3 +1382,16 @@ vqb_status launch_prefill_tc(const LinearGeometry& geo, const void* x, int x_dty
 }
 
 }  // namespace vqb
+
+extern "C" vqb_status vqb_codebook_halves(const void* codebook, int32_t num_codes, void* out, vqb_stream_t stream) {
+  if (num_codes < 1) return VQB_BAD_SHAPE;
+  if (!codebook || !out) return VQB_NULL_POINTER;
+  if ((reinterpret_cast<uintptr_t>(codebook) & 15) != 0 || (reinterpret_cast<uintptr_t>(out) & 15) != 0)
+    return VQB_BAD_ALIGNMENT;
+  vqb::split_codebook_kernel<<<static_cast<unsigned>((num_codes + 255) / 256), 256, 0,
+                               reinterpret_cast<cudaStream_t>(stream)>>>(static_cast<const uint16_t*>(codebook),
+                                                                         num_codes, static_cast<uint16_t*>(out));
+  if (cudaGetLastError() != cudaSuccess) return VQB_CUDA_ERROR;
+  vqb::note_launch();
+  return VQB_OK;
+}

@@ -42,6 +42,10 @@ vqb_status validate(const vqb_linear_desc* d, LinearGeometry* g) {
   }
   if ((reinterpret_cast<uintptr_t>(d->codebook) & 15) != 0 || (reinterpret_cast<uintptr_t>(d->scales) & 1) != 0)
     return VQB_BAD_ALIGNMENT;
+  if (d->codebook_halves) {
+    if (d->dim != 8) return VQB_BAD_SHAPE;
+    if ((reinterpret_cast<uintptr_t>(d->codebook_halves) & 15) != 0) return VQB_BAD_ALIGNMENT;
+  }
   g->E = d->num_experts;
   g->OUT = d->out_features;
   g->IN = d->in_features;
@@ -55,6 +59,7 @@ vqb_status validate(const vqb_linear_desc* d, LinearGeometry* g) {
   g->scales = d->scales;
   g->row_table = d->row_table;
   g->nrows = d->row_table ? static_cast<int64_t>(d->num_rows) : static_cast<int64_t>(g->E) * g->OUT;
+  g->codebook_halves = d->codebook_halves;
   return VQB_OK;
 }
 

@@ -17,6 +17,7 @@ struct LinearGeometry {
   const void* scales;
   const int32_t* row_table;  // SKIPZERO [E, OUT] -> compact row, -1 dead; nullptr = plain layout
   int64_t nrows;             // rows of codes / scales (E * OUT, or the compact live-row count)
+  const void* codebook_halves;  // d8: caller-built [2][K][4] halves, nullptr = derived per call
 };
 
 vqb_status validate(const vqb_linear_desc* d, LinearGeometry* out);

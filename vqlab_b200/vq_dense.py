@@ -32,6 +32,7 @@ class VQLinear(torch.nn.Module):
         self._k_expect = int(codebook.shape[0])
         self._code_bytes = _code_meta(codes, self.pack_bits)
         self.options = None
+        self._halves = _lib.CodebookHalves()  # d8: the GEMM's codebook layout, built once per codebook
 
     @property
     def input_dims(self) -> int:
@@ -59,6 +60,7 @@ class VQLinear(torch.nn.Module):
         d.codebook = self.codebook.data_ptr()
         d.scales = self.vq_scales.data_ptr()
         d.row_table = None
+        d.codebook_halves = self._halves.pointer(self.codebook)
         return d
 
     def forward(self, x: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:

@@ -90,6 +90,7 @@ class VQSwitchLinear(torch.nn.Module):
         self._k_expect = int(codebook.shape[0])
         self._code_bytes = _code_meta(codes, self.pack_bits)
         self.options = None  # optional _lib.Options for tests / A-B runs
+        self._halves = _lib.CodebookHalves()  # d8: the GEMM's codebook layout, built once per codebook
 
     @classmethod
     def from_weights(cls, codes, codebook, vq_scales):
@@ -145,6 +146,7 @@ class VQSwitchLinear(torch.nn.Module):
         else:
             d.row_table = None
             d.num_rows = 0
+        d.codebook_halves = self._halves.pointer(self.codebook)
         return d
 
     def _check_tensors(self):
