@@ -198,6 +198,16 @@ vqb_status vqb_swiglu(const void* gate, const void* up, void* out, int64_t n, vq
 vqb_status vqb_moe_combine(const void* expert_out, const float* weights, void* out, int32_t n_tokens,
                            int32_t top_k, int32_t hidden, vqb_dtype dtype, vqb_stream_t stream);
 
+/* The block's router in one kernel: for each of n_tokens rows of fp32
+ * router logits [n_tokens, num_experts], p = softmax(logits) in fp32, the
+ * top_k largest p in descending order (the lower expert id first on a tie)
+ * -> indices int32 [n_tokens, top_k], and weights fp32 [n_tokens, top_k] =
+ * p / (sum of the selected p), always renormalised -- the router convention
+ * of family/qwen3_5.py:110-118 restated by tests/test_qwen3_5_parity.py:180-204.
+ * num_experts <= 8192, top_k <= 32. */
+vqb_status vqb_moe_route(const float* logits, int32_t n_tokens, int32_t num_experts, int32_t top_k,
+                         int32_t* indices, float* weights, vqb_stream_t stream);
+
 /* Expert-parallel partial combine: out[t, :] = sum_j w[t, j] * expert_out[t, j, :]
  * over the slots whose indices[t, j] != VQB_SKIP_EXPERT (indices may be NULL:
  * every slot), slot order, fp32 out [n_tokens, hidden] with no rounding; a

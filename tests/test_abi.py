@@ -268,3 +268,15 @@ def test_codebook_halves_validation():
     d.dim, d.num_codes, d.codebook_halves = 8, 256, 264
     st = L.vqb_switch_forward(ctypes.byref(d), y, _lib.VQB_BF16, 1, y, 1, y, _lib.VQB_BF16, y, 1 << 20, None, None)
     assert st == _lib.VQB_BAD_ALIGNMENT
+
+
+def test_router_validation():
+    L = _lib.lib()
+    p = ctypes.c_void_p(256)
+    assert L.vqb_moe_route(p, 4, 512, 0, p, p, None) == _lib.VQB_BAD_SHAPE
+    assert L.vqb_moe_route(p, 4, 512, 33, p, p, None) == _lib.VQB_BAD_SHAPE
+    assert L.vqb_moe_route(p, 4, 8, 9, p, p, None) == _lib.VQB_BAD_SHAPE
+    assert L.vqb_moe_route(p, 4, 9000, 8, p, p, None) == _lib.VQB_BAD_SHAPE
+    assert L.vqb_moe_route(p, -1, 512, 8, p, p, None) == _lib.VQB_BAD_SHAPE
+    assert L.vqb_moe_route(None, 4, 512, 8, p, p, None) == _lib.VQB_NULL_POINTER
+    assert L.vqb_moe_route(None, 0, 512, 8, None, None, None) == _lib.VQB_OK

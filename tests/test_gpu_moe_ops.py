@@ -62,3 +62,37 @@ def test_empty_and_errors():
         swiglu(torch.ones(4, device="cuda"), torch.ones(5, device="cuda"))
     with pytest.raises(ValueError):
         combine(torch.ones((2, 3), device="cuda"), torch.ones((2, 3), device="cuda"))
+
+
+def _torch_route(lg, k):
+    pr = torch.softmax(lg.float(), dim=-1)
+    w, idx = torch.topk(pr, k, dim=-1, sorted=True)
+    return idx.to(torch.int32), w / w.sum(dim=-1, keepdim=True)
+
+
+@pytest.mark.parametrize("T,E,k", [(1, 512, 10), (64, 512, 10), (4096, 512, 10), (7, 600, 4), (33, 8, 1),
+                                   (5, 64, 32), (3, 5000, 8)])
+def test_router_kernel_matches_torch(T, E, k):
+    """vqb_moe_route (one kernel) against torch softmax / topk / renormalise:
+    the same experts in the same order, weights within a few fp32 ulp (the
+    softmax and selected sums are added in another order)."""
+    from vqlab_b200.moe import route
+    g = torch.Generator(device="cuda").manual_seed(T * E + k)
+    lg = torch.randn((T, E), device="cuda", generator=g) * 2
+    lg[:, 0] += 3.0  # a popular expert
+    idx, w = route(lg, k)
+    ridx, rw = _torch_route(lg, k)
+    assert idx.dtype == torch.int32 and w.dtype == torch.float32
+    assert torch.equal(idx, ridx)
+    assert torch.allclose(w, rw, rtol=2e-6, atol=1e-9)
+    assert torch.allclose(w.sum(-1), torch.ones(T, device="cuda"), rtol=1e-5)
+
+
+def test_router_kernel_ties_take_the_lower_expert():
+    from vqlab_b200.moe import route
+    lg = torch.zeros((2, 64), device="cuda")
+    lg[1, 40] = 1.0
+    idx, w = route(lg, 4)
+    assert idx[0].tolist() == [0, 1, 2, 3]
+    assert idx[1].tolist() == [40, 0, 1, 2]
+    assert torch.allclose(w[0], torch.full((4,), 0.25, device="cuda"))

@@ -117,6 +117,8 @@ def _bind(L):
     L.vqb_switch_path.argtypes = [P, i32, i32, P]
     L.vqb_moe_combine_partial.restype = i32
     L.vqb_moe_combine_partial.argtypes = [P, P, P, P, i32, i32, i32, i32, P]
+    L.vqb_moe_route.restype = i32
+    L.vqb_moe_route.argtypes = [P, i32, i32, i32, P, P, P]
     L.vqb_codebook_halves.restype = i32
     L.vqb_codebook_halves.argtypes = [P, i32, P, P]
     L.vqb_ep_region_bytes.restype = sz
@@ -182,7 +184,7 @@ def exported_symbols():
     return ["vqb_version", "vqb_status_string", "vqb_unpack", "vqb_switch_workspace_size",
             "vqb_switch_forward", "vqb_dense_workspace_size", "vqb_dense_forward", "vqb_switch_forward_static",
             "vqb_launch_count", "vqb_time_next_kernel", "vqb_swiglu", "vqb_moe_combine", "vqb_switch_path",
-            "vqb_moe_combine_partial", "vqb_codebook_halves", "vqb_ep_region_bytes", "vqb_ep_region_alloc", "vqb_ep_region_free",
+            "vqb_moe_combine_partial", "vqb_moe_route", "vqb_codebook_halves", "vqb_ep_region_bytes", "vqb_ep_region_alloc", "vqb_ep_region_free",
             "vqb_ep_ipc_handle", "vqb_ep_ipc_open", "vqb_ep_ipc_close", "vqb_ep_dispatch", "vqb_ep_combine",
             "vqb_ep_reduce"]
 

@@ -132,6 +132,77 @@ __global__ void combine_partial_kernel(const T* __restrict__ d, const float* __r
   }
 }
 
+// The router of the MoE block in one pass, one warp per token: fp32 softmax
+// over the E logits (max-subtracted exp, divided by the sum), the top_k largest
+// probabilities by top_k rounds of a warp arg-max (larger probability first,
+// the lower expert id on a tie), their weights divided by the selected sum
+// (added in selection order).  The warp keeps its row of probabilities in
+// shared memory; a chosen entry is marked -1 (probabilities are >= 0).
+__global__ void __launch_bounds__(256) route_topk_kernel(const float* __restrict__ logits, int T, int E, int k,
+                                                         int32_t* __restrict__ idx, float* __restrict__ w) {
+  extern __shared__ float s_prob[];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nw = blockDim.x >> 5;
+  float* p = s_prob + static_cast<size_t>(warp) * E;
+  for (int t = blockIdx.x * nw + warp; t < T; t += gridDim.x * nw) {
+    const float* row = logits + static_cast<int64_t>(t) * E;
+    float m = -INFINITY;
+    for (int e = lane; e < E; e += 32) {
+      const float v = row[e];
+      p[e] = v;
+      m = fmaxf(m, v);
+    }
+    for (int o = 16; o; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    float sum = 0.0f;
+    for (int e = lane; e < E; e += 32) {
+      const float ex = expf(p[e] - m);
+      p[e] = ex;
+      sum += ex;
+    }
+    for (int o = 16; o; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+    for (int e = lane; e < E; e += 32) p[e] = __fdiv_rn(p[e], sum);
+    __syncwarp();
+    float mine_w = 0.0f, wsum = 0.0f;
+    int mine_i = 0;
+    for (int j = 0; j < k; ++j) {
+      float bv = -1.0f;
+      int bi = 0x7fffffff;
+      for (int e = lane; e < E; e += 32) {
+        const float v = p[e];
+        if (v > bv) {
+          bv = v;
+          bi = e;
+        }
+      }
+      for (int o = 16; o; o >>= 1) {
+        const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+        const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+        if (ov > bv || (ov == bv && oi < bi)) {
+          bv = ov;
+          bi = oi;
+        }
+      }
+      if (bi >= E) {  // no candidate left (NaN logits): expert 0, weight 0
+        bi = 0;
+        bv = 0.0f;
+      } else if ((bi & 31) == lane) {
+        p[bi] = -1.0f;
+      }
+      __syncwarp();
+      if (lane == j) {
+        mine_w = bv;
+        mine_i = bi;
+      }
+      wsum += bv;
+    }
+    if (lane < k) {
+      idx[static_cast<int64_t>(t) * k + lane] = mine_i;
+      w[static_cast<int64_t>(t) * k + lane] = __fdiv_rn(mine_w, wsum);
+    }
+    __syncwarp();
+  }
+}
+
 int g_sms_ops = 0;
 
 vqb_status ensure_sms() {
@@ -245,4 +316,29 @@ extern "C" vqb_status vqb_moe_combine_partial(const void* expert_out, const floa
   if (dtype == VQB_F16) return launch_combine_partial<__half>(expert_out, weights, indices, out, n_tokens, top_k, hidden, s);
   if (dtype == VQB_F32) return launch_combine_partial<float>(expert_out, weights, indices, out, n_tokens, top_k, hidden, s);
   return VQB_BAD_SHAPE;
+}
+
+extern "C" vqb_status vqb_moe_route(const float* logits, int32_t n_tokens, int32_t num_experts, int32_t top_k,
+                                    int32_t* indices, float* weights, vqb_stream_t stream) {
+  if (n_tokens < 0 || num_experts < 1 || num_experts > 8192 || top_k < 1 || top_k > 32 || top_k > num_experts)
+    return VQB_BAD_SHAPE;
+  if (n_tokens == 0) return VQB_OK;
+  if (!logits || !indices || !weights) return VQB_NULL_POINTER;
+  vqb_status st = ensure_sms();
+  if (st != VQB_OK) return st;
+  const size_t row_bytes = sizeof(float) * static_cast<size_t>(num_experts);
+  int nw = static_cast<int>((48 * 1024) / row_bytes);
+  nw = nw < 1 ? 1 : (nw > 8 ? 8 : nw);
+  const size_t smem = row_bytes * nw;
+  if (smem > 48 * 1024 &&
+      cudaFuncSetAttribute(route_topk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)) !=
+          cudaSuccess)
+    return VQB_CUDA_ERROR;
+  int64_t blocks = (static_cast<int64_t>(n_tokens) + nw - 1) / nw;
+  if (blocks > 8 * static_cast<int64_t>(g_sms_ops)) blocks = 8 * static_cast<int64_t>(g_sms_ops);
+  route_topk_kernel<<<static_cast<unsigned>(blocks), nw * 32, smem, reinterpret_cast<cudaStream_t>(stream)>>>(
+      logits, n_tokens, num_experts, top_k, indices, weights);
+  if (cudaGetLastError() != cudaSuccess) return VQB_CUDA_ERROR;
+  note_launch();
+  return VQB_OK;
 }

@@ -91,7 +91,19 @@ def combine_partial(d: torch.Tensor, w: torch.Tensor, ids: torch.Tensor | None =
 
 
 def route(router_logits: torch.Tensor, top_k: int):
-    """fp32 softmax, top-k, renormalise.  Returns (indices int32 [T,k], weights fp32 [T,k])."""
+    """fp32 softmax, top-k, renormalise.  Returns (indices int32 [T,k], weights fp32 [T,k]).
+    On CUDA one library kernel (vqb_moe_route); CPU tensors (the host-side
+    expert-parallel tests) take the same steps as torch ops."""
+    if router_logits.is_cuda and router_logits.dim() == 2 and 1 <= top_k <= min(32, router_logits.shape[1]) \
+            and router_logits.shape[1] <= 8192:
+        lg = router_logits.float().contiguous()
+        T, E = lg.shape
+        idx = torch.empty((T, top_k), dtype=torch.int32, device=lg.device)
+        w = torch.empty((T, top_k), dtype=torch.float32, device=lg.device)
+        _lib.check(_lib.lib().vqb_moe_route(ctypes.c_void_p(lg.data_ptr()), T, E, top_k,
+                                            ctypes.c_void_p(idx.data_ptr()), ctypes.c_void_p(w.data_ptr()),
+                                            _stream_ptr(lg.device)), "vqb_moe_route")
+        return idx, w
     pr = torch.softmax(router_logits.float(), dim=-1)
     w, idx = torch.topk(pr, top_k, dim=-1, sorted=True)
     w = w / w.sum(dim=-1, keepdim=True)
