@@ -586,6 +586,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  // Launched as a programmatic dependent of the kernel before it (the x
+  // gather): the set-up above overlaps that kernel's tail; nothing it wrote
+  // (routing tables, gathered x) and nothing it may still read is touched
+  // before this wait returns.
+  asm volatile("griddepcontrol.wait;" ::: "memory");
 
   const int nchunks = prm.meta[0];
   const int64_t nitems = static_cast<int64_t>(nchunks) * prm.row_tiles * prm.ksplit;
@@ -953,6 +958,8 @@ __global__ void tile_base_kernel(const int32_t* __restrict__ rt, int E, int OUT,
 __global__ void gather_sorted_kernel(const void* __restrict__ x, int x_dtype, const int* __restrict__ sorted,
                                      const int* __restrict__ n_sorted, int krep, int IN, int to_bf16, int dsplit,
                                      uint16_t* __restrict__ xs) {
+  // the grouped GEMM that follows may start its set-up now (it waits for this grid's end before reading xs)
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   const int vec = IN / 8;
   const bool convert = (x_dtype == VQB_BF16) != (to_bf16 != 0);
   const int64_t total = static_cast<int64_t>(*n_sorted) * vec;  // pairs left out are not in sorted
@@ -1363,7 +1370,20 @@ vqb_status launch_prefill_tc(const LinearGeometry& geo, const void* x, int x_dty
     return VQB_CUDA_ERROR;
   void* args[] = {&xmaps[0], &xmaps[1], &xmaps[2], &cmap, &smap, &prm};
   timer_before(stream);
-  const cudaError_t ce = cudaLaunchKernel(kern, dim3(g_sms_tc), dim3(kThreads), args, smem, stream);
+  // programmatic stream serialization: the GEMM's CTAs may launch while the
+  // kernel before it finishes; the kernel waits (griddepcontrol.wait) before
+  // touching anything that kernel wrote
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(g_sms_tc);
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  const cudaError_t ce = cudaLaunchKernelExC(&cfg, kern, args);
   timer_after(stream);
   if (ce != cudaSuccess || cudaGetLastError() != cudaSuccess) return VQB_CUDA_ERROR;
   note_launch();
