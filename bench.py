@@ -179,7 +179,7 @@ class ClockSampler:
 
 # ------------------------------------------------------------------ GPU arm
 
-def make_layer(torch, dev, seed, rank=0, world=1, exchange="nccl"):
+def make_layer(torch, dev, seed, rank=0, world=1, exchange="p2p"):
     """One seeded MoE layer; with world > 1 this rank's expert shard of it
     wrapped in the expert-parallel block (codebooks are per layer, so every
     rank builds the same ones)."""
@@ -666,7 +666,7 @@ def main(argv=None) -> int:
     ap.add_argument("--extra-batches", default="1,8")
     ap.add_argument("--layers", type=int, default=8)
     ap.add_argument("--skip-e2e", action="store_true")
-    ap.add_argument("--exchange", default="nccl", choices=["p2p", "nccl"],
+    ap.add_argument("--exchange", default="p2p", choices=["p2p", "nccl"],
                     help="expert-parallel decode exchange (N > 1): peer-memory kernels or NCCL collectives")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--skip-prefill", action="store_true")
