@@ -591,6 +591,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   // (routing tables, gathered x) and nothing it may still read is touched
   // before this wait returns.
   asm volatile("griddepcontrol.wait;" ::: "memory");
+  // the split-K reduction after this kernel may be scheduled beside it (it waits for this grid's end)
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 
   const int nchunks = prm.meta[0];
   const int64_t nitems = static_cast<int64_t>(nchunks) * prm.row_tiles * prm.ksplit;
@@ -1003,6 +1005,10 @@ __global__ void splitk_reduce_kernel(const float* __restrict__ partial, const in
                                      int S, int OUT, int cmax, void* y, int y_dtype, int round_f16_first,
                                      const int32_t* __restrict__ row_table, const int* __restrict__ tile_base,
                                      int64_t nrows) {
+  // launched as a programmatic dependent of the GEMM: wait for its partials; the
+  // kernel after this one (the next projection's GEMM) may begin its set-up
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   const int64_t ntiles = static_cast<int64_t>(meta[0]) * row_tiles;
   const int64_t total = ntiles * cmax * kTileM;
   for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
@@ -1392,10 +1398,19 @@ vqb_status launch_prefill_tc(const LinearGeometry& geo, const void* x, int x_dty
     const int64_t tiles = tiles_bound(N, geo.E, geo.OUT);
     int64_t blocks = (tiles * cmax * kTileM + 255) / 256;
     if (blocks > 8 * g_sms_tc) blocks = 8 * g_sms_tc;
-    splitk_reduce_kernel<<<static_cast<unsigned>(blocks), 256, 0, stream>>>(
-        prm.partial, rw.meta, rw.chunks, rw.sorted, prm.row_tiles, prm.ksplit, geo.OUT, cmax, y, y_dtype,
-        round_f16_first ? 1 : 0, geo.row_table, rw.tile_base, geo.nrows);
-    if (cudaGetLastError() != cudaSuccess) return VQB_CUDA_ERROR;
+    cudaLaunchConfig_t rcfg = {};
+    rcfg.gridDim = dim3(static_cast<unsigned>(blocks));
+    rcfg.blockDim = dim3(256);
+    rcfg.stream = stream;
+    rcfg.attrs = attr;
+    rcfg.numAttrs = 1;
+    const int rff = round_f16_first ? 1 : 0;
+    if (cudaLaunchKernelEx(&rcfg, splitk_reduce_kernel, static_cast<const float*>(prm.partial),
+                           static_cast<const int*>(rw.meta), static_cast<const int4*>(rw.chunks),
+                           static_cast<const int*>(rw.sorted), prm.row_tiles, prm.ksplit, geo.OUT, cmax, y, y_dtype,
+                           rff, geo.row_table, static_cast<const int*>(rw.tile_base), geo.nrows) != cudaSuccess ||
+        cudaGetLastError() != cudaSuccess)
+      return VQB_CUDA_ERROR;
     note_launch();
   }
   return VQB_OK;
