@@ -5,10 +5,15 @@
  * codebook-decode matmul behind `VQSwitchLinear` (routed MoE experts) and
  * `VQLinear` (dense projections), reading the vq_pack v1 packed layout.
  *
- * Every pointer is a DEVICE pointer owned by the caller; every call is
- * asynchronous on the given stream and allocates nothing.  Calls that need
- * scratch memory take a caller-supplied workspace whose size the matching
- * *_workspace_size function returns.  No torch types cross this boundary.
+ * Every pointer is a DEVICE pointer owned by the caller.  The compute entry
+ * points (vqb_unpack, vqb_codebook_halves, vqb_switch_forward[_static],
+ * vqb_dense_forward, the MoE elementwise calls and vqb_ep_dispatch / combine /
+ * reduce) are asynchronous on the given stream and allocate nothing; calls
+ * that need scratch memory take a caller-supplied workspace whose size the
+ * matching *_workspace_size function returns.  Only the expert-parallel set-up
+ * calls (vqb_ep_region_alloc / _free, vqb_ep_ipc_open / _close) allocate,
+ * map or free device memory, synchronously.  No torch types cross this
+ * boundary.
  *
  * Tensor formats (identical to the reference's safetensors tensors):
  *   codes     packed (pack_bits > 0): uint32 [E, OUT, WPR], WPR = ceil(NSUB/32)*BITS,
@@ -176,9 +181,13 @@ int32_t vqb_switch_path(const vqb_linear_desc* desc, int32_t n_tokens, int32_t t
  *   - the array is one per GPU and is reused by every call: calls that
  *     overlap on the GPU race on it and must be serialized by the caller;
  *   - the first call on a device looks the array's address up (once per
- *     device, that device current); make it before any stream capture.
- * The status block (int32 [1] = VQB_BAD_ROUTING on a bad expert index) sits
- * at the start of that array and is not readable through this ABI. */
+ *     device and context, that device current: again after the context was
+ *     destroyed and created anew); make it before any stream capture.
+ * An expert index >= num_experts (other than VQB_SKIP_EXPERT) is not read out
+ * of range: such a pair is computed as expert 0, so its y rows hold expert 0's
+ * output.  The status block that records it (int32 [1] = VQB_BAD_ROUTING) sits
+ * at the start of the library's array and is not readable through this ABI;
+ * a caller that must detect bad indices validates them before the call. */
 vqb_status vqb_switch_forward_static(const vqb_linear_desc* desc, const void* x, vqb_dtype x_dtype,
                                      int32_t n_tokens, const uint32_t* indices, int32_t top_k,
                                      void* y, vqb_dtype y_dtype, const vqb_options* opts,

@@ -159,7 +159,7 @@ def unpack_numpy(packed: np.ndarray, nsub: int, bits: int) -> np.ndarray:
 
 # ------------------------------------------------------------ matmul paths
 
-MODE_WALK, MODE_SS, MODE_ACCS = 0, 1, 2
+MODE_WALK, MODE_SS, MODE_ACCS, MODE_PRESCALED = 0, 1, 2, 3
 
 
 def switch_fused(codes, codebook_bits, scales_bits, x_f16_bits, idx, krep, mode=MODE_WALK,
@@ -169,6 +169,9 @@ def switch_fused(codes, codebook_bits, scales_bits, x_f16_bits, idx, krep, mode=
     codes: [E, OUT, NSUB] unpacked uint16, or [E, OUT, WPR] uint32 when
     packed_bits > 0.  codebook_bits [K, D], scales_bits [E, OUT, NGRP] and
     x_f16_bits [T, IN] are fp16 bit patterns.  Pair p reads token p // krep.
+    mode: MODE_WALK / MODE_SS / MODE_ACCS (the group reductions of the walk,
+    simd_sum and gemmseg2-ACCS kernels) or MODE_PRESCALED (gemmseg2 without
+    ACCS: W = fp16(cb * s), one fp32 sum over k); orders are named in the C.
     """
     cb = np.ascontiguousarray(codebook_bits, dtype=np.uint16)
     sc = np.ascontiguousarray(scales_bits, dtype=np.uint16)
@@ -188,6 +191,28 @@ def switch_fused(codes, codebook_bits, scales_bits, x_f16_bits, idx, krep, mode=
         c = np.ascontiguousarray(codes, dtype=np.uint16)
         lib().orc_switch_fused(_p(c), _p(cb), _p(sc), E, OUT, IN, D, G, K,
                                _p(xh), T, _p(idx), N, krep, mode, _p(y))
+    return y
+
+
+def switch_fused_rowtable(codes, codebook_bits, scales_bits, x_f16_bits, idx, krep, row_table,
+                          mode=MODE_WALK, packed_bits: int = 0):
+    """The SKIPZERO switch (vq_switch.py:4958-5013 builds the row table; the
+    kernels' row hook, e.g. the packed d8 walk :1395-1415): codes
+    [R, NSUB] (or [R, WPR] packed) and scales_bits [R, NGRP] hold the R live
+    rows only, row_table int32 [E, OUT] maps (expert, out row) to its compact
+    row, -1 = dead (an entry >= R counts as dead too).  A live row is computed
+    exactly as switch_fused computes the same row of the expanded layout; a
+    dead row reads no code or scale and its output is +0.  Returns y32 [N, OUT]."""
+    rt = np.ascontiguousarray(row_table, dtype=np.int32)
+    E, OUT = rt.shape
+    R = np.asarray(codes).shape[0]
+    live = (rt >= 0) & (rt < R)
+    take = np.where(live, rt, 0).reshape(-1)
+    full_codes = np.ascontiguousarray(np.asarray(codes)[take]).reshape(E, OUT, -1)
+    full_sc = np.ascontiguousarray(np.asarray(scales_bits, dtype=np.uint16)[take]).reshape(E, OUT, -1)
+    y = switch_fused(full_codes, codebook_bits, full_sc, x_f16_bits, idx, krep, mode=mode, packed_bits=packed_bits)
+    idx = np.ascontiguousarray(idx, dtype=np.uint32).reshape(-1)
+    y[~live[idx]] = 0.0
     return y
 
 

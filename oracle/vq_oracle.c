@@ -172,7 +172,12 @@ static float group_partial(const uint16_t* crow, const float* cbf, const float* 
  *                   (vq_switch.py:1640-1644; Metal leaves the tree: UNPINNED)
  *   mode 2 "accs":  acc = fma(s[g], partial[g], acc) -- the gemmseg2 ACCS update
  *                   (vq_switch.py:4188-4191; partial order inside the MMA is
- *                   unspecified, taken as the ascending-code sum) */
+ *                   unspecified, taken as the ascending-code sum)
+ *   mode 3 "prescaled": the gemmseg2 arm without ACCS (vq_switch.py:3897-3900,
+ *                   :3960-3976: the staged weight is (half)(s * cb), one RNE
+ *                   rounding of the exact fp32 product), y = sum_k x*W in fp32
+ *                   over ascending k (the MMA's order: unspecified); computed by
+ *                   prescaled_row below, not by this reduction */
 static float reduce_groups(const float* s, const float* gacc, int ngrp, int mode) {
   float acc = 0.0f;
   if (mode == 1) {
@@ -189,6 +194,19 @@ static float reduce_groups(const float* s, const float* gacc, int ngrp, int mode
   } else {
     for (int g = 0; g < ngrp; ++g) acc = fmaf(s[g], gacc[g], acc);
   }
+  return acc;
+}
+
+/* Mode 3: one row of the non-ACCS gemmseg2 arm. */
+static float prescaled_row(const uint16_t* crow, const float* cbf, const uint16_t* srow, const float* xs,
+                           int NSUB, int D, int G) {
+  float acc = 0.0f;
+  for (int j = 0; j < NSUB; ++j)
+    for (int u = 0; u < D; ++u) {
+      const int k = j * D + u;
+      const float w = h2f(f2h(cbf[(int64_t)crow[j] * D + u] * h2f(srow[k / G])));
+      acc = acc + xs[k] * w;
+    }
   return acc;
 }
 
@@ -221,6 +239,10 @@ void orc_switch_fused(const uint16_t* codes, const uint16_t* cb, const uint16_t*
         const float* xs = xf + (int64_t)(p / krep) * IN;
         const uint16_t* crow = codes + ((int64_t)e * OUT + r) * NSUB;
         const uint16_t* srow = scales + ((int64_t)e * OUT + r) * NGRP;
+        if (mode == 3) {
+          y32[(int64_t)p * OUT + r] = prescaled_row(crow, cbf, srow, xs, NSUB, D, G);
+          continue;
+        }
         for (int g = 0; g < NGRP; ++g) {
           gacc[g] = group_partial(crow, cbf, xs, (int64_t)g * SPG, SPG, D);
           sv[g] = h2f(srow[g]);
@@ -319,6 +341,10 @@ void orc_switch_fused_packed(const uint32_t* packed, int bits, const uint16_t* c
         const uint32_t* prow = packed + ((int64_t)e * OUT + r) * WPR;
         for (int j = 0; j < NSUB; ++j) crow[j] = (uint16_t)extract_code(prow, j, bits);
         const uint16_t* srow = scales + ((int64_t)e * OUT + r) * NGRP;
+        if (mode == 3) {
+          y32[(int64_t)p * OUT + r] = prescaled_row(crow, cbf, srow, xs, NSUB, D, G);
+          continue;
+        }
         for (int g = 0; g < NGRP; ++g) {
           gacc[g] = group_partial(crow, cbf, xs, (int64_t)g * SPG, SPG, D);
           sv[g] = h2f(srow[g]);

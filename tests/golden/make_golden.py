@@ -15,6 +15,13 @@ reference is absent (the GPU boxes).
                          `ref_moe` (tests/test_qwen3_5_parity.py:180-204) on a
                          tiny dense model, shared expert zeroed so only the
                          router/top-k/renormalise/SwiGLU/combine remain.
+  writer_artifacts.json -- the VQ-layer part of the reference's writer
+                         fixtures tests/golden/writers/{pack,pack_straddle,
+                         sz_pack}.json (artifacts its own writers produced):
+                         config.json `vq_modules` / `vq_skipzero`, and the
+                         dtype, shape and shard of every tensor of those
+                         layers (the loader's input contract,
+                         src/vqlab/bundle/add_model_file.py:70-131).
 
 vq_pack.py imports only numpy, so it is loaded straight from its file; the
 parity test module imports mlx at the top, so its four numpy functions are
@@ -99,6 +106,26 @@ def make_moe(ref_moe) -> dict:
             "down": p["experts.down_proj"], "k": np.array(k), "y": y}
 
 
+def make_writer_artifacts(ref: pathlib.Path) -> dict:
+    import json
+    out = {}
+    for name in ("pack", "pack_straddle", "sz_pack"):
+        fx = json.loads((ref / "tests" / "golden" / "writers" / f"{name}.json").read_text())
+        cfg = fx["config"]
+        prefixes = set(cfg.get("vq_modules") or {})
+        sz = cfg.get("vq_skipzero")
+        if sz:
+            prefixes |= set(sz.get("modules") or {})
+        tensors = {k: {"dtype": v["dtype"], "shape": v["shape"], "shard": v["shard"]}
+                   for k, v in fx["tensors"].items() if any(k.startswith(p + ".") for p in prefixes)}
+        keep = {k: cfg[k] for k in ("vq_modules", "vq_skipzero") if k in cfg}
+        if "vq_skipzero" in keep:
+            keep["vq_skipzero"] = {"format": sz.get("format"), "version": sz.get("version"),
+                                   "modules": sz.get("modules")}
+        out[name] = {"config": keep, "tensors": tensors}
+    return out
+
+
 def main(argv) -> int:
     ref = pathlib.Path(argv[1] if len(argv) > 1 else os.environ.get("VQLAB_REF", ""))
     if not (ref / "src" / "vqlab" / "runtime" / "vq_pack.py").exists():
@@ -106,6 +133,8 @@ def main(argv) -> int:
         return 2
     np.savez_compressed(HERE / "vq_pack_golden.npz", **make_pack(_load_vq_pack(ref)))
     np.savez_compressed(HERE / "moe_block_golden.npz", **make_moe(_load_ref_moe(ref)))
+    import json
+    (HERE / "writer_artifacts.json").write_text(json.dumps(make_writer_artifacts(ref), indent=1, sort_keys=True) + "\n")
     print("wrote", HERE / "vq_pack_golden.npz", HERE / "moe_block_golden.npz")
     return 0
 

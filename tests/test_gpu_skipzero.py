@@ -98,3 +98,43 @@ def test_sz_dead_rows_are_plus_zero_even_for_inf_input():
                 e = int(T_idx[t, j])
                 dead = tbl[e] < 0
                 assert np.all(y[t, j, dead] == 0) and not np.any(np.signbit(y[t, j, dead]))
+
+
+@pytest.mark.parametrize("name,D,K,packed,IN,OUT", GEOMS)
+@pytest.mark.parametrize("T,top", [(1, 8), (3, 10), (100, 8)])
+def test_sz_matches_oracle(name, D, K, packed, IN, OUT, T, top):
+    """The compact-row module against the oracle's SKIPZERO restatement
+    (oracle.switch_fused_rowtable): live rows within max relative error 2e-3
+    of the walk accumulators (fp32 output, fp16 output rounding kept), dead
+    rows exactly +0.  T = 100 x 8 pairs runs the grouped GEMM."""
+    E, G = 8, 64
+    r = np.random.default_rng(21)
+    codes = r.integers(0, K, (E, OUT, IN // D)).astype(np.uint16)
+    cb = (r.standard_normal((K, D)) * 0.05).astype(np.float16)
+    sc = (r.standard_normal((E, OUT, IN // G)) * 0.1 + 1).astype(np.float16)
+    live = r.random((E, OUT)) >= 0.4
+    live[1, :] = False
+    live[2, :] = True
+    tbl = np.full((E, OUT), -1, np.int32)
+    tbl[live] = np.arange(int(live.sum()), dtype=np.int32)
+    ccomp, scomp = codes[live], sc[live]
+    if packed:
+        bits = int(K - 1).bit_length()
+        store = orc.pack(ccomp, bits).view(np.int32)
+        kw = dict(pack_bits=bits, in_features=IN)
+    else:
+        store = ccomp.astype(np.uint8 if K <= 256 else np.uint16)
+        kw = {}
+    sz = VQSwitchLinear(torch.from_numpy(np.ascontiguousarray(store)).cuda(), torch.from_numpy(cb).cuda(),
+                        torch.from_numpy(np.ascontiguousarray(scomp)).cuda(), group_size=G,
+                        row_table=torch.from_numpy(tbl).cuda(), **kw)
+    x = np.random.default_rng(22).standard_normal((T, 1, 1, IN)).astype(np.float16)
+    idx = _idx(T, top, E, seed=23)
+    y = sz(torch.from_numpy(x).cuda(), idx, out_dtype=torch.float32).cpu().numpy().reshape(T * top, OUT)
+    idx_np = idx.cpu().numpy().astype(np.uint32)
+    ref = orc.round_f16(orc.switch_fused_rowtable(ccomp, cb.view(np.uint16), scomp.view(np.uint16),
+                                                  x.reshape(T, IN).view(np.uint16), idx_np.reshape(-1), top, tbl))
+    dead = ~live[idx_np.reshape(-1)]
+    assert np.all(y[dead] == 0) and not np.any(np.signbit(y[dead]))
+    from vq_cases import max_rel
+    assert max_rel(ref, y) <= 2e-3

@@ -76,3 +76,46 @@ def test_router_topk_renormalised_and_tie_order():
     idx, w = orc.router_topk(lg, 2)
     assert idx.tolist() == [[1, 2]]
     assert abs(float(w.sum()) - 1.0) < 1e-6
+
+
+def test_rowtable_restatement_equals_expanded_layout():
+    """oracle.switch_fused_rowtable on compact live rows is bit-identical to
+    switch_fused on the expanded layout (dead rows: code 0, scale +0, whose walk
+    gives fma(+0, gacc, +0) = +0), the reference's own SKIPZERO claim
+    (tests/test_vq_skipzero.py:83-113); an out-of-table compact index is dead."""
+    r = np.random.default_rng(5)
+    E, OUT, IN, D, K, G = 4, 24, 128, 8, 512, 64
+    codes = r.integers(0, K, (E, OUT, IN // D)).astype(np.uint16)
+    cb = (r.standard_normal((K, D)) * 0.05).astype(np.float16).view(np.uint16)
+    sc = r.uniform(0.5, 1.5, (E, OUT, IN // G)).astype(np.float16)
+    live = r.random((E, OUT)) >= 0.5
+    live[0] = False
+    tbl = np.full((E, OUT), -1, np.int32)
+    tbl[live] = np.arange(int(live.sum()), dtype=np.int32)
+    full_c, full_s = codes.copy(), sc.copy()
+    full_c[~live] = 0
+    full_s[~live] = 0
+    x = orc.f16_bits(r.standard_normal((3, IN)))
+    idx = np.array([0, 1, 2, 3, 1, 2], dtype=np.uint32)
+    a = orc.switch_fused(full_c, cb, full_s.view(np.uint16), x, idx, 2)
+    b = orc.switch_fused_rowtable(codes[live], cb, sc[live].view(np.uint16), x, idx, 2, tbl)
+    assert np.array_equal(a.view(np.uint32), b.view(np.uint32))
+    bad = tbl.copy()
+    bad[2, 0] = int(live.sum()) + 7
+    c = orc.switch_fused_rowtable(codes[live], cb, sc[live].view(np.uint16), x, idx, 2, bad)
+    assert np.all(c[2][0:1] == 0) and np.all(c[idx == 2][:, 0] == 0)
+
+
+def test_prescaled_arm_equals_dense_decode_matmul_fp16():
+    """MODE_PRESCALED (gemmseg2 without ACCS: W = fp16(cb*s), ascending-k fp32
+    sum) on one expert is the dense _decode_matmul with fp16 weights and fp16 x,
+    bit for bit: the same weight rounding and the same summation order."""
+    L = make_layer(E=1, OUT=40, IN=256, D=8, K=1024, G=64, seed=9)
+    r = np.random.default_rng(10)
+    xv = orc.f16_vals(orc.f16_bits(r.standard_normal((3, 256))))
+    a = orc.switch_fused(L.codes, L.cb_bits, L.sc_bits, orc.f16_bits(xv), np.zeros(3, np.uint32), 1,
+                         mode=orc.MODE_PRESCALED)
+    b = orc.dense_decode_matmul(L.codes[0], L.cb_bits, L.sc_bits[0], xv, wbf16=False)
+    assert np.array_equal(a.view(np.uint32), b.view(np.uint32))
+    ex = orc.exact_f64(L.codes, L.cb_bits, L.sc_bits, xv, idx=np.zeros(3, np.uint32))
+    assert max_rel(ex, a) < 2e-3

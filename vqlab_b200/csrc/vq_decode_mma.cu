@@ -279,7 +279,8 @@ __global__ void __launch_bounds__(kThreads, 1) vq_decode_mma_kernel(const MParam
   extern __shared__ __align__(16) unsigned char smem_raw[];
   // layout: [cb prefix][x rows][per-warp code+scale windows][slice partials]
   uint16_t* cb_s = reinterpret_cast<uint16_t*>(smem_raw);
-  size_t off = (static_cast<size_t>(prm.ns) * D * 2 + 15) & ~size_t(15);
+  // the whole codebook is followed by its zero entry at index K (the host sizes (ns + 1) entries)
+  size_t off = (static_cast<size_t>(prm.ns + (CB == kCbFull ? 1 : 0)) * D * 2 + 15) & ~size_t(15);
   uint16_t* x_s = reinterpret_cast<uint16_t*>(smem_raw + off);
   off += (static_cast<size_t>(prm.pm) * prm.x_stride * 2 + 15) & ~size_t(15);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -573,8 +574,6 @@ __global__ void x_to_16bit_kernel(const void* __restrict__ x, int x_dtype, int64
   }
 }
 
-int g_num_sms_mma = 0;
-
 }  // namespace
 
 size_t mma_x16_bytes(int64_t T, int IN) { return (static_cast<size_t>(T) * IN * 2 + 255) & ~size_t(255); }
@@ -603,13 +602,9 @@ bool mma_decode_supported(const LinearGeometry& geo, int wround, int x_dtype) {
 vqb_status launch_decode_mma(const LinearGeometry& geo, const GroupedDecodeArgs& a, uint16_t* x16, int T,
                              cudaStream_t stream) {
   if (a.N <= 0) return VQB_OK;
-  if (g_num_sms_mma == 0) {
-    int dev = 0;
-    if (cudaGetDevice(&dev) != cudaSuccess) return VQB_CUDA_ERROR;
-    if (cudaDeviceGetAttribute(&g_num_sms_mma, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
-      return VQB_CUDA_ERROR;
-  }
-  const int nsm = g_num_sms_mma;
+  DeviceInfo di;
+  if (device_info(&di) != VQB_OK) return VQB_CUDA_ERROR;
+  const int nsm = di.sms;
   const int WR = a.wround;
   // x -> 16-bit B-operand rows (the reference's host cast for the MoE path):
   // converted while the kernel stages x when its rows are 16-byte aligned
@@ -701,7 +696,10 @@ vqb_status launch_decode_mma(const LinearGeometry& geo, const GroupedDecodeArgs&
 
   const size_t x_bytes = (static_cast<size_t>(a.pmax) * prm.x_stride * 2 + 15) & ~size_t(15);
   const size_t win_bytes = (static_cast<size_t>(16) * prm.cs_stride * 4 + 16 * prm.sc_stride * 2 + 15) & ~size_t(15);
-  const size_t budget = 227 * 1024;
+  // the device's opt-in limit less 1 KB: a launch never asks for the last
+  // bytes of shared memory (an ncu launch list once reported LaunchFailed for
+  // a launch that left 64 bytes; the margin costs 64 d8 codebook entries)
+  const size_t budget = static_cast<size_t>(di.smem_optin) - 1024;
   const size_t entry = static_cast<size_t>(geo.D) * 2;
   // A codebook larger than what one SM can hold next to the staging buffers is
   // split across a CTA pair (d8/K16384: 2 x 128 KB), so no lookup leaves

@@ -266,14 +266,12 @@ __global__ void __launch_bounds__(256) ep_reduce_kernel(const float4* __restrict
   }
 }
 
-int g_ep_sms = 0;
+thread_local int g_ep_sms = 0;  // the current device's SM count, refreshed by ep_sms()
 
 vqb_status ep_sms() {
-  if (g_ep_sms == 0) {
-    int dev = 0;
-    if (cudaGetDevice(&dev) != cudaSuccess) return VQB_CUDA_ERROR;
-    if (cudaDeviceGetAttribute(&g_ep_sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return VQB_CUDA_ERROR;
-  }
+  DeviceInfo di;
+  if (device_info(&di) != VQB_OK) return VQB_CUDA_ERROR;
+  g_ep_sms = di.sms;
   return VQB_OK;
 }
 

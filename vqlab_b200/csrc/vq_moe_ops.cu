@@ -203,14 +203,12 @@ __global__ void __launch_bounds__(256) route_topk_kernel(const float* __restrict
   }
 }
 
-int g_sms_ops = 0;
+thread_local int g_sms_ops = 0;  // the current device's SM count, refreshed by ensure_sms()
 
 vqb_status ensure_sms() {
-  if (g_sms_ops == 0) {
-    int dev = 0;
-    if (cudaGetDevice(&dev) != cudaSuccess) return VQB_CUDA_ERROR;
-    if (cudaDeviceGetAttribute(&g_sms_ops, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return VQB_CUDA_ERROR;
-  }
+  DeviceInfo di;
+  if (device_info(&di) != VQB_OK) return VQB_CUDA_ERROR;
+  g_sms_ops = di.sms;
   return VQB_OK;
 }
 

@@ -1085,8 +1085,10 @@ bool encode_x3d(EncodeTiledFn enc, CUtensorMap* map, bool bf16, const void* xs, 
              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-int g_sms_tc = 0;
-int g_smem_optin = 0;
+// the current device's attributes, refreshed by ensure_device_attrs() at the
+// start of every host entry that reads them (per thread: no shared state)
+thread_local int g_sms_tc = 0;
+thread_local int g_smem_optin = 0;
 
 template <int D>
 void* pick_kernel(int bits) {
@@ -1177,13 +1179,10 @@ bool dsplit_eligible(const LinearGeometry& geo, const TParams& one_pass_plan) {
 }
 
 vqb_status ensure_device_attrs() {
-  if (g_sms_tc == 0) {
-    int dev = 0;
-    if (cudaGetDevice(&dev) != cudaSuccess) return VQB_CUDA_ERROR;
-    if (cudaDeviceGetAttribute(&g_sms_tc, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return VQB_CUDA_ERROR;
-    if (cudaDeviceGetAttribute(&g_smem_optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev) != cudaSuccess)
-      return VQB_CUDA_ERROR;
-  }
+  DeviceInfo di;
+  if (device_info(&di) != VQB_OK) return VQB_CUDA_ERROR;
+  g_sms_tc = di.sms;
+  g_smem_optin = di.smem_optin;
   return VQB_OK;
 }
 

@@ -70,6 +70,39 @@ thread_local cudaEvent_t t_timer_start = nullptr, t_timer_stop = nullptr;
 
 void note_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
 
+namespace {
+constexpr int kMaxDeviceIndex = 64;
+std::atomic<int> g_dev_sms[kMaxDeviceIndex];
+std::atomic<int> g_dev_optin[kMaxDeviceIndex];
+}  // namespace
+
+// SM count and opt-in shared memory per block of the current device, read
+// once per device index (every GPU of a process may differ).
+vqb_status device_info(DeviceInfo* out) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0) return VQB_CUDA_ERROR;
+  if (dev < kMaxDeviceIndex) {
+    const int s = g_dev_sms[dev].load(std::memory_order_relaxed);
+    const int o = g_dev_optin[dev].load(std::memory_order_relaxed);
+    if (s > 0 && o > 0) {
+      out->sms = s;
+      out->smem_optin = o;
+      return VQB_OK;
+    }
+  }
+  int s = 0, o = 0;
+  if (cudaDeviceGetAttribute(&s, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess ||
+      cudaDeviceGetAttribute(&o, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev) != cudaSuccess || s <= 0 || o <= 0)
+    return VQB_CUDA_ERROR;
+  if (dev < kMaxDeviceIndex) {
+    g_dev_sms[dev].store(s, std::memory_order_relaxed);
+    g_dev_optin[dev].store(o, std::memory_order_relaxed);
+  }
+  out->sms = s;
+  out->smem_optin = o;
+  return VQB_OK;
+}
+
 void timer_before(cudaStream_t stream) {
   if (t_timer_start) cudaEventRecord(t_timer_start, stream);
 }

@@ -86,6 +86,13 @@ constexpr int kPrefillTileTokens = 128;
 // (the decode or grouped-GEMM kernel) is bracketed by timer_before/after,
 // which record the events armed by vqb_time_next_kernel on its stream.
 void note_launch();
+
+// Attributes of the current device (cached per device index).
+struct DeviceInfo {
+  int sms;
+  int smem_optin;
+};
+vqb_status device_info(DeviceInfo* out);
 void timer_before(cudaStream_t stream);
 void timer_after(cudaStream_t stream);
 

@@ -15,13 +15,16 @@
 //     held until the process exits;
 //   * a call whose scratch would not fit returns VQB_WORKSPACE_TOO_SMALL
 //     before touching the GPU;
-//   * the first call on a device resolves the array's device address (once
-//     per device, with that device current) -- make that first call before
-//     any stream capture;
+//   * the first call on a device (and the first call after that device's
+//     context was destroyed and created again) resolves the array's device
+//     address, with that device current -- make that first call before any
+//     stream capture;
 //   * every call reuses the same bytes and leaves the previous call's data in
 //     them; the call clears the part that must start at zero itself.  Two
 //     calls that overlap on the GPU (other streams, other host threads) race
 //     on the array: serialize them.
+#include <cuda.h>
+
 #include <mutex>
 
 #include "vqb_common.cuh"
@@ -35,22 +38,67 @@ constexpr int kMaxDevices = 64;
 
 static __device__ __align__(256) unsigned char g_static_scratch[kStaticScratchBytes];
 
-std::mutex g_scratch_mu;
-void* g_scratch_dev[kMaxDevices] = {};
+using CtxGetCurrentFn = CUresult (*)(CUcontext*);
+using CtxGetIdFn = CUresult (*)(CUcontext, unsigned long long*);
 
-// Device address of g_static_scratch on the current device.  The symbol's
-// name is only a host-side handle; the address must come from the runtime.
+// The resolved address of the array for one device, valid for the context
+// whose process-unique id (cuCtxGetId) it was resolved in.
+struct ScratchSlot {
+  unsigned long long ctx_id;
+  void* ptr;
+};
+
+std::mutex g_scratch_mu;
+ScratchSlot g_scratch[kMaxDevices] = {};
+bool g_driver_looked_up = false;
+CtxGetCurrentFn g_ctx_get_current = nullptr;
+CtxGetIdFn g_ctx_get_id = nullptr;
+
+void* driver_entry(const char* name) {
+  void* p = nullptr;
+  cudaDriverEntryPointQueryResult q;
+  if (cudaGetDriverEntryPoint(name, &p, cudaEnableDefault, &q) != cudaSuccess || q != cudaDriverEntryPointSuccess)
+    return nullptr;
+  return p;
+}
+
+// Process-unique id of the current context, 0 when it cannot be read.
+unsigned long long current_ctx_id() {
+  if (!g_ctx_get_current || !g_ctx_get_id) return 0;
+  CUcontext ctx = nullptr;
+  unsigned long long id = 0;
+  if (g_ctx_get_current(&ctx) != CUDA_SUCCESS || !ctx) return 0;
+  if (g_ctx_get_id(ctx, &id) != CUDA_SUCCESS) return 0;
+  return id;
+}
+
+// Device address of g_static_scratch in the current context.  The symbol's
+// name is only a host-side handle; the address must come from the runtime,
+// and it is re-resolved whenever the current context is not the one the
+// cached address belongs to (a device reset, or a context destroyed and
+// created again, unloads the module the old address pointed into).
 vqb_status scratch_address(void** out) {
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return VQB_CUDA_ERROR;
   if (dev < 0 || dev >= kMaxDevices) return VQB_CUDA_ERROR;
   std::lock_guard<std::mutex> lock(g_scratch_mu);
-  if (!g_scratch_dev[dev]) {
-    void* p = nullptr;
-    if (cudaGetSymbolAddress(&p, g_static_scratch) != cudaSuccess || !p) return VQB_CUDA_ERROR;
-    g_scratch_dev[dev] = p;
+  if (!g_driver_looked_up) {
+    g_ctx_get_current = reinterpret_cast<CtxGetCurrentFn>(driver_entry("cuCtxGetCurrent"));
+    g_ctx_get_id = reinterpret_cast<CtxGetIdFn>(driver_entry("cuCtxGetId"));
+    g_driver_looked_up = true;
   }
-  *out = g_scratch_dev[dev];
+  ScratchSlot& slot = g_scratch[dev];
+  const unsigned long long id = current_ctx_id();
+  if (slot.ptr && id != 0 && slot.ctx_id == id) {
+    *out = slot.ptr;
+    return VQB_OK;
+  }
+  // first call in this context (or no context id available: resolve every call)
+  void* p = nullptr;
+  if (cudaGetSymbolAddress(&p, g_static_scratch) != cudaSuccess || !p) return VQB_CUDA_ERROR;
+  slot.ptr = p;
+  slot.ctx_id = current_ctx_id();  // the lookup above makes the device's primary context current
+  *out = p;
   return VQB_OK;
 }
 

@@ -63,7 +63,10 @@ class VQLinear(torch.nn.Module):
         d.codebook_halves = self._halves.pointer(self.codebook)
         return d
 
-    def forward(self, x: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+    def forward(self, x: torch.Tensor, out: torch.Tensor | None = None,
+                out_dtype: torch.dtype | None = None) -> torch.Tensor:
+        """The reference call (vq_dense.py:346).  Extension: `out_dtype` stores y
+        in another dtype than x's (float32 keeps the fp32 accumulators)."""
         if int(self.codebook.shape[0]) != self._k_expect:
             raise RuntimeError(
                 f"VQ codebook was sharded: K={self.codebook.shape[0]}, expected {self._k_expect}. The "
@@ -83,19 +86,22 @@ class VQLinear(torch.nn.Module):
             raise ValueError("x must be a CUDA tensor on the module's device")
         xf = x.reshape(-1, IN).contiguous()
         n = xf.shape[0]
+        ydt = x.dtype if out_dtype is None else out_dtype
+        if ydt not in _DTYPES:
+            raise ValueError(f"out_dtype {ydt} not supported")
         if out is None:
-            y = torch.empty((n, OUT), dtype=x.dtype, device=x.device)
+            y = torch.empty((n, OUT), dtype=ydt, device=x.device)
         else:
             y = out
-            if y.shape != (n, OUT) or y.dtype != x.dtype or not y.is_contiguous():
-                raise ValueError("out must be a contiguous [N, OUT] tensor of x's dtype")
+            if y.shape != (n, OUT) or y.dtype != ydt or not y.is_contiguous():
+                raise ValueError("out must be a contiguous [N, OUT] tensor of the output dtype")
         d = self.desc()
         optp = ctypes.byref(self.options) if self.options is not None else None
         L = _lib.lib()
         ws_bytes = L.vqb_dense_workspace_size(ctypes.byref(d), n, optp)
         ws = torch.empty(ws_bytes, dtype=torch.uint8, device=x.device)
         st = L.vqb_dense_forward(ctypes.byref(d), ctypes.c_void_p(xf.data_ptr()), _DTYPES[x.dtype], n,
-                                 ctypes.c_void_p(y.data_ptr()), _DTYPES[x.dtype], ctypes.c_void_p(ws.data_ptr()),
+                                 ctypes.c_void_p(y.data_ptr()), _DTYPES[ydt], ctypes.c_void_p(ws.data_ptr()),
                                  ws_bytes, optp, _stream_ptr(x.device))
         _lib.check(st, "vqb_dense_forward")
         return y.reshape(*x.shape[:-1], OUT)

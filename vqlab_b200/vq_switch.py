@@ -187,12 +187,14 @@ class VQSwitchLinear(torch.nn.Module):
 
     def forward(self, x: torch.Tensor, indices: torch.Tensor, sorted_indices: bool = False,
                 out: torch.Tensor | None = None, workspace: torch.Tensor | None = None,
-                reuse: int = 0) -> torch.Tensor:
+                reuse: int = 0, out_dtype: torch.dtype | None = None) -> torch.Tensor:
         """The reference call (vq_switch.py:5284).  Extensions for a block that
         runs several projections on one routing: `workspace` (a uint8 CUDA
         tensor of at least workspace_bytes) is used instead of a fresh one, and
         `reuse` (VQB_REUSE_* flags) tells the library that it already holds
-        this call's routing tables / gathered x from the previous call."""
+        this call's routing tables / gathered x from the previous call.
+        `out_dtype` stores y in another dtype than x's (float32 keeps the
+        fp16-rounded result without the second rounding to x's dtype)."""
         self._check_tensors()
         IN = self.input_dims
         OUT = self.output_dims
@@ -220,12 +222,15 @@ class VQSwitchLinear(torch.nn.Module):
             krep = 1
         x2 = x2.contiguous()
         ntok = x2.shape[0]
+        ydt = x.dtype if out_dtype is None else out_dtype
+        if ydt not in _DTYPES:
+            raise ValueError(f"out_dtype {ydt} not supported")
         if out is None:
-            y = torch.empty((N, OUT), dtype=x.dtype, device=x.device)
+            y = torch.empty((N, OUT), dtype=ydt, device=x.device)
         else:
             y = out
-            if y.shape != (N, OUT) or y.dtype != x.dtype or not y.is_contiguous():
-                raise ValueError("out must be a contiguous [N, OUT] tensor of x's dtype")
+            if y.shape != (N, OUT) or y.dtype != ydt or not y.is_contiguous():
+                raise ValueError("out must be a contiguous [N, OUT] tensor of the output dtype")
         d = self.desc()
         opts = self.options
         if reuse:
@@ -245,7 +250,7 @@ class VQSwitchLinear(torch.nn.Module):
             ws = torch.empty(ws_bytes, dtype=torch.uint8, device=x.device)
         st = L.vqb_switch_forward(ctypes.byref(d), ctypes.c_void_p(x2.data_ptr()), _DTYPES[x.dtype], ntok,
                                   ctypes.c_void_p(idx.data_ptr()), krep, ctypes.c_void_p(y.data_ptr()),
-                                  _DTYPES[x.dtype], ctypes.c_void_p(ws.data_ptr()), ws_bytes, optp,
+                                  _DTYPES[ydt], ctypes.c_void_p(ws.data_ptr()), ws_bytes, optp,
                                   _stream_ptr(x.device))
         _lib.check(st, "vqb_switch_forward")
         if os.environ.get("VQB_CHECK_ROUTING") == "1":
