@@ -475,15 +475,6 @@ __device__ __forceinline__ void item_pass_windows(const TParams& prm, int64_t it
   lo = max(wlo - h * nwin, 0);
   hi = min(whi - h * nwin, nwin);
 }
-__device__ __forceinline__ int item_windows(const TParams& prm, int64_t it, int nwin) {
-  const int S = prm.ksplit, sp = static_cast<int>(it % S), nwt = prm.npass * nwin;
-  return (sp + 1) * nwt / S - sp * nwt / S;
-}
-__device__ __forceinline__ int item_first_window(const TParams& prm, int64_t it, int nwin) {
-  const int S = prm.ksplit, sp = static_cast<int>(it % S);
-  return sp * (prm.npass * nwin) / S;
-}
-
 __device__ __forceinline__ int tile_n16(const TParams& prm, int64_t it) {
   return (prm.chunks[item_chunk(prm, it)].z + 15) & ~15;
 }
@@ -638,10 +629,15 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else if (warp == kWarpMma0 || warp == kWarpMma1) {
     // ---------------- MMA issuers.  A tile's K positions come in slots of pp
-    // positions sharing one B stage (pp > 1 for tiles of <= 64 tokens); a
-    // tile's slots alternate between the two issuers, each accumulating into
-    // its own D_i of that tile, and the epilogue adds D_0 + D_1.  Tile t of a
-    // group owns accumulator columns [2 t n16, 2 t n16 + 2 n16).
+    // positions sharing one B stage (pp > 1 for tiles of <= 64 tokens).  Slot
+    // gs of the CTA's slot sequence goes to issuer gs & 1, which accumulates
+    // into its own D_i of the tile; the epilogue adds D_0 + D_1 when both took
+    // part.  With an even number of B stages every stage then belongs to one
+    // issuer, and a slot is one window (pp = 4) or a window is cut into 2 or 4
+    // slots (pp = 2, 1): each issuer waits on b_full[bs] and on a_full[w & 1]
+    // for consecutive phases only -- an issuer that skipped a phase could take
+    // the previous phase's completion for the one it wants.  Tile t of a group
+    // owns accumulator columns [2 t n16, 2 t n16 + 2 n16).
     if (lane == 0) {
       const int iss = warp == kWarpMma0 ? 0 : 1;
       // descriptor of B stage 0; later stages / positions start further on (the start-address field counts 16-byte units)
@@ -666,10 +662,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             const int rows = slot_rows(ch.z);
             const int pp = slot_positions(rows);
             const uint32_t d_tmem = tmem_base + static_cast<uint32_t>((2 * t + iss) * grp.n16);
-            // slot index inside the work item
-            int k = ((pass_slice(prm.npass, jg, pass) * nwin + lo - item_first_window(prm, it, nwin)) * kSets) / pp;
-            for (int p0 = lo * kSets; p0 < hi * kSets; p0 += pp, ++gs, ++k) {
-              if ((k & 1) != iss) continue;
+            for (int p0 = lo * kSets; p0 < hi * kSets; p0 += pp, ++gs) {
+              if ((gs & 1u) != static_cast<uint32_t>(iss)) continue;
               const uint32_t bs = gs % kBStages;
               if (!(ok = mbar_wait(&b_full[bs], (gs / kBStages) & 1u, abort_flag))) break;
               for (int q = 0; q < pp; ++q) {
@@ -783,12 +777,15 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int lrow = q * 32 + lane;                 // row inside the tile
     uint32_t ws = 0, wp = 0;
     uint32_t g = 0;                                 // position sequence number
+    uint32_t gsl = 0;                               // B slot sequence number (the issuers' gs)
     int cur = -1;
     uint32_t cb_loads = 0;
     bool ok = true;
     int jg = 0;
     for (int64_t it0 = blockIdx.x; it0 < nitems && ok; ++jg) {
       const TileGroup grp = form_group(prm, it0, nitems);
+      // accumulators the issuers wrote, per tile: bit 2t = D_0, bit 2t + 1 = D_1
+      uint32_t used = 0;
       for (int pass = 0; pass < prm.npass && ok; ++pass) {
         const int h = pass_slice(prm.npass, jg, pass);
         if (h != cur) {
@@ -805,6 +802,11 @@ __global__ void __launch_bounds__(kThreads, 1)
           int lo, hi;
           item_pass_windows(prm, it, pass_slice(prm.npass, jg, pass), nwin, lo, hi);
           if (lo >= hi) continue;
+          {
+            const int nslots = (hi - lo) * kSets / slot_positions(slot_rows(prm.chunks[item_chunk(prm, it)].z));
+            used |= (nslots >= 2 ? 3u : (1u << (gsl & 1u))) << (2 * t);
+            gsl += static_cast<uint32_t>(nslots);
+          }
           const TileRow tr = tile_row(prm, it, lrow, prm.chunks[item_chunk(prm, it)].x);
           const int xr = prm.wswz == 1 ? ((tr.woff >> 1) & 3) : (prm.wswz == 2 ? (tr.woff & 7) : 0);
           const uint16_t* srow = prm.scales + (tr.live ? tr.crow : 0) * prm.NGRP;
@@ -886,7 +888,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         const TileRow tr = tile_row(prm, it, lrow, ch.x);
         const int ntok = ch.z;
         const int n = (ntok + 15) & ~15;
-        const bool two = item_windows(prm, it, nwin) * kSets / slot_positions(slot_rows(ntok)) > 1;
+        const bool u0 = (used >> (2 * t)) & 1u, u1 = (used >> (2 * t + 1)) & 1u;
+        // D_0 + D_1 in that order when both issuers wrote the tile
+        auto tile_acc = [&](uint32_t a, uint32_t b) {
+          return u0 && u1 ? __uint_as_float(a) + __uint_as_float(b) : __uint_as_float(u1 ? b : a);
+        };
         float* part = prm.ksplit > 1 ? prm.partial + it * (static_cast<int64_t>(prm.pcols) * kTileM) : nullptr;
         const uint32_t d0 = static_cast<uint32_t>(2 * t * grp.n16), d1 = d0 + static_cast<uint32_t>(grp.n16);
         for (int c0 = 0; c0 < n; c0 += 16, ++blk) {
@@ -899,7 +905,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             // split-K: this item's fp32 partial, column-major so a warp's 32 rows are one 128-byte line
 #pragma unroll
             for (int jj = 0; jj < 16; ++jj) {
-              const float v = two ? __uint_as_float(v0[jj]) + __uint_as_float(v1[jj]) : __uint_as_float(v0[jj]);
+              const float v = tile_acc(v0[jj], v1[jj]);
               if (c0 + jj < ntok) part[(c0 + jj) * kTileM + lrow] = v;
             }
           } else if (tr.r < prm.OUT) {
@@ -907,7 +913,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             for (int jj = 0; jj < 16; ++jj) {
               if (c0 + jj < ntok) {
                 const int pair = prm.sorted[ch.y + c0 + jj];
-                float acc = two ? __uint_as_float(v0[jj]) + __uint_as_float(v1[jj]) : __uint_as_float(v0[jj]);
+                float acc = tile_acc(v0[jj], v1[jj]);
                 if (!tr.live) acc = 0.0f;  // dead row (row table): exact +0
                 store_y(prm.y, static_cast<int64_t>(pair) * prm.OUT + tr.r, acc, prm.y_dtype, prm.round_f16_first != 0);
               }
