@@ -18,11 +18,17 @@ step touches, times the rotation, exceed the 126 MB L2).
 Multi-GPU (torchrun, one rank per GPU): expert parallelism (benchmark configuration
 C5): rank r holds experts [r*E/N, (r+1)*E/N) of every projection, each rank
 brings its own batch of tokens (weak scaling), and every layer sends the
-(token, slot) pairs to the owning ranks and combines the outputs back over
-NCCL (vqlab_b200.ep: a graph-captured fixed-shape path for decode batches, a
-dynamic all-to-all path for prefill).  `value` is all ranks' tokens over the
-max-over-ranks time.  The dispatch reads its split sizes on the host, so
-multi-GPU steps run eagerly (single-GPU steps replay CUDA graphs).
+(token, slot) pairs to the owning ranks and combines the outputs back
+(vqlab_b200.ep: the fixed-shape peer-memory path -- dispatch / combine / reduce
+kernels over NVLink, no host synchronisation -- for decode batches and for the
+prefill leg alike).  `value` is all ranks' tokens over the max-over-ranks time.
+The decode legs replay CUDA graphs.
+
+Other legs in the same JSON line: `batches` (C2 at 1, 8, 64 tokens with each
+batch's gate-projection kernel roofline), `dense` (C4, with the attention and
+MLP kernels' rooflines), `c1` (C1: the 4096 x 4096 d8/K4096 matvec),
+`prefill` (C3; with N > 1 each rank's expert busy time), `c5` (C5 at its stated
+global shapes, 256 decode and 8192 prefill tokens split over the N GPUs).
 
 `--impl reference` times the reference's CPU path (the oracle port of the
 reference arithmetic, OpenMP over all host cores) on a bounded sample of the
@@ -305,6 +311,15 @@ def make_dense_layer(torch, dev, seed):
     return attn, mlp
 
 
+# packed codes + scales + codebooks of one C4 layer: q, k, v, o (d2/K256, 8-bit) and gate, up, down (d8/K16384)
+def _dense_proj_bytes(out, inn, d, k, bits):
+    return out * ((inn // d + 31) // 32 * bits) * 4 + out * (inn // G) * 2 + k * d * 2
+
+
+DENSE_LAYER_BYTES = (2 * _dense_proj_bytes(DH, DH, 2, 256, 8) + 2 * _dense_proj_bytes(DKV, DH, 2, 256, 8) +
+                     2 * _dense_proj_bytes(DI, DH, 8, K, BITS) + _dense_proj_bytes(DH, DI, 8, K, BITS))
+
+
 def dense_step(layer, x):
     """The seven projections of one dense layer (the attention kernel itself is
     outside the VQ runtime: o is applied to q as its stand-in input)."""
@@ -317,10 +332,12 @@ def dense_step(layer, x):
     return h + wd(swiglu(wg(h), wu(h)))
 
 
-def dense_leg(torch, dev, args):
+def dense_leg(torch, dev, args, peak_gbs, peak_kind):
     """benchmark configuration C4: a 64-layer dense stack at batch 1 and 32 decode
-    tokens, timed per layer (4 seeded layers rotated: ~90 MB of packed weights
-    each, 360 MB per cycle > 126 MB L2) and scaled to 64 layers."""
+    tokens, timed per layer (4 seeded layers rotated: ~100 MB of packed weights
+    each, 400 MB per cycle > 126 MB L2) and scaled to 64 layers; the attention
+    (d2/K256, q 5120 x 5120) and MLP (d8/K16384, gate 17408 x 5120)
+    projections' dominant kernels are timed alone for their rooflines."""
     layers = [make_dense_layer(torch, dev, 7000 + l) for l in range(4)]
     gen = torch.Generator(device=dev)
     gen.manual_seed(23)
@@ -339,10 +356,82 @@ def dense_leg(torch, dev, args):
         steps = max(20, args.steps)
         secs = time_graph_steps(torch, graphs, steps, args.warmup)
         ms = secs * 1e3 / steps
-        out[str(B)] = {"ms_per_layer": round(ms, 4), "tokens_per_s_64_layers": round(B / (64 * ms / 1e3), 2)}
+        out[str(B)] = {"ms_per_layer": round(ms, 4), "tokens_per_s_64_layers": round(B / (64 * ms / 1e3), 2),
+                       "packed_weight_gbs": round(DENSE_LAYER_BYTES / (ms / 1e3) / 1e9, 1)}
         del graphs
+        # dominant kernel of one attention and one MLP projection, timed alone
+        s = torch.cuda.current_stream()
+        roofs = {}
+        for name, pick, geom in (("attn_q", lambda L: L[0][0], (DH, DH, 2, 256, 8)),
+                                 ("mlp_gate", lambda L: L[1][0], (DI, DH, 8, K, BITS))):
+            dur = kernel_seconds(torch, s, lambda i: pick(layers[i % len(layers)])(xs[i % len(layers)]), 8)
+            byt = dense_bytes(*geom, n=B)
+            ach = byt / dur / 1e9
+            kname = "vq_decode_mma_kernel" if (name == "attn_q" and B <= 8) else "vq_prefill_tc_kernel"
+            roofs[name] = {"bound": "hbm", "achieved": round(ach, 1), "peak": peak_gbs, "unit": "GB/s",
+                           "frac": round(ach / peak_gbs, 4),
+                           "traffic": profiled_traffic(kname, f"c4_{name}_n{B}"),
+                           "kernel": f"{kname}, timed alone", "algorithmic_bytes_per_launch": byt,
+                           "us_per_launch": round(dur * 1e6, 2), "peak_kind": f"{peak_kind} burst copy bandwidth"}
+        out[str(B)]["rooflines"] = roofs
     return {"metric": "dense VQ decode, benchmark configuration C4 (64 x [q,k,v,o d2/K256 + gate,up,down d8/K16384])",
             "unit": "tokens/s", "batches": out}
+
+
+C1_OUT = C1_IN = 4096  # benchmark configuration C1: one dense 4096 x 4096 matvec, d8/K4096 (12-bit codes)
+
+
+def _vq_linear(torch, dev, gen, out, inn, d, k, bits, g=G):
+    from vqlab_b200 import VQLinear
+    wpr = (inn // d + 31) // 32 * bits
+    # uniform random words are uniform codes when K = 2^bits and NSUB % 32 == 0
+    # (every benchmark geometry)
+    assert k == 1 << bits and (inn // d) % 32 == 0
+    codes = torch.randint(-2 ** 31, 2 ** 31 - 1, (out, wpr), dtype=torch.int32, device=dev, generator=gen)
+    cb = (torch.randn((k, d), device=dev, generator=gen) * 0.02).to(torch.float16)
+    sc = (torch.rand((out, inn // g), device=dev, generator=gen) + 0.5).to(torch.float16)
+    return VQLinear(codes, cb, sc, group_size=g, pack_bits=bits, in_features=inn)
+
+
+def dense_bytes(out, inn, d, k, bits, g=G, n=1):
+    """Algorithmic bytes of one dense VQ projection call: packed codes, scales,
+    the codebook, x and y (bf16)."""
+    wpr = (inn // d + 31) // 32 * bits
+    return out * wpr * 4 + out * (inn // g) * 2 + k * d * 2 + n * (inn + out) * 2
+
+
+def c1_leg(torch, dev, args, peak_gbs, peak_kind):
+    """benchmark configuration C1: the single 4096 x 4096 d8/K4096 vq_dense matvec
+    (N = 1, bf16 x).  64 independently seeded layers (3.75 MB each, 240 MB per
+    cycle > L2) are called round-robin from a CUDA graph; the dominant kernel
+    is also timed alone for the roofline."""
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(31)
+    lins = [_vq_linear(torch, dev, gen, C1_OUT, C1_IN, 8, 4096, 12) for _ in range(64)]
+    xs = [torch.randn((1, C1_IN), device=dev, generator=gen).to(torch.bfloat16) for _ in lins]
+    for L, x in zip(lins, xs):
+        L(x)
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        for L, x in zip(lins, xs):
+            L(x)
+    reps = max(5, args.steps // 4)
+    secs = time_graph_steps(torch, [g], reps, args.warmup)
+    del g
+    per_call = secs / (reps * len(lins))
+    byt = dense_bytes(C1_OUT, C1_IN, 8, 4096, 12)
+    s = torch.cuda.current_stream()
+    dur = kernel_seconds(torch, s, lambda i: lins[i % len(lins)](xs[i % len(lins)]), 16)
+    ach = byt / dur / 1e9
+    return {"metric": "dense VQ matvec, benchmark configuration C1 (4096 x 4096, d8/K4096 12-bit, N = 1, bf16)",
+            "us_per_call": round(per_call * 1e6, 2), "calls_per_s": round(1.0 / per_call, 1),
+            "packed_weight_gbs": round(byt / per_call / 1e9, 1),
+            "roofline": {"bound": "hbm", "achieved": round(ach, 1), "peak": peak_gbs, "unit": "GB/s",
+                         "frac": round(ach / peak_gbs, 4), "traffic": profiled_traffic("vq_decode_mma_kernel", "c1"),
+                         "kernel": "vq_decode_mma_kernel (bf16 weights, whole codebook in shared memory), timed alone",
+                         "algorithmic_bytes_per_launch": byt, "us_per_launch": round(dur * 1e6, 2),
+                         "peak_kind": f"{peak_kind} burst copy bandwidth"}}
 
 
 def zipf_logits(torch, dev, gen, T, alpha=1.1):
@@ -355,10 +444,41 @@ def zipf_logits(torch, dev, gen, T, alpha=1.1):
     return pop.log()[None, :] - torch.log(-torch.log(u))
 
 
-def prefill_leg(torch, dev, args, peak_tf, peak_kind, rank, world):
-    """benchmark configuration C3: one MoE layer on 4096 tokens, Zipf(1.1) routing."""
-    T = 4096
-    layer = make_layer(torch, dev, 5000, rank, world)
+def expert_busy_seconds(torch, layer, reps=3):
+    """Device time of this rank's expert projections (gate, up, SwiGLU, down)
+    on the pairs it served in the layer's last expert-parallel step."""
+    from vqlab_b200.moe import expert_mlp
+    X, ids = layer.last_pairs
+    s = torch.cuda.current_stream()
+    expert_mlp(layer.gate_proj, layer.up_proj, layer.down_proj, X, ids)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(s)
+    for _ in range(reps):
+        expert_mlp(layer.gate_proj, layer.up_proj, layer.down_proj, X, ids)
+    e1.record(s)
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1) / 1e3 / reps
+
+
+def gather_floats(torch, dev, v, world):
+    """[v of every rank] (an all-gather of one float), or [v] on one GPU."""
+    if world == 1:
+        return [v]
+    t = torch.tensor([v], device=dev)
+    out = torch.empty(world, device=dev)
+    torch.distributed.all_gather_into_tensor(out, t)
+    return [float(a) for a in out.tolist()]
+
+
+def prefill_leg(torch, dev, args, peak_tf, peak_kind, rank, world, T=4096, seed=5000):
+    """benchmark configuration C3: one MoE layer on T tokens per rank, Zipf(1.1)
+    routing.  With several ranks the layer takes the fixed-shape peer-memory
+    path at T tokens per rank (no host synchronisation: the exchange regions
+    hold every rank's T token rows, pairs of other ranks' experts are skipped)."""
+    layer = make_layer(torch, dev, seed, rank, world)
+    if world > 1:
+        layer.static_tokens = T
     gen = torch.Generator(device=dev)
     gen.manual_seed(17 + rank)
     x = torch.randn((T, HIDDEN), device=dev, generator=gen).to(torch.bfloat16)
@@ -394,17 +514,78 @@ def prefill_leg(torch, dev, args, peak_tf, peak_kind, rank, world):
     dur = kernel_seconds(torch, s, lambda i: layer.gate_proj(xg, gidx), 5)
     kflops = 2 * INTER * HIDDEN * int((gidx >= 0).sum())
     ach = kflops / dur / 1e12
-    return {"metric": "VQ-MoE prefill TFLOP/s (one MoE layer, C3: 4096 tokens, Zipf(1.1) top-10)",
+    busy = None
+    if world > 1:
+        # per-rank expert compute against the layer time: Zipf imbalance vs the exchange
+        busy = [round(b * 1e3, 3) for b in gather_floats(torch, dev, expert_busy_seconds(torch, layer), world)]
+        layer.close()
+    return {"metric": f"VQ-MoE prefill TFLOP/s (one MoE layer, {T} tokens per GPU, Zipf(1.1) top-10)",
             "value": round(flops * steps * world / secs / 1e12, 2), "unit": "TFLOP/s", "steps": steps,
             "ms_per_layer": round(secs * 1e3 / steps, 3), "tokens_per_s": round(T * steps * world / secs, 1),
             "tokens_per_expert": {"max": int(counts.max()), "median": float(counts.float().median()),
                                   "min": int(counts.min())},
             "flops_per_layer": flops, "clocks": clk.summary(),
+            "expert_busy_ms_per_rank": busy,
             "roofline": {"bound": "tensor", "achieved": round(ach, 1), "peak": peak_tf, "unit": "TFLOP/s",
                          "frac": round(ach / peak_tf, 4),
                          "traffic": profiled_traffic("vq_prefill_tc_kernel", "c3") if world == 1 else None,
                          "kernel": "vq_prefill_tc_kernel (gate projection, %d pairs on this rank), timed alone" % int((gidx >= 0).sum()),
                          "us_per_launch": round(dur * 1e6, 1), "peak_kind": f"{peak_kind} burst bf16 GEMM"}}
+
+
+C5_DECODE_TOKENS, C5_PREFILL_TOKENS, C5_LAYERS = 256, 8192, 60
+
+
+def c5_leg(torch, dev, args, rank, world):
+    """benchmark configuration C5 at its stated global shapes: 256 concurrent
+    decode tokens and an 8192-token prefill over the box, split evenly over the
+    `world` ranks (strong scaling), experts sharded expert-parallel (E / world
+    per rank), per layer; the 60-layer figures are 60 x the per-layer time of
+    2 independently seeded layers rotated (each rank's weights per layer
+    >= 600 MB, far above L2)."""
+    B = C5_DECODE_TOKENS // world
+    layers = [make_layer(torch, dev, 9000 + l, rank, world) for l in range(2)]
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(41 + rank)
+    if world > 1:
+        for L in layers:
+            L.static_tokens = B
+    xs = [torch.randn((B, HIDDEN), device=dev, generator=gen).to(torch.bfloat16) for _ in layers]
+    lg = [torch.randn((B, E), device=dev, generator=gen) for _ in layers]
+    outs = [L(x, l) for L, x, l in zip(layers, xs, lg)]
+    torch.cuda.synchronize()
+    graphs = []
+    for i, L in enumerate(layers):
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            outs[i] = L(xs[i], lg[i])
+        graphs.append(g)
+    if world > 1:
+        torch.distributed.barrier()
+    steps = max(20, args.steps // 2)
+    secs = time_graph_steps(torch, graphs, steps, args.warmup)
+    del graphs
+    if world > 1:
+        t = torch.tensor([secs], device=dev)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        secs = float(t.item())
+        for L in layers:
+            L.close()
+    del layers
+    torch.cuda.synchronize()
+    dec_ms = secs * 1e3 / steps
+    _, peak_tf, peak_kind = _peaks()
+    pre = prefill_leg(torch, dev, args, peak_tf, peak_kind, rank, world, T=C5_PREFILL_TOKENS // world, seed=9500)
+    return {"metric": "benchmark configuration C5 at its global shapes: 256 decode tokens and an 8192-token "
+                      "prefill split over the GPUs, experts sharded expert-parallel",
+            "scaling": "strong", "decode_tokens_per_gpu": B, "prefill_tokens_per_gpu": C5_PREFILL_TOKENS // world,
+            "decode_ms_per_layer": round(dec_ms, 4),
+            "decode_tokens_per_s": round(C5_DECODE_TOKENS / (dec_ms / 1e3), 1),
+            "decode_ms_per_60_layers": round(C5_LAYERS * dec_ms, 3),
+            "decode_tokens_per_s_60_layers": round(C5_DECODE_TOKENS / (C5_LAYERS * dec_ms / 1e3), 1),
+            "prefill_ms_per_layer": pre["ms_per_layer"], "prefill_tflops": pre["value"],
+            "prefill_ms_per_60_layers": round(C5_LAYERS * pre["ms_per_layer"], 2),
+            "prefill_expert_busy_ms_per_rank": pre.get("expert_busy_ms_per_rank")}
 
 
 def gpu_arm(args, rank, world, dev):
@@ -464,35 +645,41 @@ def gpu_arm(args, rank, world, dev):
         torch.cuda.synchronize()
         xs_last, lg_last = xs, lg
 
-    # ---- dominant kernel: the expert decode launch (gate projection), timed alone
-    B = args.batch
+    # ---- dominant kernel: the expert decode launch (gate projection), timed
+    # alone at every batch (the headline roofline is the one at --batch)
     projs = [layers[l].gate_proj for l in range(n_layers)]
-    if world == 1:
-        x = torch.randn((B, 1, 1, HIDDEN), device=dev, generator=gen).to(torch.bfloat16)
-        lgt = torch.randn((B, E), device=dev, generator=gen)
-        from vqlab_b200.moe import route
-        idx, _ = route(lgt, TOPK)
-    else:
-        # the pairs this rank's experts served in the last expert-parallel step (-1: another rank's)
-        x, idx = layers[0].last_pairs
-    npairs = int((idx >= 0).sum())
-    nd = int(torch.unique(idx[idx >= 0]).numel())
-    for p in projs:
-        p(x, idx)
-    torch.cuda.synchronize()
     s = torch.cuda.current_stream()
-    dur = kernel_seconds(torch, s, lambda i: projs[i % n_layers](x, idx), max(3, args.steps))
-    rows = int((idx >= 0).reshape(x.shape[0], -1).any(dim=1).sum())  # token rows the served pairs read
-    alg = nd * EXPERT_BYTES["gate"] + CODEBOOK_BYTES + rows * HIDDEN * 2 + npairs * INTER * 2
-    achieved = alg / dur / 1e9
-    kname = ("vq_prefill_tc_kernel" if projs[0].kernel_path(x.shape[0], idx.shape[-1]) == "gemm"
-             else "vq_decode_mma_kernel")
-    traffic = profiled_traffic(kname, "c2") if world == 1 else None
-    roof = {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak_gbs, "unit": "GB/s",
-            "frac": round(achieved / peak_gbs, 4), "traffic": traffic,
-            "kernel": "%s (gate projection, %d pairs, %d distinct experts), timed alone" % (kname, npairs, nd),
-            "algorithmic_bytes_per_launch": alg, "us_per_launch": round(dur * 1e6, 2),
-            "peak_kind": f"{peak_kind} burst copy bandwidth"}
+    roofs = {}
+    for Bq in batches:
+        if world == 1:
+            x = torch.randn((Bq, 1, 1, HIDDEN), device=dev, generator=gen).to(torch.bfloat16)
+            lgt = torch.randn((Bq, E), device=dev, generator=gen)
+            from vqlab_b200.moe import route
+            idx, _ = route(lgt, TOPK)
+        elif Bq == batches[-1]:
+            # the pairs this rank's experts served in the last expert-parallel step (-1: another rank's)
+            x, idx = layers[0].last_pairs
+        else:
+            continue
+        npairs = int((idx >= 0).sum())
+        nd = int(torch.unique(idx[idx >= 0]).numel())
+        for p_ in projs:
+            p_(x, idx)
+        torch.cuda.synchronize()
+        dur = kernel_seconds(torch, s, lambda i: projs[i % n_layers](x, idx), max(3, args.steps))
+        rows = int((idx >= 0).reshape(x.shape[0], -1).any(dim=1).sum())  # token rows the served pairs read
+        alg = nd * EXPERT_BYTES["gate"] + CODEBOOK_BYTES + rows * HIDDEN * 2 + npairs * INTER * 2
+        achieved = alg / dur / 1e9
+        kname = ("vq_prefill_tc_kernel" if projs[0].kernel_path(x.shape[0], idx.shape[-1]) == "gemm"
+                 else "vq_decode_mma_kernel")
+        traffic = profiled_traffic(kname, f"c2_b{Bq}") if world == 1 else None
+        roofs[Bq] = {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak_gbs, "unit": "GB/s",
+                     "frac": round(achieved / peak_gbs, 4), "traffic": traffic,
+                     "kernel": "%s (gate projection, %d pairs, %d distinct experts), timed alone" % (kname, npairs, nd),
+                     "algorithmic_bytes_per_launch": alg, "us_per_launch": round(dur * 1e6, 2),
+                     "peak_kind": f"{peak_kind} burst copy bandwidth"}
+    roof = roofs.get(args.batch)
+    B = args.batch
 
     # ---- e2e through the public API with host buffers: every step copies its
     # inputs from pinned host memory into the layer's input buffers, runs the
@@ -564,6 +751,8 @@ def gpu_arm(args, rank, world, dev):
     if world > 1:
         for L in layers:
             L.close()  # collective: peer regions are released together
+    for Bq, r in roofs.items():
+        results[Bq]["roofline"] = r
     return results, roof, e2e, launches
 
 
@@ -610,10 +799,22 @@ def cpu_sample(tokens: int, seed: int = 11):
     return time.perf_counter() - t0
 
 
+def cpu_model() -> str:
+    """The host CPU's model name (the first "model name" of /proc/cpuinfo)."""
+    try:
+        for line in pathlib.Path("/proc/cpuinfo").read_text().splitlines():
+            if line.startswith("model name"):
+                return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
+
+
 def cpu_baseline_block(tokens):
     from oracle import oracle as orc
     secs = cpu_sample(tokens)
-    return {"value": round(tokens / secs, 3), "unit": UNIT, "cores": orc.num_threads(), "kind": "port",
+    return {"value": round(tokens / secs, 3), "unit": UNIT, "cores": orc.num_threads(), "cpu_model": cpu_model(),
+            "kind": "port",
             "sample": f"{tokens} token(s) of the C2 layer (10 pairs each x gate/up/down, walk-order decode of "
                       f"packed 14-bit codes, SwiGLU, combine) on the oracle port, {secs:.2f} s"}
 
@@ -631,14 +832,19 @@ def reference_arm(args, rank, world):
         times.append(cpu_sample(tokens, seed=200 + i))
     secs = sum(times)
     value = tokens * args.steps / secs
-    cb = {"value": round(value, 3), "unit": UNIT, "cores": orc.num_threads(), "kind": "port",
+    cb = {"value": round(value, 3), "unit": UNIT, "cores": orc.num_threads(), "cpu_model": cpu_model(), "kind": "port",
           "sample": f"{tokens} token of the C2 layer per step (router, 3 x 10-pair walk decode, SwiGLU, "
                     f"combine) on the oracle port of the reference arithmetic"}
     line = {"metric": METRIC, "value": round(value, 3), "unit": UNIT, "n_gpus": args.gpus, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(secs * 1e3 / args.steps, 3), "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "f32 accumulate over fp16 (bf16 I/O)",
             "data": "synthetic (seeded)", "impl": "reference",
-            "config": _config(args, world), "cpu_baseline": cb,
+            "config": dict(_config(args, world),
+                           workload="C2 one VQ-MoE layer decode, 1 token per step on the host (oracle port of the "
+                                    "reference arithmetic: router, 10-pair walk decode of gate/up/down, SwiGLU, "
+                                    "combine; hidden 4096, 512 experts, inter 1024, top-10, d8 K16384 14-bit, G64)",
+                           global_batch=1),
+            "cpu_baseline": cb,
             "e2e": {"value": round(value, 3), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
     return 0
@@ -671,7 +877,11 @@ def main(argv=None) -> int:
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--skip-prefill", action="store_true")
     ap.add_argument("--skip-dense", action="store_true")
+    ap.add_argument("--skip-c1", action="store_true")
+    ap.add_argument("--skip-c5", action="store_true")
     ap.add_argument("--prefill-only", action="store_true", help="run only the C3 prefill leg (for profiling)")
+    ap.add_argument("--only", choices=["c1", "dense", "c5"],
+                    help="run one leg alone and print its JSON (profiling runs)")
     ap.add_argument("--cpu-tokens", type=int, default=2048,
                     help="tokens of the CPU baseline sample (~12 s of oracle work on 16 host threads)")
     args = ap.parse_args(argv)
@@ -693,10 +903,17 @@ def main(argv=None) -> int:
                                              device_id=dev)
     from vqlab_b200 import _lib
     _lib.lib()
-    if args.prefill_only:
-        # the C3 leg alone (profiling runs): its own JSON line
+    if args.prefill_only or args.only:
+        # one leg alone (profiling runs): its own JSON line
         _, peak_tf, peak_kind = _peaks()
-        p = prefill_leg(torch, dev, args, peak_tf, peak_kind, rank, world)
+        if args.only == "c1":
+            p = c1_leg(torch, dev, args, *_peaks()[::2]) if world == 1 else {}
+        elif args.only == "dense":
+            p = dense_leg(torch, dev, args, *_peaks()[::2]) if world == 1 else {}
+        elif args.only == "c5":
+            p = c5_leg(torch, dev, args, rank, world)
+        else:
+            p = prefill_leg(torch, dev, args, peak_tf, peak_kind, rank, world)
         if rank == 0:
             print(json.dumps(p), flush=True)
         if world > 1:
@@ -706,11 +923,17 @@ def main(argv=None) -> int:
     results, roof, e2e, launches = gpu_arm(args, rank, world, dev)
     dense = None
     if not args.skip_dense and world == 1:
-        dense = dense_leg(torch, dev, args)
+        dense = dense_leg(torch, dev, args, *_peaks()[::2])
+    c1 = None
+    if not args.skip_c1 and world == 1:
+        c1 = c1_leg(torch, dev, args, *_peaks()[::2])
     prefill = None
     if not args.skip_prefill:
         _, peak_tf, peak_kind = _peaks()
         prefill = prefill_leg(torch, dev, args, peak_tf, peak_kind, rank, world)
+    c5 = None
+    if not args.skip_c5:
+        c5 = c5_leg(torch, dev, args, rank, world)
     if rank == 0:
         head = results[args.batch]
         line = {"metric": METRIC, "value": round(head["tokens_per_s"], 1), "unit": UNIT, "n_gpus": world,
@@ -722,7 +945,8 @@ def main(argv=None) -> int:
                 "batches": {str(b): {"tokens_per_s": round(r["tokens_per_s"], 1),
                                      "ms_per_step": round(r["ms_per_step"], 4),
                                      "hbm_gbs": round(r["hbm_gbs"], 1) if r["hbm_gbs"] else None,
-                                     "distinct_experts": round(r["distinct_experts_mean"], 1)}
+                                     "distinct_experts": round(r["distinct_experts_mean"], 1),
+                                     "roofline": r.get("roofline")}
                             for b, r in results.items()},
                 "roofline": roof, "e2e": e2e, "gpu_launches": launches * args.steps,
                 "gpu_launches_per_step": launches}
@@ -730,6 +954,10 @@ def main(argv=None) -> int:
             line["prefill"] = prefill
         if dense is not None:
             line["dense"] = dense
+        if c1 is not None:
+            line["c1"] = c1
+        if c5 is not None:
+            line["c5"] = c5
         if not args.no_cpu_baseline and world == 1:
             line["cpu_baseline"] = cpu_baseline_block(args.cpu_tokens)
         print(json.dumps(line), flush=True)
