@@ -203,6 +203,90 @@ __global__ void __launch_bounds__(256) route_topk_kernel(const float* __restrict
   }
 }
 
+// The same router for E <= 32 * VPL experts with each lane's VPL
+// probabilities in registers: the loads are independent (no chain of global
+// loads), and a top-k round rescans only the winning lane's values -- every
+// other lane's best is unchanged.  Same arithmetic, same order and same
+// tie-breaking as route_topk_kernel, so the results are bit-identical.
+template <int VPL>
+__global__ void __launch_bounds__(256) route_topk_reg_kernel(const float* __restrict__ logits, int T, int E, int k,
+                                                             int32_t* __restrict__ idx, float* __restrict__ w) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nw = blockDim.x >> 5;
+  for (int t = blockIdx.x * nw + warp; t < T; t += gridDim.x * nw) {
+    const float* row = logits + static_cast<int64_t>(t) * E;
+    float p[VPL];
+#pragma unroll
+    for (int i = 0; i < VPL; ++i) {
+      const int e = lane + 32 * i;
+      p[i] = e < E ? __ldg(row + e) : -INFINITY;
+    }
+    float m = -INFINITY;
+#pragma unroll
+    for (int i = 0; i < VPL; ++i)
+      if (lane + 32 * i < E) m = fmaxf(m, p[i]);
+    for (int o = 16; o; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    float sum = 0.0f;
+#pragma unroll
+    for (int i = 0; i < VPL; ++i) {
+      if (lane + 32 * i < E) {
+        p[i] = expf(p[i] - m);
+        sum += p[i];
+      }
+    }
+    for (int o = 16; o; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+#pragma unroll
+    for (int i = 0; i < VPL; ++i) p[i] = lane + 32 * i < E ? __fdiv_rn(p[i], sum) : -1.0f;
+    // this lane's best remaining entry (strictly larger wins: the lowest index among equals)
+    auto local_best = [&](float& bv, int& bi) {
+      bv = -1.0f;
+      bi = 0x7fffffff;
+#pragma unroll
+      for (int i = 0; i < VPL; ++i) {
+        if (p[i] > bv) {
+          bv = p[i];
+          bi = lane + 32 * i;
+        }
+      }
+    };
+    float lv;
+    int li;
+    local_best(lv, li);
+    float mine_w = 0.0f, wsum = 0.0f;
+    int mine_i = 0;
+    for (int j = 0; j < k; ++j) {
+      float bv = lv;
+      int bi = li;
+      for (int o = 16; o; o >>= 1) {
+        const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+        const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+        if (ov > bv || (ov == bv && oi < bi)) {
+          bv = ov;
+          bi = oi;
+        }
+      }
+      if (bi >= E) {  // no candidate left (NaN logits): expert 0, weight 0
+        bi = 0;
+        bv = 0.0f;
+      } else if ((bi & 31) == lane) {
+#pragma unroll
+        for (int i = 0; i < VPL; ++i)
+          if (lane + 32 * i == bi) p[i] = -1.0f;
+        local_best(lv, li);
+      }
+      if (lane == j) {
+        mine_w = bv;
+        mine_i = bi;
+      }
+      wsum += bv;
+    }
+    if (lane < k) {
+      idx[static_cast<int64_t>(t) * k + lane] = mine_i;
+      w[static_cast<int64_t>(t) * k + lane] = __fdiv_rn(mine_w, wsum);
+    }
+  }
+}
+
 thread_local int g_sms_ops = 0;  // the current device's SM count, refreshed by ensure_sms()
 
 vqb_status ensure_sms() {
@@ -324,6 +408,21 @@ extern "C" vqb_status vqb_moe_route(const float* logits, int32_t n_tokens, int32
   if (!logits || !indices || !weights) return VQB_NULL_POINTER;
   vqb_status st = ensure_sms();
   if (st != VQB_OK) return st;
+  if (num_experts <= 1024) {
+    // probabilities in registers: 8 tokens (warps) per 256-thread block
+    const int nwr = 8;
+    int64_t blocks = (static_cast<int64_t>(n_tokens) + nwr - 1) / nwr;
+    if (blocks > 8 * static_cast<int64_t>(g_sms_ops)) blocks = 8 * static_cast<int64_t>(g_sms_ops);
+    const unsigned nb = static_cast<unsigned>(blocks);
+    cudaStream_t cs = reinterpret_cast<cudaStream_t>(stream);
+    if (num_experts <= 128) route_topk_reg_kernel<4><<<nb, 256, 0, cs>>>(logits, n_tokens, num_experts, top_k, indices, weights);
+    else if (num_experts <= 256) route_topk_reg_kernel<8><<<nb, 256, 0, cs>>>(logits, n_tokens, num_experts, top_k, indices, weights);
+    else if (num_experts <= 512) route_topk_reg_kernel<16><<<nb, 256, 0, cs>>>(logits, n_tokens, num_experts, top_k, indices, weights);
+    else route_topk_reg_kernel<32><<<nb, 256, 0, cs>>>(logits, n_tokens, num_experts, top_k, indices, weights);
+    if (cudaGetLastError() != cudaSuccess) return VQB_CUDA_ERROR;
+    note_launch();
+    return VQB_OK;
+  }
   const size_t row_bytes = sizeof(float) * static_cast<size_t>(num_experts);
   int nw = static_cast<int>((48 * 1024) / row_bytes);
   nw = nw < 1 ? 1 : (nw > 8 ? 8 : nw);

@@ -104,6 +104,7 @@ struct TParams {
   const int* tile_base;      // SKIPZERO: first compact row of each (expert, 128-row tile), -1 = all dead
   int64_t nrows;             // rows of codes / scales
   int max_group;             // tiles per group allowed by the L2 budget for re-read code windows
+  int cb_early;              // the codebook (slice source) predates the kernel this one depends on
   int ksplit;                // work items per tile: split-K over its windows (1 = whole tiles)
   float* partial;            // ksplit > 1: fp32 partial tiles [item][pcols columns][128 rows]
   int pcols;                 // columns of a partial slot (tokens a chunk can hold, rounded to 16)
@@ -580,12 +581,14 @@ __global__ void __launch_bounds__(kThreads, 1)
   // Launched as a programmatic dependent of the kernel before it (the x
   // gather): the set-up above overlaps that kernel's tail; nothing it wrote
   // (routing tables, gathered x) and nothing it may still read is touched
-  // before this wait returns.
-  asm volatile("griddepcontrol.wait;" ::: "memory");
+  // before this wait returns.  The codebook loader thread waits in its own
+  // role, after it has started the first codebook slice (prm.cb_early).
+  const bool cb_thread = warp == kWarpCbLoad && lane == 0;
+  if (!cb_thread) asm volatile("griddepcontrol.wait;" ::: "memory");
   // the split-K reduction after this kernel may be scheduled beside it (it waits for this grid's end)
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 
-  const int nchunks = prm.meta[0];
+  const int nchunks = cb_thread ? 0 : prm.meta[0];
   const int64_t nitems = static_cast<int64_t>(nchunks) * prm.row_tiles * prm.ksplit;
   const int nwin = prm.n_pos / kSets;
 
@@ -741,27 +744,40 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else if (warp == kWarpCbLoad) {
     // ---------------- codebook slice loader
     if (lane == 0) {
+      // slice h: entries [h * kp, ...), or (dimension split) dims [4h, 4h + 4)
+      // of all entries from the [2][K][4] copy of the codebook
+      auto load_slice = [&](int h) {
+        const int64_t first = DS ? 0 : static_cast<int64_t>(h) * prm.kp;
+        const int64_t cnt = DS ? static_cast<int64_t>(prm.K)
+                               : min(static_cast<int64_t>(prm.kp), static_cast<int64_t>(prm.K) - first);
+        const uint32_t bytes = static_cast<uint32_t>(cnt * (DS ? 8 : D * 2));
+        mbar_expect_tx(cb_full, bytes);
+        const unsigned char* src = reinterpret_cast<const unsigned char*>(prm.codebook) +
+                                   (DS ? static_cast<int64_t>(h) * prm.K * 8 : first * D * 2);
+        for (uint32_t off = 0; off < bytes; off += 8192u)
+          bulk_load(reinterpret_cast<unsigned char*>(cb_s) + off, src + off, min(8192u, bytes - off), cb_full);
+      };
       int resident = -1;
       uint32_t loads = 0;
+      if (prm.cb_early) {
+        // the first group's first pass always reads slice 0, and the codebook
+        // (its halves built by an earlier call) is not written by the kernel
+        // this one depends on: load it before waiting for that kernel
+        load_slice(0);
+        resident = 0;
+        loads = 1;
+      }
+      asm volatile("griddepcontrol.wait;" ::: "memory");
+      const int64_t nitems_cb = static_cast<int64_t>(prm.meta[0]) * prm.row_tiles * prm.ksplit;
       bool ok = true;
       int jg = 0;
-      for (int64_t it0 = blockIdx.x; it0 < nitems && ok; ++jg) {
-        const TileGroup grp = form_group(prm, it0, nitems);
+      for (int64_t it0 = blockIdx.x; it0 < nitems_cb && ok; ++jg) {
+        const TileGroup grp = form_group(prm, it0, nitems_cb);
         for (int pass = 0; pass < prm.npass; ++pass) {
           const int h = pass_slice(prm.npass, jg, pass);
           if (h == resident) continue;
           if (loads > 0 && !mbar_wait(cb_empty, (loads - 1) & 1u, abort_flag)) { ok = false; break; }
-          // a slice of entries, or (dimension split) dims [4h, 4h + 4) of all
-          // entries from the [2][K][4] copy of the codebook
-          const int64_t first = DS ? 0 : static_cast<int64_t>(h) * prm.kp;
-          const int64_t cnt = DS ? static_cast<int64_t>(prm.K)
-                                 : min(static_cast<int64_t>(prm.kp), static_cast<int64_t>(prm.K) - first);
-          const uint32_t bytes = static_cast<uint32_t>(cnt * (DS ? 8 : D * 2));
-          mbar_expect_tx(cb_full, bytes);
-          const unsigned char* src = reinterpret_cast<const unsigned char*>(prm.codebook) +
-                                     (DS ? static_cast<int64_t>(h) * prm.K * 8 : first * D * 2);
-          for (uint32_t off = 0; off < bytes; off += 8192u)
-            bulk_load(reinterpret_cast<unsigned char*>(cb_s) + off, src + off, min(8192u, bytes - off), cb_full);
+          load_slice(h);
           resident = h;
           ++loads;
         }
@@ -1335,6 +1351,11 @@ vqb_status launch_prefill_tc(const LinearGeometry& geo, const void* x, int x_dty
     note_launch();
   }
   // 1a. dimension halves of the codebook (the caller's, when it built them once)
+  // the caller's codebook, or the halves it built once, are not written by the
+  // kernels of this call: the GEMM may start loading them before its
+  // programmatic-dependency wait; halves derived here come from the kernel
+  // right before it
+  prm.cb_early = (!ds || geo.codebook_halves) ? 1 : 0;
   if (ds && geo.codebook_halves) {
     prm.codebook = static_cast<const uint16_t*>(geo.codebook_halves);
   } else if (ds) {
