@@ -512,13 +512,15 @@ def prefill_leg(torch, dev, args, peak_tf, peak_kind, rank, world, T=4096, seed=
     else:
         xg, gidx = layer.last_pairs
     dur = kernel_seconds(torch, s, lambda i: layer.gate_proj(xg, gidx), 5)
-    kflops = 2 * INTER * HIDDEN * int((gidx >= 0).sum())
+    served = int((gidx >= 0).sum())  # this rank's pairs (read before the exchange regions are released)
+    kflops = 2 * INTER * HIDDEN * served
     ach = kflops / dur / 1e12
     busy = None
     if world > 1:
         # per-rank expert compute against the layer time: Zipf imbalance vs the exchange
         busy = [round(b * 1e3, 3) for b in gather_floats(torch, dev, expert_busy_seconds(torch, layer), world)]
-        layer.close()
+        del xg, gidx
+        layer.close()  # collective; xg / gidx were views of this rank's exchange region
     return {"metric": f"VQ-MoE prefill TFLOP/s (one MoE layer, {T} tokens per GPU, Zipf(1.1) top-10)",
             "value": round(flops * steps * world / secs / 1e12, 2), "unit": "TFLOP/s", "steps": steps,
             "ms_per_layer": round(secs * 1e3 / steps, 3), "tokens_per_s": round(T * steps * world / secs, 1),
@@ -529,7 +531,7 @@ def prefill_leg(torch, dev, args, peak_tf, peak_kind, rank, world, T=4096, seed=
             "roofline": {"bound": "tensor", "achieved": round(ach, 1), "peak": peak_tf, "unit": "TFLOP/s",
                          "frac": round(ach / peak_tf, 4),
                          "traffic": profiled_traffic("vq_prefill_tc_kernel", "c3") if world == 1 else None,
-                         "kernel": "vq_prefill_tc_kernel (gate projection, %d pairs on this rank), timed alone" % int((gidx >= 0).sum()),
+                         "kernel": "vq_prefill_tc_kernel (gate projection, %d pairs on this rank), timed alone" % served,
                          "us_per_launch": round(dur * 1e6, 1), "peak_kind": f"{peak_kind} burst bf16 GEMM"}}
 
 

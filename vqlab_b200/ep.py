@@ -331,7 +331,10 @@ class EPMoEBlock(torch.nn.Module):
         return self._peer
 
     def close(self) -> None:
-        """Release the peer exchange (collective); the NCCL path holds nothing."""
+        """Release the peer exchange (collective); the NCCL path holds nothing.
+        `last_pairs` may be views of the exchange region: dropped here."""
+        if getattr(self, "last_pairs", None) is not None and self._peer is not None:
+            self.last_pairs = None
         if self._peer is not None:
             self._peer.close()
             self._peer = None
