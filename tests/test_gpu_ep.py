@@ -32,7 +32,7 @@ def _proj_np(rng, out, inn):
     return packed, cb, sc
 
 
-def _worker(rank, world, port, out_dir, static=None, exchange="nccl"):
+def _worker(rank, world, port, out_dir, static=None, exchange="nccl", tokens=T):
     import datetime
     import torch.distributed as dist
     from vqlab_b200 import VQSwitchLinear
@@ -65,8 +65,8 @@ def _worker(rank, world, port, out_dir, static=None, exchange="nccl"):
         ep = EPMoEBlock(shard(P[0], H), shard(P[1], H), shard(P[2], I), K, num_experts=E, static_tokens=static,
                         exchange=exchange)
         g = torch.Generator().manual_seed(7 + rank)
-        x = torch.randn((T + 3 * rank, H), generator=g).to(torch.bfloat16).to(dev)
-        lg = torch.randn((T + 3 * rank, E), generator=g).to(dev)
+        x = torch.randn((tokens + 3 * rank, H), generator=g).to(torch.bfloat16).to(dev)
+        lg = torch.randn((tokens + 3 * rank, E), generator=g).to(dev)
         lg[:, 0] += 4.0 * rank  # rank 1's tokens lean on rank 0's experts
         y_ep = ep(x, lg)
         y_ref = single(x, lg)
@@ -89,16 +89,20 @@ def _worker(rank, world, port, out_dir, static=None, exchange="nccl"):
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
-@pytest.mark.parametrize("static,exchange", [(None, "nccl"), (64, "nccl"), (64, "p2p")])
-def test_ep_two_gpus_matches_single_gpu_block(tmp_path, static, exchange):
+@pytest.mark.parametrize("static,exchange,tokens", [(None, "nccl", T), (64, "nccl", T), (64, "p2p", T),
+                                                   (320, "p2p", 300)])
+def test_ep_two_gpus_matches_single_gpu_block(tmp_path, static, exchange, tokens):
     """Every dispatch path: the dynamic one (exact split sizes read on the
     host), the fixed-shape decode path (all-gather, skipped pairs, fp32
     partial combine), which must also replay from a CUDA graph with its NCCL
     calls, and the same fixed-shape step over peer memory (IPC-mapped
-    regions, no NCCL on the data path), also replayed from a graph."""
+    regions, no NCCL on the data path), also replayed from a graph -- at a
+    decode batch (the decode kernel) and at a prefill-size batch (300 tokens
+    per rank: the grouped GEMM on the gathered pairs, as bench.py's
+    multi-GPU prefill leg runs it)."""
     world = 2
-    mp.start_processes(_worker, args=(world, _free_port(), str(tmp_path), static, exchange), nprocs=world, join=True,
-                       start_method="spawn")
+    mp.start_processes(_worker, args=(world, _free_port(), str(tmp_path), static, exchange, tokens), nprocs=world,
+                       join=True, start_method="spawn")
     for r in range(world):
         d = torch.load(tmp_path / f"r{r}.pt")
         ep, ref = d["ep"], d["ref"]
