@@ -312,6 +312,14 @@ __global__ void __launch_bounds__(kThreads, 1) vq_decode_mma_kernel(const MParam
     }
   }
 
+  // Launched as a programmatic dependent of the routing sort (or of the x
+  // conversion after it): the codebook load above overlaps that kernel's tail
+  // -- the routing sort waited for every kernel launched before this call, and
+  // no kernel of this call writes the codebook -- and nothing that kernel
+  // writes or may still read is touched before this wait returns.
+  pdl_wait();
+  pdl_trigger();
+
   // the partner CTA must be running before its shared memory is written
   if constexpr (SPLIT) cluster_sync_all();
 
@@ -567,6 +575,8 @@ __global__ void __launch_bounds__(kThreads, 1) vq_decode_mma_kernel(const MParam
 // bf16 (WR 1), for x whose rows the kernel cannot read in place.
 __global__ void x_to_16bit_kernel(const void* __restrict__ x, int x_dtype, int64_t n, int to_bf16,
                                   uint16_t* __restrict__ out) {
+  pdl_wait();
+  pdl_trigger();
   for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n;
        i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
     const float v = load_x(x, i, x_dtype, false);
@@ -615,8 +625,9 @@ vqb_status launch_decode_mma(const LinearGeometry& geo, const GroupedDecodeArgs&
     const int64_t n = static_cast<int64_t>(T) * geo.IN;
     int64_t blocks = (n + 255) / 256;
     if (blocks > 4 * nsm) blocks = 4 * nsm;
-    x_to_16bit_kernel<<<static_cast<unsigned>(blocks), 256, 0, stream>>>(a.x, a.x_dtype, n, WR == 1 ? 1 : 0, x16);
-    if (cudaGetLastError() != cudaSuccess) return VQB_CUDA_ERROR;
+    if (launch_pdl(x_to_16bit_kernel, static_cast<unsigned>(blocks), 256, 0, stream, a.x, a.x_dtype, n,
+                   WR == 1 ? 1 : 0, x16) != cudaSuccess)
+      return VQB_CUDA_ERROR;
     note_launch();
   }
   MParams prm{};
@@ -745,13 +756,15 @@ vqb_status launch_decode_mma(const LinearGeometry& geo, const GroupedDecodeArgs&
     cfg.blockDim = dim3(kThreads);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = stream;
-    cudaLaunchAttribute attr[1];
+    cudaLaunchAttribute attr[2];
     attr[0].id = cudaLaunchAttributeClusterDimension;
     attr[0].val.clusterDim.x = is_split ? 2 : 1;
     attr[0].val.clusterDim.y = 1;
     attr[0].val.clusterDim.z = 1;
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
-    cfg.numAttrs = 1;
+    cfg.numAttrs = 2;
     timer_before(stream);
     ce = cudaLaunchKernelEx(&cfg, kern, prm);
     timer_after(stream);

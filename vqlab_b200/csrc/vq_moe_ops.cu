@@ -34,6 +34,8 @@ __device__ __forceinline__ float silu(float v) { return v / (1.0f + expf(-v)); }
 // VEC elements of T per thread-step (16 bytes when VEC * sizeof(T) == 16)
 template <typename T, int VEC>
 __global__ void swiglu_kernel(const T* __restrict__ g, const T* __restrict__ u, T* __restrict__ h, int64_t n) {
+  pdl_wait();
+  pdl_trigger();
   const int64_t nv = n / VEC;
   for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < nv;
        i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
@@ -60,6 +62,8 @@ __global__ void swiglu_kernel(const T* __restrict__ g, const T* __restrict__ u, 
 template <typename T, int VEC>
 __global__ void combine_kernel(const T* __restrict__ d, const float* __restrict__ w, T* __restrict__ y, int Tn, int k,
                                int H) {
+  pdl_wait();
+  pdl_trigger();
   const int per_tok = H / VEC;
   const int64_t total = static_cast<int64_t>(Tn) * per_tok;
   for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
@@ -103,6 +107,8 @@ template <typename T, int VEC>
 __global__ void combine_partial_kernel(const T* __restrict__ d, const float* __restrict__ w,
                                        const uint32_t* __restrict__ skip, float* __restrict__ y, int Tn, int k,
                                        int H) {
+  pdl_wait();
+  pdl_trigger();
   const int per_tok = H / VEC;
   const int64_t total = static_cast<int64_t>(Tn) * per_tok;
   for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
@@ -141,6 +147,8 @@ __global__ void combine_partial_kernel(const T* __restrict__ d, const float* __r
 __global__ void __launch_bounds__(256) route_topk_kernel(const float* __restrict__ logits, int T, int E, int k,
                                                          int32_t* __restrict__ idx, float* __restrict__ w) {
   extern __shared__ float s_prob[];
+  pdl_wait();
+  pdl_trigger();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int nw = blockDim.x >> 5;
   float* p = s_prob + static_cast<size_t>(warp) * E;
@@ -212,6 +220,8 @@ template <int VPL>
 __global__ void __launch_bounds__(256) route_topk_reg_kernel(const float* __restrict__ logits, int T, int E, int k,
                                                              int32_t* __restrict__ idx, float* __restrict__ w) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  pdl_wait();
+  pdl_trigger();
   const int nw = blockDim.x >> 5;
   for (int t = blockIdx.x * nw + warp; t < T; t += gridDim.x * nw) {
     const float* row = logits + static_cast<int64_t>(t) * E;
@@ -306,30 +316,32 @@ bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 
 
 template <typename T>
 vqb_status launch_swiglu(const void* g, const void* u, void* h, int64_t n, cudaStream_t s) {
+  cudaError_t ce;
   constexpr int V = 16 / sizeof(T);
   if (n % V == 0 && aligned16(g) && aligned16(u) && aligned16(h)) {
-    swiglu_kernel<T, V><<<grid_for(n / V), 256, 0, s>>>(static_cast<const T*>(g), static_cast<const T*>(u),
+    ce = launch_pdl(swiglu_kernel<T, V>, grid_for(n / V), 256, 0, s, static_cast<const T*>(g), static_cast<const T*>(u),
                                                         static_cast<T*>(h), n);
   } else {
-    swiglu_kernel<T, 1><<<grid_for(n), 256, 0, s>>>(static_cast<const T*>(g), static_cast<const T*>(u),
+    ce = launch_pdl(swiglu_kernel<T, 1>, grid_for(n), 256, 0, s, static_cast<const T*>(g), static_cast<const T*>(u),
                                                     static_cast<T*>(h), n);
   }
-  if (cudaGetLastError() != cudaSuccess) return VQB_CUDA_ERROR;
+  if (ce != cudaSuccess) return VQB_CUDA_ERROR;
   note_launch();
   return VQB_OK;
 }
 
 template <typename T>
 vqb_status launch_combine(const void* d, const float* w, void* y, int Tn, int k, int H, cudaStream_t s) {
+  cudaError_t ce;
   constexpr int V = 16 / sizeof(T);
   if (H % V == 0 && aligned16(d) && aligned16(y)) {
-    combine_kernel<T, V><<<grid_for(static_cast<int64_t>(Tn) * (H / V)), 256, 0, s>>>(
+    ce = launch_pdl(combine_kernel<T, V>, grid_for(static_cast<int64_t>(Tn) * (H / V)), 256, 0, s,
         static_cast<const T*>(d), w, static_cast<T*>(y), Tn, k, H);
   } else {
-    combine_kernel<T, 1><<<grid_for(static_cast<int64_t>(Tn) * H), 256, 0, s>>>(static_cast<const T*>(d), w,
+    ce = launch_pdl(combine_kernel<T, 1>, grid_for(static_cast<int64_t>(Tn) * H), 256, 0, s, static_cast<const T*>(d), w,
                                                                                static_cast<T*>(y), Tn, k, H);
   }
-  if (cudaGetLastError() != cudaSuccess) return VQB_CUDA_ERROR;
+  if (ce != cudaSuccess) return VQB_CUDA_ERROR;
   note_launch();
   return VQB_OK;
 }
@@ -337,15 +349,16 @@ vqb_status launch_combine(const void* d, const float* w, void* y, int Tn, int k,
 template <typename T>
 vqb_status launch_combine_partial(const void* d, const float* w, const uint32_t* skip, float* y, int Tn, int k, int H,
                                   cudaStream_t s) {
+  cudaError_t ce;
   constexpr int V = 16 / sizeof(T);
   if (H % V == 0 && aligned16(d)) {
-    combine_partial_kernel<T, V><<<grid_for(static_cast<int64_t>(Tn) * (H / V)), 256, 0, s>>>(
+    ce = launch_pdl(combine_partial_kernel<T, V>, grid_for(static_cast<int64_t>(Tn) * (H / V)), 256, 0, s,
         static_cast<const T*>(d), w, skip, y, Tn, k, H);
   } else {
-    combine_partial_kernel<T, 1><<<grid_for(static_cast<int64_t>(Tn) * H), 256, 0, s>>>(static_cast<const T*>(d), w,
+    ce = launch_pdl(combine_partial_kernel<T, 1>, grid_for(static_cast<int64_t>(Tn) * H), 256, 0, s, static_cast<const T*>(d), w,
                                                                                        skip, y, Tn, k, H);
   }
-  if (cudaGetLastError() != cudaSuccess) return VQB_CUDA_ERROR;
+  if (ce != cudaSuccess) return VQB_CUDA_ERROR;
   note_launch();
   return VQB_OK;
 }
@@ -415,11 +428,12 @@ extern "C" vqb_status vqb_moe_route(const float* logits, int32_t n_tokens, int32
     if (blocks > 8 * static_cast<int64_t>(g_sms_ops)) blocks = 8 * static_cast<int64_t>(g_sms_ops);
     const unsigned nb = static_cast<unsigned>(blocks);
     cudaStream_t cs = reinterpret_cast<cudaStream_t>(stream);
-    if (num_experts <= 128) route_topk_reg_kernel<4><<<nb, 256, 0, cs>>>(logits, n_tokens, num_experts, top_k, indices, weights);
-    else if (num_experts <= 256) route_topk_reg_kernel<8><<<nb, 256, 0, cs>>>(logits, n_tokens, num_experts, top_k, indices, weights);
-    else if (num_experts <= 512) route_topk_reg_kernel<16><<<nb, 256, 0, cs>>>(logits, n_tokens, num_experts, top_k, indices, weights);
-    else route_topk_reg_kernel<32><<<nb, 256, 0, cs>>>(logits, n_tokens, num_experts, top_k, indices, weights);
-    if (cudaGetLastError() != cudaSuccess) return VQB_CUDA_ERROR;
+    cudaError_t ce;
+    if (num_experts <= 128) ce = launch_pdl(route_topk_reg_kernel<4>, nb, 256, 0, cs, logits, n_tokens, num_experts, top_k, indices, weights);
+    else if (num_experts <= 256) ce = launch_pdl(route_topk_reg_kernel<8>, nb, 256, 0, cs, logits, n_tokens, num_experts, top_k, indices, weights);
+    else if (num_experts <= 512) ce = launch_pdl(route_topk_reg_kernel<16>, nb, 256, 0, cs, logits, n_tokens, num_experts, top_k, indices, weights);
+    else ce = launch_pdl(route_topk_reg_kernel<32>, nb, 256, 0, cs, logits, n_tokens, num_experts, top_k, indices, weights);
+    if (ce != cudaSuccess) return VQB_CUDA_ERROR;
     note_launch();
     return VQB_OK;
   }
@@ -431,11 +445,12 @@ extern "C" vqb_status vqb_moe_route(const float* logits, int32_t n_tokens, int32
       cudaFuncSetAttribute(route_topk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)) !=
           cudaSuccess)
     return VQB_CUDA_ERROR;
+  cudaError_t ce;
   int64_t blocks = (static_cast<int64_t>(n_tokens) + nw - 1) / nw;
   if (blocks > 8 * static_cast<int64_t>(g_sms_ops)) blocks = 8 * static_cast<int64_t>(g_sms_ops);
-  route_topk_kernel<<<static_cast<unsigned>(blocks), nw * 32, smem, reinterpret_cast<cudaStream_t>(stream)>>>(
+  ce = launch_pdl(route_topk_kernel, static_cast<unsigned>(blocks), nw * 32, smem, reinterpret_cast<cudaStream_t>(stream), 
       logits, n_tokens, num_experts, top_k, indices, weights);
-  if (cudaGetLastError() != cudaSuccess) return VQB_CUDA_ERROR;
+  if (ce != cudaSuccess) return VQB_CUDA_ERROR;
   note_launch();
   return VQB_OK;
 }

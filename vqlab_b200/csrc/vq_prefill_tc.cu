@@ -982,8 +982,11 @@ __global__ void tile_base_kernel(const int32_t* __restrict__ rt, int E, int OUT,
 __global__ void gather_sorted_kernel(const void* __restrict__ x, int x_dtype, const int* __restrict__ sorted,
                                      const int* __restrict__ n_sorted, int krep, int IN, int to_bf16, int dsplit,
                                      uint16_t* __restrict__ xs) {
-  // the grouped GEMM that follows may start its set-up now (it waits for this grid's end before reading xs)
-  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  // launched as a programmatic dependent of the routing sort: wait for its
+  // tables; the grouped GEMM that follows may start its set-up now (it waits
+  // for this grid's end before reading xs)
+  pdl_wait();
+  pdl_trigger();
   const int vec = IN / 8;
   const bool convert = (x_dtype == VQB_BF16) != (to_bf16 != 0);
   const int64_t total = static_cast<int64_t>(*n_sorted) * vec;  // pairs left out are not in sorted
@@ -1344,18 +1347,20 @@ vqb_status launch_prefill_tc(const LinearGeometry& geo, const void* x, int x_dty
     if ((reinterpret_cast<uintptr_t>(x) & 15) != 0) return VQB_BAD_ALIGNMENT;
     int64_t blocks = (static_cast<int64_t>(N) * (geo.IN / 8) + 255) / 256;
     if (blocks > 16 * g_sms_tc) blocks = 16 * g_sms_tc;
-    gather_sorted_kernel<<<static_cast<unsigned>(blocks), 256, 0, stream>>>(x, x_dtype, rw.sorted, rw.offsets + geo.E,
-                                                                            krep, geo.IN,
-                                                                            bf16_operands ? 1 : 0, ds ? 1 : 0, xs);
-    if (cudaGetLastError() != cudaSuccess) return VQB_CUDA_ERROR;
+    if (launch_pdl(gather_sorted_kernel, static_cast<unsigned>(blocks), 256, 0, stream, x, x_dtype,
+                   static_cast<const int*>(rw.sorted), static_cast<const int*>(rw.offsets + geo.E), krep, geo.IN,
+                   bf16_operands ? 1 : 0, ds ? 1 : 0, xs) != cudaSuccess)
+      return VQB_CUDA_ERROR;
     note_launch();
   }
   // 1a. dimension halves of the codebook (the caller's, when it built them once)
-  // the caller's codebook, or the halves it built once, are not written by the
-  // kernels of this call: the GEMM may start loading them before its
-  // programmatic-dependency wait; halves derived here come from the kernel
-  // right before it
-  prm.cb_early = (!ds || geo.codebook_halves) ? 1 : 0;
+  // The GEMM may start loading the caller's codebook, or the halves it built
+  // once, before its programmatic-dependency wait when the kernel right before
+  // it is the x gather: that kernel waited for everything the caller launched
+  // earlier, and no kernel of this call writes them.  Halves derived here come
+  // from the kernel right before the GEMM, and after a call that reuses the
+  // gathered x the kernel before it may be the caller's own.
+  prm.cb_early = gather_x && (!ds || geo.codebook_halves) ? 1 : 0;
   if (ds && geo.codebook_halves) {
     prm.codebook = static_cast<const uint16_t*>(geo.codebook_halves);
   } else if (ds) {

@@ -73,8 +73,10 @@ __global__ void __launch_bounds__(kRouteWarps * 32) route_small_kernel(const uin
   const int lo = min(N, wid * per), hi = min(N, lo + per);
   const uint32_t lt = (1u << lane) - 1u;
 
-  if (threadIdx.x < 4) ws.meta[threadIdx.x] = 0;  // status block, before any thread can report into it
   for (int i = threadIdx.x; i < kRouteWarps * E; i += blockDim.x) tab[i] = 0;
+  pdl_wait();  // the previous kernel may still read this workspace
+  pdl_trigger();
+  if (threadIdx.x < 4) ws.meta[threadIdx.x] = 0;  // status block, before any thread can report into it
   __syncthreads();
   // 1. per-warp counts (the range's expert ids are read kBatch steps at a
   // time, so the loads of a warp are in flight together)
@@ -224,8 +226,8 @@ static vqb_status launch_route_w(const uint32_t* idx, int N, int E, int max_pair
     ce = cudaFuncSetAttribute(route_small_kernel<W>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                               static_cast<int>(smem));
   if (ce != cudaSuccess) return VQB_CUDA_ERROR;
-  route_small_kernel<W><<<1, W * 32, smem, stream>>>(idx, N, E, max_pairs, ws);
-  if (cudaGetLastError() != cudaSuccess) return VQB_CUDA_ERROR;
+  if (launch_pdl(route_small_kernel<W>, 1, W * 32, smem, stream, idx, N, E, max_pairs, ws) != cudaSuccess)
+    return VQB_CUDA_ERROR;
   note_launch();
   return VQB_OK;
 }

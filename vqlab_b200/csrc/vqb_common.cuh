@@ -44,6 +44,18 @@ __device__ __forceinline__ void store_y(void* y, int64_t i, float acc, int dtype
   else reinterpret_cast<float*>(y)[i] = acc;
 }
 
+// ------------------------------------------------- programmatic dependent launch
+
+// Wait until the kernel before this one on the stream has finished and its
+// writes are visible.  A kernel launched with launch_pdl (vqb_internal.h) calls
+// this before its first global access; without the launch attribute it
+// returns at once.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
+// Let the next kernel on the stream start its CTAs (it still waits for this
+// one's completion in its own pdl_wait).
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 // ------------------------------------------------------------ global loads
 
 __device__ __forceinline__ uint4 ldg_stream_v4(const void* p) {

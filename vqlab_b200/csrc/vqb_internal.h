@@ -2,6 +2,7 @@
 #pragma once
 
 #include <cstdint>
+#include <utility>
 #include <cuda_runtime.h>
 
 #include "../../include/vqb.h"
@@ -80,6 +81,28 @@ vqb_status launch_prefill_tc(const LinearGeometry& geo, const void* x, int x_dty
                              int N, uint16_t* xs, void* y, int y_dtype, bool round_f16_first, bool bf16_operands, bool gather_x,
                              int* status, cudaStream_t stream);
 constexpr int kPrefillTileTokens = 128;
+
+// Launch `kern` as a programmatic dependent of the kernel before it on the
+// stream: its CTAs may start while that kernel finishes, so the kernel must
+// execute griddepcontrol.wait (pdl_wait) before it reads or writes memory the
+// previous kernel touches; griddepcontrol.launch_dependents (pdl_trigger) lets
+// the kernel after it do the same.  Both are no-ops in a kernel launched
+// without the attribute.
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                       Args&&... args) {
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
+}
 
 // Launch accounting and the one-shot kernel timer (vqb_api.cu): every kernel
 // launch of the library calls note_launch(); the dominant kernel of a call
