@@ -226,6 +226,13 @@ def layer_bytes(n_distinct, batch):
     return n_distinct * per_expert + 3 * CODEBOOK_BYTES + act
 
 
+def fused_layer_bytes(n_distinct, batch):
+    """Algorithmic bytes of the one-launch layer: the routed experts' packed
+    codes and scales, the three codebooks, router logits, x and y (its
+    intermediate partials never need to leave the chip in principle)."""
+    return n_distinct * sum(EXPERT_BYTES.values()) + 3 * CODEBOOK_BYTES + batch * (E * 4 + HIDDEN * 2 * 2)
+
+
 def time_eager_steps(torch, layers, xs, lg, steps, warmup):
     """Eager layer steps (the expert-parallel dispatch reads split sizes on the host)."""
     s = torch.cuda.current_stream()
@@ -665,19 +672,32 @@ def gpu_arm(args, rank, world, dev):
             continue
         npairs = int((idx >= 0).sum())
         nd = int(torch.unique(idx[idx >= 0]).numel())
-        for p_ in projs:
-            p_(x, idx)
-        torch.cuda.synchronize()
-        dur = kernel_seconds(torch, s, lambda i: projs[i % n_layers](x, idx), max(3, args.steps))
-        rows = int((idx >= 0).reshape(x.shape[0], -1).any(dim=1).sum())  # token rows the served pairs read
-        alg = nd * EXPERT_BYTES["gate"] + CODEBOOK_BYTES + rows * HIDDEN * 2 + npairs * INTER * 2
+        fused = world == 1 and layers[0].fused != "off" and layers[0].fused_status(Bq) == 0
+        if fused:
+            # the whole layer is one launch (vqb_moe_block_forward): its bytes are
+            # the three projections of every routed expert, the codebooks, x and y
+            x2, lg2 = x.reshape(Bq, HIDDEN), lgt
+            for L_ in layers:
+                L_(x2, lg2)
+            torch.cuda.synchronize()
+            dur = kernel_seconds(torch, s, lambda i: layers[i % n_layers](x2, lg2), max(3, args.steps))
+            alg = fused_layer_bytes(nd, Bq)
+            kname, what = "moe_block_kernel", "the fused MoE block: router, gate, up, SwiGLU, down, combine"
+        else:
+            for p_ in projs:
+                p_(x, idx)
+            torch.cuda.synchronize()
+            dur = kernel_seconds(torch, s, lambda i: projs[i % n_layers](x, idx), max(3, args.steps))
+            rows = int((idx >= 0).reshape(x.shape[0], -1).any(dim=1).sum())  # token rows the served pairs read
+            alg = nd * EXPERT_BYTES["gate"] + CODEBOOK_BYTES + rows * HIDDEN * 2 + npairs * INTER * 2
+            kname = ("vq_prefill_tc_kernel" if projs[0].kernel_path(x.shape[0], idx.shape[-1]) == "gemm"
+                     else "vq_decode_mma_kernel")
+            what = "gate projection"
         achieved = alg / dur / 1e9
-        kname = ("vq_prefill_tc_kernel" if projs[0].kernel_path(x.shape[0], idx.shape[-1]) == "gemm"
-                 else "vq_decode_mma_kernel")
         traffic = profiled_traffic(kname, f"c2_b{Bq}") if world == 1 else None
         roofs[Bq] = {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak_gbs, "unit": "GB/s",
                      "frac": round(achieved / peak_gbs, 4), "traffic": traffic,
-                     "kernel": "%s (gate projection, %d pairs, %d distinct experts), timed alone" % (kname, npairs, nd),
+                     "kernel": "%s (%s, %d pairs, %d distinct experts), timed alone" % (kname, what, npairs, nd),
                      "algorithmic_bytes_per_launch": alg, "us_per_launch": round(dur * 1e6, 2),
                      "peak_kind": f"{peak_kind} burst copy bandwidth"}
     roof = roofs.get(args.batch)

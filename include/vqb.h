@@ -226,6 +226,44 @@ vqb_status vqb_moe_combine_partial(const void* expert_out, const float* weights,
                                    int32_t n_tokens, int32_t top_k, int32_t hidden, vqb_dtype dtype,
                                    vqb_stream_t stream);
 
+/* ---- The whole MoE block in one launch (decode batches) ----
+ *
+ * y = combine(down(swiglu(gate(x), up(x)))) routed by router_logits: the
+ * block of tests/test_qwen3_5_parity.py:180-204 around three VQSwitchLinear
+ * projections (vq_switch.py:5284-5423), with the routing of vqb_moe_route
+ * (bit-identical indices and weights) and the roundings of the per-step
+ * calls -- each projection's output to fp16 and then to x's dtype, h = dtype(
+ * silu(g) * u) narrowed to fp16 as the down projection's input, the combine
+ * in fp32 in slot order -- in ONE persistent cooperative kernel.  The
+ * projections take W = fp16(cb * s) weights with fp32 accumulation (the
+ * reference's non-ACCS arm).  No reference counterpart as one call (the
+ * reference dispatches each step).
+ *
+ * gate / up: [E, I, H]; down: [E, H, I]; each descriptor's codebook_halves
+ * must be set (vqb_codebook_halves).  Served shapes (else
+ * VQB_UNSUPPORTED_GEOMETRY, and the caller runs the per-step calls): d8
+ * codebooks with K = 2^BITS, BITS 12 or 14, packed codes, group size 64, the
+ * same K for the three projections, H and I multiples of 512, E <= 1024,
+ * n_tokens * top_k <= 640, no SKIPZERO row table, bf16 / fp16 x, codes and
+ * scales 16-byte aligned.  indices / weights (both or neither) receive the
+ * routing [n_tokens, top_k].  The first 16 bytes of the workspace are a status
+ * block the call rewrites (int32 [1] = VQB_TIMEOUT when a bounded device wait
+ * gave up).  Calls of this kernel on one GPU must not overlap: each holds one
+ * CTA on every SM until it ends (a cooperative launch), and their grid
+ * barriers share one arrival counter per device. */
+typedef struct vqb_moe_block_desc {
+  vqb_linear_desc gate;
+  vqb_linear_desc up;
+  vqb_linear_desc down;
+  int32_t top_k;
+} vqb_moe_block_desc;
+
+vqb_status vqb_moe_block_supported(const vqb_moe_block_desc* desc, int32_t n_tokens, vqb_dtype x_dtype);
+size_t vqb_moe_block_workspace_size(const vqb_moe_block_desc* desc, int32_t n_tokens);
+vqb_status vqb_moe_block_forward(const vqb_moe_block_desc* desc, const float* router_logits, const void* x,
+                                 vqb_dtype x_dtype, int32_t n_tokens, void* y, int32_t* indices, float* weights,
+                                 void* workspace, size_t workspace_bytes, vqb_stream_t stream);
+
 /* ---- Expert-parallel exchange over peer memory (fixed-shape decode path) ----
  *
  * No reference counterpart: the reference runs every expert on one device

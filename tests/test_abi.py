@@ -280,3 +280,34 @@ def test_router_validation():
     assert L.vqb_moe_route(p, -1, 512, 8, p, p, None) == _lib.VQB_BAD_SHAPE
     assert L.vqb_moe_route(None, 4, 512, 8, p, p, None) == _lib.VQB_NULL_POINTER
     assert L.vqb_moe_route(None, 0, 512, 8, None, None, None) == _lib.VQB_OK
+
+
+def _block_desc(top_k=4, **kw):
+    d = _lib.MoeBlockDesc()
+    kw.setdefault("codebook_halves", 0x9000)
+    d.gate = _desc(out_features=512, in_features=512, codes_last_dim=24, **kw)
+    d.up = _desc(out_features=512, in_features=512, codes_last_dim=24, **kw)
+    d.down = _desc(out_features=512, in_features=512, codes_last_dim=24, **kw)
+    d.top_k = top_k
+    return d
+
+
+def test_moe_block_host_validation():
+    """The fused block's shape checks, before any device query."""
+    L = _lib.lib()
+    d = _block_desc()
+    d.down.in_features = 1024
+    d.down.codes_last_dim = 48
+    assert L.vqb_moe_block_supported(ctypes.byref(d), 4, _lib.VQB_BF16) == _lib.VQB_BAD_SHAPE  # down IN != I
+    assert L.vqb_moe_block_supported(ctypes.byref(_block_desc(top_k=0)), 4, _lib.VQB_BF16) == _lib.VQB_BAD_SHAPE
+    assert L.vqb_moe_block_supported(ctypes.byref(_block_desc(top_k=5)), 4, _lib.VQB_BF16) == _lib.VQB_BAD_SHAPE
+    assert L.vqb_moe_block_supported(ctypes.byref(_block_desc()), 0, _lib.VQB_BF16) == _lib.VQB_BAD_SHAPE
+    assert L.vqb_moe_block_supported(None, 4, _lib.VQB_BF16) == _lib.VQB_NULL_POINTER
+    unsupported = _lib.VQB_UNSUPPORTED_GEOMETRY
+    assert L.vqb_moe_block_supported(ctypes.byref(_block_desc()), 4, _lib.VQB_F32) == unsupported
+    assert L.vqb_moe_block_supported(ctypes.byref(_block_desc()), 161, _lib.VQB_BF16) == unsupported  # > 640 pairs
+    assert L.vqb_moe_block_supported(ctypes.byref(_block_desc(group_size=128)), 4, _lib.VQB_BF16) == unsupported
+    assert L.vqb_moe_block_supported(ctypes.byref(_block_desc(codebook_halves=None)), 4, _lib.VQB_BF16) == unsupported
+    # workspace: status block + fp32 partial slots + fp16 SwiGLU rows
+    n = L.vqb_moe_block_workspace_size(ctypes.byref(_block_desc()), 4)
+    assert n >= 256 + (4 * 64 * 512 + 2 * 64 * 512) * 4 + 16 * 512 * 2

@@ -54,6 +54,10 @@ class LinearDesc(ctypes.Structure):
     ]
 
 
+class MoeBlockDesc(ctypes.Structure):
+    _fields_ = [("gate", LinearDesc), ("up", LinearDesc), ("down", LinearDesc), ("top_k", ctypes.c_int32)]
+
+
 class Options(ctypes.Structure):
     _fields_ = [
         ("path", ctypes.c_int32),
@@ -121,6 +125,12 @@ def _bind(L):
     L.vqb_moe_route.argtypes = [P, i32, i32, i32, P, P, P]
     L.vqb_codebook_halves.restype = i32
     L.vqb_codebook_halves.argtypes = [P, i32, P, P]
+    L.vqb_moe_block_supported.restype = i32
+    L.vqb_moe_block_supported.argtypes = [P, i32, i32]
+    L.vqb_moe_block_workspace_size.restype = sz
+    L.vqb_moe_block_workspace_size.argtypes = [P, i32]
+    L.vqb_moe_block_forward.restype = i32
+    L.vqb_moe_block_forward.argtypes = [P, P, P, i32, i32, P, P, P, P, sz, P]
     L.vqb_ep_region_bytes.restype = sz
     L.vqb_ep_region_bytes.argtypes = [P, P]
     L.vqb_ep_region_alloc.restype = i32
@@ -184,7 +194,8 @@ def exported_symbols():
     return ["vqb_version", "vqb_status_string", "vqb_unpack", "vqb_switch_workspace_size",
             "vqb_switch_forward", "vqb_dense_workspace_size", "vqb_dense_forward", "vqb_switch_forward_static",
             "vqb_launch_count", "vqb_time_next_kernel", "vqb_swiglu", "vqb_moe_combine", "vqb_switch_path",
-            "vqb_moe_combine_partial", "vqb_moe_route", "vqb_codebook_halves", "vqb_ep_region_bytes", "vqb_ep_region_alloc", "vqb_ep_region_free",
+            "vqb_moe_combine_partial", "vqb_moe_route", "vqb_codebook_halves", "vqb_moe_block_supported",
+            "vqb_moe_block_workspace_size", "vqb_moe_block_forward", "vqb_ep_region_bytes", "vqb_ep_region_alloc", "vqb_ep_region_free",
             "vqb_ep_ipc_handle", "vqb_ep_ipc_open", "vqb_ep_ipc_close", "vqb_ep_dispatch", "vqb_ep_combine",
             "vqb_ep_reduce"]
 

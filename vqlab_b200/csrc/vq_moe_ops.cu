@@ -6,6 +6,7 @@
 // Both are HBM-bound streams; 16-byte vectors when the tensors allow it.
 #include "vqb_common.cuh"
 #include "vqb_internal.h"
+#include "vq_router.cuh"
 
 namespace vqb {
 
@@ -212,10 +213,9 @@ __global__ void __launch_bounds__(256) route_topk_kernel(const float* __restrict
 }
 
 // The same router for E <= 32 * VPL experts with each lane's VPL
-// probabilities in registers: the loads are independent (no chain of global
-// loads), and a top-k round rescans only the winning lane's values -- every
-// other lane's best is unchanged.  Same arithmetic, same order and same
-// tie-breaking as route_topk_kernel, so the results are bit-identical.
+// probabilities in registers (route_row_reg, vq_router.cuh): same arithmetic,
+// same order and same tie-breaking as route_topk_kernel, so the results are
+// bit-identical.
 template <int VPL>
 __global__ void __launch_bounds__(256) route_topk_reg_kernel(const float* __restrict__ logits, int T, int E, int k,
                                                              int32_t* __restrict__ idx, float* __restrict__ w) {
@@ -224,75 +224,12 @@ __global__ void __launch_bounds__(256) route_topk_reg_kernel(const float* __rest
   pdl_trigger();
   const int nw = blockDim.x >> 5;
   for (int t = blockIdx.x * nw + warp; t < T; t += gridDim.x * nw) {
-    const float* row = logits + static_cast<int64_t>(t) * E;
-    float p[VPL];
-#pragma unroll
-    for (int i = 0; i < VPL; ++i) {
-      const int e = lane + 32 * i;
-      p[i] = e < E ? __ldg(row + e) : -INFINITY;
-    }
-    float m = -INFINITY;
-#pragma unroll
-    for (int i = 0; i < VPL; ++i)
-      if (lane + 32 * i < E) m = fmaxf(m, p[i]);
-    for (int o = 16; o; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-    float sum = 0.0f;
-#pragma unroll
-    for (int i = 0; i < VPL; ++i) {
-      if (lane + 32 * i < E) {
-        p[i] = expf(p[i] - m);
-        sum += p[i];
-      }
-    }
-    for (int o = 16; o; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
-#pragma unroll
-    for (int i = 0; i < VPL; ++i) p[i] = lane + 32 * i < E ? __fdiv_rn(p[i], sum) : -1.0f;
-    // this lane's best remaining entry (strictly larger wins: the lowest index among equals)
-    auto local_best = [&](float& bv, int& bi) {
-      bv = -1.0f;
-      bi = 0x7fffffff;
-#pragma unroll
-      for (int i = 0; i < VPL; ++i) {
-        if (p[i] > bv) {
-          bv = p[i];
-          bi = lane + 32 * i;
-        }
-      }
-    };
-    float lv;
-    int li;
-    local_best(lv, li);
-    float mine_w = 0.0f, wsum = 0.0f;
-    int mine_i = 0;
-    for (int j = 0; j < k; ++j) {
-      float bv = lv;
-      int bi = li;
-      for (int o = 16; o; o >>= 1) {
-        const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
-        const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-        if (ov > bv || (ov == bv && oi < bi)) {
-          bv = ov;
-          bi = oi;
-        }
-      }
-      if (bi >= E) {  // no candidate left (NaN logits): expert 0, weight 0
-        bi = 0;
-        bv = 0.0f;
-      } else if ((bi & 31) == lane) {
-#pragma unroll
-        for (int i = 0; i < VPL; ++i)
-          if (lane + 32 * i == bi) p[i] = -1.0f;
-        local_best(lv, li);
-      }
-      if (lane == j) {
-        mine_w = bv;
-        mine_i = bi;
-      }
-      wsum += bv;
-    }
+    int mine_i;
+    float mine_w;
+    route_row_reg<VPL>(logits + static_cast<int64_t>(t) * E, E, k, lane, mine_i, mine_w);
     if (lane < k) {
       idx[static_cast<int64_t>(t) * k + lane] = mine_i;
-      w[static_cast<int64_t>(t) * k + lane] = __fdiv_rn(mine_w, wsum);
+      w[static_cast<int64_t>(t) * k + lane] = mine_w;
     }
   }
 }

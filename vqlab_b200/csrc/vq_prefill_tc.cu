@@ -45,6 +45,7 @@
 
 #include "vqb_common.cuh"
 #include "vqb_internal.h"
+#include "vqb_tma.cuh"
 
 namespace vqb {
 
@@ -67,7 +68,6 @@ constexpr int kFirstDecodeWarp = 5;
 constexpr int kThreads = (kFirstDecodeWarp + kDecodeWarps) * 32;
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kTmemA = kIssuers * kMaxN;        // columns: [0,128) D0, [128,256) D1, then 8 A stages of 32
-constexpr uint64_t kWaitLimitNs = 2000000000ull;  // a bounded wait gives up after 2 s
 constexpr int kScaleRowBytes = 16;                   // 8 fp16 scales per row per window
 constexpr int kNumBars = 2 * kBStages + 2 + kAStages + 2 * kWStages + 2 + kIssuers + 1 + kIssuers;
 
@@ -109,78 +109,6 @@ struct TParams {
   float* partial;            // ksplit > 1: fp32 partial tiles [item][pcols columns][128 rows]
   int pcols;                 // columns of a partial slot (tokens a chunk can hold, rounded to 16)
 };
-
-// ------------------------------------------------------------ PTX helpers
-
-__device__ __forceinline__ uint32_t smem_u32(const void* p) {
-  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
-}
-
-__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
-  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" :: "r"(smem_u32(bar)), "r"(count) : "memory");
-}
-__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
-  asm volatile("{\n\t.reg .b64 st;\n\tmbarrier.arrive.shared::cta.b64 st, [%0];\n\t}" :: "r"(smem_u32(bar)) : "memory");
-}
-__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
-  asm volatile("{\n\t.reg .b64 st;\n\tmbarrier.arrive.expect_tx.shared::cta.b64 st, [%0], %1;\n\t}"
-               :: "r"(smem_u32(bar)), "r"(bytes) : "memory");
-}
-// One try (the hardware may suspend the thread briefly while the phase is
-// pending).  A suspend-time hint measured slower on the prefill pipeline.
-__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
-  uint32_t ok;
-  asm volatile("{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\tselp.u32 %0, 1, 0, p;\n\t}"
-               : "=r"(ok) : "r"(smem_u32(bar)), "r"(parity) : "memory");
-  return ok != 0;
-}
-__device__ __forceinline__ uint64_t global_ns() {
-  uint64_t t;
-  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-  return t;
-}
-// bounded wait: false when the time limit expired or another role aborted
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag) {
-  if (mbar_try_wait(bar, parity)) return true;
-  const uint64_t t0 = global_ns();
-  for (uint32_t i = 1;; ++i) {
-    if (mbar_try_wait(bar, parity)) return true;
-    if ((i & 63u) == 0u) {
-      if (*abort_flag) return false;
-      if (global_ns() - t0 > kWaitLimitNs) break;
-    }
-  }
-  *abort_flag = 1;
-  return false;
-}
-// the same for a whole warp: every lane waits, the warp agrees on the outcome
-__device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag) {
-  return __all_sync(0xffffffffu, mbar_wait(bar, parity, abort_flag)) != 0;
-}
-// bounded drain used at teardown (no abort check: a copy in flight must land)
-__device__ __forceinline__ void mbar_drain(uint64_t* bar, uint32_t parity) {
-  const uint64_t t0 = global_ns();
-  while (!mbar_try_wait(bar, parity) && global_ns() - t0 <= kWaitLimitNs) {
-  }
-}
-
-__device__ __forceinline__ void tma_load_2d(const CUtensorMap* map, uint64_t* bar, void* dst, int x, int y) {
-  asm volatile(
-      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];"
-      :: "r"(smem_u32(dst)), "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(x), "r"(y) : "memory");
-}
-__device__ __forceinline__ void tma_load_3d(const CUtensorMap* map, uint64_t* bar, void* dst, int x, int y, int z) {
-  asm volatile(
-      "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5}], [%2];"
-      :: "r"(smem_u32(dst)), "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(x), "r"(y), "r"(z)
-      : "memory");
-}
-// plain (non-tensor) bulk copy global -> shared; 16-byte aligned, size % 16 == 0
-__device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
-  asm volatile(
-      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
-      :: "r"(smem_u32(dst)), "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(smem_u32(bar)) : "memory");
-}
 
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
@@ -1069,32 +997,6 @@ __global__ void split_codebook_kernel(const uint16_t* __restrict__ cb, int K, ui
   const uint4 v = __ldg(reinterpret_cast<const uint4*>(cb) + c);
   reinterpret_cast<uint2*>(out)[c] = make_uint2(v.x, v.y);
   reinterpret_cast<uint2*>(out)[K + c] = make_uint2(v.z, v.w);
-}
-
-using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
-                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
-                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
-
-EncodeTiledFn encode_fn() {
-  static EncodeTiledFn fn = nullptr;
-  if (!fn) {
-    void* p = nullptr;
-    cudaDriverEntryPointQueryResult q;
-    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
-        q == cudaDriverEntryPointSuccess)
-      fn = reinterpret_cast<EncodeTiledFn>(p);
-  }
-  return fn;
-}
-
-bool encode_2d(EncodeTiledFn enc, CUtensorMap* map, CUtensorMapDataType dt, int esize, const void* ptr, uint64_t inner,
-               uint64_t rows, uint32_t box_inner, uint32_t box_rows, CUtensorMapSwizzle swz) {
-  cuuint64_t dims[2] = {static_cast<cuuint64_t>(inner), static_cast<cuuint64_t>(rows)};
-  cuuint64_t strides[1] = {static_cast<cuuint64_t>(inner) * esize};
-  cuuint32_t box[2] = {box_inner, box_rows};
-  cuuint32_t estr[2] = {1, 1};
-  return enc(map, dt, 2, const_cast<void*>(ptr), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swz,
-             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
 // xs [N, IN] 16-bit as a 3-d tensor (64 k, N tokens, IN / 64 chunks): a box

@@ -111,19 +111,77 @@ def route(router_logits: torch.Tensor, top_k: int):
 
 
 class VQMoEBlock(torch.nn.Module):
-    """gate_proj / up_proj: [E, I, H] experts; down_proj: [E, H, I]."""
+    """gate_proj / up_proj: [E, I, H] experts; down_proj: [E, H, I].
+
+    fused: "auto" runs the whole block as one library launch
+    (vqb_moe_block_forward) whenever the library serves the shape -- decode
+    batches of d8 layers, n_tokens * top_k <= 640 -- and the per-step kernels
+    otherwise; "on" requires the fused launch (ValueError when the shape is not
+    served); "off" always runs the per-step kernels."""
 
     def __init__(self, gate_proj: VQSwitchLinear, up_proj: VQSwitchLinear, down_proj: VQSwitchLinear,
-                 top_k: int):
+                 top_k: int, fused: str = "auto"):
         super().__init__()
+        if fused not in ("auto", "on", "off"):
+            raise ValueError("fused must be 'auto', 'on' or 'off'")
         self.gate_proj, self.up_proj, self.down_proj = gate_proj, up_proj, down_proj
         self.top_k = int(top_k)
+        self.fused = fused
+
+    def block_desc(self) -> _lib.MoeBlockDesc:
+        d = _lib.MoeBlockDesc()
+        d.gate, d.up, d.down = self.gate_proj.desc(), self.up_proj.desc(), self.down_proj.desc()
+        d.top_k = self.top_k
+        return d
+
+    def fused_status(self, n_tokens: int, dtype: torch.dtype = torch.bfloat16) -> int:
+        """vqb_moe_block_supported for this block at n_tokens (0 = served)."""
+        if dtype not in (torch.bfloat16, torch.float16):
+            return _lib.VQB_UNSUPPORTED_GEOMETRY
+        d = self.block_desc()
+        return int(_lib.lib().vqb_moe_block_supported(ctypes.byref(d), int(n_tokens), _DTYPES[dtype]))
 
     def forward(self, x: torch.Tensor, router_logits: torch.Tensor) -> torch.Tensor:
         """x [T, H] (bf16), router_logits [T, E] -> y [T, H] in x's dtype."""
         T, H = x.shape
+        if self.fused != "off" and x.is_cuda and router_logits.is_cuda:
+            st = self.fused_status(T, x.dtype)
+            if st == _lib.VQB_OK:
+                return self.forward_fused(x, router_logits)[0]
+            if self.fused == "on":
+                raise ValueError(f"fused MoE block: {_lib.status_string(st)}")
         idx, w = route(router_logits, self.top_k)
         return self.project(x, idx, w)
+
+    def forward_fused(self, x: torch.Tensor, router_logits: torch.Tensor, workspace: torch.Tensor | None = None):
+        """The block in one launch: returns (y [T, H], indices int32 [T, k],
+        weights fp32 [T, k]) -- the routing is vqb_moe_route's, bit for bit.
+        workspace: optional uint8 CUDA tensor of at least
+        vqb_moe_block_workspace_size bytes (its first 16 bytes are the call's
+        status block); allocated per call when None."""
+        T, H = x.shape
+        x = x.contiguous()
+        lg = router_logits.to(torch.float32).contiguous()
+        if lg.dim() != 2 or lg.shape[0] != T:
+            raise ValueError("router_logits must be [T, E]")
+        d = self.block_desc()
+        L = _lib.lib()
+        nbytes = int(L.vqb_moe_block_workspace_size(ctypes.byref(d), T))
+        if workspace is None:
+            ws = torch.empty(max(nbytes, 256), dtype=torch.uint8, device=x.device)
+        else:
+            if workspace.dtype != torch.uint8 or not workspace.is_cuda or workspace.numel() < nbytes:
+                raise ValueError(f"workspace must be a uint8 CUDA tensor of >= {nbytes} bytes")
+            ws = workspace
+        y = torch.empty((T, H), dtype=x.dtype, device=x.device)
+        idx = torch.empty((T, self.top_k), dtype=torch.int32, device=x.device)
+        w = torch.empty((T, self.top_k), dtype=torch.float32, device=x.device)
+        _lib.check(L.vqb_moe_block_forward(ctypes.byref(d), ctypes.c_void_p(lg.data_ptr()),
+                                           ctypes.c_void_p(x.data_ptr()), _DTYPES[x.dtype], T,
+                                           ctypes.c_void_p(y.data_ptr()), ctypes.c_void_p(idx.data_ptr()),
+                                           ctypes.c_void_p(w.data_ptr()), ctypes.c_void_p(ws.data_ptr()), nbytes,
+                                           _stream_ptr(x.device)), "vqb_moe_block_forward")
+        return y, idx, w
 
     def project(self, x: torch.Tensor, idx: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
         """The three projections, SwiGLU and combine for given routing."""
