@@ -310,4 +310,4 @@ def test_moe_block_host_validation():
     assert L.vqb_moe_block_supported(ctypes.byref(_block_desc(codebook_halves=None)), 4, _lib.VQB_BF16) == unsupported
     # workspace: status block + fp32 partial slots + fp16 SwiGLU rows
     n = L.vqb_moe_block_workspace_size(ctypes.byref(_block_desc()), 4)
-    assert n >= 256 + (4 * 64 * 512 + 2 * 64 * 512) * 4 + 16 * 512 * 2
+    assert n >= 256 + (4 * 64 * 512 + 2 * 64 * 512) * 4 + 16 * 512 * 2 + 4 * 512 * 2 + 2 * 16 * 4

@@ -96,3 +96,23 @@ def test_router_kernel_ties_take_the_lower_expert():
     assert idx[0].tolist() == [0, 1, 2, 3]
     assert idx[1].tolist() == [40, 0, 1, 2]
     assert torch.allclose(w[0], torch.full((4,), 0.25, device="cuda"))
+
+
+@pytest.mark.parametrize("E,k", [(512, 10), (96, 8), (1000, 16)])
+def test_router_kernel_ties_within_and_across_lanes(E, k):
+    """Integer logits with many exact ties (equal logits give equal
+    probabilities in any correct arithmetic): the experts come out in the
+    order (larger probability, then the lower id) -- also when the tied
+    entries sit in the same lane of the register router (ids 32 apart)."""
+    from vqlab_b200.moe import route
+    g = torch.Generator(device="cpu").manual_seed(E + k)
+    T = 48
+    lg = torch.randint(0, 4, (T, E), generator=g).float()
+    lg[0, :] = 0.0
+    lg[0, 64] = lg[0, 32] = lg[0, 0] = 2.0  # one lane (0) holds all three of the top entries
+    idx, w = route(lg.cuda(), k)
+    keys = lg.numpy()
+    for t in range(T):
+        order = sorted(range(E), key=lambda e: (-keys[t, e], e))[:k]
+        assert idx[t].tolist() == order, t
+    assert torch.allclose(w.sum(-1), torch.ones(T, device="cuda"), rtol=1e-5)

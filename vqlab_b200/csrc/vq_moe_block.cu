@@ -8,10 +8,12 @@
 //
 // One CTA per SM, cooperative launch (every CTA resident), phases separated by
 // grid barriers:
-//   0. every CTA routes the whole batch itself (the same arithmetic as the
-//      router kernel, vq_router.cuh), groups the (token, slot) pairs by expert
-//      (a stable counting sort) into chunks of <= 8 tokens of one expert, and
-//      meanwhile its copy thread loads the codebook half it needs first;
+//   0. the CTAs narrow x to fp16 (the MoE host cast) and route the tokens
+//      (one warp per token, the arithmetic of the router kernel,
+//      vq_router.cuh) into the workspace; after a grid barrier every CTA
+//      groups the (token, slot) pairs by expert (a stable counting sort) into
+//      chunks of <= 8 tokens of one expert.  Meanwhile the copy thread loads
+//      the codebook half the CTA needs first;
 //   1. gate and up: CTAs form four groups (gate, up) x (dims 0-3, dims 4-7);
 //      a group's CTA keeps that projection's codebook half [K][4] resident in
 //      shared memory (128 KB for K = 16384) and computes, for its work items,
@@ -84,6 +86,9 @@ struct MbParams {
   float* part1;            // [(proj * 2 + half) * S1 + split][pair][I]
   float* part3;            // [half * S3 + split][pair][H]
   uint16_t* h16;           // [pair][I] fp16: the down projection's input
+  uint16_t* x16;           // [T][H] fp16: x narrowed once (the MoE host cast)
+  int32_t* ridx;           // [T * k] routing: expert of each pair
+  float* rw;               // [T * k] routing: weight of each pair
   int* status;             // workspace status block: [1] = VQB_TIMEOUT when a wait expired
 };
 
@@ -130,8 +135,8 @@ __host__ __device__ inline MbLayout mb_layout(int K, int words) {
 constexpr int kStAbort = 0, kStChunks = 1, kStErr = 4, kStBarOk = 5, kStScan = 8;  // scan: 16 int2 from word 8
 
 // Split of a phase's windows: S pieces per (chunk, row block) minimising the
-// busiest CTA's windows (+ half a window of per-item cost), slots S * P
-// within the partial buffer.
+// busiest CTA's windows (+ 1/8 window per item: its partial store), slots
+// S * P within the partial buffer.
 __host__ __device__ inline int mb_split(int nseg, int ng, int nw, int P) {
   int smax = nw < kMbMaxSplit ? nw : kMbMaxSplit;
   const int cap = kMbSlotBudget / P > 1 ? kMbSlotBudget / P : 1;
@@ -140,7 +145,7 @@ __host__ __device__ inline int mb_split(int nseg, int ng, int nw, int P) {
   long long best_cost = -1;
   for (int S = 1; S <= smax; ++S) {
     const long long items = (static_cast<long long>(nseg) * S + ng - 1) / ng;
-    const long long cost = items * (2LL * ((nw + S - 1) / S) + 1);
+    const long long cost = items * (8LL * ((nw + S - 1) / S) + 1);
     if (best_cost < 0 || cost < best_cost) {
       best_cost = cost;
       best = S;
@@ -158,8 +163,8 @@ __host__ __device__ inline int mb_slots(int P) {
 // ------------------------------------------------------------ device helpers
 
 // Grid-wide arrivals of this device's fused-block launches.  Every CTA of a
-// launch arrives exactly once at each of its three barriers -- also after a
-// timeout -- so a launch advances the count by 3 * gridDim.x and a barrier's
+// launch arrives exactly once at each of its four barriers -- also after a
+// timeout -- so a launch advances the count by 4 * gridDim.x and a barrier's
 // round is (count before the arrival) / gridDim.x.  Zero when the module loads.
 __device__ unsigned long long g_mb_arrivals;
 
@@ -233,7 +238,7 @@ __device__ __forceinline__ float mb_silu(float v) { return v / (1.0f + expf(-v))
 // CTA's dimension half h.  Thread t takes codes 4t .. 4t+3 of each group of
 // 16; for code c the MMA's k slots (2t, 2t+1, 2t+8, 2t+9) hold dims 4h .. 4h+3
 // of W (A) and of x (B).
-template <int BITS, bool CVT>
+template <int BITS>
 __device__ __forceinline__ void mb_window(const uint32_t* __restrict__ cw, const uint16_t* __restrict__ sc,
                                           const unsigned char* __restrict__ xr, const uint16_t* __restrict__ cb,
                                           int warp, int g, int t, int n, int h, float (&acc)[2][4]) {
@@ -290,8 +295,8 @@ __device__ __forceinline__ void mb_window(const uint32_t* __restrict__ cw, const
       uint32_t x0 = 0, x1 = 0;
       if (has_x) {
         const uint2 xv = *reinterpret_cast<const uint2*>(xg + 16 * (16 * q + 4 * t + s));
-        x0 = CVT ? bf16x2_to_f16x2(xv.x) : xv.x;
-        x1 = CVT ? bf16x2_to_f16x2(xv.y) : xv.y;
+        x0 = xv.x;
+        x1 = xv.y;
       }
       uint2 e[4];
 #pragma unroll
@@ -312,7 +317,7 @@ struct MbPhase {
   int proj, half, j, ng, S, nseg, rts, nw, OUT;
   float* part;
   int pg;       // partial group: slots [pg * S, pg * S + S)
-  bool x_h16;   // token rows from h16 (down) instead of x (gate / up)
+  bool x_h16;   // token rows from h16 (down) instead of x16 (gate / up)
 };
 
 struct MbItem {
@@ -354,7 +359,7 @@ __device__ void mb_produce(const CUtensorMap* cmap, const CUtensorMap* smap, con
         const unsigned char* src =
             ph.x_h16 ? reinterpret_cast<const unsigned char*>(prm.h16) +
                            (static_cast<size_t>(pair) * prm.I + static_cast<size_t>(w) * kMbWinK) * 2
-                     : static_cast<const unsigned char*>(prm.x) +
+                     : reinterpret_cast<const unsigned char*>(prm.x16) +
                            (static_cast<size_t>(pair / prm.k) * prm.H + static_cast<size_t>(w) * kMbWinK) * 2;
         bulk_load(smem + L.xrows[st] + m * kMbXStride, src, kMbWinK * 2, &full[st]);
       }
@@ -365,7 +370,7 @@ __device__ void mb_produce(const CUtensorMap* cmap, const CUtensorMap* smap, con
 
 // consumer warps: decode every window of the phase's items, then store the
 // item's fp32 partial for its (pair, row) cells into the item's slot
-template <int BITS, bool CVT>
+template <int BITS>
 __device__ bool mb_consume(const MbParams& prm, const MbPhase& ph, const uint2* chunks, const uint16_t* sorted,
                            const unsigned char* smem, const MbLayout& L, uint64_t* full, uint64_t* empty,
                            uint32_t& gw, volatile int* abort_flag, int warp, int lane) {
@@ -381,7 +386,7 @@ __device__ bool mb_consume(const MbParams& prm, const MbPhase& ph, const uint2* 
     for (int w = it.w0; w < it.w1; ++w) {
       const int st = static_cast<int>(gw & 1u);
       if (!warp_wait(&full[st], (gw >> 1) & 1u, abort_flag)) return false;
-      mb_window<BITS, CVT>(reinterpret_cast<const uint32_t*>(smem + L.codes[st]),
+      mb_window<BITS>(reinterpret_cast<const uint32_t*>(smem + L.codes[st]),
                            reinterpret_cast<const uint16_t*>(smem + L.scales[st]), smem + L.xrows[st], cb, warp, g,
                            t, n, ph.half, acc);
       __syncwarp();
@@ -417,12 +422,54 @@ __device__ void mb_load_half(const uint16_t* halves, int half, int K, unsigned c
     bulk_load(dst + off, src + off, bytes - off < 8192u ? bytes - off : 8192u, bar);
 }
 
-// Phase 0 (consumer warps, every CTA): top-k of each token, then the pairs
-// grouped by expert -- counts, exclusive scans of pairs and of chunks
-// (<= 8 tokens each), chunk records in expert order, and a stable placement
-// (pairs keep their index order inside an expert).  Results: w[P] (weights),
-// sorted[P] (pair ids in chunk order), chunks[NC] = (expert | n << 16, first
-// sorted slot), st[kStChunks] = NC.
+// Phase 0a (all CTAs together): token t is routed by warp (t / nC) % warps of
+// CTA t % nC into prm.ridx / prm.rw (and the caller's indices / weights), and
+// x is narrowed to fp16 into prm.x16, an even share of it per CTA.
+__device__ void mb_route_tokens(const MbParams& prm, int warp, int lane) {
+  const int T = prm.T, E = prm.E, k = prm.k;
+  const int nC = static_cast<int>(gridDim.x), cta = static_cast<int>(blockIdx.x);
+  if (warp < kMbWarps) {
+    for (int t = cta + nC * warp; t < T; t += nC * kMbWarps) {
+      const float* row = prm.logits + static_cast<size_t>(t) * E;
+      int ei;
+      float ew;
+      if (E <= 128) route_row_reg<4>(row, E, k, lane, ei, ew);
+      else if (E <= 256) route_row_reg<8>(row, E, k, lane, ei, ew);
+      else if (E <= 512) route_row_reg<16>(row, E, k, lane, ei, ew);
+      else route_row_reg<32>(row, E, k, lane, ei, ew);
+      if (lane < k) {
+        prm.ridx[t * k + lane] = ei;
+        prm.rw[t * k + lane] = ew;
+        if (prm.idx_out) {
+          prm.idx_out[t * k + lane] = ei;
+          prm.w_out[t * k + lane] = ew;
+        }
+      }
+    }
+  }
+  // x -> fp16, 8 elements per thread-step (H is a multiple of 512)
+  const int64_t nv = static_cast<int64_t>(T) * prm.H / 8;
+  const int64_t per = (nv + nC - 1) / nC;
+  const int64_t v0 = static_cast<int64_t>(cta) * per, v1 = v0 + per < nv ? v0 + per : nv;
+  for (int64_t v = v0 + threadIdx.x; v < v1; v += blockDim.x) {
+    uint4 u = reinterpret_cast<const uint4*>(prm.x)[v];
+    if (prm.x_bf16) {
+      u.x = bf16x2_to_f16x2(u.x);
+      u.y = bf16x2_to_f16x2(u.y);
+      u.z = bf16x2_to_f16x2(u.z);
+      u.w = bf16x2_to_f16x2(u.w);
+    }
+    reinterpret_cast<uint4*>(prm.x16)[v] = u;
+  }
+  asm volatile("fence.proxy.async.global;" ::: "memory");  // x16 is read by bulk copies after the barrier
+}
+
+// Phase 0b (consumer warps, every CTA): the routed pairs grouped by expert --
+// counts, exclusive scans of pairs and of chunks (<= 8 tokens each), chunk
+// records in expert order, and a stable placement (pairs keep their index
+// order inside an expert).  Results: w[P] (weights), sorted[P] (pair ids in
+// chunk order), chunks[NC] = (expert | n << 16, first sorted slot),
+// st[kStChunks] = NC.
 __device__ void mb_route(const MbParams& prm, unsigned char* scratch, float* wsm, uint16_t* sorted, uint2* chunks,
                          int* st, int warp, int lane) {
   const int T = prm.T, E = prm.E, k = prm.k, P = T * k;
@@ -431,22 +478,10 @@ __device__ void mb_route(const MbParams& prm, unsigned char* scratch, float* wsm
   int* poff = cnt + kMbMaxExperts;               // [E] pair offset, then the placement cursor
   int* coff = poff + kMbMaxExperts;              // [E] chunk offset
   uint16_t* eid = reinterpret_cast<uint16_t*>(coff + kMbMaxExperts);  // [P] expert of each pair
-  for (int t = warp; t < T; t += kMbWarps) {
-    const float* row = prm.logits + static_cast<size_t>(t) * E;
-    int ei;
-    float ew;
-    if (E <= 128) route_row_reg<4>(row, E, k, lane, ei, ew);
-    else if (E <= 256) route_row_reg<8>(row, E, k, lane, ei, ew);
-    else if (E <= 512) route_row_reg<16>(row, E, k, lane, ei, ew);
-    else route_row_reg<32>(row, E, k, lane, ei, ew);
-    if (lane < k) {
-      eid[t * k + lane] = static_cast<uint16_t>(ei);
-      wsm[t * k + lane] = ew;
-      if (blockIdx.x == 0 && prm.idx_out) {
-        prm.idx_out[t * k + lane] = ei;
-        prm.w_out[t * k + lane] = ew;
-      }
-    }
+  for (int q = tid; q < P; q += kMbWarps * 32) {
+    const int e = __ldcg(prm.ridx + q);
+    eid[q] = static_cast<uint16_t>(e >= 0 && e < E ? e : 0);
+    wsm[q] = __ldcg(prm.rw + q);
   }
   for (int e = tid; e < E; e += kMbWarps * 32) cnt[e] = 0;
   asm volatile("bar.sync 1, %0;" :: "r"(kMbWarps * 32) : "memory");
@@ -571,7 +606,10 @@ __global__ void __launch_bounds__(kMbThreads, 1) moe_block_kernel(const __grid_c
     asm volatile("prefetch.tensormap [%0];" :: "l"(reinterpret_cast<uint64_t>(&maps.scales[g1 >> 1])) : "memory");
     mb_load_half(prm.proj[g1 >> 1].halves, g1 & 1, prm.K, smem + L.cb, cbar);
   }
-  if (warp < kMbWarps) {
+  mb_route_tokens(prm, warp, lane);
+  if (!mb_grid_barrier(true, st) && tid == 0) *abort_flag = 1;
+  __syncthreads();
+  if (warp < kMbWarps && !*abort_flag) {
     mb_route(prm, smem + L.codes[0], wsm, sorted, chunks, st, warp, lane);
     // the routing scratch in stage 0 is overwritten by tensor copies next
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
@@ -593,10 +631,8 @@ __global__ void __launch_bounds__(kMbThreads, 1) moe_block_kernel(const __grid_c
     mb_produce<BITS>(&maps.codes[ph1.proj], &maps.scales[ph1.proj], prm, ph1, chunks, sorted, smem, L, full, empty,
                      gw, abort_flag);
   } else if (warp < kMbWarps && ph1.j < ph1.nseg * ph1.S) {
-    if (warp_wait(cbar, 0, abort_flag)) {
-      if (prm.x_bf16) mb_consume<BITS, true>(prm, ph1, chunks, sorted, smem, L, full, empty, gw, abort_flag, warp, lane);
-      else mb_consume<BITS, false>(prm, ph1, chunks, sorted, smem, L, full, empty, gw, abort_flag, warp, lane);
-    }
+    if (warp_wait(cbar, 0, abort_flag))
+      mb_consume<BITS>(prm, ph1, chunks, sorted, smem, L, full, empty, gw, abort_flag, warp, lane);
   }
   __syncthreads();  // every consumer is done with the phase-1 codebook half
   if (copier) {
@@ -611,19 +647,34 @@ __global__ void __launch_bounds__(kMbThreads, 1) moe_block_kernel(const __grid_c
   bool ok = mb_grid_barrier(*abort_flag == 0, st);
 
   // ---------------- phase 2: SwiGLU -> the down projection's fp16 input
+  // (elements spread evenly over the CTAs; an element's partial loads are
+  // issued together, then summed in the fixed order: split, then half)
   if (ok && warp < kMbWarps) {
     const int I = prm.I;
     const int64_t n2 = static_cast<int64_t>(P) * I;
+    const int64_t per = (n2 + nC - 1) / nC;
+    const int64_t e0 = static_cast<int64_t>(cta) * per, e1 = e0 + per < n2 ? e0 + per : n2;
     const size_t gstride = static_cast<size_t>(S1) * P * I;  // one partial group
-    for (int64_t e = static_cast<int64_t>(cta) * (kMbWarps * 32) + tid; e < n2;
-         e += static_cast<int64_t>(nC) * (kMbWarps * 32)) {
+#pragma unroll 4
+    for (int64_t e = e0 + tid; e < e1; e += kMbWarps * 32) {
+      float v[4][kMbMaxSplit];
+#pragma unroll
+      for (int s = 0; s < kMbMaxSplit; ++s) {
+        if (s < S1) {
+          const size_t o = static_cast<size_t>(s) * P * I + static_cast<size_t>(e);
+#pragma unroll
+          for (int q = 0; q < 4; ++q) v[q][s] = prm.part1[q * gstride + o];
+        }
+      }
       float gs = 0.0f, us = 0.0f;
-      for (int s = 0; s < S1; ++s) {
-        const size_t o = static_cast<size_t>(s) * P * I + static_cast<size_t>(e);
-        gs += prm.part1[o];
-        gs += prm.part1[gstride + o];
-        us += prm.part1[2 * gstride + o];
-        us += prm.part1[3 * gstride + o];
+#pragma unroll
+      for (int s = 0; s < kMbMaxSplit; ++s) {
+        if (s < S1) {
+          gs += v[0][s];
+          gs += v[1][s];
+          us += v[2][s];
+          us += v[3][s];
+        }
       }
       const float hv = __fmul_rn(mb_silu(round_out(gs, prm.x_bf16)), round_out(us, prm.x_bf16));
       const float hd = prm.x_bf16 ? __bfloat162float(__float2bfloat16_rn(hv)) : __half2float(__float2half_rn(hv));
@@ -642,32 +693,59 @@ __global__ void __launch_bounds__(kMbThreads, 1) moe_block_kernel(const __grid_c
                        abort_flag);
     } else if (warp < kMbWarps && ph3.j < ph3.nseg * ph3.S) {
       if (warp_wait(cbar, 1, abort_flag))
-        mb_consume<BITS, false>(prm, ph3, chunks, sorted, smem, L, full, empty, gw, abort_flag, warp, lane);
+        mb_consume<BITS>(prm, ph3, chunks, sorted, smem, L, full, empty, gw, abort_flag, warp, lane);
     }
   }
   ok = mb_grid_barrier(ok && *abort_flag == 0, st);
 
-  // ---------------- phase 4: combine over the slots
-  if (ok && warp < kMbWarps) {
+  // ---------------- phase 4: combine over the slots.  The elements are
+  // spread evenly over the CTAs; each CTA first forms every (element, slot)
+  // product d * w with one thread per product (the slot's partial loads
+  // issued together) into its free stage memory, then adds each element's
+  // products in slot order.
+  if (ok) {
     const int H = prm.H, k = prm.k;
     const int64_t n4 = static_cast<int64_t>(prm.T) * H;
+    const int64_t per = (n4 + nC - 1) / nC;
+    const int64_t e0 = static_cast<int64_t>(cta) * per, e1 = e0 + per < n4 ? e0 + per : n4;
     const size_t hstride = static_cast<size_t>(S3) * P * H;
-    for (int64_t e = static_cast<int64_t>(cta) * (kMbWarps * 32) + tid; e < n4;
-         e += static_cast<int64_t>(nC) * (kMbWarps * 32)) {
-      const int t = static_cast<int>(e / H), r = static_cast<int>(e - static_cast<int64_t>(t) * H);
-      float acc = 0.0f;
-      for (int j = 0; j < k; ++j) {
-        const int pair = t * k + j;
-        float ds = 0.0f;
-        for (int s = 0; s < S3; ++s) {
-          const size_t o = (static_cast<size_t>(s) * P + pair) * H + r;
-          ds += prm.part3[o];
-          ds += prm.part3[hstride + o];
+    float* prod = reinterpret_cast<float*>(smem + L.codes[0]);
+    const int cap = static_cast<int>((L.w - L.codes[0]) / (4u * static_cast<uint32_t>(k)));  // elements per pass
+    for (int64_t sub = e0; sub < e1; sub += cap) {
+      const int ne = static_cast<int>(e1 - sub < cap ? e1 - sub : cap);
+#pragma unroll 4
+      for (int q = tid; q < ne * k; q += kMbThreads) {
+        const int j = q / ne, el = q - j * ne;
+        const int64_t e = sub + el;
+        const int t = static_cast<int>(e / H), r = static_cast<int>(e - static_cast<int64_t>(t) * H);
+        float v[2 * kMbMaxSplit];
+#pragma unroll
+        for (int s = 0; s < kMbMaxSplit; ++s) {
+          if (s < S3) {
+            const size_t o = (static_cast<size_t>(s) * P + t * k + j) * H + r;
+            v[2 * s] = prm.part3[o];
+            v[2 * s + 1] = prm.part3[hstride + o];
+          }
         }
-        acc = __fadd_rn(acc, __fmul_rn(round_out(ds, prm.x_bf16), wsm[pair]));
+        float ds = 0.0f;
+#pragma unroll
+        for (int s = 0; s < kMbMaxSplit; ++s) {
+          if (s < S3) {
+            ds += v[2 * s];
+            ds += v[2 * s + 1];
+          }
+        }
+        prod[el * k + j] = __fmul_rn(round_out(ds, prm.x_bf16), wsm[t * k + j]);
       }
-      if (prm.x_bf16) reinterpret_cast<__nv_bfloat16*>(prm.y)[e] = __float2bfloat16_rn(acc);
-      else reinterpret_cast<__half*>(prm.y)[e] = __float2half_rn(acc);
+      __syncthreads();
+      for (int el = tid; el < ne; el += kMbThreads) {
+        float acc = 0.0f;
+        for (int j = 0; j < k; ++j) acc = __fadd_rn(acc, prod[el * k + j]);
+        const int64_t e = sub + el;
+        if (prm.x_bf16) reinterpret_cast<__nv_bfloat16*>(prm.y)[e] = __float2bfloat16_rn(acc);
+        else reinterpret_cast<__half*>(prm.y)[e] = __float2half_rn(acc);
+      }
+      __syncthreads();
     }
   }
 
@@ -727,7 +805,7 @@ vqb_status mb_check(const vqb_moe_block_desc* d, int T, int x_dtype, MbGeo* g) {
 }
 
 struct MbWorkspace {
-  size_t status, part1, part3, h16, total;
+  size_t status, part1, part3, h16, x16, ridx, rw, total;
 };
 
 MbWorkspace mb_workspace(int T, int k, int H, int I) {
@@ -739,7 +817,10 @@ MbWorkspace mb_workspace(int T, int k, int H, int I) {
   w.part1 = 256;
   w.part3 = w.part1 + up(4 * slots * I * sizeof(float));
   w.h16 = w.part3 + up(2 * slots * H * sizeof(float));
-  w.total = w.h16 + up(static_cast<size_t>(P) * I * 2);
+  w.x16 = w.h16 + up(static_cast<size_t>(P) * I * 2);
+  w.ridx = w.x16 + up(static_cast<size_t>(T) * H * 2);
+  w.rw = w.ridx + up(static_cast<size_t>(P) * 4);
+  w.total = w.rw + up(static_cast<size_t>(P) * 4);
   return w;
 }
 
@@ -813,6 +894,9 @@ extern "C" vqb_status vqb_moe_block_forward(const vqb_moe_block_desc* desc, cons
   prm.part1 = reinterpret_cast<float*>(base + ws.part1);
   prm.part3 = reinterpret_cast<float*>(base + ws.part3);
   prm.h16 = reinterpret_cast<uint16_t*>(base + ws.h16);
+  prm.x16 = reinterpret_cast<uint16_t*>(base + ws.x16);
+  prm.ridx = reinterpret_cast<int32_t*>(base + ws.ridx);
+  prm.rw = reinterpret_cast<float*>(base + ws.rw);
 
   const MbLayout L = mb_layout(g.K, W);
   void (*kern)(MbMaps, MbParams) = g.bits == 14 ? moe_block_kernel<14> : moe_block_kernel<12>;
