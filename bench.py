@@ -9,7 +9,8 @@ bf16 activations.  Seeded synthetic weights (codes uniform over K, codebook
 
 A step is one MoE layer forward (router top-k, gate, up, SwiGLU, down,
 weighted combine) on the headline batch (64 tokens; 1 and 8 are reported
-beside it).  The prefill leg (benchmark configuration C3) runs the same layer on 4096
+beside it); on one GPU the layer is the library's fused block (one launch,
+vqb_moe_block_forward), `--no-fused` runs it as per-step kernels.  The prefill leg (benchmark configuration C3) runs the same layer on 4096
 tokens with top-10 routing drawn from Zipf(1.1) expert popularity and
 reports TFLOP/s of the three expert projections.  Several independently seeded layers are rotated so the
 weights a step reads are not in L2 from the previous step (the bytes each
@@ -25,7 +26,8 @@ prefill leg alike).  `value` is all ranks' tokens over the max-over-ranks time.
 The decode legs replay CUDA graphs.
 
 Other legs in the same JSON line: `batches` (C2 at 1, 8, 64 tokens with each
-batch's gate-projection kernel roofline), `dense` (C4, with the attention and
+batch's dominant-kernel roofline: the fused block, or the gate projection's
+kernel on the per-step path), `dense` (C4, with the attention and
 MLP kernels' rooflines), `c1` (C1: the 4096 x 4096 d8/K4096 matvec),
 `prefill` (C3; with N > 1 each rank's expert busy time), `c5` (C5 at its stated
 global shapes, 256 decode and 8192 prefill tokens split over the N GPUs).
@@ -185,7 +187,7 @@ class ClockSampler:
 
 # ------------------------------------------------------------------ GPU arm
 
-def make_layer(torch, dev, seed, rank=0, world=1, exchange="p2p"):
+def make_layer(torch, dev, seed, rank=0, world=1, exchange="p2p", fused="auto"):
     """One seeded MoE layer; with world > 1 this rank's expert shard of it
     wrapped in the expert-parallel block (codebooks are per layer, so every
     rank builds the same ones)."""
@@ -207,7 +209,7 @@ def make_layer(torch, dev, seed, rank=0, world=1, exchange="p2p"):
         return VQSwitchLinear(codes, cb, sc, group_size=G, pack_bits=BITS, in_features=inn)
 
     if world == 1:
-        return VQMoEBlock(proj(INTER, HIDDEN), proj(INTER, HIDDEN), proj(HIDDEN, INTER), TOPK)
+        return VQMoEBlock(proj(INTER, HIDDEN), proj(INTER, HIDDEN), proj(HIDDEN, INTER), TOPK, fused=fused)
     # decode batches take the fixed-shape path that CUDA graphs capture (gpu_arm sets
     # static_tokens to the batch it runs; larger batches take the dynamic path)
     return EPMoEBlock(proj(INTER, HIDDEN), proj(INTER, HIDDEN), proj(HIDDEN, INTER), TOPK, num_experts=E,
@@ -603,7 +605,8 @@ def gpu_arm(args, rank, world, dev):
     peak_gbs, peak_tf, peak_kind = _peaks()
     batches = sorted(set([args.batch] + [int(b) for b in args.extra_batches.split(",") if b]))
     n_layers = args.layers
-    layers = [make_layer(torch, dev, 1000 + l, rank, world, args.exchange) for l in range(n_layers)]
+    layers = [make_layer(torch, dev, 1000 + l, rank, world, args.exchange, "off" if args.no_fused else "auto")
+              for l in range(n_layers)]
     gen = torch.Generator(device=dev)
     gen.manual_seed(7 + rank)
     results = {}
@@ -901,6 +904,8 @@ def main(argv=None) -> int:
     ap.add_argument("--skip-dense", action="store_true")
     ap.add_argument("--skip-c1", action="store_true")
     ap.add_argument("--skip-c5", action="store_true")
+    ap.add_argument("--no-fused", action="store_true",
+                    help="run the C2 decode layer as per-step kernels instead of the one-launch fused block")
     ap.add_argument("--prefill-only", action="store_true", help="run only the C3 prefill leg (for profiling)")
     ap.add_argument("--only", choices=["c1", "dense", "c5"],
                     help="run one leg alone and print its JSON (profiling runs)")
