@@ -422,13 +422,155 @@ __device__ void mb_load_half(const uint16_t* halves, int half, int K, unsigned c
     bulk_load(dst + off, src + off, bytes - off < 8192u ? bytes - off : 8192u, bar);
 }
 
-// Phase 0a (all CTAs together): token t is routed by warp (t / nC) % warps of
-// CTA t % nC into prm.ridx / prm.rw (and the caller's indices / weights), and
-// x is narrowed to fp16 into prm.x16, an even share of it per CTA.
-__device__ void mb_route_tokens(const MbParams& prm, int warp, int lane) {
+// One token routed by all kMbWarps warps of the CTA (E <= 1024, k <= 32),
+// with route_row_reg's arithmetic and result: the same max, the same exps,
+// the per-lane sums added in the same order (lane l: entries l, l + 32, ...)
+// and combined by the same butterfly, the same divisions; the top_k by
+// (probability, then the lower id) as a per-warp top-k of each warp's entries
+// merged by warp 0.  scr: >= 1600 floats of shared memory.  Warp 0 lane j < k
+// receives slot j.
+__device__ void mb_route_one(const float* __restrict__ row, int E, int k, float* scr, int warp, int lane, int& out_i,
+                             float& out_w) {
+  constexpr int NT = kMbWarps * 32;
+  float* ex = scr;                                         // [1024] exp(logit - max)
+  float* red = scr + kMbMaxExperts;                        // [kMbWarps] per-warp max, then [0] the sum
+  float* cv = red + 32;                                    // [kMbWarps][32] per-warp top-k values
+  int* ci = reinterpret_cast<int*>(cv + kMbWarps * 32);    // [kMbWarps][32] their ids
+  const int tid = warp * 32 + lane;
+  float lg[kMbMaxExperts / NT];
+  float m = -INFINITY;
+#pragma unroll
+  for (int j = 0; j < kMbMaxExperts / NT; ++j) {
+    const int e = tid + NT * j;
+    lg[j] = e < E ? __ldg(row + e) : -INFINITY;
+    if (e < E) m = fmaxf(m, lg[j]);
+  }
+  for (int o = 16; o; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+  if (lane == 0) red[warp] = m;
+  asm volatile("bar.sync 1, %0;" :: "r"(NT) : "memory");
+#pragma unroll
+  for (int w = 0; w < kMbWarps; ++w) m = fmaxf(m, red[w]);
+#pragma unroll
+  for (int j = 0; j < kMbMaxExperts / NT; ++j) {
+    const int e = tid + NT * j;
+    if (e < E) ex[e] = expf(lg[j] - m);
+  }
+  asm volatile("bar.sync 1, %0;" :: "r"(NT) : "memory");
+  if (warp == 0) {
+    float sum = 0.0f;
+    for (int e = lane; e < E; e += 32) sum += ex[e];
+    for (int o = 16; o; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+    if (lane == 0) red[0] = sum;
+  }
+  asm volatile("bar.sync 1, %0;" :: "r"(NT) : "memory");
+  const float sum = red[0];
+  // this thread's entries, sorted: larger probability first, the lower id among equals
+  constexpr int J = kMbMaxExperts / NT;
+  float p[J];
+  int ix[J];
+#pragma unroll
+  for (int j = 0; j < J; ++j) {
+    const int e = tid + NT * j;
+    const float q = e < E ? __fdiv_rn(ex[e], sum) : -1.0f;
+    const bool live = q > -1.0f;
+    p[j] = live ? q : -1.0f;
+    ix[j] = live ? e : 0x7fffffff;
+  }
+#pragma unroll
+  for (int size = 2; size <= J; size <<= 1) {
+#pragma unroll
+    for (int stride = size >> 1; stride > 0; stride >>= 1) {
+#pragma unroll
+      for (int i = 0; i < J; ++i) {
+        const int j2 = i ^ stride;
+        if (j2 > i) {
+          const bool i_first = p[i] > p[j2] || (p[i] == p[j2] && ix[i] < ix[j2]);
+          const bool swap = ((i & size) == 0) ? !i_first : i_first;
+          const float tv = p[i];
+          const int ti = ix[i];
+          p[i] = swap ? p[j2] : p[i];
+          ix[i] = swap ? ix[j2] : ix[i];
+          p[j2] = swap ? tv : p[j2];
+          ix[j2] = swap ? ti : ix[j2];
+        }
+      }
+    }
+  }
+  // the warp's top k, in order
+  for (int r = 0; r < k; ++r) {
+    const uint32_t key = p[0] >= 0.0f ? __float_as_uint(p[0]) + 1u : 0u;
+    const uint32_t top = __reduce_max_sync(0xffffffffu, key);
+    const uint32_t bi = __reduce_min_sync(0xffffffffu, key == top ? static_cast<uint32_t>(ix[0]) : 0xffffffffu);
+    if (lane == 0) {
+      cv[warp * 32 + r] = top ? __uint_as_float(top - 1u) : -1.0f;
+      ci[warp * 32 + r] = top ? static_cast<int>(bi) : 0x7fffffff;
+    }
+    const bool pop = top != 0u && static_cast<uint32_t>(ix[0]) == bi;
+#pragma unroll
+    for (int i = 0; i + 1 < J; ++i) {
+      p[i] = pop ? p[i + 1] : p[i];
+      ix[i] = pop ? ix[i + 1] : ix[i];
+    }
+    p[J - 1] = pop ? -1.0f : p[J - 1];
+    ix[J - 1] = pop ? 0x7fffffff : ix[J - 1];
+  }
+  asm volatile("bar.sync 1, %0;" :: "r"(NT) : "memory");
+  if (warp == 0) {
+    // merge the warps' lists: lane q < kMbWarps holds the head of list q
+    int h = 0;
+    float hv = lane < kMbWarps ? cv[lane * 32] : -1.0f;
+    int hi = lane < kMbWarps ? ci[lane * 32] : 0x7fffffff;
+    float mine_w = 0.0f, wsum = 0.0f;
+    int mine_i = 0;
+    for (int j = 0; j < k; ++j) {
+      const uint32_t key = hv >= 0.0f ? __float_as_uint(hv) + 1u : 0u;
+      const uint32_t top = __reduce_max_sync(0xffffffffu, key);
+      const uint32_t bi = __reduce_min_sync(0xffffffffu, key == top ? static_cast<uint32_t>(hi) : 0xffffffffu);
+      float bv = 0.0f;  // no candidate left (NaN logits): expert 0, weight 0
+      int sel = 0;
+      if (top != 0u) {
+        bv = __uint_as_float(top - 1u);
+        sel = static_cast<int>(bi);
+        if (lane < kMbWarps && static_cast<uint32_t>(hi) == bi) {
+          ++h;
+          hv = h < k ? cv[lane * 32 + h] : -1.0f;
+          hi = h < k ? ci[lane * 32 + h] : 0x7fffffff;
+        }
+      }
+      if (lane == j) {
+        mine_w = bv;
+        mine_i = sel;
+      }
+      wsum += bv;
+    }
+    out_i = mine_i;
+    out_w = __fdiv_rn(mine_w, wsum);
+  }
+}
+
+// Phase 0a (all CTAs together): the tokens are routed into prm.ridx / prm.rw
+// (and the caller's indices / weights) -- with no more tokens than CTAs, token
+// t by all warps of CTA t; else token t by warp (t / nC) % warps of CTA
+// t % nC -- and x is narrowed to fp16 into prm.x16, an even share of it per
+// CTA.  scr: shared memory no one else uses in this phase.
+__device__ void mb_route_tokens(const MbParams& prm, float* scr, int warp, int lane) {
   const int T = prm.T, E = prm.E, k = prm.k;
   const int nC = static_cast<int>(gridDim.x), cta = static_cast<int>(blockIdx.x);
-  if (warp < kMbWarps) {
+  if (T <= nC) {
+    if (cta < T && warp < kMbWarps) {
+      int ei = 0;
+      float ew = 0.0f;
+      mb_route_one(prm.logits + static_cast<size_t>(cta) * E, E, k, scr, warp, lane, ei, ew);
+      if (warp == 0 && lane < k) {
+        prm.ridx[cta * k + lane] = ei;
+        prm.rw[cta * k + lane] = ew;
+        if (prm.idx_out) {
+          prm.idx_out[cta * k + lane] = ei;
+          prm.w_out[cta * k + lane] = ew;
+        }
+      }
+    }
+  } else if (warp < kMbWarps) {
     for (int t = cta + nC * warp; t < T; t += nC * kMbWarps) {
       const float* row = prm.logits + static_cast<size_t>(t) * E;
       int ei;
@@ -606,7 +748,7 @@ __global__ void __launch_bounds__(kMbThreads, 1) moe_block_kernel(const __grid_c
     asm volatile("prefetch.tensormap [%0];" :: "l"(reinterpret_cast<uint64_t>(&maps.scales[g1 >> 1])) : "memory");
     mb_load_half(prm.proj[g1 >> 1].halves, g1 & 1, prm.K, smem + L.cb, cbar);
   }
-  mb_route_tokens(prm, warp, lane);
+  mb_route_tokens(prm, reinterpret_cast<float*>(smem + L.codes[1]), warp, lane);
   if (!mb_grid_barrier(true, st) && tid == 0) *abort_flag = 1;
   __syncthreads();
   if (warp < kMbWarps && !*abort_flag) {
