@@ -7,8 +7,9 @@
  *
  * Every pointer is a DEVICE pointer owned by the caller.  The compute entry
  * points (vqb_unpack, vqb_codebook_halves, vqb_switch_forward[_static],
- * vqb_dense_forward, the MoE elementwise calls and vqb_ep_dispatch / combine /
- * reduce) are asynchronous on the given stream and allocate nothing; calls
+ * vqb_dense_forward, the MoE elementwise calls, vqb_moe_block_forward and
+ * vqb_ep_dispatch / combine / reduce) are asynchronous on the given stream and
+ * allocate nothing; calls
  * that need scratch memory take a caller-supplied workspace whose size the
  * matching *_workspace_size function returns.  Only the expert-parallel set-up
  * calls (vqb_ep_region_alloc / _free, vqb_ep_ipc_open / _close) allocate,
@@ -258,11 +259,23 @@ typedef struct vqb_moe_block_desc {
   int32_t top_k;
 } vqb_moe_block_desc;
 
+/* Optional knobs of vqb_moe_block_forward (NULL = defaults).  wait_limit_us:
+ * the kernel's bounded waits for its own copies give up after this long
+ * (0 = 2 s; its grid barriers always wait up to 2 s); stall_cta: tests of the
+ * failure path only -- that CTA waits for a signal nothing sends, gives up
+ * after wait_limit_us and the call reports VQB_TIMEOUT (-1 = none; 0 is a real
+ * CTA, so a zero-filled struct must set it to -1). */
+typedef struct vqb_moe_block_options {
+  int32_t wait_limit_us;
+  int32_t stall_cta;
+} vqb_moe_block_options;
+
 vqb_status vqb_moe_block_supported(const vqb_moe_block_desc* desc, int32_t n_tokens, vqb_dtype x_dtype);
 size_t vqb_moe_block_workspace_size(const vqb_moe_block_desc* desc, int32_t n_tokens);
 vqb_status vqb_moe_block_forward(const vqb_moe_block_desc* desc, const float* router_logits, const void* x,
                                  vqb_dtype x_dtype, int32_t n_tokens, void* y, int32_t* indices, float* weights,
-                                 void* workspace, size_t workspace_bytes, vqb_stream_t stream);
+                                 void* workspace, size_t workspace_bytes, const vqb_moe_block_options* opts,
+                                 vqb_stream_t stream);
 
 /* ---- Expert-parallel exchange over peer memory (fixed-shape decode path) ----
  *

@@ -177,3 +177,25 @@ def test_unserved_shapes_take_the_per_step_path():
         blk(x, lg)
     _, blk2, _ = _block(18, 16, 512, 512, 3000, 4)
     assert blk2.fused_status(4) == _lib.VQB_UNSUPPORTED_GEOMETRY
+
+
+def test_fused_block_bounded_wait_reports_timeout():
+    """The failure path without a fault: one CTA waits for a signal nothing
+    sends (vqb_moe_block_options.stall_cta) and gives up after 20 ms; the call
+    ends, the status block reads VQB_TIMEOUT, and the next call on the same
+    device is correct again (every CTA still arrived at every grid barrier)."""
+    _, blk, rng = _block(23, 16, 512, 512, 4096, 4)
+    T = 9
+    x = torch.from_numpy(rng.standard_normal((T, 512)).astype(np.float32)).cuda().to(torch.bfloat16)
+    lg = torch.from_numpy(rng.standard_normal((T, 16)).astype(np.float32)).cuda()
+    good, _, _ = blk.forward_fused(x, lg)
+    nb = int(_lib.lib().vqb_moe_block_workspace_size(ctypes.byref(blk.block_desc()), T))
+    ws = torch.zeros(nb, dtype=torch.uint8, device="cuda")
+    opts = _lib.MoeBlockOptions(wait_limit_us=20000, stall_cta=5)
+    blk.forward_fused(x, lg, workspace=ws, options=opts)
+    torch.cuda.synchronize()
+    assert int(ws[:16].view(torch.int32)[1]) == _lib.VQB_TIMEOUT
+    again, _, _ = blk.forward_fused(x, lg, workspace=ws)
+    torch.cuda.synchronize()
+    assert int(ws[:16].view(torch.int32)[1]) == 0
+    assert torch.equal(again.view(torch.int16), good.view(torch.int16))

@@ -58,6 +58,10 @@ class MoeBlockDesc(ctypes.Structure):
     _fields_ = [("gate", LinearDesc), ("up", LinearDesc), ("down", LinearDesc), ("top_k", ctypes.c_int32)]
 
 
+class MoeBlockOptions(ctypes.Structure):
+    _fields_ = [("wait_limit_us", ctypes.c_int32), ("stall_cta", ctypes.c_int32)]
+
+
 class Options(ctypes.Structure):
     _fields_ = [
         ("path", ctypes.c_int32),
@@ -130,7 +134,7 @@ def _bind(L):
     L.vqb_moe_block_workspace_size.restype = sz
     L.vqb_moe_block_workspace_size.argtypes = [P, i32]
     L.vqb_moe_block_forward.restype = i32
-    L.vqb_moe_block_forward.argtypes = [P, P, P, i32, i32, P, P, P, P, sz, P]
+    L.vqb_moe_block_forward.argtypes = [P, P, P, i32, i32, P, P, P, P, sz, P, P]
     L.vqb_ep_region_bytes.restype = sz
     L.vqb_ep_region_bytes.argtypes = [P, P]
     L.vqb_ep_region_alloc.restype = i32

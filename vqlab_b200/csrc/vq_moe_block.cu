@@ -90,6 +90,8 @@ struct MbParams {
   int32_t* ridx;           // [T * k] routing: expert of each pair
   float* rw;               // [T * k] routing: weight of each pair
   int* status;             // workspace status block: [1] = VQB_TIMEOUT when a wait expired
+  uint64_t wait_ns;        // limit of the bounded mbarrier waits
+  int stall_cta;           // tests: this CTA waits for a signal nothing sends (-1: none)
 };
 
 struct MbMaps {
@@ -350,7 +352,7 @@ __device__ void mb_produce(const CUtensorMap* cmap, const CUtensorMap* smap, con
     const int row0 = e * ph.OUT + it.rt * kMbRows;
     for (int w = it.w0; w < it.w1; ++w) {
       const int st = static_cast<int>(gw & 1u);
-      if (!mbar_wait(&empty[st], ((gw >> 1) & 1u) ^ 1u, abort_flag)) return;
+      if (!mbar_wait(&empty[st], ((gw >> 1) & 1u) ^ 1u, abort_flag, prm.wait_ns)) return;
       mbar_expect_tx(&full[st], kMbRows * W * 4 + kMbRows * kMbScaleRow + n * kMbWinK * 2);
       tma_load_2d(cmap, &full[st], smem + L.codes[st], w * W, row0);
       tma_load_2d(smap, &full[st], smem + L.scales[st], w * (kMbWinK / 64), row0);
@@ -385,7 +387,7 @@ __device__ bool mb_consume(const MbParams& prm, const MbPhase& ph, const uint2* 
     float acc[2][4] = {{0.0f, 0.0f, 0.0f, 0.0f}, {0.0f, 0.0f, 0.0f, 0.0f}};
     for (int w = it.w0; w < it.w1; ++w) {
       const int st = static_cast<int>(gw & 1u);
-      if (!warp_wait(&full[st], (gw >> 1) & 1u, abort_flag)) return false;
+      if (!warp_wait(&full[st], (gw >> 1) & 1u, abort_flag, prm.wait_ns)) return false;
       mb_window<BITS>(reinterpret_cast<const uint32_t*>(smem + L.codes[st]),
                            reinterpret_cast<const uint16_t*>(smem + L.scales[st]), smem + L.xrows[st], cb, warp, g,
                            t, n, ph.half, acc);
@@ -734,6 +736,7 @@ __global__ void __launch_bounds__(kMbThreads, 1) moe_block_kernel(const __grid_c
       mbar_init(&empty[i], kMbWarps);
     }
     mbar_init(cbar, 1);
+    mbar_init(cbar + 1, 1);  // the test stall's signal: nothing arrives on it
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     for (int i = 0; i < 64; ++i) st[i] = 0;
     if (cta == 0)
@@ -769,11 +772,12 @@ __global__ void __launch_bounds__(kMbThreads, 1) moe_block_kernel(const __grid_c
   bool cb3_issued = false;
 
   // ---------------- phase 1: gate and up partials
+  if (cta == prm.stall_cta && warp < kMbWarps) warp_wait(cbar + 1, 0, abort_flag, prm.wait_ns);  // tests only
   if (copier) {
     mb_produce<BITS>(&maps.codes[ph1.proj], &maps.scales[ph1.proj], prm, ph1, chunks, sorted, smem, L, full, empty,
                      gw, abort_flag);
   } else if (warp < kMbWarps && ph1.j < ph1.nseg * ph1.S) {
-    if (warp_wait(cbar, 0, abort_flag))
+    if (warp_wait(cbar, 0, abort_flag, prm.wait_ns))
       mb_consume<BITS>(prm, ph1, chunks, sorted, smem, L, full, empty, gw, abort_flag, warp, lane);
   }
   __syncthreads();  // every consumer is done with the phase-1 codebook half
@@ -834,7 +838,7 @@ __global__ void __launch_bounds__(kMbThreads, 1) moe_block_kernel(const __grid_c
       mb_produce<BITS>(&maps.codes[2], &maps.scales[2], prm, ph3, chunks, sorted, smem, L, full, empty, gw,
                        abort_flag);
     } else if (warp < kMbWarps && ph3.j < ph3.nseg * ph3.S) {
-      if (warp_wait(cbar, 1, abort_flag))
+      if (warp_wait(cbar, 1, abort_flag, prm.wait_ns))
         mb_consume<BITS>(prm, ph3, chunks, sorted, smem, L, full, empty, gw, abort_flag, warp, lane);
     }
   }
@@ -987,7 +991,8 @@ extern "C" size_t vqb_moe_block_workspace_size(const vqb_moe_block_desc* desc, i
 extern "C" vqb_status vqb_moe_block_forward(const vqb_moe_block_desc* desc, const float* router_logits,
                                             const void* x, vqb_dtype x_dtype, int32_t n_tokens, void* y,
                                             int32_t* indices, float* weights, void* workspace,
-                                            size_t workspace_bytes, vqb_stream_t stream) {
+                                            size_t workspace_bytes, const vqb_moe_block_options* opts,
+                                            vqb_stream_t stream) {
   MbGeo g;
   vqb_status st = mb_check(desc, n_tokens, x_dtype, &g);
   if (st != VQB_OK) return st;
@@ -1026,6 +1031,9 @@ extern "C" vqb_status vqb_moe_block_forward(const vqb_moe_block_desc* desc, cons
   prm.I = g.I;
   prm.K = g.K;
   prm.x_bf16 = x_dtype == VQB_BF16 ? 1 : 0;
+  if (opts && opts->wait_limit_us < 0) return VQB_BAD_SHAPE;
+  prm.wait_ns = opts && opts->wait_limit_us > 0 ? static_cast<uint64_t>(opts->wait_limit_us) * 1000ull : kWaitLimitNs;
+  prm.stall_cta = opts ? opts->stall_cta : -1;
   for (int i = 0; i < 3; ++i) {
     prm.proj[i].halves = static_cast<const uint16_t*>(g.p[i].codebook_halves);
     prm.proj[i].OUT = g.p[i].OUT;

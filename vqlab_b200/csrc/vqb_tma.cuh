@@ -38,22 +38,24 @@ __device__ __forceinline__ uint64_t global_ns() {
   return t;
 }
 // bounded wait: false when the time limit expired or another role aborted
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag) {
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
+                                          uint64_t limit_ns = kWaitLimitNs) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = global_ns();
   for (uint32_t i = 1;; ++i) {
     if (mbar_try_wait(bar, parity)) return true;
     if ((i & 63u) == 0u) {
       if (*abort_flag) return false;
-      if (global_ns() - t0 > kWaitLimitNs) break;
+      if (global_ns() - t0 > limit_ns) break;
     }
   }
   *abort_flag = 1;
   return false;
 }
 // the same for a whole warp: every lane waits, the warp agrees on the outcome
-__device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag) {
-  return __all_sync(0xffffffffu, mbar_wait(bar, parity, abort_flag)) != 0;
+__device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
+                                          uint64_t limit_ns = kWaitLimitNs) {
+  return __all_sync(0xffffffffu, mbar_wait(bar, parity, abort_flag, limit_ns)) != 0;
 }
 // bounded drain used at teardown (no abort check: a copy in flight must land)
 __device__ __forceinline__ void mbar_drain(uint64_t* bar, uint32_t parity) {

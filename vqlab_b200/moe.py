@@ -153,12 +153,14 @@ class VQMoEBlock(torch.nn.Module):
         idx, w = route(router_logits, self.top_k)
         return self.project(x, idx, w)
 
-    def forward_fused(self, x: torch.Tensor, router_logits: torch.Tensor, workspace: torch.Tensor | None = None):
+    def forward_fused(self, x: torch.Tensor, router_logits: torch.Tensor, workspace: torch.Tensor | None = None,
+                      options: _lib.MoeBlockOptions | None = None):
         """The block in one launch: returns (y [T, H], indices int32 [T, k],
         weights fp32 [T, k]) -- the routing is vqb_moe_route's, bit for bit.
         workspace: optional uint8 CUDA tensor of at least
         vqb_moe_block_workspace_size bytes (its first 16 bytes are the call's
-        status block); allocated per call when None."""
+        status block); allocated per call when None.  options: vqb_moe_block_options
+        (bounded-wait limit; the failure-path test knob)."""
         T, H = x.shape
         x = x.contiguous()
         lg = router_logits.to(torch.float32).contiguous()
@@ -180,6 +182,7 @@ class VQMoEBlock(torch.nn.Module):
                                            ctypes.c_void_p(x.data_ptr()), _DTYPES[x.dtype], T,
                                            ctypes.c_void_p(y.data_ptr()), ctypes.c_void_p(idx.data_ptr()),
                                            ctypes.c_void_p(w.data_ptr()), ctypes.c_void_p(ws.data_ptr()), nbytes,
+                                           ctypes.byref(options) if options is not None else None,
                                            _stream_ptr(x.device)), "vqb_moe_block_forward")
         return y, idx, w
 
