@@ -301,7 +301,7 @@ def profiled_traffic(kernel, workload):
 DH, DI, DKV = 5120, 17408, 1024   # benchmark configuration C4: hidden, MLP intermediate, kv width
 
 
-def make_dense_layer(torch, dev, seed):
+def make_dense_layer(torch, dev, seed, no_fused=False):
     """One C4 benchmark layer as VQLinear projections: attention q/k/v/o
     with d2/K256 (8-bit codes), MLP gate/up/down with d8/K16384 (14-bit)."""
     from vqlab_b200 import VQLinear
@@ -315,8 +315,10 @@ def make_dense_layer(torch, dev, seed):
         sc = (torch.rand((out, inn // G), device=dev, generator=g) + 0.5).to(torch.float16)
         return VQLinear(codes, cb, sc, group_size=G, pack_bits=bits, in_features=inn)
 
+    from vqlab_b200.mlp import VQDenseMLP
     attn = [lin(DH, DH, 2, 256, 8), lin(DKV, DH, 2, 256, 8), lin(DKV, DH, 2, 256, 8), lin(DH, DH, 2, 256, 8)]
-    mlp = [lin(DI, DH, 8, K, BITS), lin(DI, DH, 8, K, BITS), lin(DH, DI, 8, K, BITS)]
+    mlp = VQDenseMLP(lin(DI, DH, 8, K, BITS), lin(DI, DH, 8, K, BITS), lin(DH, DI, 8, K, BITS),
+                     fused="off" if no_fused else "auto")
     return attn, mlp
 
 
@@ -331,14 +333,14 @@ DENSE_LAYER_BYTES = (2 * _dense_proj_bytes(DH, DH, 2, 256, 8) + 2 * _dense_proj_
 
 def dense_step(layer, x):
     """The seven projections of one dense layer (the attention kernel itself is
-    outside the VQ runtime: o is applied to q as its stand-in input)."""
-    from vqlab_b200.moe import swiglu
-    (wq, wk, wv, wo), (wg, wu, wd) = layer
+    outside the VQ runtime: o is applied to q as its stand-in input); the MLP is
+    VQDenseMLP (one launch at decode batches, the per-step calls otherwise)."""
+    (wq, wk, wv, wo), mlp = layer
     q = wq(x)
     wk(x)
     wv(x)
     h = x + wo(q)
-    return h + wd(swiglu(wg(h), wu(h)))
+    return h + mlp(h)
 
 
 def dense_leg(torch, dev, args, peak_gbs, peak_kind):
@@ -347,7 +349,7 @@ def dense_leg(torch, dev, args, peak_gbs, peak_kind):
     each, 400 MB per cycle > 126 MB L2) and scaled to 64 layers; the attention
     (d2/K256, q 5120 x 5120) and MLP (d8/K16384, gate 17408 x 5120)
     projections' dominant kernels are timed alone for their rooflines."""
-    layers = [make_dense_layer(torch, dev, 7000 + l) for l in range(4)]
+    layers = [make_dense_layer(torch, dev, 7000 + l, args.no_fused) for l in range(4)]
     gen = torch.Generator(device=dev)
     gen.manual_seed(23)
     out = {}
@@ -371,12 +373,21 @@ def dense_leg(torch, dev, args, peak_gbs, peak_kind):
         # dominant kernel of one attention and one MLP projection, timed alone
         s = torch.cuda.current_stream()
         roofs = {}
-        for name, pick, geom in (("attn_q", lambda L: L[0][0], (DH, DH, 2, 256, 8)),
-                                 ("mlp_gate", lambda L: L[1][0], (DI, DH, 8, K, BITS))):
+        mlp_fused = layers[0][1].fused != "off" and B <= 8 and layers[0][1].fused_status(B) == 0
+        legs = [("attn_q", lambda L: L[0][0], (DH, DH, 2, 256, 8))]
+        if mlp_fused:
+            legs.append(("mlp", lambda L: L[1], None))
+        else:
+            legs.append(("mlp_gate", lambda L: L[1].gate_proj, (DI, DH, 8, K, BITS)))
+        for name, pick, geom in legs:
             dur = kernel_seconds(torch, s, lambda i: pick(layers[i % len(layers)])(xs[i % len(layers)]), 8)
-            byt = dense_bytes(*geom, n=B)
+            if geom is None:  # the fused MLP: gate, up and down in one launch
+                byt = (dense_bytes(DI, DH, 8, K, BITS, n=B) * 2 + dense_bytes(DH, DI, 8, K, BITS, n=B))
+            else:
+                byt = dense_bytes(*geom, n=B)
             ach = byt / dur / 1e9
-            kname = "vq_decode_mma_kernel" if (name == "attn_q" and B <= 8) else "vq_prefill_tc_kernel"
+            kname = ("vq_decode_mma_kernel" if (name == "attn_q" and B <= 8)
+                     else "moe_block_kernel" if name == "mlp" else "vq_prefill_tc_kernel")
             roofs[name] = {"bound": "hbm", "achieved": round(ach, 1), "peak": peak_gbs, "unit": "GB/s",
                            "frac": round(ach / peak_gbs, 4),
                            "traffic": profiled_traffic(kname, f"c4_{name}_n{B}"),
@@ -610,7 +621,6 @@ def gpu_arm(args, rank, world, dev):
     gen = torch.Generator(device=dev)
     gen.manual_seed(7 + rank)
     results = {}
-    launches_per_step = None
     for B in batches:
         if world > 1:
             for L in layers:

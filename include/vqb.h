@@ -270,6 +270,33 @@ typedef struct vqb_moe_block_options {
   int32_t stall_cta;
 } vqb_moe_block_options;
 
+/* ---- A dense VQ MLP in one launch (decode batches) ----
+ *
+ * y = down(swiglu(gate(x), up(x))) for three VQLinear projections (gate / up
+ * [I, H], down [H, I], num_experts = 1): the caller-side composition of
+ * VQLinear.__call__ (vq_dense.py:346-441) in a dense model's MLP, with the
+ * numerics of the per-step calls on the d8 path (_decode_matmul,
+ * vq_dense.py:267-312): weights bf16(fp16(cb * s)) for bf16 x (fp16 for fp16
+ * x), x kept in its dtype, fp32 accumulation, each projection's output
+ * rounded once to x's dtype, h = dtype(silu(g) * u) (vqb_swiglu).  The same
+ * persistent kernel as vqb_moe_block_forward with one expert and no router;
+ * served shapes as there (d8, K = 2^BITS at 12 / 14 bits, G = 64, H and I
+ * multiples of 512, codebook_halves set, n_tokens <= 640), else
+ * VQB_UNSUPPORTED_GEOMETRY.  It decodes every weight once per 8 tokens, so it
+ * pays at small n_tokens; the Python module takes it up to 8.  The same
+ * status block and calls-must-not-overlap rule as the MoE block. */
+typedef struct vqb_dense_mlp_desc {
+  vqb_linear_desc gate;
+  vqb_linear_desc up;
+  vqb_linear_desc down;
+} vqb_dense_mlp_desc;
+
+vqb_status vqb_dense_mlp_supported(const vqb_dense_mlp_desc* desc, int32_t n_tokens, vqb_dtype x_dtype);
+size_t vqb_dense_mlp_workspace_size(const vqb_dense_mlp_desc* desc, int32_t n_tokens);
+vqb_status vqb_dense_mlp_forward(const vqb_dense_mlp_desc* desc, const void* x, vqb_dtype x_dtype, int32_t n_tokens,
+                                 void* y, void* workspace, size_t workspace_bytes, const vqb_moe_block_options* opts,
+                                 vqb_stream_t stream);
+
 vqb_status vqb_moe_block_supported(const vqb_moe_block_desc* desc, int32_t n_tokens, vqb_dtype x_dtype);
 size_t vqb_moe_block_workspace_size(const vqb_moe_block_desc* desc, int32_t n_tokens);
 vqb_status vqb_moe_block_forward(const vqb_moe_block_desc* desc, const float* router_logits, const void* x,

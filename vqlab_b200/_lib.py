@@ -58,6 +58,10 @@ class MoeBlockDesc(ctypes.Structure):
     _fields_ = [("gate", LinearDesc), ("up", LinearDesc), ("down", LinearDesc), ("top_k", ctypes.c_int32)]
 
 
+class DenseMlpDesc(ctypes.Structure):
+    _fields_ = [("gate", LinearDesc), ("up", LinearDesc), ("down", LinearDesc)]
+
+
 class MoeBlockOptions(ctypes.Structure):
     _fields_ = [("wait_limit_us", ctypes.c_int32), ("stall_cta", ctypes.c_int32)]
 
@@ -135,6 +139,12 @@ def _bind(L):
     L.vqb_moe_block_workspace_size.argtypes = [P, i32]
     L.vqb_moe_block_forward.restype = i32
     L.vqb_moe_block_forward.argtypes = [P, P, P, i32, i32, P, P, P, P, sz, P, P]
+    L.vqb_dense_mlp_supported.restype = i32
+    L.vqb_dense_mlp_supported.argtypes = [P, i32, i32]
+    L.vqb_dense_mlp_workspace_size.restype = sz
+    L.vqb_dense_mlp_workspace_size.argtypes = [P, i32]
+    L.vqb_dense_mlp_forward.restype = i32
+    L.vqb_dense_mlp_forward.argtypes = [P, P, i32, i32, P, P, sz, P, P]
     L.vqb_ep_region_bytes.restype = sz
     L.vqb_ep_region_bytes.argtypes = [P, P]
     L.vqb_ep_region_alloc.restype = i32
@@ -199,7 +209,8 @@ def exported_symbols():
             "vqb_switch_forward", "vqb_dense_workspace_size", "vqb_dense_forward", "vqb_switch_forward_static",
             "vqb_launch_count", "vqb_time_next_kernel", "vqb_swiglu", "vqb_moe_combine", "vqb_switch_path",
             "vqb_moe_combine_partial", "vqb_moe_route", "vqb_codebook_halves", "vqb_moe_block_supported",
-            "vqb_moe_block_workspace_size", "vqb_moe_block_forward", "vqb_ep_region_bytes", "vqb_ep_region_alloc", "vqb_ep_region_free",
+            "vqb_moe_block_workspace_size", "vqb_moe_block_forward", "vqb_dense_mlp_supported",
+            "vqb_dense_mlp_workspace_size", "vqb_dense_mlp_forward", "vqb_ep_region_bytes", "vqb_ep_region_alloc", "vqb_ep_region_free",
             "vqb_ep_ipc_handle", "vqb_ep_ipc_open", "vqb_ep_ipc_close", "vqb_ep_dispatch", "vqb_ep_combine",
             "vqb_ep_reduce"]
 

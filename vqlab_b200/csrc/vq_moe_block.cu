@@ -90,6 +90,7 @@ struct MbParams {
   int32_t* ridx;           // [T * k] routing: expert of each pair
   float* rw;               // [T * k] routing: weight of each pair
   int* status;             // workspace status block: [1] = VQB_TIMEOUT when a wait expired
+  int dense;               // a dense MLP (E = 1, no router): x kept in its dtype, outputs rounded once
   uint64_t wait_ns;        // limit of the bounded mbarrier waits
   int stall_cta;           // tests: this CTA waits for a signal nothing sends (-1: none)
 };
@@ -227,8 +228,26 @@ __device__ __forceinline__ void mma_16816(float (&d)[4], uint32_t a0, uint32_t a
       : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 
-// the output rounding of a projection: fp16, then x's dtype
-__device__ __forceinline__ float round_out(float v, int x_bf16) {
+__device__ __forceinline__ void mma_16816_bf16(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                               uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};\n"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+// two fp16 -> two bf16, round to nearest even (the dense weights' cast to x's dtype)
+__device__ __forceinline__ uint32_t f16x2_to_bf16x2(uint32_t v) {
+  const float2 f = __half22float2(*reinterpret_cast<__half2*>(&v));
+  __nv_bfloat162 b = __floats2bfloat162_rn(f.x, f.y);
+  return *reinterpret_cast<uint32_t*>(&b);
+}
+
+// the output rounding of a projection: fp16, then x's dtype (the MoE
+// projections, vq_switch.py:5423); a dense layer rounds its fp32 accumulator
+// to x's dtype once (vq_dense.py:294-312)
+__device__ __forceinline__ float round_out(float v, int x_bf16, int dense = 0) {
+  if (dense && x_bf16) return __bfloat162float(__float2bfloat16_rn(v));
   const __half h = __float2half_rn(v);
   return x_bf16 ? __bfloat162float(__float2bfloat16_rn(__half2float(h))) : __half2float(h);
 }
@@ -240,7 +259,7 @@ __device__ __forceinline__ float mb_silu(float v) { return v / (1.0f + expf(-v))
 // CTA's dimension half h.  Thread t takes codes 4t .. 4t+3 of each group of
 // 16; for code c the MMA's k slots (2t, 2t+1, 2t+8, 2t+9) hold dims 4h .. 4h+3
 // of W (A) and of x (B).
-template <int BITS>
+template <int BITS, bool WBF16>
 __device__ __forceinline__ void mb_window(const uint32_t* __restrict__ cw, const uint16_t* __restrict__ sc,
                                           const unsigned char* __restrict__ xr, const uint16_t* __restrict__ cb,
                                           int warp, int g, int t, int n, int h, float (&acc)[2][4]) {
@@ -307,9 +326,16 @@ __device__ __forceinline__ void mb_window(const uint32_t* __restrict__ cw, const
         e[r] = *reinterpret_cast<const uint2*>(cb + c * 4);
       }
 #pragma unroll
-      for (int j = 0; j < 2; ++j)
-        mma_16816(acc[j], hmul2_bits(e[2 * j].x, s2[2 * j]), hmul2_bits(e[2 * j + 1].x, s2[2 * j + 1]),
-                  hmul2_bits(e[2 * j].y, s2[2 * j]), hmul2_bits(e[2 * j + 1].y, s2[2 * j + 1]), x0, x1);
+      for (int j = 0; j < 2; ++j) {
+        uint32_t w0 = hmul2_bits(e[2 * j].x, s2[2 * j]), w1 = hmul2_bits(e[2 * j + 1].x, s2[2 * j + 1]);
+        uint32_t w2 = hmul2_bits(e[2 * j].y, s2[2 * j]), w3 = hmul2_bits(e[2 * j + 1].y, s2[2 * j + 1]);
+        if constexpr (WBF16) {
+          mma_16816_bf16(acc[j], f16x2_to_bf16x2(w0), f16x2_to_bf16x2(w1), f16x2_to_bf16x2(w2),
+                         f16x2_to_bf16x2(w3), x0, x1);
+        } else {
+          mma_16816(acc[j], w0, w1, w2, w3, x0, x1);
+        }
+      }
     }
   }
 }
@@ -372,7 +398,7 @@ __device__ void mb_produce(const CUtensorMap* cmap, const CUtensorMap* smap, con
 
 // consumer warps: decode every window of the phase's items, then store the
 // item's fp32 partial for its (pair, row) cells into the item's slot
-template <int BITS>
+template <int BITS, bool WBF16>
 __device__ bool mb_consume(const MbParams& prm, const MbPhase& ph, const uint2* chunks, const uint16_t* sorted,
                            const unsigned char* smem, const MbLayout& L, uint64_t* full, uint64_t* empty,
                            uint32_t& gw, volatile int* abort_flag, int warp, int lane) {
@@ -388,7 +414,7 @@ __device__ bool mb_consume(const MbParams& prm, const MbPhase& ph, const uint2* 
     for (int w = it.w0; w < it.w1; ++w) {
       const int st = static_cast<int>(gw & 1u);
       if (!warp_wait(&full[st], (gw >> 1) & 1u, abort_flag, prm.wait_ns)) return false;
-      mb_window<BITS>(reinterpret_cast<const uint32_t*>(smem + L.codes[st]),
+      mb_window<BITS, WBF16>(reinterpret_cast<const uint32_t*>(smem + L.codes[st]),
                            reinterpret_cast<const uint16_t*>(smem + L.scales[st]), smem + L.xrows[st], cb, warp, g,
                            t, n, ph.half, acc);
       __syncwarp();
@@ -558,7 +584,13 @@ __device__ void mb_route_one(const float* __restrict__ row, int E, int k, float*
 __device__ void mb_route_tokens(const MbParams& prm, float* scr, int warp, int lane) {
   const int T = prm.T, E = prm.E, k = prm.k;
   const int nC = static_cast<int>(gridDim.x), cta = static_cast<int>(blockIdx.x);
-  if (T <= nC) {
+  if (prm.dense) {
+    // one expert, every token to it with weight 1
+    for (int t = cta * blockDim.x + threadIdx.x; t < T; t += nC * blockDim.x) {
+      prm.ridx[t] = 0;
+      prm.rw[t] = 1.0f;
+    }
+  } else if (T <= nC) {
     if (cta < T && warp < kMbWarps) {
       int ei = 0;
       float ew = 0.0f;
@@ -597,7 +629,7 @@ __device__ void mb_route_tokens(const MbParams& prm, float* scr, int warp, int l
   const int64_t v0 = static_cast<int64_t>(cta) * per, v1 = v0 + per < nv ? v0 + per : nv;
   for (int64_t v = v0 + threadIdx.x; v < v1; v += blockDim.x) {
     uint4 u = reinterpret_cast<const uint4*>(prm.x)[v];
-    if (prm.x_bf16) {
+    if (prm.x_bf16 && !prm.dense) {
       u.x = bf16x2_to_f16x2(u.x);
       u.y = bf16x2_to_f16x2(u.y);
       u.z = bf16x2_to_f16x2(u.z);
@@ -712,7 +744,7 @@ __device__ void mb_route(const MbParams& prm, unsigned char* scratch, float* wsm
   }
 }
 
-template <int BITS>
+template <int BITS, bool WBF16>
 __global__ void __launch_bounds__(kMbThreads, 1) moe_block_kernel(const __grid_constant__ MbMaps maps,
                                                                    const __grid_constant__ MbParams prm) {
   extern __shared__ __align__(1024) unsigned char smem[];
@@ -778,7 +810,7 @@ __global__ void __launch_bounds__(kMbThreads, 1) moe_block_kernel(const __grid_c
                      gw, abort_flag);
   } else if (warp < kMbWarps && ph1.j < ph1.nseg * ph1.S) {
     if (warp_wait(cbar, 0, abort_flag, prm.wait_ns))
-      mb_consume<BITS>(prm, ph1, chunks, sorted, smem, L, full, empty, gw, abort_flag, warp, lane);
+      mb_consume<BITS, WBF16>(prm, ph1, chunks, sorted, smem, L, full, empty, gw, abort_flag, warp, lane);
   }
   __syncthreads();  // every consumer is done with the phase-1 codebook half
   if (copier) {
@@ -822,9 +854,13 @@ __global__ void __launch_bounds__(kMbThreads, 1) moe_block_kernel(const __grid_c
           us += v[3][s];
         }
       }
-      const float hv = __fmul_rn(mb_silu(round_out(gs, prm.x_bf16)), round_out(us, prm.x_bf16));
-      const float hd = prm.x_bf16 ? __bfloat162float(__float2bfloat16_rn(hv)) : __half2float(__float2half_rn(hv));
-      prm.h16[e] = __half_as_ushort(__float2half_rn(hd));
+      const float hv = __fmul_rn(mb_silu(round_out(gs, prm.x_bf16, prm.dense)), round_out(us, prm.x_bf16, prm.dense));
+      if (prm.dense && prm.x_bf16) {
+        prm.h16[e] = __bfloat16_as_ushort(__float2bfloat16_rn(hv));  // the down layer's bf16 input
+      } else {
+        const float hd = prm.x_bf16 ? __bfloat162float(__float2bfloat16_rn(hv)) : __half2float(__float2half_rn(hv));
+        prm.h16[e] = __half_as_ushort(__float2half_rn(hd));
+      }
     }
     asm volatile("fence.proxy.async.global;" ::: "memory");  // h16 is read by bulk copies after the barrier
   }
@@ -839,7 +875,7 @@ __global__ void __launch_bounds__(kMbThreads, 1) moe_block_kernel(const __grid_c
                        abort_flag);
     } else if (warp < kMbWarps && ph3.j < ph3.nseg * ph3.S) {
       if (warp_wait(cbar, 1, abort_flag, prm.wait_ns))
-        mb_consume<BITS>(prm, ph3, chunks, sorted, smem, L, full, empty, gw, abort_flag, warp, lane);
+        mb_consume<BITS, WBF16>(prm, ph3, chunks, sorted, smem, L, full, empty, gw, abort_flag, warp, lane);
     }
   }
   ok = mb_grid_barrier(ok && *abort_flag == 0, st);
@@ -881,7 +917,7 @@ __global__ void __launch_bounds__(kMbThreads, 1) moe_block_kernel(const __grid_c
             ds += v[2 * s + 1];
           }
         }
-        prod[el * k + j] = __fmul_rn(round_out(ds, prm.x_bf16), wsm[t * k + j]);
+        prod[el * k + j] = __fmul_rn(round_out(ds, prm.x_bf16, prm.dense), wsm[t * k + j]);
       }
       __syncthreads();
       for (int el = tid; el < ne; el += kMbThreads) {
@@ -912,25 +948,10 @@ struct MbGeo {
   int E, H, I, K, bits, k;
 };
 
-// The block shapes the fused kernel serves (else VQB_UNSUPPORTED_GEOMETRY:
-// the caller runs the per-step kernels).
-vqb_status mb_check(const vqb_moe_block_desc* d, int T, int x_dtype, MbGeo* g) {
-  if (!d) return VQB_NULL_POINTER;
-  const vqb_linear_desc* ds[3] = {&d->gate, &d->up, &d->down};
-  for (int i = 0; i < 3; ++i) {
-    const vqb_status st = validate(ds[i], &g->p[i]);
-    if (st != VQB_OK) return st;
-  }
-  const LinearGeometry &ga = g->p[0], &gu = g->p[1], &gd = g->p[2];
-  if (ga.E != gu.E || ga.E != gd.E || ga.OUT != gu.OUT || ga.IN != gu.IN || gd.IN != ga.OUT || gd.OUT != ga.IN)
-    return VQB_BAD_SHAPE;
-  if (T < 1 || d->top_k < 1 || d->top_k > 32 || d->top_k > ga.E) return VQB_BAD_SHAPE;
-  g->E = ga.E;
-  g->H = ga.IN;
-  g->I = ga.OUT;
-  g->K = ga.K;
-  g->bits = ga.bits;
-  g->k = d->top_k;
+// The shape checks common to the MoE block and the dense MLP once the three
+// projections are validated and g's sizes are set (else
+// VQB_UNSUPPORTED_GEOMETRY: the caller runs the per-step kernels).
+vqb_status mb_check_common(const vqb_linear_desc* const ds[3], int T, int x_dtype, MbGeo* g) {
   if (x_dtype != VQB_BF16 && x_dtype != VQB_F16) return VQB_UNSUPPORTED_GEOMETRY;
   if (g->E > kMbMaxExperts || static_cast<int64_t>(T) * g->k > kMbMaxPairs) return VQB_UNSUPPORTED_GEOMETRY;
   if (g->H % kMbWinK != 0 || g->I % kMbWinK != 0) return VQB_UNSUPPORTED_GEOMETRY;
@@ -948,6 +969,42 @@ vqb_status mb_check(const vqb_moe_block_desc* d, int T, int x_dtype, MbGeo* g) {
   if (di.sms < 4 || mb_layout(g->K, 2 * g->bits).total > static_cast<uint32_t>(di.smem_optin))
     return VQB_UNSUPPORTED_GEOMETRY;
   return VQB_OK;
+}
+
+vqb_status mb_validate3(const vqb_linear_desc* const ds[3], MbGeo* g) {
+  for (int i = 0; i < 3; ++i) {
+    const vqb_status st = validate(ds[i], &g->p[i]);
+    if (st != VQB_OK) return st;
+  }
+  const LinearGeometry &ga = g->p[0], &gu = g->p[1], &gd = g->p[2];
+  if (ga.E != gu.E || ga.E != gd.E || ga.OUT != gu.OUT || ga.IN != gu.IN || gd.IN != ga.OUT || gd.OUT != ga.IN)
+    return VQB_BAD_SHAPE;
+  g->E = ga.E;
+  g->H = ga.IN;
+  g->I = ga.OUT;
+  g->K = ga.K;
+  g->bits = ga.bits;
+  return VQB_OK;
+}
+
+vqb_status mb_check(const vqb_moe_block_desc* d, int T, int x_dtype, MbGeo* g) {
+  if (!d) return VQB_NULL_POINTER;
+  const vqb_linear_desc* const ds[3] = {&d->gate, &d->up, &d->down};
+  vqb_status st = mb_validate3(ds, g);
+  if (st != VQB_OK) return st;
+  if (T < 1 || d->top_k < 1 || d->top_k > 32 || d->top_k > g->E) return VQB_BAD_SHAPE;
+  g->k = d->top_k;
+  return mb_check_common(ds, T, x_dtype, g);
+}
+
+vqb_status mb_check_dense(const vqb_dense_mlp_desc* d, int T, int x_dtype, MbGeo* g) {
+  if (!d) return VQB_NULL_POINTER;
+  const vqb_linear_desc* const ds[3] = {&d->gate, &d->up, &d->down};
+  vqb_status st = mb_validate3(ds, g);
+  if (st != VQB_OK) return st;
+  if (T < 1 || g->E != 1) return VQB_BAD_SHAPE;
+  g->k = 1;
+  return mb_check_common(ds, T, x_dtype, g);
 }
 
 struct MbWorkspace {
@@ -968,6 +1025,90 @@ MbWorkspace mb_workspace(int T, int k, int H, int I) {
   w.rw = w.ridx + up(static_cast<size_t>(P) * 4);
   w.total = w.rw + up(static_cast<size_t>(P) * 4);
   return w;
+}
+
+// One launch of the block kernel for a checked geometry (dense: no router,
+// every token to the one expert with weight 1, the dense layers' numerics).
+vqb_status mb_launch(const MbGeo& g, bool dense, const float* logits, const void* x, int x_dtype, int T, void* y,
+                     int32_t* indices, float* weights, void* workspace, size_t workspace_bytes,
+                     const vqb_moe_block_options* opts, vqb_stream_t stream) {
+  if (!x || !y || !workspace) return VQB_NULL_POINTER;
+  if ((reinterpret_cast<uintptr_t>(x) & 15) != 0 || (reinterpret_cast<uintptr_t>(workspace) & 255) != 0)
+    return VQB_BAD_ALIGNMENT;
+  if (opts && opts->wait_limit_us < 0) return VQB_BAD_SHAPE;
+  const MbWorkspace ws = mb_workspace(T, g.k, g.H, g.I);
+  if (workspace_bytes < ws.total) return VQB_WORKSPACE_TOO_SMALL;
+  DeviceInfo di;
+  if (device_info(&di) != VQB_OK) return VQB_CUDA_ERROR;
+  EncodeTiledFn enc = encode_fn();
+  if (!enc) return VQB_CUDA_ERROR;
+
+  const int W = 2 * g.bits;
+  MbMaps maps;
+  for (int i = 0; i < 3; ++i) {
+    const LinearGeometry& q = g.p[i];
+    const uint64_t rows = static_cast<uint64_t>(q.E) * q.OUT;
+    if (!encode_2d(enc, &maps.codes[i], CU_TENSOR_MAP_DATA_TYPE_UINT32, 4, q.codes, static_cast<uint64_t>(q.row_words),
+                   rows, static_cast<uint32_t>(W), kMbRows, CU_TENSOR_MAP_SWIZZLE_NONE) ||
+        !encode_2d(enc, &maps.scales[i], CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, q.scales,
+                   static_cast<uint64_t>(q.IN / 64), rows, kMbWinK / 64, kMbRows, CU_TENSOR_MAP_SWIZZLE_NONE))
+      return VQB_CUDA_ERROR;
+  }
+  MbParams prm{};
+  prm.logits = logits;
+  prm.x = x;
+  prm.y = y;
+  prm.idx_out = indices;
+  prm.w_out = weights;
+  prm.T = T;
+  prm.E = g.E;
+  prm.k = g.k;
+  prm.H = g.H;
+  prm.I = g.I;
+  prm.K = g.K;
+  prm.x_bf16 = x_dtype == VQB_BF16 ? 1 : 0;
+  prm.dense = dense ? 1 : 0;
+  prm.wait_ns = opts && opts->wait_limit_us > 0 ? static_cast<uint64_t>(opts->wait_limit_us) * 1000ull : kWaitLimitNs;
+  prm.stall_cta = opts ? opts->stall_cta : -1;
+  for (int i = 0; i < 3; ++i) {
+    prm.proj[i].halves = static_cast<const uint16_t*>(g.p[i].codebook_halves);
+    prm.proj[i].OUT = g.p[i].OUT;
+    prm.proj[i].IN = g.p[i].IN;
+  }
+  char* base = static_cast<char*>(workspace);
+  prm.status = reinterpret_cast<int*>(base + ws.status);
+  prm.part1 = reinterpret_cast<float*>(base + ws.part1);
+  prm.part3 = reinterpret_cast<float*>(base + ws.part3);
+  prm.h16 = reinterpret_cast<uint16_t*>(base + ws.h16);
+  prm.x16 = reinterpret_cast<uint16_t*>(base + ws.x16);
+  prm.ridx = reinterpret_cast<int32_t*>(base + ws.ridx);
+  prm.rw = reinterpret_cast<float*>(base + ws.rw);
+
+  const MbLayout L = mb_layout(g.K, W);
+  // bf16 operands for a dense layer with bf16 x (its weights take x's dtype, vq_dense.py:294)
+  const bool wbf16 = dense && x_dtype == VQB_BF16;
+  void (*kern)(MbMaps, MbParams) =
+      g.bits == 14 ? (wbf16 ? moe_block_kernel<14, true> : moe_block_kernel<14, false>)
+                   : (wbf16 ? moe_block_kernel<12, true> : moe_block_kernel<12, false>);
+  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(L.total)) !=
+      cudaSuccess)
+    return VQB_CUDA_ERROR;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeCooperative;
+  attr[0].val.cooperative = 1;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(di.sms));
+  cfg.blockDim = dim3(kMbThreads);
+  cfg.dynamicSmemBytes = L.total;
+  cfg.stream = reinterpret_cast<cudaStream_t>(stream);
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  timer_before(cfg.stream);
+  const cudaError_t ce = cudaLaunchKernelEx(&cfg, kern, maps, prm);
+  timer_after(cfg.stream);
+  if (ce != cudaSuccess) return VQB_CUDA_ERROR;
+  note_launch();
+  return VQB_OK;
 }
 
 }  // namespace
@@ -996,77 +1137,30 @@ extern "C" vqb_status vqb_moe_block_forward(const vqb_moe_block_desc* desc, cons
   MbGeo g;
   vqb_status st = mb_check(desc, n_tokens, x_dtype, &g);
   if (st != VQB_OK) return st;
-  if (!router_logits || !x || !y || !workspace) return VQB_NULL_POINTER;
+  if (!router_logits) return VQB_NULL_POINTER;
   if ((indices == nullptr) != (weights == nullptr)) return VQB_NULL_POINTER;
-  if ((reinterpret_cast<uintptr_t>(x) & 15) != 0 || (reinterpret_cast<uintptr_t>(workspace) & 255) != 0)
-    return VQB_BAD_ALIGNMENT;
-  const MbWorkspace ws = mb_workspace(n_tokens, g.k, g.H, g.I);
-  if (workspace_bytes < ws.total) return VQB_WORKSPACE_TOO_SMALL;
-  DeviceInfo di;
-  if (device_info(&di) != VQB_OK) return VQB_CUDA_ERROR;
-  EncodeTiledFn enc = encode_fn();
-  if (!enc) return VQB_CUDA_ERROR;
+  return mb_launch(g, false, router_logits, x, x_dtype, n_tokens, y, indices, weights, workspace, workspace_bytes,
+                   opts, stream);
+}
 
-  const int W = 2 * g.bits;
-  MbMaps maps;
-  for (int i = 0; i < 3; ++i) {
-    const LinearGeometry& q = g.p[i];
-    const uint64_t rows = static_cast<uint64_t>(q.E) * q.OUT;
-    if (!encode_2d(enc, &maps.codes[i], CU_TENSOR_MAP_DATA_TYPE_UINT32, 4, q.codes, static_cast<uint64_t>(q.row_words),
-                   rows, static_cast<uint32_t>(W), kMbRows, CU_TENSOR_MAP_SWIZZLE_NONE) ||
-        !encode_2d(enc, &maps.scales[i], CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, q.scales,
-                   static_cast<uint64_t>(q.IN / 64), rows, kMbWinK / 64, kMbRows, CU_TENSOR_MAP_SWIZZLE_NONE))
-      return VQB_CUDA_ERROR;
-  }
-  MbParams prm{};
-  prm.logits = router_logits;
-  prm.x = x;
-  prm.y = y;
-  prm.idx_out = indices;
-  prm.w_out = weights;
-  prm.T = n_tokens;
-  prm.E = g.E;
-  prm.k = g.k;
-  prm.H = g.H;
-  prm.I = g.I;
-  prm.K = g.K;
-  prm.x_bf16 = x_dtype == VQB_BF16 ? 1 : 0;
-  if (opts && opts->wait_limit_us < 0) return VQB_BAD_SHAPE;
-  prm.wait_ns = opts && opts->wait_limit_us > 0 ? static_cast<uint64_t>(opts->wait_limit_us) * 1000ull : kWaitLimitNs;
-  prm.stall_cta = opts ? opts->stall_cta : -1;
-  for (int i = 0; i < 3; ++i) {
-    prm.proj[i].halves = static_cast<const uint16_t*>(g.p[i].codebook_halves);
-    prm.proj[i].OUT = g.p[i].OUT;
-    prm.proj[i].IN = g.p[i].IN;
-  }
-  char* base = static_cast<char*>(workspace);
-  prm.status = reinterpret_cast<int*>(base + ws.status);
-  prm.part1 = reinterpret_cast<float*>(base + ws.part1);
-  prm.part3 = reinterpret_cast<float*>(base + ws.part3);
-  prm.h16 = reinterpret_cast<uint16_t*>(base + ws.h16);
-  prm.x16 = reinterpret_cast<uint16_t*>(base + ws.x16);
-  prm.ridx = reinterpret_cast<int32_t*>(base + ws.ridx);
-  prm.rw = reinterpret_cast<float*>(base + ws.rw);
+extern "C" vqb_status vqb_dense_mlp_supported(const vqb_dense_mlp_desc* desc, int32_t n_tokens, vqb_dtype x_dtype) {
+  MbGeo g;
+  return mb_check_dense(desc, n_tokens, x_dtype, &g);
+}
 
-  const MbLayout L = mb_layout(g.K, W);
-  void (*kern)(MbMaps, MbParams) = g.bits == 14 ? moe_block_kernel<14> : moe_block_kernel<12>;
-  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(L.total)) !=
-      cudaSuccess)
-    return VQB_CUDA_ERROR;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeCooperative;
-  attr[0].val.cooperative = 1;
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(static_cast<unsigned>(di.sms));
-  cfg.blockDim = dim3(kMbThreads);
-  cfg.dynamicSmemBytes = L.total;
-  cfg.stream = reinterpret_cast<cudaStream_t>(stream);
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  timer_before(cfg.stream);
-  const cudaError_t ce = cudaLaunchKernelEx(&cfg, kern, maps, prm);
-  timer_after(cfg.stream);
-  if (ce != cudaSuccess) return VQB_CUDA_ERROR;
-  note_launch();
-  return VQB_OK;
+extern "C" size_t vqb_dense_mlp_workspace_size(const vqb_dense_mlp_desc* desc, int32_t n_tokens) {
+  if (!desc || n_tokens < 1) return 0;
+  return mb_workspace(n_tokens, 1, desc->gate.in_features > 0 ? desc->gate.in_features : 0,
+                      desc->gate.out_features > 0 ? desc->gate.out_features : 0)
+      .total;
+}
+
+extern "C" vqb_status vqb_dense_mlp_forward(const vqb_dense_mlp_desc* desc, const void* x, vqb_dtype x_dtype,
+                                            int32_t n_tokens, void* y, void* workspace, size_t workspace_bytes,
+                                            const vqb_moe_block_options* opts, vqb_stream_t stream) {
+  MbGeo g;
+  vqb_status st = mb_check_dense(desc, n_tokens, x_dtype, &g);
+  if (st != VQB_OK) return st;
+  return mb_launch(g, true, nullptr, x, x_dtype, n_tokens, y, nullptr, nullptr, workspace, workspace_bytes, opts,
+                   stream);
 }
