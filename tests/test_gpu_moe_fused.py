@@ -96,10 +96,11 @@ def test_fused_block_matches_oracle(E, H, I, K, topk, T):
     _check(y.float().cpu().numpy(), ref, allow)
 
 
-@pytest.mark.parametrize("T", [1, 8])
+@pytest.mark.parametrize("T", [1, 8, 64])
 def test_fused_block_c2_shape(T):
     """BASELINE C2's layer: 512 experts, hidden 4096, intermediate 1024,
-    d8 / K16384 / 14-bit codes, top-10, at decode batches 1 and 8."""
+    d8 / K16384 / 14-bit codes, top-10, at decode batches 1, 8 and 64 (the
+    headline: 640 pairs, the most the fused launch serves)."""
     P, blk, rng = _block(100 + T, 512, 4096, 1024, 16384, 10)
     x = orc.round_bf16(rng.standard_normal((T, 4096)).astype(np.float32))
     lg = rng.standard_normal((T, 512)).astype(np.float32)
