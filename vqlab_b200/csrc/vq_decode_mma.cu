@@ -74,7 +74,17 @@ struct MParams {
   int y_dtype;
   int round_f16_first;
   int cb_half;              // SPLIT: codebook entries held by each CTA of the pair
+  int nbuf;                 // code-window buffers per warp: 2 = the next window's rows copied asynchronously
 };
+
+// asynchronous 16-byte global -> shared copy (L2 only), and its group fences
+__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;"
+               :: "r"(static_cast<uint32_t>(__cvta_generic_to_shared(dst))), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" :: "n"(N) : "memory"); }
 
 __device__ __forceinline__ void mma_f16(float* c, const uint32_t* a, uint32_t b0, uint32_t b1) {
   asm volatile(
@@ -284,9 +294,11 @@ __global__ void __launch_bounds__(kThreads, 1) vq_decode_mma_kernel(const MParam
   uint16_t* x_s = reinterpret_cast<uint16_t*>(smem_raw + off);
   off += (static_cast<size_t>(prm.pm) * prm.x_stride * 2 + 15) & ~size_t(15);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const size_t win_bytes = (static_cast<size_t>(16) * prm.cs_stride * 4 + 16 * prm.sc_stride * 2 + 15) & ~size_t(15);
-  uint32_t* c_s = reinterpret_cast<uint32_t*>(smem_raw + off + warp * win_bytes);
-  uint16_t* s_s = reinterpret_cast<uint16_t*>(reinterpret_cast<unsigned char*>(c_s) + 16 * prm.cs_stride * 4);
+  // per warp: nbuf code-window buffers, then the window's scales
+  const size_t cwin_words = static_cast<size_t>(16) * prm.cs_stride;
+  const size_t win_bytes = (prm.nbuf * cwin_words * 4 + 16 * prm.sc_stride * 2 + 15) & ~size_t(15);
+  uint32_t* c_base = reinterpret_cast<uint32_t*>(smem_raw + off + warp * win_bytes);
+  uint16_t* s_s = reinterpret_cast<uint16_t*>(reinterpret_cast<unsigned char*>(c_base) + prm.nbuf * cwin_words * 4);
   off += kWarps * win_bytes;
   float* red = reinterpret_cast<float*>(smem_raw + off);
 
@@ -388,29 +400,63 @@ __global__ void __launch_bounds__(kThreads, 1) vq_decode_mma_kernel(const MParam
     float part[NT][4];
 #pragma unroll
     for (int n = 0; n < NT; ++n) part[n][0] = part[n][1] = part[n][2] = part[n][3] = 0.0f;
-    // scale-group tracking: k at which the current group ends, its slot in s_s
-    int gend = ((wb * prm.win_k) / gk + 1) * gk;
-    for (int w = wb; w < we; ++w) {
-      // stage this window's code rows and scales (16-byte streaming loads)
-      __syncwarp();
-      const int g0 = (w * prm.win_k) / gk;
+    // this warp's code rows of window w into buffer cs: asynchronous copies
+    // when double-buffered (the next window's rows land while this one is
+    // decoded), else 16-byte streaming loads; a dead row stages zeros
+    auto stage_codes = [&](int w, uint32_t* cs) {
       if (l_chunk_ok) {
         const uint32_t* src = prm.codes + static_cast<int64_t>(w) * prm.win_words + l_chunk * 4;
 #pragma unroll 4
         for (int rr = l_row; rr < 16; rr += rows_per_pass) {
           const int64_t cr = code_row(prm, e, min(r0 + rr, prm.OUT - 1));
-          uint4 v = make_uint4(0, 0, 0, 0);
-          if (cr >= 0) v = ldg_stream_v4(src + cr * prm.row_words);
-          *reinterpret_cast<uint4*>(c_s + rr * prm.cs_stride + l_chunk * 4) = v;
+          uint32_t* dst = cs + rr * prm.cs_stride + l_chunk * 4;
+          if (prm.nbuf == 2 && cr >= 0) {
+            cp_async16(dst, src + cr * prm.row_words);
+          } else {
+            uint4 v = make_uint4(0, 0, 0, 0);
+            if (cr >= 0) v = ldg_stream_v4(src + cr * prm.row_words);
+            *reinterpret_cast<uint4*>(dst) = v;
+          }
         }
       }
+    };
+    // window w's scales, loaded into registers one window ahead
+    uint16_t sv[4] = {0, 0, 0, 0};
+    auto load_scales = [&](int w) {
+      const int g0 = (w * prm.win_k) / gk;
       if (s_ok) {
 #pragma unroll
-        for (int rr = s_row; rr < 16; rr += 4) {
-          const int64_t cr = code_row(prm, e, min(r0 + rr, prm.OUT - 1));
-          s_s[rr * prm.sc_stride + s_gi] = cr >= 0 ? __ldg(prm.scales + cr * prm.NGRP + g0 + s_gi) : uint16_t(0);
+        for (int q = 0; q < 4; ++q) {
+          const int64_t cr = code_row(prm, e, min(r0 + s_row + 4 * q, prm.OUT - 1));
+          sv[q] = cr >= 0 ? __ldg(prm.scales + cr * prm.NGRP + g0 + s_gi) : uint16_t(0);
         }
       }
+    };
+    __syncwarp();
+    if (wb < we) {
+      if (prm.nbuf == 2) {
+        stage_codes(wb, c_base);
+        cp_async_commit();
+      }
+      load_scales(wb);
+    }
+    // scale-group tracking: k at which the current group ends, its slot in s_s
+    int gend = ((wb * prm.win_k) / gk + 1) * gk;
+    for (int w = wb; w < we; ++w) {
+      uint32_t* c_s = c_base + (prm.nbuf == 2 ? static_cast<size_t>((w - wb) & 1) * cwin_words : 0);
+      __syncwarp();  // every lane is done with the previous window's buffers
+      if (s_ok) {
+#pragma unroll
+        for (int q = 0; q < 4; ++q) s_s[(s_row + 4 * q) * prm.sc_stride + s_gi] = sv[q];
+      }
+      if (prm.nbuf == 2) {
+        if (w + 1 < we) stage_codes(w + 1, c_base + static_cast<size_t>((w + 1 - wb) & 1) * cwin_words);
+        cp_async_commit();
+        cp_async_wait<1>();  // this window's copies have landed
+      } else {
+        stage_codes(w, c_s);
+      }
+      if (w + 1 < we) load_scales(w + 1);
       __syncwarp();
       const int kw0 = w * prm.win_k;
       int bit0 = ((16 / D) * t) * prm.bits;      // this thread's first code in the window row
@@ -744,7 +790,16 @@ vqb_status launch_decode_mma(const LinearGeometry& geo, const GroupedDecodeArgs&
   const bool full = !split && ns == static_cast<size_t>(geo.K) &&
                     fixed + ((static_cast<size_t>(geo.K + 1) * entry + 15) & ~size_t(15)) <= budget;
   prm.ns = static_cast<int>(ns);
-  const size_t smem = (((full ? ns + 1 : ns) * entry + 15) & ~size_t(15)) + fixed;
+  size_t smem = (((full ? ns + 1 : ns) * entry + 15) & ~size_t(15)) + fixed;
+  // a second code-window buffer per warp (the next window copied while this
+  // one is decoded) when the whole codebook is resident and it still fits; the
+  // prefix and pair-split modes spend that memory on codebook entries
+  const size_t cwin = static_cast<size_t>(16) * prm.cs_stride * 4;
+  prm.nbuf = 1;
+  if (full && smem + kWarps * cwin <= budget) {
+    prm.nbuf = 2;
+    smem += kWarps * cwin;
+  }
   const int grid = split ? (nsm & ~1) : nsm;
 
   cudaError_t ce = cudaSuccess;
