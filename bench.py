@@ -386,7 +386,7 @@ def dense_leg(torch, dev, args, peak_gbs, peak_kind):
             else:
                 byt = dense_bytes(*geom, n=B)
             ach = byt / dur / 1e9
-            kname = ("vq_decode_mma_kernel" if (name == "attn_q" and B <= 8)
+            kname = ("dense_lut_kernel" if (name == "attn_q" and B <= 8)
                      else "moe_block_kernel" if name == "mlp" else "vq_prefill_tc_kernel")
             roofs[name] = {"bound": "hbm", "achieved": round(ach, 1), "peak": peak_gbs, "unit": "GB/s",
                            "frac": round(ach / peak_gbs, 4),

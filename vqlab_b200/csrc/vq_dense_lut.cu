@@ -1,0 +1,451 @@
+// Small-codebook dense decode on the tensor cores (sm_100a): a VQLinear whose
+// d2 codebook has at most 256 entries and 8-bit codes (the attention
+// projections of a dense model: d2/K256) at decode batches of up to 8 rows,
+// in the reference's fused dense arm (vq_switch.py:2319-2327, taken by
+// vq_dense.py:401-441 for d2 layers at small N): x narrowed to fp16, the fp32
+// partial sum of each 64-input scale group multiplied by the group's scale,
+// y stored once in the output dtype.
+//
+// One launch of 288-thread CTAs (8 decode warps of 32 output rows + a copy
+// warp), one CTA per SM at a time:
+//   * the codebook is replicated per lane in shared memory: entry e for lane l
+//     is the word at byte e * 256 + 4 * l, so the 32 lookups of a warp always
+//     hit 32 different banks, and one byte permute (the code byte next to
+//     4 * lane) forms the address;
+//   * a CTA takes 256 output rows and a range of 512-input windows (split s
+//     of S); each window's codes (256 bytes per row: two TMA boxes of 128
+//     bytes x 256 rows with the 128-byte swizzle), its scales (8 x 256 fp16)
+//     and the tokens' x rows (bulk copies) arrive in two stages the copy
+//     thread refills;
+//   * inside a scale group (32 codes of a row), thread t of a quad takes codes
+//     8t .. 8t+7 (one 8-byte read per row) and the inputs they cover (two
+//     16-byte reads of x): MMA step m uses codes 8t+2m and 8t+2m+1 as the A
+//     slots t and t+4 of an m16n8k16 -- a permutation of k applied to A and B
+//     alike, so the sum is the group's dot product; the four steps accumulate
+//     the group partial, which is added, times the row's scale, to the row's
+//     accumulator;
+//   * with one split per row block a CTA stores y itself; otherwise the S
+//     CTAs of a row block form a thread-block cluster: each leaves its fp32
+//     partial tile in shared memory, and after a cluster barrier each CTA
+//     sums a share of the rows over the S tiles (distributed shared memory,
+//     in split order) and stores y.  No CTA waits on global memory.
+//
+// Every mbarrier wait is bounded (2 s); a CTA whose wait expires computes
+// nothing further, still reaches the cluster barriers, waits for its copies
+// in flight and writes VQB_TIMEOUT to the workspace status block (int32 [1]),
+// which block 0 clears when it starts (the launch's first CTAs are resident
+// long before any wait could expire).
+#include <cuda.h>
+
+#include "vqb_common.cuh"
+#include "vqb_internal.h"
+#include "vqb_tma.cuh"
+
+namespace vqb {
+
+namespace {
+
+constexpr int kLtWarps = 8;                      // decode warps, 32 output rows each
+constexpr int kLtThreads = (kLtWarps + 1) * 32;  // + the copy warp
+constexpr int kLtConsumers = kLtWarps * 32;
+constexpr int kLtRows = 256;                     // output rows of a CTA
+constexpr int kLtWinK = 512;                     // inputs per window: 256 codes, 256 bytes per row
+constexpr int kLtStages = 2;
+constexpr int kLtTok = 8;                        // tokens (the MMA's N)
+constexpr int kLtXStride = kLtWinK * 2 + 16;     // bytes of a staged x row (16 B pad: conflict-free reads)
+constexpr int kLtMaxSplit = 8;                   // portable cluster size
+constexpr uint32_t kLtTable = 256 * 256;         // 256 entries x (32 lanes x 4 B, 128 B unused)
+constexpr uint32_t kLtHalfBox = 128 * kLtRows;   // one 128-byte-wide code box
+constexpr uint32_t kLtScaleOff = 2 * kLtHalfBox;
+constexpr uint32_t kLtXOff = kLtScaleOff + 16 * kLtRows;
+constexpr uint32_t kLtStageBytes = (kLtXOff + kLtTok * kLtXStride + 1023) & ~1023u;
+constexpr uint32_t kLtBarOff = kLtStages * kLtStageBytes;  // from the aligned stage base
+// the table at the start of dynamic shared memory, then up to 1023 bytes to
+// align the stages to 1024 (the 128-byte swizzle's 8-row pattern), stages, barriers
+constexpr uint32_t kLtSmem = kLtTable + 1024 + kLtBarOff + 64;
+// the partial tile [token][row] (in stage 0 once the pipeline is done), rows
+// padded by 4 floats so the fragment stores of a warp hit distinct banks
+constexpr int kLtPartStride = kLtRows + 4;
+
+struct LtParams {
+  const uint32_t* codebook;  // [K] entries of two fp16
+  int K;
+  const void* x;             // [T][IN] fp16 / bf16
+  void* y;                   // [T][OUT]
+  int y_dtype;
+  int T, OUT, IN;
+  int S, nw;                 // CTAs (splits) per row block = cluster size, windows per row
+  int* status;               // workspace status block
+};
+
+struct LtMaps {
+  CUtensorMap codes;   // uint32 [OUT][IN / 8], box 32 words x 256 rows, 128-byte swizzle
+  CUtensorMap scales;  // fp16 [OUT][IN / 64], box 8 x 256
+};
+
+__device__ __forceinline__ void lt_prefetch_2d(const CUtensorMap* map, int x, int y) {
+  asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global [%0, {%1, %2}];"
+               :: "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y) : "memory");
+}
+
+__device__ __forceinline__ void lt_mma(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
+                                       uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};\n"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+// the 256 consumer threads only (the copy warp never joins)
+__device__ __forceinline__ void lt_consumer_sync() { asm volatile("bar.sync 1, %0;" :: "n"(kLtConsumers) : "memory"); }
+
+__device__ __forceinline__ uint32_t lt_bf16x2_to_f16x2(uint32_t v) {
+  __half2 h = __floats2half2_rn(__uint_as_float(v << 16), __uint_as_float(v & 0xFFFF0000u));
+  return *reinterpret_cast<uint32_t*>(&h);
+}
+
+// every thread of every CTA in the cluster (a hardware barrier; all CTAs of a
+// cluster are co-scheduled)
+__device__ __forceinline__ void lt_cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release;\nbarrier.cluster.wait.acquire;" ::: "memory");
+}
+
+__device__ __forceinline__ float lt_ld_cluster(const float* local, uint32_t rank) {
+  uint32_t remote;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(smem_u32(local)), "r"(rank));
+  float v;
+  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(remote) : "memory");
+  return v;
+}
+
+// One staged window for one warp: rows 32 * warp + 8 * r + g (r = 0..3; MMA
+// tile j holds r = 2j and 2j + 1), tokens 2t and 2t + 1 of each tile.
+//   off[qq]: swizzled byte offset of this thread's 8 codes of group 4h + qq
+//   inside a 128-byte box row (chunk (2qq + t/2) ^ g, half t & 1).
+__device__ __forceinline__ void lt_window(const unsigned char* table, const unsigned char* sb, int warp, int g, int t,
+                                          uint32_t lane4, const uint32_t (&off)[4], float (&acc)[2][4]) {
+  const unsigned char* cbase = sb + (warp * 32 + g) * 128;
+  const unsigned char* xb = sb + kLtXOff + g * kLtXStride + 32 * t;
+  const unsigned char* sbase = sb + kLtScaleOff + (warp * 32 + g) * 16;
+  uint4 sc[4];
+#pragma unroll
+  for (int r = 0; r < 4; ++r) sc[r] = *reinterpret_cast<const uint4*>(sbase + r * 8 * 16);
+#pragma unroll
+  for (int q = 0; q < 8; ++q) {
+    const int h = q >> 2, qq = q & 3;
+    uint2 cw[4];
+#pragma unroll
+    for (int r = 0; r < 4; ++r)
+      cw[r] = *reinterpret_cast<const uint2*>(cbase + h * kLtHalfBox + r * 1024 + off[qq]);
+    const uint4 v0 = *reinterpret_cast<const uint4*>(xb + 128 * q);
+    const uint4 v1 = *reinterpret_cast<const uint4*>(xb + 128 * q + 16);
+    float part[2][4] = {{0.0f, 0.0f, 0.0f, 0.0f}, {0.0f, 0.0f, 0.0f, 0.0f}};
+#pragma unroll
+    for (int m = 0; m < 4; ++m) {
+      const uint32_t b0 = m == 0 ? v0.x : (m == 1 ? v0.z : (m == 2 ? v1.x : v1.z));
+      const uint32_t b1 = m == 0 ? v0.y : (m == 1 ? v0.w : (m == 2 ? v1.y : v1.w));
+      // codes 8t + 2m and 8t + 2m + 1 of the row: bytes 2(m & 1), +1 of word m >> 1;
+      // the permute puts the code byte above 4 * lane (table byte code * 256 + 4 * lane)
+      const uint32_t s_lo = (m & 1) ? 0x5524u : 0x5504u, s_hi = (m & 1) ? 0x5534u : 0x5514u;
+#pragma unroll
+      for (int j = 0; j < 2; ++j) {
+        const uint32_t w0 = (m >> 1) ? cw[2 * j].y : cw[2 * j].x;
+        const uint32_t w1 = (m >> 1) ? cw[2 * j + 1].y : cw[2 * j + 1].x;
+        const uint32_t a0 = *reinterpret_cast<const uint32_t*>(table + __byte_perm(w0, lane4, s_lo));
+        const uint32_t a1 = *reinterpret_cast<const uint32_t*>(table + __byte_perm(w1, lane4, s_lo));
+        const uint32_t a2 = *reinterpret_cast<const uint32_t*>(table + __byte_perm(w0, lane4, s_hi));
+        const uint32_t a3 = *reinterpret_cast<const uint32_t*>(table + __byte_perm(w1, lane4, s_hi));
+        lt_mma(part[j], a0, a1, a2, a3, b0, b1);
+      }
+    }
+    // the group's scales: fp16 number q of each row's 8
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+      const uint4& u0 = sc[2 * j];
+      const uint4& u1 = sc[2 * j + 1];
+      const uint32_t p0 = (q >> 1) == 0 ? u0.x : ((q >> 1) == 1 ? u0.y : ((q >> 1) == 2 ? u0.z : u0.w));
+      const uint32_t p1 = (q >> 1) == 0 ? u1.x : ((q >> 1) == 1 ? u1.y : ((q >> 1) == 2 ? u1.z : u1.w));
+      const float s0 = __half2float(__ushort_as_half(static_cast<unsigned short>((q & 1) ? (p0 >> 16) : p0)));
+      const float s1 = __half2float(__ushort_as_half(static_cast<unsigned short>((q & 1) ? (p1 >> 16) : p1)));
+      acc[j][0] = fmaf(s0, part[j][0], acc[j][0]);
+      acc[j][1] = fmaf(s0, part[j][1], acc[j][1]);
+      acc[j][2] = fmaf(s1, part[j][2], acc[j][2]);
+      acc[j][3] = fmaf(s1, part[j][3], acc[j][3]);
+    }
+  }
+}
+
+template <bool XBF16>
+__global__ void __launch_bounds__(kLtThreads, 1) dense_lut_kernel(const __grid_constant__ LtMaps maps,
+                                                                  const __grid_constant__ LtParams p) {
+  extern __shared__ __align__(16) unsigned char smem[];
+  unsigned char* stages = smem + kLtTable + ((1024u - ((smem_u32(smem) + kLtTable) & 1023u)) & 1023u);
+  uint64_t* full = reinterpret_cast<uint64_t*>(stages + kLtBarOff);
+  uint64_t* empty = full + kLtStages;
+  int* sflags = reinterpret_cast<int*>(full + 2 * kLtStages);  // [0] abort, [1] windows issued
+  volatile int* abort_flag = sflags;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, tid = threadIdx.x;
+  // 1-d clusters of S CTAs: the split is the CTA's rank in its cluster
+  const int rb = blockIdx.x / p.S, split = blockIdx.x - rb * p.S;
+  const int w0 = split * p.nw / p.S, w1 = (split + 1) * p.nw / p.S;
+
+  if (tid == 0) {
+    for (int s = 0; s < kLtStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], kLtWarps);
+    }
+    sflags[0] = 0;
+    sflags[1] = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  // tokens T..7 read zeros: their x rows are never copied
+  {
+    const int per = (kLtTok - p.T) * (kLtXStride / 16);
+    for (int i = tid; i < kLtStages * per; i += kLtThreads) {
+      const int s = i / per, r = i - s * per;
+      *reinterpret_cast<uint4*>(stages + s * kLtStageBytes + kLtXOff + p.T * kLtXStride + r * 16) =
+          make_uint4(0u, 0u, 0u, 0u);
+    }
+  }
+  // this CTA's weights into L2 while the previous kernel finishes (a prefetch
+  // returns no data, so it cannot observe a stale value)
+  if (warp == kLtWarps && lane == 0) {
+    for (int w = w0; w < w1; ++w) {
+      lt_prefetch_2d(&maps.codes, w * 64, rb * kLtRows);
+      lt_prefetch_2d(&maps.codes, w * 64 + 32, rb * kLtRows);
+      lt_prefetch_2d(&maps.scales, w * 8, rb * kLtRows);
+    }
+  }
+  __syncthreads();
+  pdl_wait();
+  pdl_trigger();
+  if (blockIdx.x == 0 && tid == 0) p.status[1] = 0;
+
+  float acc[2][4] = {{0.0f, 0.0f, 0.0f, 0.0f}, {0.0f, 0.0f, 0.0f, 0.0f}};
+  const int g = lane >> 2, t = lane & 3;
+  if (warp == kLtWarps) {
+    // ------------------------------------------------------------ copy warp
+    if (lane == 0) {
+      const unsigned char* xg = static_cast<const unsigned char*>(p.x);
+      const uint32_t tx = 2 * kLtHalfBox + 16 * kLtRows + static_cast<uint32_t>(p.T) * kLtWinK * 2;
+      for (int w = w0, n = 0; w < w1; ++w, ++n) {
+        const int st = n & 1;
+        if (n >= kLtStages && !mbar_wait(&empty[st], ((n >> 1) - 1) & 1, abort_flag)) break;
+        unsigned char* sb = stages + st * kLtStageBytes;
+        mbar_expect_tx(&full[st], tx);
+        tma_load_2d(&maps.codes, &full[st], sb, w * 64, rb * kLtRows);
+        tma_load_2d(&maps.codes, &full[st], sb + kLtHalfBox, w * 64 + 32, rb * kLtRows);
+        tma_load_2d(&maps.scales, &full[st], sb + kLtScaleOff, w * 8, rb * kLtRows);
+        for (int j = 0; j < p.T; ++j)
+          bulk_load(sb + kLtXOff + j * kLtXStride,
+                    xg + (static_cast<size_t>(j) * p.IN + static_cast<size_t>(w) * kLtWinK) * 2, kLtWinK * 2,
+                    &full[st]);
+        *reinterpret_cast<volatile int*>(&sflags[1]) = n + 1;
+      }
+    }
+  } else {
+    // -------------------------------------------------------- decode warps
+    // the replicated codebook: entry e for lane l at byte e * 256 + 4 l; codes >= K read zeros
+    for (int i = tid; i < 256 * 32; i += kLtConsumers) {
+      const int e = i >> 5;
+      const uint32_t v = e < p.K ? __ldg(p.codebook + e) : 0u;
+      *reinterpret_cast<uint32_t*>(smem + e * 256 + (i & 31) * 4) = v;
+    }
+    lt_consumer_sync();
+    const uint32_t lane4 = static_cast<uint32_t>(lane) * 4u;
+    uint32_t off[4];
+#pragma unroll
+    for (int qq = 0; qq < 4; ++qq) off[qq] = ((static_cast<uint32_t>(2 * qq + (t >> 1)) ^ g) << 4) | (8u * (t & 1));
+    bool alive = true;
+    for (int w = w0, n = 0; w < w1; ++w, ++n) {
+      const int st = n & 1;
+      unsigned char* sb = stages + st * kLtStageBytes;
+      if (alive) alive = warp_wait(&full[st], (n >> 1) & 1, abort_flag);
+      if (XBF16) {
+        // x narrowed to fp16 in place (each consumer thread a share), then every warp reads it
+        if (alive) {
+          for (int k = tid; k < p.T * (kLtWinK / 8); k += kLtConsumers) {
+            uint4* q = reinterpret_cast<uint4*>(sb + kLtXOff + (k >> 6) * kLtXStride + (k & 63) * 16);
+            uint4 v = *q;
+            v.x = lt_bf16x2_to_f16x2(v.x);
+            v.y = lt_bf16x2_to_f16x2(v.y);
+            v.z = lt_bf16x2_to_f16x2(v.z);
+            v.w = lt_bf16x2_to_f16x2(v.w);
+            *q = v;
+          }
+        }
+        lt_consumer_sync();
+      }
+      if (alive) lt_window(smem, sb, warp, g, t, lane4, off, acc);
+      // the in-place narrowing's writes before the next copy into this stage
+      if (XBF16) asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[st]);
+    }
+    if (p.S == 1) {
+      // rows 32 warp + 16 j + g (+ 8), tokens 2t, 2t + 1
+      const int row0 = rb * kLtRows + warp * 32 + g;
+#pragma unroll
+      for (int j = 0; j < 2; ++j)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int row = row0 + 16 * j + 8 * (e >> 1), tok = 2 * t + (e & 1);
+          if (row < p.OUT && tok < p.T)
+            store_y(p.y, static_cast<int64_t>(tok) * p.OUT + row, acc[j][e], p.y_dtype, false);
+        }
+    }
+  }
+  __syncthreads();
+  if (tid == 0) {
+    // copies still in flight (only after an expired wait) land before stage 0 is reused or the CTA exits
+    const int issued = *reinterpret_cast<volatile int*>(&sflags[1]);
+    for (int k = issued > kLtStages ? issued - kLtStages : 0; k < issued; ++k) mbar_drain(&full[k & 1], (k >> 1) & 1);
+    if (*abort_flag) p.status[1] = static_cast<int>(VQB_TIMEOUT);
+  }
+  if (p.S == 1) return;
+  __syncthreads();
+  // ---- split-K over the cluster: partial tiles [token][row] in stage 0
+  float* part = reinterpret_cast<float*>(stages);
+  if (warp < kLtWarps) {
+#pragma unroll
+    for (int j = 0; j < 2; ++j)
+#pragma unroll
+      for (int e = 0; e < 4; ++e)
+        part[(2 * t + (e & 1)) * kLtPartStride + warp * 32 + 16 * j + 8 * (e >> 1) + g] = acc[j][e];
+  }
+  lt_cluster_sync();
+  // rank `split` sums rows [r0, r1) of the row block over the S tiles in split order
+  const int r0 = split * kLtRows / p.S, r1 = (split + 1) * kLtRows / p.S, nr = r1 - r0;
+  for (int k = tid; k < p.T * nr; k += kLtThreads) {
+    const int tok = k / nr, r = r0 + (k - tok * nr);
+    const int row = rb * kLtRows + r;
+    if (row < p.OUT) {
+      const float* src = part + tok * kLtPartStride + r;
+      float s = 0.0f;
+      for (int q = 0; q < p.S; ++q) s += lt_ld_cluster(src, static_cast<uint32_t>(q));
+      store_y(p.y, static_cast<int64_t>(tok) * p.OUT + row, s, p.y_dtype, false);
+    }
+  }
+  // no CTA leaves while another still reads its tile
+  lt_cluster_sync();
+}
+
+}  // namespace
+
+// ------------------------------------------------------------------ host
+
+bool dense_lut_geometry(const LinearGeometry& g) {
+  return g.E == 1 && g.row_table == nullptr && g.D == 2 && g.bits == 8 && g.K >= 1 && g.K <= 256 && g.G == 64 &&
+         g.OUT >= 1 && g.IN >= kLtWinK && g.IN % kLtWinK == 0 && g.row_words == g.IN / 8;
+}
+
+bool dense_lut_eligible(const LinearGeometry& g, const void* x, int x_dtype, int T) {
+  const auto a16 = [](const void* q) { return (reinterpret_cast<uintptr_t>(q) & 15) == 0; };
+  return dense_lut_geometry(g) && T >= 1 && T <= kLtTok && (x_dtype == VQB_F16 || x_dtype == VQB_BF16) && a16(x) &&
+         a16(g.codes) && a16(g.scales) && (reinterpret_cast<uintptr_t>(g.codebook) & 3) == 0;
+}
+
+// Clusters of S CTAs that fit on the device at once (cached per device and
+// S); 0 when the query fails, and that cluster size is not used.
+static int lt_cluster_capacity(void (*kern)(LtMaps, LtParams), int S, int sms) {
+  static int cache[16][kLtMaxSplit + 1];
+  static bool init = false;
+  if (!init) {
+    for (auto& r : cache)
+      for (int& v : r) v = -1;
+    init = true;
+  }
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 16) return 0;
+  int& c = cache[dev][S];
+  if (c < 0) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(static_cast<unsigned>(S * sms));
+    cfg.blockDim = dim3(kLtThreads);
+    cfg.dynamicSmemBytes = kLtSmem;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = static_cast<unsigned>(S);
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    int n = 0;
+    if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess || n <= 0) {
+      cudaGetLastError();
+      n = 0;
+    }
+    c = n;
+  }
+  return c;
+}
+
+vqb_status launch_dense_lut(const LinearGeometry& g, const void* x, int x_dtype, int T, void* y, int y_dtype,
+                            int* status, cudaStream_t stream) {
+  DeviceInfo di;
+  if (device_info(&di) != VQB_OK) return VQB_CUDA_ERROR;
+  EncodeTiledFn enc = encode_fn();
+  if (!enc) return VQB_CUDA_ERROR;
+  LtMaps maps;
+  if (!encode_2d(enc, &maps.codes, CU_TENSOR_MAP_DATA_TYPE_UINT32, 4, g.codes, static_cast<uint64_t>(g.row_words),
+                 static_cast<uint64_t>(g.OUT), 32, kLtRows, CU_TENSOR_MAP_SWIZZLE_128B) ||
+      !encode_2d(enc, &maps.scales, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, g.scales, static_cast<uint64_t>(g.IN / 64),
+                 static_cast<uint64_t>(g.OUT), kLtWinK / 64, kLtRows, CU_TENSOR_MAP_SWIZZLE_NONE))
+    return VQB_CUDA_ERROR;
+  void (*kern)(LtMaps, LtParams) = x_dtype == VQB_BF16 ? dense_lut_kernel<true> : dense_lut_kernel<false>;
+  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kLtSmem)) !=
+      cudaSuccess)
+    return VQB_CUDA_ERROR;
+  LtParams p{};
+  p.codebook = static_cast<const uint32_t*>(g.codebook);
+  p.K = g.K;
+  p.x = x;
+  p.y = y;
+  p.y_dtype = y_dtype;
+  p.T = T;
+  p.OUT = g.OUT;
+  p.IN = g.IN;
+  p.nw = g.IN / kLtWinK;
+  p.status = status;
+  const int nrb = (g.OUT + kLtRows - 1) / kLtRows;
+  // CTAs per row block: the fewest that reach the smallest (waves of
+  // clusters) x (windows per CTA); e.g. 5120 x 5120: 20 row blocks x 5
+  // splits of 2 windows in one wave
+  const int smax = p.nw < kLtMaxSplit ? p.nw : kLtMaxSplit;
+  int best = 1;
+  int64_t best_cost = INT64_MAX;
+  for (int S = 1; S <= smax; ++S) {
+    const int cap = S == 1 ? di.sms : lt_cluster_capacity(kern, S, di.sms);
+    if (cap <= 0) continue;
+    const int64_t waves = (nrb + cap - 1) / cap;
+    const int64_t cost = waves * ((p.nw + S - 1) / S);
+    if (cost < best_cost) {
+      best_cost = cost;
+      best = S;
+    }
+  }
+  p.S = best;
+
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  attr[1].id = cudaLaunchAttributeClusterDimension;
+  attr[1].val.clusterDim.x = static_cast<unsigned>(best);
+  attr[1].val.clusterDim.y = 1;
+  attr[1].val.clusterDim.z = 1;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(nrb * best));
+  cfg.blockDim = dim3(kLtThreads);
+  cfg.dynamicSmemBytes = kLtSmem;
+  cfg.stream = stream;
+  cfg.attrs = attr;
+  cfg.numAttrs = best > 1 ? 2 : 1;
+  timer_before(stream);
+  const cudaError_t ce = cudaLaunchKernelEx(&cfg, kern, maps, p);
+  timer_after(stream);
+  if (ce != cudaSuccess) return VQB_CUDA_ERROR;
+  note_launch();
+  return VQB_OK;
+}
+
+}  // namespace vqb

@@ -354,6 +354,13 @@ vqb_status vqb_dense_forward(const vqb_linear_desc* desc, const void* x, vqb_dty
   // 5120 x 5120 at N = 16 30 vs 73 us, N = 32 31 vs 118 us.
   const bool large = path == VQB_PATH_PREFILL || (!fused && (n > 16 || tc_prefill_dsplit(geo))) ||
                      (fused && path == VQB_PATH_AUTO && n > 8);
+  // a d2 codebook of <= 256 entries at <= 8 rows: the small-codebook kernel
+  // (the codebook replicated per lane in shared memory, one launch, no routing
+  // step, split-K reduced inside thread-block clusters)
+  if (fused && path == VQB_PATH_AUTO && !(opts && (opts->decode_variant != 0 || opts->k_split != 0)) &&
+      (reinterpret_cast<uintptr_t>(workspace) & 3) == 0 && dense_lut_eligible(geo, x, x_dtype, n))
+    return launch_dense_lut(geo, x, x_dtype, n, y, y_dtype, static_cast<int*>(workspace),
+                            reinterpret_cast<cudaStream_t>(stream));
   return run_linear(geo, x, x_dtype, n, nullptr, 1, n, y, y_dtype, workspace, opts, /*narrow_x_f16=*/fused,
                     /*round_f16_first=*/false, wround, large, reinterpret_cast<cudaStream_t>(stream));
 }

@@ -72,6 +72,14 @@ size_t mma_x16_bytes(int64_t T, int IN);
 vqb_status launch_decode_mma(const LinearGeometry& geo, const GroupedDecodeArgs& a, uint16_t* x16, int T,
                              cudaStream_t stream);
 
+// Small-codebook dense decode (vq_dense_lut.cu): d2, K <= 256, 8-bit codes,
+// group 64, IN a multiple of 512, up to 8 rows, fp16/bf16 x; `status` is the
+// workspace status block (int32 [1] = VQB_TIMEOUT after an expired wait, else 0).
+bool dense_lut_geometry(const LinearGeometry& g);
+bool dense_lut_eligible(const LinearGeometry& g, const void* x, int x_dtype, int T);
+vqb_status launch_dense_lut(const LinearGeometry& g, const void* x, int x_dtype, int T, void* y, int y_dtype,
+                            int* status, cudaStream_t stream);
+
 // Grouped tcgen05 GEMM for large token counts (vq_prefill_tc.cu).
 bool tc_prefill_supported(const LinearGeometry& geo);
 bool tc_prefill_dsplit(const LinearGeometry& geo);  // the GEMM would run dimension-split passes
