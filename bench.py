@@ -270,7 +270,10 @@ def time_graph_steps(torch, graphs, steps, warmup):
 
 def kernel_seconds(torch, stream, call, reps):
     """Mean device time of the dominant kernel of `call(i)`: the library
-    records two events on the launch stream around that kernel alone."""
+    records two events on the launch stream around that kernel alone.  A
+    ~0.1 ms spin kernel queued before each call keeps the stream busy while
+    the host prepares the launch, so the interval holds the kernel's device
+    time and not the host's launch overhead."""
     from vqlab_b200 import _lib
     pairs = []
     for i in range(reps):
@@ -280,6 +283,7 @@ def kernel_seconds(torch, stream, call, reps):
         pairs.append((a, b))
     torch.cuda.synchronize()
     for i, (a, b) in enumerate(pairs):
+        torch.cuda._sleep(200_000)
         _lib.time_next_kernel(a, b)
         call(i)
     torch.cuda.synchronize()

@@ -6,8 +6,8 @@
 // partial sum of each 64-input scale group multiplied by the group's scale,
 // y stored once in the output dtype.
 //
-// One launch of 288-thread CTAs (8 decode warps of 32 output rows + a copy
-// warp), one CTA per SM at a time:
+// One launch of 512-thread CTAs (16 warps of 16 output rows; thread 0 also
+// issues the copies), one CTA per SM at a time:
 //   * the codebook is replicated per lane in shared memory: entry e for lane l
 //     is the word at byte e * 256 + 4 * l, so the 32 lookups of a warp always
 //     hit 32 different banks, and one byte permute (the code byte next to
@@ -15,8 +15,8 @@
 //   * a CTA takes 256 output rows and a range of 512-input windows (split s
 //     of S); each window's codes (256 bytes per row: two TMA boxes of 128
 //     bytes x 256 rows with the 128-byte swizzle), its scales (8 x 256 fp16)
-//     and the tokens' x rows (bulk copies) arrive in two stages the copy
-//     thread refills;
+//     and the tokens' x rows (bulk copies) arrive in two stages, refilled
+//     once every warp has released the stage;
 //   * inside a scale group (32 codes of a row), thread t of a quad takes codes
 //     8t .. 8t+7 (one 8-byte read per row) and the inputs they cover (two
 //     16-byte reads of x): MMA step m uses codes 8t+2m and 8t+2m+1 as the A
@@ -25,10 +25,12 @@
 //     the group partial, which is added, times the row's scale, to the row's
 //     accumulator;
 //   * with one split per row block a CTA stores y itself; otherwise the S
-//     CTAs of a row block form a thread-block cluster: each leaves its fp32
-//     partial tile in shared memory, and after a cluster barrier each CTA
-//     sums a share of the rows over the S tiles (distributed shared memory,
-//     in split order) and stores y.  No CTA waits on global memory.
+//     CTAs of a row block form a thread-block cluster: each CTA owns a share
+//     of the rows, every CTA stores its fp32 partials of those rows into the
+//     owner's shared memory (distributed shared memory, into the table's
+//     unused upper halves), and after one cluster barrier each owner sums its
+//     rows over the S partials in split order and stores y.  No CTA waits on
+//     global memory.
 //
 // Every mbarrier wait is bounded (2 s); a CTA whose wait expires computes
 // nothing further, still reaches the cluster barriers, waits for its copies
@@ -45,10 +47,11 @@ namespace vqb {
 
 namespace {
 
-constexpr int kLtWarps = 8;                      // decode warps, 32 output rows each
-constexpr int kLtThreads = (kLtWarps + 1) * 32;  // + the copy warp
-constexpr int kLtConsumers = kLtWarps * 32;
+constexpr int kLtWarps = 16;                     // decode warps
+constexpr int kLtThreads = kLtWarps * 32;        // thread 0 also issues the copies
 constexpr int kLtRows = 256;                     // output rows of a CTA
+constexpr int kLtTiles = kLtRows / (16 * kLtWarps);  // 16-row MMA tiles per warp
+constexpr int kLtWarpRows = 16 * kLtTiles;
 constexpr int kLtWinK = 512;                     // inputs per window: 256 codes, 256 bytes per row
 constexpr int kLtStages = 2;
 constexpr int kLtTok = 8;                        // tokens (the MMA's N)
@@ -63,9 +66,13 @@ constexpr uint32_t kLtBarOff = kLtStages * kLtStageBytes;  // from the aligned s
 // the table at the start of dynamic shared memory, then up to 1023 bytes to
 // align the stages to 1024 (the 128-byte swizzle's 8-row pattern), stages, barriers
 constexpr uint32_t kLtSmem = kLtTable + 1024 + kLtBarOff + 64;
-// the partial tile [token][row] (in stage 0 once the pipeline is done), rows
-// padded by 4 floats so the fragment stores of a warp hit distinct banks
-constexpr int kLtPartStride = kLtRows + 4;
+// split-K partials a row's owner receives: float i at byte (i / 32) * 256 +
+// 128 + 4 (i % 32) -- the upper halves of the table's 256-byte entries, which
+// lookups never read; [source split][token][owned row], at most
+// 8 x 8 x 37 floats (< 8192)
+__device__ __forceinline__ uint32_t lt_recv_off(int i) {
+  return (static_cast<uint32_t>(i >> 5) << 8) + 128u + (static_cast<uint32_t>(i & 31) << 2);
+}
 
 struct LtParams {
   const uint32_t* codebook;  // [K] entries of two fp16
@@ -96,50 +103,56 @@ __device__ __forceinline__ void lt_mma(float (&d)[4], uint32_t a0, uint32_t a1, 
       : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 
-// the 256 consumer threads only (the copy warp never joins)
-__device__ __forceinline__ void lt_consumer_sync() { asm volatile("bar.sync 1, %0;" :: "n"(kLtConsumers) : "memory"); }
-
 __device__ __forceinline__ uint32_t lt_bf16x2_to_f16x2(uint32_t v) {
   __half2 h = __floats2half2_rn(__uint_as_float(v << 16), __uint_as_float(v & 0xFFFF0000u));
   return *reinterpret_cast<uint32_t*>(&h);
 }
 
-// every thread of every CTA in the cluster (a hardware barrier; all CTAs of a
-// cluster are co-scheduled)
+// cluster barrier halves, every thread of every CTA in the cluster (a
+// hardware barrier; all CTAs of a cluster are co-scheduled)
+__device__ __forceinline__ void lt_cluster_arrive_relaxed() {
+  asm volatile("barrier.cluster.arrive.relaxed;" ::: "memory");
+}
+__device__ __forceinline__ void lt_cluster_wait() { asm volatile("barrier.cluster.wait;" ::: "memory"); }
 __device__ __forceinline__ void lt_cluster_sync() {
   asm volatile("barrier.cluster.arrive.release;\nbarrier.cluster.wait.acquire;" ::: "memory");
 }
 
-__device__ __forceinline__ float lt_ld_cluster(const float* local, uint32_t rank) {
+__device__ __forceinline__ void lt_st_cluster(uint32_t local_smem, uint32_t rank, float v) {
   uint32_t remote;
-  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(smem_u32(local)), "r"(rank));
-  float v;
-  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(remote) : "memory");
-  return v;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(local_smem), "r"(rank));
+  asm volatile("st.shared::cluster.f32 [%0], %1;" :: "r"(remote), "f"(v) : "memory");
 }
 
-// One staged window for one warp: rows 32 * warp + 8 * r + g (r = 0..3; MMA
-// tile j holds r = 2j and 2j + 1), tokens 2t and 2t + 1 of each tile.
+// One staged window for one warp: rows kLtWarpRows * warp + 8 * r + g (MMA
+// tile j holds r = 2j and 2j + 1), tokens 2t and 2t + 1 of each tile.  Lanes
+// of tokens >= T read no x (their B values are zero).
 //   off[qq]: swizzled byte offset of this thread's 8 codes of group 4h + qq
 //   inside a 128-byte box row (chunk (2qq + t/2) ^ g, half t & 1).
 __device__ __forceinline__ void lt_window(const unsigned char* table, const unsigned char* sb, int warp, int g, int t,
-                                          uint32_t lane4, const uint32_t (&off)[4], float (&acc)[2][4]) {
-  const unsigned char* cbase = sb + (warp * 32 + g) * 128;
+                                          uint32_t lane4, const uint32_t (&off)[4], bool has_x,
+                                          float (&acc)[kLtTiles][4]) {
+  const unsigned char* cbase = sb + (warp * kLtWarpRows + g) * 128;
   const unsigned char* xb = sb + kLtXOff + g * kLtXStride + 32 * t;
-  const unsigned char* sbase = sb + kLtScaleOff + (warp * 32 + g) * 16;
-  uint4 sc[4];
+  const unsigned char* sbase = sb + kLtScaleOff + (warp * kLtWarpRows + g) * 16;
+  uint4 sc[2 * kLtTiles];
 #pragma unroll
-  for (int r = 0; r < 4; ++r) sc[r] = *reinterpret_cast<const uint4*>(sbase + r * 8 * 16);
+  for (int r = 0; r < 2 * kLtTiles; ++r) sc[r] = *reinterpret_cast<const uint4*>(sbase + r * 8 * 16);
 #pragma unroll
   for (int q = 0; q < 8; ++q) {
     const int h = q >> 2, qq = q & 3;
-    uint2 cw[4];
+    uint2 cw[2 * kLtTiles];
 #pragma unroll
-    for (int r = 0; r < 4; ++r)
+    for (int r = 0; r < 2 * kLtTiles; ++r)
       cw[r] = *reinterpret_cast<const uint2*>(cbase + h * kLtHalfBox + r * 1024 + off[qq]);
-    const uint4 v0 = *reinterpret_cast<const uint4*>(xb + 128 * q);
-    const uint4 v1 = *reinterpret_cast<const uint4*>(xb + 128 * q + 16);
-    float part[2][4] = {{0.0f, 0.0f, 0.0f, 0.0f}, {0.0f, 0.0f, 0.0f, 0.0f}};
+    uint4 v0 = make_uint4(0u, 0u, 0u, 0u), v1 = v0;
+    if (has_x) {
+      v0 = *reinterpret_cast<const uint4*>(xb + 128 * q);
+      v1 = *reinterpret_cast<const uint4*>(xb + 128 * q + 16);
+    }
+    float part[kLtTiles][4];
+#pragma unroll
+    for (int j = 0; j < kLtTiles; ++j) part[j][0] = part[j][1] = part[j][2] = part[j][3] = 0.0f;
 #pragma unroll
     for (int m = 0; m < 4; ++m) {
       const uint32_t b0 = m == 0 ? v0.x : (m == 1 ? v0.z : (m == 2 ? v1.x : v1.z));
@@ -148,7 +161,7 @@ __device__ __forceinline__ void lt_window(const unsigned char* table, const unsi
       // the permute puts the code byte above 4 * lane (table byte code * 256 + 4 * lane)
       const uint32_t s_lo = (m & 1) ? 0x5524u : 0x5504u, s_hi = (m & 1) ? 0x5534u : 0x5514u;
 #pragma unroll
-      for (int j = 0; j < 2; ++j) {
+      for (int j = 0; j < kLtTiles; ++j) {
         const uint32_t w0 = (m >> 1) ? cw[2 * j].y : cw[2 * j].x;
         const uint32_t w1 = (m >> 1) ? cw[2 * j + 1].y : cw[2 * j + 1].x;
         const uint32_t a0 = *reinterpret_cast<const uint32_t*>(table + __byte_perm(w0, lane4, s_lo));
@@ -160,7 +173,7 @@ __device__ __forceinline__ void lt_window(const unsigned char* table, const unsi
     }
     // the group's scales: fp16 number q of each row's 8
 #pragma unroll
-    for (int j = 0; j < 2; ++j) {
+    for (int j = 0; j < kLtTiles; ++j) {
       const uint4& u0 = sc[2 * j];
       const uint4& u1 = sc[2 * j + 1];
       const uint32_t p0 = (q >> 1) == 0 ? u0.x : ((q >> 1) == 1 ? u0.y : ((q >> 1) == 2 ? u0.z : u0.w));
@@ -175,6 +188,20 @@ __device__ __forceinline__ void lt_window(const unsigned char* table, const unsi
   }
 }
 
+// Thread 0: the copies of window w into stage st (codes: two swizzled boxes;
+// scales; the tokens' x rows).
+__device__ __forceinline__ void lt_issue(const LtMaps& maps, const LtParams& p, unsigned char* sb, uint64_t* bar,
+                                         int w, int rb) {
+  const unsigned char* xg = static_cast<const unsigned char*>(p.x);
+  mbar_expect_tx(bar, 2 * kLtHalfBox + 16 * kLtRows + static_cast<uint32_t>(p.T) * kLtWinK * 2);
+  tma_load_2d(&maps.codes, bar, sb, w * 64, rb * kLtRows);
+  tma_load_2d(&maps.codes, bar, sb + kLtHalfBox, w * 64 + 32, rb * kLtRows);
+  tma_load_2d(&maps.scales, bar, sb + kLtScaleOff, w * 8, rb * kLtRows);
+  for (int j = 0; j < p.T; ++j)
+    bulk_load(sb + kLtXOff + j * kLtXStride, xg + (static_cast<size_t>(j) * p.IN + static_cast<size_t>(w) * kLtWinK) * 2,
+              kLtWinK * 2, bar);
+}
+
 template <bool XBF16>
 __global__ void __launch_bounds__(kLtThreads, 1) dense_lut_kernel(const __grid_constant__ LtMaps maps,
                                                                   const __grid_constant__ LtParams p) {
@@ -187,7 +214,7 @@ __global__ void __launch_bounds__(kLtThreads, 1) dense_lut_kernel(const __grid_c
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, tid = threadIdx.x;
   // 1-d clusters of S CTAs: the split is the CTA's rank in its cluster
   const int rb = blockIdx.x / p.S, split = blockIdx.x - rb * p.S;
-  const int w0 = split * p.nw / p.S, w1 = (split + 1) * p.nw / p.S;
+  const int w0 = split * p.nw / p.S, w1 = (split + 1) * p.nw / p.S, nwin = w1 - w0;
 
   if (tid == 0) {
     for (int s = 0; s < kLtStages; ++s) {
@@ -197,6 +224,15 @@ __global__ void __launch_bounds__(kLtThreads, 1) dense_lut_kernel(const __grid_c
     sflags[0] = 0;
     sflags[1] = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    // this CTA's weights into L2 while the previous kernel finishes (a
+    // prefetch returns no data, so it cannot observe a stale value)
+    for (int b = 0; b < p.K * 4; b += 128)
+      asm volatile("prefetch.global.L2 [%0];" :: "l"(reinterpret_cast<const char*>(p.codebook) + b));
+    for (int w = w0; w < w1; ++w) {
+      lt_prefetch_2d(&maps.codes, w * 64, rb * kLtRows);
+      lt_prefetch_2d(&maps.codes, w * 64 + 32, rb * kLtRows);
+      lt_prefetch_2d(&maps.scales, w * 8, rb * kLtRows);
+    }
   }
   // tokens T..7 read zeros: their x rows are never copied
   {
@@ -207,127 +243,118 @@ __global__ void __launch_bounds__(kLtThreads, 1) dense_lut_kernel(const __grid_c
           make_uint4(0u, 0u, 0u, 0u);
     }
   }
-  // this CTA's weights into L2 while the previous kernel finishes (a prefetch
-  // returns no data, so it cannot observe a stale value)
-  if (warp == kLtWarps && lane == 0) {
-    for (int w = w0; w < w1; ++w) {
-      lt_prefetch_2d(&maps.codes, w * 64, rb * kLtRows);
-      lt_prefetch_2d(&maps.codes, w * 64 + 32, rb * kLtRows);
-      lt_prefetch_2d(&maps.scales, w * 8, rb * kLtRows);
+  __syncthreads();
+  // first half of the barrier that tells every CTA of the cluster its peers have started
+  if (p.S > 1) lt_cluster_arrive_relaxed();
+  pdl_wait();
+  pdl_trigger();
+  if (tid == 0) {
+    if (blockIdx.x == 0) p.status[1] = 0;
+    for (int n = 0; n < kLtStages && n < nwin; ++n) lt_issue(maps, p, stages + n * kLtStageBytes, &full[n], w0 + n, rb);
+    sflags[1] = nwin < kLtStages ? nwin : kLtStages;
+  }
+  // the replicated codebook: entry e for lane l at byte e * 256 + 4 l; codes >= K read zeros.
+  // Warp w writes entries w + kLtWarps * k: one global load per lane, then shuffles.
+  {
+    constexpr int kPer = 256 / kLtWarps;
+    const int mine_e = warp + kLtWarps * (lane % kPer);
+    const uint32_t mine = mine_e < p.K ? __ldg(p.codebook + mine_e) : 0u;
+#pragma unroll
+    for (int k = 0; k < kPer; ++k) {
+      const uint32_t v = __shfl_sync(0xffffffffu, mine, k);
+      *reinterpret_cast<uint32_t*>(smem + (warp + kLtWarps * k) * 256 + lane * 4) = v;
     }
   }
   __syncthreads();
-  pdl_wait();
-  pdl_trigger();
-  if (blockIdx.x == 0 && tid == 0) p.status[1] = 0;
 
-  float acc[2][4] = {{0.0f, 0.0f, 0.0f, 0.0f}, {0.0f, 0.0f, 0.0f, 0.0f}};
+  float acc[kLtTiles][4];
+#pragma unroll
+  for (int j = 0; j < kLtTiles; ++j) acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0.0f;
   const int g = lane >> 2, t = lane & 3;
-  if (warp == kLtWarps) {
-    // ------------------------------------------------------------ copy warp
-    if (lane == 0) {
-      const unsigned char* xg = static_cast<const unsigned char*>(p.x);
-      const uint32_t tx = 2 * kLtHalfBox + 16 * kLtRows + static_cast<uint32_t>(p.T) * kLtWinK * 2;
-      for (int w = w0, n = 0; w < w1; ++w, ++n) {
-        const int st = n & 1;
-        if (n >= kLtStages && !mbar_wait(&empty[st], ((n >> 1) - 1) & 1, abort_flag)) break;
-        unsigned char* sb = stages + st * kLtStageBytes;
-        mbar_expect_tx(&full[st], tx);
-        tma_load_2d(&maps.codes, &full[st], sb, w * 64, rb * kLtRows);
-        tma_load_2d(&maps.codes, &full[st], sb + kLtHalfBox, w * 64 + 32, rb * kLtRows);
-        tma_load_2d(&maps.scales, &full[st], sb + kLtScaleOff, w * 8, rb * kLtRows);
-        for (int j = 0; j < p.T; ++j)
-          bulk_load(sb + kLtXOff + j * kLtXStride,
-                    xg + (static_cast<size_t>(j) * p.IN + static_cast<size_t>(w) * kLtWinK) * 2, kLtWinK * 2,
-                    &full[st]);
-        *reinterpret_cast<volatile int*>(&sflags[1]) = n + 1;
+  const uint32_t lane4 = static_cast<uint32_t>(lane) * 4u;
+  uint32_t off[4];
+#pragma unroll
+  for (int qq = 0; qq < 4; ++qq) off[qq] = ((static_cast<uint32_t>(2 * qq + (t >> 1)) ^ g) << 4) | (8u * (t & 1));
+  bool alive = true;
+  for (int n = 0; n < nwin; ++n) {
+    const int st = n & 1;
+    unsigned char* sb = stages + st * kLtStageBytes;
+    if (alive) alive = warp_wait(&full[st], (n >> 1) & 1, abort_flag);
+    if (XBF16) {
+      // x narrowed to fp16 in place (each thread a share), then every warp reads it
+      if (alive) {
+        for (int k = tid; k < p.T * (kLtWinK / 8); k += kLtThreads) {
+          uint4* q = reinterpret_cast<uint4*>(sb + kLtXOff + (k >> 6) * kLtXStride + (k & 63) * 16);
+          uint4 v = *q;
+          v.x = lt_bf16x2_to_f16x2(v.x);
+          v.y = lt_bf16x2_to_f16x2(v.y);
+          v.z = lt_bf16x2_to_f16x2(v.z);
+          v.w = lt_bf16x2_to_f16x2(v.w);
+          *q = v;
+        }
+      }
+      __syncthreads();
+    }
+    if (alive) lt_window(smem, sb, warp, g, t, lane4, off, g < p.T, acc);
+    // the in-place narrowing's writes before the next copy into this stage
+    if (XBF16) asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[st]);
+    if (tid == 0 && n + kLtStages < nwin && !*abort_flag) {
+      // refill this stage once every warp has released it
+      if (mbar_wait(&empty[st], (n >> 1) & 1, abort_flag)) {
+        lt_issue(maps, p, sb, &full[st], w0 + n + kLtStages, rb);
+        sflags[1] = n + kLtStages + 1;
       }
     }
-  } else {
-    // -------------------------------------------------------- decode warps
-    // the replicated codebook: entry e for lane l at byte e * 256 + 4 l; codes >= K read zeros
-    for (int i = tid; i < 256 * 32; i += kLtConsumers) {
-      const int e = i >> 5;
-      const uint32_t v = e < p.K ? __ldg(p.codebook + e) : 0u;
-      *reinterpret_cast<uint32_t*>(smem + e * 256 + (i & 31) * 4) = v;
-    }
-    lt_consumer_sync();
-    const uint32_t lane4 = static_cast<uint32_t>(lane) * 4u;
-    uint32_t off[4];
+  }
+  if (p.S == 1) {
+    // rows kLtWarpRows warp + 16 j + g (+ 8), tokens 2t, 2t + 1
+    const int row0 = rb * kLtRows + warp * kLtWarpRows + g;
 #pragma unroll
-    for (int qq = 0; qq < 4; ++qq) off[qq] = ((static_cast<uint32_t>(2 * qq + (t >> 1)) ^ g) << 4) | (8u * (t & 1));
-    bool alive = true;
-    for (int w = w0, n = 0; w < w1; ++w, ++n) {
-      const int st = n & 1;
-      unsigned char* sb = stages + st * kLtStageBytes;
-      if (alive) alive = warp_wait(&full[st], (n >> 1) & 1, abort_flag);
-      if (XBF16) {
-        // x narrowed to fp16 in place (each consumer thread a share), then every warp reads it
-        if (alive) {
-          for (int k = tid; k < p.T * (kLtWinK / 8); k += kLtConsumers) {
-            uint4* q = reinterpret_cast<uint4*>(sb + kLtXOff + (k >> 6) * kLtXStride + (k & 63) * 16);
-            uint4 v = *q;
-            v.x = lt_bf16x2_to_f16x2(v.x);
-            v.y = lt_bf16x2_to_f16x2(v.y);
-            v.z = lt_bf16x2_to_f16x2(v.z);
-            v.w = lt_bf16x2_to_f16x2(v.w);
-            *q = v;
-          }
-        }
-        lt_consumer_sync();
+    for (int j = 0; j < kLtTiles; ++j)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int row = row0 + 16 * j + 8 * (e >> 1), tok = 2 * t + (e & 1);
+        if (row < p.OUT && tok < p.T)
+          store_y(p.y, static_cast<int64_t>(tok) * p.OUT + row, acc[j][e], p.y_dtype, false);
       }
-      if (alive) lt_window(smem, sb, warp, g, t, lane4, off, acc);
-      // the in-place narrowing's writes before the next copy into this stage
-      if (XBF16) asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&empty[st]);
-    }
-    if (p.S == 1) {
-      // rows 32 warp + 16 j + g (+ 8), tokens 2t, 2t + 1
-      const int row0 = rb * kLtRows + warp * 32 + g;
-#pragma unroll
-      for (int j = 0; j < 2; ++j)
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const int row = row0 + 16 * j + 8 * (e >> 1), tok = 2 * t + (e & 1);
-          if (row < p.OUT && tok < p.T)
-            store_y(p.y, static_cast<int64_t>(tok) * p.OUT + row, acc[j][e], p.y_dtype, false);
-        }
-    }
   }
   __syncthreads();
   if (tid == 0) {
     // copies still in flight (only after an expired wait) land before stage 0 is reused or the CTA exits
-    const int issued = *reinterpret_cast<volatile int*>(&sflags[1]);
+    const int issued = sflags[1];
     for (int k = issued > kLtStages ? issued - kLtStages : 0; k < issued; ++k) mbar_drain(&full[k & 1], (k >> 1) & 1);
     if (*abort_flag) p.status[1] = static_cast<int>(VQB_TIMEOUT);
   }
   if (p.S == 1) return;
-  __syncthreads();
-  // ---- split-K over the cluster: partial tiles [token][row] in stage 0
-  float* part = reinterpret_cast<float*>(stages);
-  if (warp < kLtWarps) {
+  // ---- split-K over the cluster: the owner of local row lr is rank lr / R
+  const int R = (kLtRows + p.S - 1) / p.S;
+  lt_cluster_wait();  // every peer has started: its shared memory may be written
 #pragma unroll
-    for (int j = 0; j < 2; ++j)
+  for (int j = 0; j < kLtTiles; ++j)
 #pragma unroll
-      for (int e = 0; e < 4; ++e)
-        part[(2 * t + (e & 1)) * kLtPartStride + warp * 32 + 16 * j + 8 * (e >> 1) + g] = acc[j][e];
-  }
+    for (int e = 0; e < 4; ++e) {
+      const int lr = warp * kLtWarpRows + 16 * j + 8 * (e >> 1) + g, tok = 2 * t + (e & 1);
+      if (tok < p.T) {
+        const int owner = lr / R;
+        lt_st_cluster(smem_u32(smem) + lt_recv_off((split * kLtTok + tok) * R + (lr - owner * R)),
+                      static_cast<uint32_t>(owner), acc[j][e]);
+      }
+    }
   lt_cluster_sync();
-  // rank `split` sums rows [r0, r1) of the row block over the S tiles in split order
-  const int r0 = split * kLtRows / p.S, r1 = (split + 1) * kLtRows / p.S, nr = r1 - r0;
+  // this rank's rows, summed over the S partials in split order
+  const int r0 = split * R, nr = (r0 + R < kLtRows ? R : kLtRows - r0);
   for (int k = tid; k < p.T * nr; k += kLtThreads) {
-    const int tok = k / nr, r = r0 + (k - tok * nr);
-    const int row = rb * kLtRows + r;
+    const int tok = k / nr, r = k - tok * nr;
+    const int row = rb * kLtRows + r0 + r;
     if (row < p.OUT) {
-      const float* src = part + tok * kLtPartStride + r;
-      float s = 0.0f;
-      for (int q = 0; q < p.S; ++q) s += lt_ld_cluster(src, static_cast<uint32_t>(q));
-      store_y(p.y, static_cast<int64_t>(tok) * p.OUT + row, s, p.y_dtype, false);
+      float sum = 0.0f;
+      for (int q = 0; q < p.S; ++q)
+        sum += *reinterpret_cast<const float*>(smem + lt_recv_off((q * kLtTok + tok) * R + r));
+      store_y(p.y, static_cast<int64_t>(tok) * p.OUT + row, sum, p.y_dtype, false);
     }
   }
-  // no CTA leaves while another still reads its tile
-  lt_cluster_sync();
 }
 
 }  // namespace
