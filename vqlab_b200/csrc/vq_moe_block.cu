@@ -140,18 +140,27 @@ constexpr int kStAbort = 0, kStChunks = 1, kStErr = 4, kStBarOk = 5, kStScan = 8
 // Split of a phase's windows: S pieces per (chunk, row block) minimising the
 // busiest CTA's windows (+ 1/8 window per item: its partial store), slots
 // S * P within the partial buffer.
-__host__ __device__ inline int mb_split(int nseg, int ng, int nw, int P) {
+__device__ __forceinline__ int mb_split(int nseg, int ng, int nw, int P) {
+  // lane S - 1 prices S (32-bit divisions: nseg * S stays far below 2^32), then
+  // the warp takes the smallest cost, the smaller S among equal costs; every
+  // lane of the calling warp gets the answer
   int smax = nw < kMbMaxSplit ? nw : kMbMaxSplit;
   const int cap = kMbSlotBudget / P > 1 ? kMbSlotBudget / P : 1;
   if (smax > cap) smax = cap;
-  int best = 1;
-  long long best_cost = -1;
-  for (int S = 1; S <= smax; ++S) {
-    const long long items = (static_cast<long long>(nseg) * S + ng - 1) / ng;
-    const long long cost = items * (8LL * ((nw + S - 1) / S) + 1);
-    if (best_cost < 0 || cost < best_cost) {
-      best_cost = cost;
-      best = S;
+  const int lane = static_cast<int>(threadIdx.x & 31u);
+  int best = lane + 1;
+  long long best_cost = 0x7fffffffffffffffLL;
+  if (best <= smax) {
+    const unsigned items = (static_cast<unsigned>(nseg) * static_cast<unsigned>(best) + static_cast<unsigned>(ng) - 1u) /
+                           static_cast<unsigned>(ng);
+    best_cost = static_cast<long long>(items) * (8LL * ((nw + best - 1) / best) + 1);
+  }
+  for (int o = 16; o; o >>= 1) {
+    const long long oc = __shfl_xor_sync(0xffffffffu, best_cost, o);
+    const int os = __shfl_xor_sync(0xffffffffu, best, o);
+    if (oc < best_cost || (oc == best_cost && os < best)) {
+      best_cost = oc;
+      best = os;
     }
   }
   return best;
@@ -184,7 +193,13 @@ __device__ bool mb_grid_barrier(bool wait, int* st) {
   if (threadIdx.x == 0) {
     __threadfence();
     const unsigned long long old = atomicAdd(&g_mb_arrivals, 1ull);
-    const unsigned long long target = (old / gridDim.x + 1ull) * gridDim.x;
+    // round = old / grid, through an fp64 quotient made exact (a 64-bit
+    // integer division is a long serial routine)
+    const unsigned long long grid = gridDim.x;
+    unsigned long long round = static_cast<unsigned long long>(static_cast<double>(old) / static_cast<double>(grid));
+    while (round * grid > old) --round;
+    while ((round + 1ull) * grid <= old) ++round;
+    const unsigned long long target = (round + 1ull) * grid;
     int ok = wait ? 1 : 0;
     if (wait) {
       const uint64_t t0 = global_ns();
@@ -624,10 +639,10 @@ __device__ void mb_route_tokens(const MbParams& prm, float* scr, int warp, int l
     }
   }
   // x -> fp16, 8 elements per thread-step (H is a multiple of 512)
-  const int64_t nv = static_cast<int64_t>(T) * prm.H / 8;
-  const int64_t per = (nv + nC - 1) / nC;
-  const int64_t v0 = static_cast<int64_t>(cta) * per, v1 = v0 + per < nv ? v0 + per : nv;
-  for (int64_t v = v0 + threadIdx.x; v < v1; v += blockDim.x) {
+  const int nv = T * prm.H / 8;  // the host keeps T * H below 2^31
+  const int per = (nv + nC - 1) / nC;
+  const int v0 = cta * per, v1 = v0 + per < nv ? v0 + per : nv;
+  for (int v = v0 + static_cast<int>(threadIdx.x); v < v1; v += static_cast<int>(blockDim.x)) {
     uint4 u = reinterpret_cast<const uint4*>(prm.x)[v];
     if (prm.x_bf16 && !prm.dense) {
       u.x = bf16x2_to_f16x2(u.x);
@@ -744,6 +759,18 @@ __device__ void mb_route(const MbParams& prm, unsigned char* scratch, float* wsm
   }
 }
 
+// SwiGLU of one element from its gate / up sums, stored as the down
+// projection's 16-bit input
+__device__ __forceinline__ void mb_store_h(const MbParams& prm, int64_t e, float gs, float us) {
+  const float hv = __fmul_rn(mb_silu(round_out(gs, prm.x_bf16, prm.dense)), round_out(us, prm.x_bf16, prm.dense));
+  if (prm.dense && prm.x_bf16) {
+    prm.h16[e] = __bfloat16_as_ushort(__float2bfloat16_rn(hv));  // the down layer's bf16 input
+  } else {
+    const float hd = prm.x_bf16 ? __bfloat162float(__float2bfloat16_rn(hv)) : __half2float(__float2half_rn(hv));
+    prm.h16[e] = __half_as_ushort(__float2half_rn(hd));
+  }
+}
+
 template <int BITS, bool WBF16>
 __global__ void __launch_bounds__(kMbThreads, 1) moe_block_kernel(const __grid_constant__ MbMaps maps,
                                                                    const __grid_constant__ MbParams prm) {
@@ -833,6 +860,32 @@ __global__ void __launch_bounds__(kMbThreads, 1) moe_block_kernel(const __grid_c
     const int64_t per = (n2 + nC - 1) / nC;
     const int64_t e0 = static_cast<int64_t>(cta) * per, e1 = e0 + per < n2 ? e0 + per : n2;
     const size_t gstride = static_cast<size_t>(S1) * P * I;  // one partial group
+    if (S1 == 1) {
+      // one split (the large batches): eight elements' partial loads in flight
+      // per thread before any store, then the same sums as below
+      constexpr int kB = 8;
+      for (int64_t eb = e0 + tid; eb < e1; eb += kB * kMbWarps * 32) {
+        float v[kB][4];
+#pragma unroll
+        for (int b = 0; b < kB; ++b) {
+          const int64_t e = eb + static_cast<int64_t>(b) * kMbWarps * 32;
+#pragma unroll
+          for (int q = 0; q < 4; ++q) v[b][q] = e < e1 ? __ldcg(prm.part1 + q * gstride + static_cast<size_t>(e)) : 0.0f;
+        }
+#pragma unroll
+        for (int b = 0; b < kB; ++b) {
+          const int64_t e = eb + static_cast<int64_t>(b) * kMbWarps * 32;
+          if (e < e1) {
+            float gs = 0.0f, us = 0.0f;
+            gs += v[b][0];
+            gs += v[b][1];
+            us += v[b][2];
+            us += v[b][3];
+            mb_store_h(prm, e, gs, us);
+          }
+        }
+      }
+    } else
 #pragma unroll 4
     for (int64_t e = e0 + tid; e < e1; e += kMbWarps * 32) {
       float v[4][kMbMaxSplit];
@@ -854,13 +907,7 @@ __global__ void __launch_bounds__(kMbThreads, 1) moe_block_kernel(const __grid_c
           us += v[3][s];
         }
       }
-      const float hv = __fmul_rn(mb_silu(round_out(gs, prm.x_bf16, prm.dense)), round_out(us, prm.x_bf16, prm.dense));
-      if (prm.dense && prm.x_bf16) {
-        prm.h16[e] = __bfloat16_as_ushort(__float2bfloat16_rn(hv));  // the down layer's bf16 input
-      } else {
-        const float hd = prm.x_bf16 ? __bfloat162float(__float2bfloat16_rn(hv)) : __half2float(__float2half_rn(hv));
-        prm.h16[e] = __half_as_ushort(__float2half_rn(hd));
-      }
+      mb_store_h(prm, e, gs, us);
     }
     asm volatile("fence.proxy.async.global;" ::: "memory");  // h16 is read by bulk copies after the barrier
   }
@@ -887,19 +934,52 @@ __global__ void __launch_bounds__(kMbThreads, 1) moe_block_kernel(const __grid_c
   // products in slot order.
   if (ok) {
     const int H = prm.H, k = prm.k;
-    const int64_t n4 = static_cast<int64_t>(prm.T) * H;
-    const int64_t per = (n4 + nC - 1) / nC;
-    const int64_t e0 = static_cast<int64_t>(cta) * per, e1 = e0 + per < n4 ? e0 + per : n4;
+    const int n4 = prm.T * H;  // below 2^31 (host check): 32-bit index math, no 64-bit divisions per product
+    const int per = (n4 + nC - 1) / nC;
+    const int e0 = cta * per, e1 = e0 + per < n4 ? e0 + per : n4;
     const size_t hstride = static_cast<size_t>(S3) * P * H;
     float* prod = reinterpret_cast<float*>(smem + L.codes[0]);
     const int cap = static_cast<int>((L.w - L.codes[0]) / (4u * static_cast<uint32_t>(k)));  // elements per pass
-    for (int64_t sub = e0; sub < e1; sub += cap) {
-      const int ne = static_cast<int>(e1 - sub < cap ? e1 - sub : cap);
+    for (int sub = e0; sub < e1; sub += cap) {
+      const int ne = e1 - sub < cap ? e1 - sub : cap;
+      if (S3 == 1) {
+        // one split (the large batches): eight products' partial loads in
+        // flight per thread before any store, then the same sums as below
+        constexpr int kB = 8;
+        for (int qb = tid; qb < ne * k; qb += kB * kMbThreads) {
+          float v[kB][2];
+#pragma unroll
+          for (int b = 0; b < kB; ++b) {
+            const int q = qb + b * kMbThreads;
+            v[b][0] = v[b][1] = 0.0f;
+            if (q < ne * k) {
+              const int j = q / ne, el = q - j * ne;
+              const int e = sub + el;
+              const int t = e / H, r = e - t * H;
+              const size_t o = static_cast<size_t>(t * k + j) * H + r;
+              v[b][0] = __ldcg(prm.part3 + o);
+              v[b][1] = __ldcg(prm.part3 + hstride + o);
+            }
+          }
+#pragma unroll
+          for (int b = 0; b < kB; ++b) {
+            const int q = qb + b * kMbThreads;
+            if (q < ne * k) {
+              const int j = q / ne, el = q - j * ne;
+              const int t = (sub + el) / H;
+              float ds = 0.0f;
+              ds += v[b][0];
+              ds += v[b][1];
+              prod[el * k + j] = __fmul_rn(round_out(ds, prm.x_bf16, prm.dense), wsm[t * k + j]);
+            }
+          }
+        }
+      } else
 #pragma unroll 4
       for (int q = tid; q < ne * k; q += kMbThreads) {
         const int j = q / ne, el = q - j * ne;
-        const int64_t e = sub + el;
-        const int t = static_cast<int>(e / H), r = static_cast<int>(e - static_cast<int64_t>(t) * H);
+        const int e = sub + el;
+        const int t = e / H, r = e - t * H;
         float v[2 * kMbMaxSplit];
 #pragma unroll
         for (int s = 0; s < kMbMaxSplit; ++s) {
@@ -923,7 +1003,7 @@ __global__ void __launch_bounds__(kMbThreads, 1) moe_block_kernel(const __grid_c
       for (int el = tid; el < ne; el += kMbThreads) {
         float acc = 0.0f;
         for (int j = 0; j < k; ++j) acc = __fadd_rn(acc, prod[el * k + j]);
-        const int64_t e = sub + el;
+        const int e = sub + el;
         if (prm.x_bf16) reinterpret_cast<__nv_bfloat16*>(prm.y)[e] = __float2bfloat16_rn(acc);
         else reinterpret_cast<__half*>(prm.y)[e] = __float2half_rn(acc);
       }
@@ -955,6 +1035,7 @@ vqb_status mb_check_common(const vqb_linear_desc* const ds[3], int T, int x_dtyp
   if (x_dtype != VQB_BF16 && x_dtype != VQB_F16) return VQB_UNSUPPORTED_GEOMETRY;
   if (g->E > kMbMaxExperts || static_cast<int64_t>(T) * g->k > kMbMaxPairs) return VQB_UNSUPPORTED_GEOMETRY;
   if (g->H % kMbWinK != 0 || g->I % kMbWinK != 0) return VQB_UNSUPPORTED_GEOMETRY;
+  if (static_cast<int64_t>(T) * g->H > 0x7fffffff) return VQB_UNSUPPORTED_GEOMETRY;  // 32-bit element indices
   if (g->bits != 12 && g->bits != 14) return VQB_UNSUPPORTED_GEOMETRY;
   for (int i = 0; i < 3; ++i) {
     const LinearGeometry& q = g->p[i];
