@@ -397,7 +397,9 @@ vqb_status vqb_ep_reduce(const vqb_ep_layout* layout, void* region, void* y, vqb
 uint64_t vqb_launch_count(void);
 vqb_status vqb_time_next_kernel(void* start_event, void* stop_event);
 
-/* Scratch bytes vqb_dense_forward needs for n_rows input rows. */
+/* Scratch bytes vqb_dense_forward needs for n_rows input rows.  The first 16
+ * bytes of the workspace are a status block the call rewrites: int32 [1] is
+ * VQB_TIMEOUT when a bounded device wait of the call gave up, else 0. */
 size_t vqb_dense_workspace_size(const vqb_linear_desc* desc, int64_t n_rows, const vqb_options* opts);
 
 /* y[n, :] = W x[n, :] for a dense VQ projection (E = 1).
@@ -405,7 +407,10 @@ size_t vqb_dense_workspace_size(const vqb_linear_desc* desc, int64_t n_rows, con
  * small-N fused kernel narrows x to fp16 in-kernel and stores y_dtype
  * directly (vq_switch.py:2319-2327); the large-N path materialises
  * W = fp16(cb*s) in x's dtype tile by tile and runs the GEMM
- * (_decode_matmul, vq_dense.py:267-312). */
+ * (_decode_matmul, vq_dense.py:267-312).  Under VQB_PATH_AUTO a d2 layer with
+ * <= 256 codebook entries stored as 8-bit codes (IN a multiple of 512, group
+ * 64, 16-byte aligned x / codes / scales) at <= 8 rows runs as one launch with
+ * the codebook replicated per lane in shared memory; same numerics. */
 vqb_status vqb_dense_forward(const vqb_linear_desc* desc, const void* x, vqb_dtype x_dtype,
                              int64_t n_rows, void* y, vqb_dtype y_dtype,
                              void* workspace, size_t workspace_bytes,
