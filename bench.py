@@ -452,8 +452,9 @@ def c1_leg(torch, dev, args, peak_gbs, peak_kind):
             "us_per_call": round(per_call * 1e6, 2), "calls_per_s": round(1.0 / per_call, 1),
             "packed_weight_gbs": round(byt / per_call / 1e9, 1),
             "roofline": {"bound": "hbm", "achieved": round(ach, 1), "peak": peak_gbs, "unit": "GB/s",
-                         "frac": round(ach / peak_gbs, 4), "traffic": profiled_traffic("vq_decode_mma_kernel", "c1"),
-                         "kernel": "vq_decode_mma_kernel (bf16 weights, whole codebook in shared memory), timed alone",
+                         "frac": round(ach / peak_gbs, 4), "traffic": profiled_traffic("dense_lut8_kernel", "c1"),
+                         "kernel": "dense_lut8_kernel (bf16 weights, whole codebook in shared memory, one launch), "
+                                   "timed alone",
                          "algorithmic_bytes_per_launch": byt, "us_per_launch": round(dur * 1e6, 2),
                          "peak_kind": f"{peak_kind} burst copy bandwidth"}}
 

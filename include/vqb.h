@@ -410,7 +410,9 @@ size_t vqb_dense_workspace_size(const vqb_linear_desc* desc, int64_t n_rows, con
  * (_decode_matmul, vq_dense.py:267-312).  Under VQB_PATH_AUTO a d2 layer with
  * <= 256 codebook entries stored as 8-bit codes (IN a multiple of 512, group
  * 64, 16-byte aligned x / codes / scales) at <= 8 rows runs as one launch with
- * the codebook replicated per lane in shared memory; same numerics. */
+ * the codebook replicated per lane in shared memory, and a d8 layer with
+ * <= 4096 entries and an even code width likewise with the codebook whole in
+ * shared memory; same numerics. */
 vqb_status vqb_dense_forward(const vqb_linear_desc* desc, const void* x, vqb_dtype x_dtype,
                              int64_t n_rows, void* y, vqb_dtype y_dtype,
                              void* workspace, size_t workspace_bytes,

@@ -1,4 +1,4 @@
-"""The small-codebook dense kernel (dense_lut_kernel: d2, K <= 256, 8-bit
+"""The small-codebook dense kernels: dense_lut_kernel (d2, K <= 256, 8-bit
 codes, up to 8 rows -- the attention projections of benchmark configuration C4)
 against the oracle's fused dense arm (vq_switch.py:2319-2327 restated by
 oracle.switch_fused: x narrowed to fp16, fp32 group partials times the
@@ -144,4 +144,75 @@ def test_lut_agrees_with_the_grouped_decode_kernel():
     xb = _x(np.random.default_rng(14), 6, 4096, torch.bfloat16).cuda()
     ya = a(xb).float().cpu().numpy()
     yb = b(xb).float().cpu().numpy()
+    assert np.all(np.abs(ya - yb) <= 4e-3 * np.abs(yb).max() + 2 * bf16_ulp(yb))
+
+
+# ------------------------------------------------------------------ d8 variant
+# dense_lut8_kernel: a d8 codebook of <= 4096 entries (C1: 4096 x 4096, K4096,
+# 12-bit) at <= 8 rows, in the _decode_matmul arithmetic (vq_dense.py:267-312
+# restated by oracle.dense_decode_matmul: W = fp16(cb * s), bf16 for bf16 x,
+# fp32 accumulation, one rounding).  Same tolerance as above.
+
+def _ref8(L, xv, bf16):
+    return orc.dense_decode_matmul(L.codes[0], L.cb_bits, L.sc_bits[0], xv, wbf16=bf16)
+
+
+@pytest.mark.parametrize("OUT,IN,K,n", [(4096, 4096, 4096, 1), (4096, 4096, 4096, 3), (4096, 4096, 4096, 8),
+                                        (1000, 2048, 4096, 2), (512, 512, 4096, 5), (768, 1536, 1000, 4),
+                                        (2048, 1024, 256, 7)])
+def test_lut8_matches_oracle_bf16(OUT, IN, K, n):
+    """C1's matvec at one, three and eight rows; a ragged last row block; one
+    window per row (no split); 10-bit and 8-bit codebooks."""
+    L = make_layer(E=1, OUT=OUT, IN=IN, D=8, K=K, G=64, seed=OUT + IN + K + n)
+    lin = _lin(L)
+    xb = _x(np.random.default_rng(n + 3), n, IN, torch.bfloat16)
+    lin(xb.cuda())  # a d8 module's first call also builds its codebook halves (one more launch)
+    torch.cuda.synchronize()
+    n0 = _lib.launch_count()
+    y = lin(xb.cuda())
+    torch.cuda.synchronize()
+    assert _lib.launch_count() - n0 == 1, "one launch: no routing step"
+    ref = orc.round_bf16(_ref8(L, xb.float().numpy(), True))
+    assert within_tol_bf16(ref, y.float().cpu().numpy())
+
+
+@pytest.mark.parametrize("ydt", [torch.float16, torch.float32])
+def test_lut8_fp16_x_and_output_dtypes(ydt):
+    L = make_layer(E=1, OUT=1024, IN=2048, D=8, K=4096, G=64, seed=21)
+    lin = _lin(L)
+    x = _x(np.random.default_rng(22), 6, 2048, torch.float16)
+    y = lin(x.cuda(), out_dtype=ydt).float().cpu().numpy()
+    ref = _ref8(L, x.float().numpy(), False)
+    if ydt == torch.float32:
+        assert max_rel(ref, y) <= 2e-3
+    else:
+        r16 = orc.round_f16(ref)
+        assert np.all(np.abs(y - r16) <= 2e-3 * np.abs(r16).max() + _ulp16(r16))
+
+
+def test_lut8_repeatable_graph_replay_and_decode_path():
+    """Repeated calls and graph replays give the same bytes; the explicit
+    decode path (routing step + grouped MMA kernel) agrees within two output
+    roundings."""
+    from vqlab_b200.vq_switch import make_options
+    L = make_layer(E=1, OUT=4096, IN=4096, D=8, K=4096, G=64, seed=23)
+    lin = _lin(L)
+    x = _x(np.random.default_rng(24), 2, 4096, torch.bfloat16).cuda()
+    y0 = lin(x)
+    assert torch.equal(y0.view(torch.int16), lin(x).view(torch.int16))
+    out = torch.empty_like(y0)
+    lin(x, out=out)
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        lin(x, out=out)
+    for _ in range(3):
+        out.zero_()
+        g.replay()
+        torch.cuda.synchronize()
+        assert torch.equal(out.view(torch.int16), y0.view(torch.int16))
+    del g
+    b = _lin(L)
+    b.options = make_options(path=_lib.PATH_DECODE)
+    ya, yb = y0.float().cpu().numpy(), b(x).float().cpu().numpy()
     assert np.all(np.abs(ya - yb) <= 4e-3 * np.abs(yb).max() + 2 * bf16_ulp(yb))

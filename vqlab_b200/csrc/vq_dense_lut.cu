@@ -357,6 +357,254 @@ __global__ void __launch_bounds__(kLtThreads, 1) dense_lut_kernel(const __grid_c
   }
 }
 
+// ============================================================================
+// d8 variant: a dense d8 projection whose whole codebook fits shared memory
+// (K <= 4096 entries of 8 fp16 = 64 KB; benchmark configuration C1:
+// 4096 x 4096, K4096, 12-bit codes) at up to 8 rows, in the reference's
+// _decode_matmul arithmetic (vq_dense.py:267-312): W = fp16(cb * s), then bf16
+// for bf16 x; x as it is; fp32 accumulation; y rounded once.
+//   * the codebook (plus a zero entry at index K: codes >= K read zeros) is
+//     copied whole into shared memory; a lookup is one 16-byte read;
+//   * a window's codes are 64 codes x bits of each of 256 rows (8 * bits bytes
+//     per row, one TMA box, even bits only so a row is whole 16-byte units);
+//   * inside a 64-input group thread t of a quad owns inputs 16t .. 16t+15,
+//     i.e. codes 2t and 2t+1 (one funnel shift of two words holds both), and
+//     MMA step m takes inputs 16t+4m .. 16t+4m+3 (a permutation of k applied
+//     to A and B alike); W is prescaled per element (HMUL2 by the row's group
+//     scale) and accumulated by the MMA directly;
+//   * work split, copies, bounded waits, cluster split-K and the status word
+//     as in the d2 kernel above.
+constexpr int kL8MaxK = 4096;
+constexpr uint32_t kL8RecvBytes = 8448;  // [split][token][owned row] floats: S x 8 x ceil(256 / S) <= 2080
+constexpr uint32_t kL8ScaleOff(int bits) { return 256u * 8u * static_cast<uint32_t>(bits); }
+constexpr uint32_t kL8XOff(int bits) { return kL8ScaleOff(bits) + 16u * kLtRows; }
+constexpr uint32_t kL8StageBytes(int bits) { return (kL8XOff(bits) + kLtTok * kLtXStride + 1023u) & ~1023u; }
+
+struct L8Params {
+  const uint4* codebook;  // [K] entries of eight fp16
+  int K, bits;
+  const void* x;          // [T][IN] fp16 / bf16
+  void* y;                // [T][OUT]
+  int y_dtype;
+  int T, OUT, IN;
+  int S, nw;
+  uint32_t table_bytes;   // (K + 1) * 16 rounded up to 1024
+  uint32_t stage_bytes;
+  int* status;
+};
+
+__device__ __forceinline__ uint32_t l8_scale_word(uint32_t w, uint32_t s2, bool bf16) {
+  __half2 h = __hmul2(*reinterpret_cast<const __half2*>(&w), *reinterpret_cast<const __half2*>(&s2));
+  uint32_t r = *reinterpret_cast<uint32_t*>(&h);
+  if (bf16) {
+    const float2 f = __half22float2(h);
+    __nv_bfloat162 b = __floats2bfloat162_rn(f.x, f.y);
+    r = *reinterpret_cast<uint32_t*>(&b);
+  }
+  return r;
+}
+
+__device__ __forceinline__ void l8_mma(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1, bool bf16) {
+  if (bf16)
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};\n"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+  else
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};\n"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+// One staged window for one warp: rows 16 warp + g and + 8, tokens 2t, 2t + 1.
+template <bool XBF16>
+__device__ __forceinline__ void l8_window(const unsigned char* table, const unsigned char* sb, const L8Params& p,
+                                          int warp, int g, int t, bool has_x, float (&acc)[4]) {
+  const int bits = p.bits;
+  const uint32_t mask = (1u << bits) - 1u;
+  const int rw = 2 * bits;  // code words per row
+  const uint32_t* crow0 = reinterpret_cast<const uint32_t*>(sb) + (warp * 16 + g) * rw;
+  const uint32_t* crow1 = crow0 + 8 * rw;
+  const uint32_t kmax = static_cast<uint32_t>(p.K);
+  const uint4 sc0 = *reinterpret_cast<const uint4*>(sb + kL8ScaleOff(bits) + (warp * 16 + g) * 16);
+  const uint4 sc1 = *reinterpret_cast<const uint4*>(sb + kL8ScaleOff(bits) + (warp * 16 + g + 8) * 16);
+  const unsigned char* xb = sb + kL8XOff(bits) + g * kLtXStride + 32 * t;
+  const int tb = 2 * t * bits;  // bit offset of code 2t inside a group's 8 codes
+#pragma unroll
+  for (int q = 0; q < 8; ++q) {
+    const int b0 = 8 * q * bits + tb;
+    const int wi = b0 >> 5, sh = b0 & 31;
+    const uint32_t v0 = __funnelshift_r(crow0[wi], crow0[wi + 1], sh);
+    const uint32_t v1 = __funnelshift_r(crow1[wi], crow1[wi + 1], sh);
+    const uint32_t c00 = min(v0 & mask, kmax), c01 = min((v0 >> bits) & mask, kmax);
+    const uint32_t c10 = min(v1 & mask, kmax), c11 = min((v1 >> bits) & mask, kmax);
+    const uint4 e00 = *reinterpret_cast<const uint4*>(table + c00 * 16u);
+    const uint4 e01 = *reinterpret_cast<const uint4*>(table + c01 * 16u);
+    const uint4 e10 = *reinterpret_cast<const uint4*>(table + c10 * 16u);
+    const uint4 e11 = *reinterpret_cast<const uint4*>(table + c11 * 16u);
+    uint4 xv0 = make_uint4(0u, 0u, 0u, 0u), xv1 = xv0;
+    if (has_x) {
+      xv0 = *reinterpret_cast<const uint4*>(xb + 128 * q);
+      xv1 = *reinterpret_cast<const uint4*>(xb + 128 * q + 16);
+    }
+    // the rows' group-q scales as fp16 pairs
+    const uint32_t p0 = (q >> 1) == 0 ? sc0.x : ((q >> 1) == 1 ? sc0.y : ((q >> 1) == 2 ? sc0.z : sc0.w));
+    const uint32_t p1 = (q >> 1) == 0 ? sc1.x : ((q >> 1) == 1 ? sc1.y : ((q >> 1) == 2 ? sc1.z : sc1.w));
+    const uint32_t h0 = (q & 1) ? (p0 >> 16) : (p0 & 0xFFFFu), h1 = (q & 1) ? (p1 >> 16) : (p1 & 0xFFFFu);
+    const uint32_t s0 = h0 | (h0 << 16), s1 = h1 | (h1 << 16);
+#pragma unroll
+    for (int m = 0; m < 4; ++m) {
+      // step m: code 2t (m < 2) or 2t + 1, dimensions 4 (m & 1) .. + 3
+      const uint4& r0 = m < 2 ? e00 : e01;
+      const uint4& r1 = m < 2 ? e10 : e11;
+      uint32_t a[4];
+      a[0] = l8_scale_word((m & 1) ? r0.z : r0.x, s0, XBF16);
+      a[2] = l8_scale_word((m & 1) ? r0.w : r0.y, s0, XBF16);
+      a[1] = l8_scale_word((m & 1) ? r1.z : r1.x, s1, XBF16);
+      a[3] = l8_scale_word((m & 1) ? r1.w : r1.y, s1, XBF16);
+      const uint32_t bb0 = m == 0 ? xv0.x : (m == 1 ? xv0.z : (m == 2 ? xv1.x : xv1.z));
+      const uint32_t bb1 = m == 0 ? xv0.y : (m == 1 ? xv0.w : (m == 2 ? xv1.y : xv1.w));
+      l8_mma(acc, a, bb0, bb1, XBF16);
+    }
+  }
+}
+
+template <bool XBF16>
+__global__ void __launch_bounds__(kLtThreads, 1) dense_lut8_kernel(const __grid_constant__ LtMaps maps,
+                                                                   const __grid_constant__ L8Params p) {
+  extern __shared__ __align__(16) unsigned char smem[];
+  // [table (K + 1 entries)][recv][pad to 1024][stages][barriers]
+  float* recv = reinterpret_cast<float*>(smem + p.table_bytes);
+  const uint32_t pre = p.table_bytes + kL8RecvBytes;
+  unsigned char* stages = smem + pre + ((1024u - ((smem_u32(smem) + pre) & 1023u)) & 1023u);
+  uint64_t* full = reinterpret_cast<uint64_t*>(stages + kLtStages * p.stage_bytes);
+  uint64_t* empty = full + kLtStages;
+  uint64_t* tbar = empty + kLtStages;
+  int* sflags = reinterpret_cast<int*>(tbar + 1);  // [0] abort, [1] windows issued
+  volatile int* abort_flag = sflags;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, tid = threadIdx.x;
+  const int rb = blockIdx.x / p.S, split = blockIdx.x - rb * p.S;
+  const int w0 = split * p.nw / p.S, w1 = (split + 1) * p.nw / p.S, nwin = w1 - w0;
+  const int rw = 2 * p.bits;  // code words of a row per window
+
+  if (tid == 0) {
+    for (int s = 0; s < kLtStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], kLtWarps);
+    }
+    mbar_init(tbar, 1);
+    sflags[0] = 0;
+    sflags[1] = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    // this CTA's windows into L2 while the previous kernel finishes (a
+    // prefetch returns no data, so it cannot observe a stale value)
+    for (int w = w0; w < w1; ++w) {
+      lt_prefetch_2d(&maps.codes, w * rw, rb * kLtRows);
+      lt_prefetch_2d(&maps.scales, w * 8, rb * kLtRows);
+    }
+    // the zero entry at index K
+    *reinterpret_cast<uint4*>(smem + static_cast<uint32_t>(p.K) * 16u) = make_uint4(0u, 0u, 0u, 0u);
+  }
+  // the codebook's 128-byte lines into L2, one per thread
+  for (int b = tid * 128; b < p.K * 16; b += kLtThreads * 128)
+    asm volatile("prefetch.global.L2 [%0];" :: "l"(reinterpret_cast<const char*>(p.codebook) + b));
+  {
+    const int per = (kLtTok - p.T) * (kLtXStride / 16);
+    for (int i = tid; i < kLtStages * per; i += kLtThreads) {
+      const int s = i / per, r = i - s * per;
+      *reinterpret_cast<uint4*>(stages + s * p.stage_bytes + kL8XOff(p.bits) + p.T * kLtXStride + r * 16) =
+          make_uint4(0u, 0u, 0u, 0u);
+    }
+  }
+  __syncthreads();
+  if (p.S > 1) lt_cluster_arrive_relaxed();
+  pdl_wait();
+  pdl_trigger();
+  const unsigned char* xg = static_cast<const unsigned char*>(p.x);
+  const uint32_t tx = static_cast<uint32_t>(kLtRows) * 8u * static_cast<uint32_t>(p.bits) + 16u * kLtRows +
+                      static_cast<uint32_t>(p.T) * kLtWinK * 2u;
+  auto issue = [&](int n) {
+    unsigned char* sb = stages + (n & 1) * p.stage_bytes;
+    const int w = w0 + n;
+    mbar_expect_tx(&full[n & 1], tx);
+    tma_load_2d(&maps.codes, &full[n & 1], sb, w * rw, rb * kLtRows);
+    tma_load_2d(&maps.scales, &full[n & 1], sb + kL8ScaleOff(p.bits), w * 8, rb * kLtRows);
+    for (int j = 0; j < p.T; ++j)
+      bulk_load(sb + kL8XOff(p.bits) + j * kLtXStride,
+                xg + (static_cast<size_t>(j) * p.IN + static_cast<size_t>(w) * kLtWinK) * 2, kLtWinK * 2, &full[n & 1]);
+  };
+  if (tid == 0) {
+    if (blockIdx.x == 0) p.status[1] = 0;
+    // the codebook, whole (16-byte pieces of up to 16 KB)
+    const uint32_t cbytes = static_cast<uint32_t>(p.K) * 16u;
+    mbar_expect_tx(tbar, cbytes);
+    for (uint32_t off = 0; off < cbytes; off += 16384u)
+      bulk_load(smem + off, reinterpret_cast<const unsigned char*>(p.codebook) + off,
+                cbytes - off < 16384u ? cbytes - off : 16384u, tbar);
+    for (int n = 0; n < kLtStages && n < nwin; ++n) issue(n);
+    sflags[1] = nwin < kLtStages ? nwin : kLtStages;
+  }
+  __syncthreads();
+
+  float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+  const int g = lane >> 2, t = lane & 3;
+  bool alive = warp_wait(tbar, 0, abort_flag);
+  for (int n = 0; n < nwin; ++n) {
+    const int st = n & 1;
+    const unsigned char* sb = stages + st * p.stage_bytes;
+    if (alive) alive = warp_wait(&full[st], (n >> 1) & 1, abort_flag);
+    if (alive) l8_window<XBF16>(smem, sb, p, warp, g, t, g < p.T, acc);
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[st]);
+    if (tid == 0 && n + kLtStages < nwin && !*abort_flag) {
+      if (mbar_wait(&empty[st], (n >> 1) & 1, abort_flag)) {
+        issue(n + kLtStages);
+        sflags[1] = n + kLtStages + 1;
+      }
+    }
+  }
+  if (p.S == 1) {
+    const int row0 = rb * kLtRows + warp * 16 + g;
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const int row = row0 + 8 * (e >> 1), tok = 2 * t + (e & 1);
+      if (row < p.OUT && tok < p.T) store_y(p.y, static_cast<int64_t>(tok) * p.OUT + row, acc[e], p.y_dtype, false);
+    }
+  }
+  __syncthreads();
+  if (tid == 0) {
+    const int issued = sflags[1];
+    for (int k = issued > kLtStages ? issued - kLtStages : 0; k < issued; ++k) mbar_drain(&full[k & 1], (k >> 1) & 1);
+    mbar_drain(tbar, 0);
+    if (*abort_flag) p.status[1] = static_cast<int>(VQB_TIMEOUT);
+  }
+  if (p.S == 1) return;
+  // ---- split-K over the cluster: the owner of local row lr is rank lr / R
+  const int R = (kLtRows + p.S - 1) / p.S;
+  lt_cluster_wait();
+#pragma unroll
+  for (int e = 0; e < 4; ++e) {
+    const int lr = warp * 16 + 8 * (e >> 1) + g, tok = 2 * t + (e & 1);
+    if (tok < p.T) {
+      const int owner = lr / R;
+      lt_st_cluster(smem_u32(recv + (split * kLtTok + tok) * R + (lr - owner * R)), static_cast<uint32_t>(owner),
+                    acc[e]);
+    }
+  }
+  lt_cluster_sync();
+  const int r0 = split * R, nr = (r0 + R < kLtRows ? R : kLtRows - r0);
+  for (int k = tid; k < p.T * nr; k += kLtThreads) {
+    const int tok = k / nr, r = k - tok * nr;
+    const int row = rb * kLtRows + r0 + r;
+    if (row < p.OUT) {
+      float sum = 0.0f;
+      for (int q = 0; q < p.S; ++q) sum += recv[(q * kLtTok + tok) * R + r];
+      store_y(p.y, static_cast<int64_t>(tok) * p.OUT + row, sum, p.y_dtype, false);
+    }
+  }
+}
+
 }  // namespace
 
 // ------------------------------------------------------------------ host
@@ -464,6 +712,100 @@ vqb_status launch_dense_lut(const LinearGeometry& g, const void* x, int x_dtype,
   cfg.gridDim = dim3(static_cast<unsigned>(nrb * best));
   cfg.blockDim = dim3(kLtThreads);
   cfg.dynamicSmemBytes = kLtSmem;
+  cfg.stream = stream;
+  cfg.attrs = attr;
+  cfg.numAttrs = best > 1 ? 2 : 1;
+  timer_before(stream);
+  const cudaError_t ce = cudaLaunchKernelEx(&cfg, kern, maps, p);
+  timer_after(stream);
+  if (ce != cudaSuccess) return VQB_CUDA_ERROR;
+  note_launch();
+  return VQB_OK;
+}
+
+// ------------------------------------------------------------- host: d8
+
+bool dense_lut8_eligible(const LinearGeometry& g, const void* x, int x_dtype, int T) {
+  const auto a16 = [](const void* q) { return (reinterpret_cast<uintptr_t>(q) & 15) == 0; };
+  return g.E == 1 && g.row_table == nullptr && g.D == 8 && g.K >= 1 && g.K <= kL8MaxK && g.bits >= 2 &&
+         g.bits <= 16 && (g.bits & 1) == 0 && g.K <= (1 << g.bits) && g.G == 64 && g.OUT >= 1 && g.IN >= kLtWinK &&
+         g.IN % kLtWinK == 0 && g.row_words == g.IN / 256 * g.bits && T >= 1 && T <= kLtTok &&
+         (x_dtype == VQB_F16 || x_dtype == VQB_BF16) && a16(x) && a16(g.codes) && a16(g.scales) && a16(g.codebook);
+}
+
+vqb_status launch_dense_lut8(const LinearGeometry& g, const void* x, int x_dtype, int T, void* y, int y_dtype,
+                             int* status, cudaStream_t stream) {
+  DeviceInfo di;
+  if (device_info(&di) != VQB_OK) return VQB_CUDA_ERROR;
+  EncodeTiledFn enc = encode_fn();
+  if (!enc) return VQB_CUDA_ERROR;
+  LtMaps maps;
+  if (!encode_2d(enc, &maps.codes, CU_TENSOR_MAP_DATA_TYPE_UINT32, 4, g.codes, static_cast<uint64_t>(g.row_words),
+                 static_cast<uint64_t>(g.OUT), static_cast<uint32_t>(2 * g.bits), kLtRows, CU_TENSOR_MAP_SWIZZLE_NONE) ||
+      !encode_2d(enc, &maps.scales, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, g.scales, static_cast<uint64_t>(g.IN / 64),
+                 static_cast<uint64_t>(g.OUT), kLtWinK / 64, kLtRows, CU_TENSOR_MAP_SWIZZLE_NONE))
+    return VQB_CUDA_ERROR;
+  L8Params p{};
+  p.codebook = static_cast<const uint4*>(g.codebook);
+  p.K = g.K;
+  p.bits = g.bits;
+  p.x = x;
+  p.y = y;
+  p.y_dtype = y_dtype;
+  p.T = T;
+  p.OUT = g.OUT;
+  p.IN = g.IN;
+  p.nw = g.IN / kLtWinK;
+  p.status = status;
+  p.table_bytes = (static_cast<uint32_t>(g.K + 1) * 16u + 1023u) & ~1023u;
+  p.stage_bytes = kL8StageBytes(g.bits);
+  const uint32_t smem = p.table_bytes + kL8RecvBytes + 1024u + kLtStages * p.stage_bytes + 64u;
+  if (smem > static_cast<uint32_t>(di.smem_optin)) return VQB_UNSUPPORTED_GEOMETRY;
+  void (*kern)(LtMaps, L8Params) = x_dtype == VQB_BF16 ? dense_lut8_kernel<true> : dense_lut8_kernel<false>;
+  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)) != cudaSuccess)
+    return VQB_CUDA_ERROR;
+  const int nrb = (g.OUT + kLtRows - 1) / kLtRows;
+  const int smax = p.nw < kLtMaxSplit ? p.nw : kLtMaxSplit;
+  int best = 1;
+  int64_t best_cost = INT64_MAX;
+  for (int S = 1; S <= smax; ++S) {
+    int cap = di.sms;
+    if (S > 1) {
+      cudaLaunchConfig_t cfg = {};
+      cfg.gridDim = dim3(static_cast<unsigned>(S * di.sms));
+      cfg.blockDim = dim3(kLtThreads);
+      cfg.dynamicSmemBytes = smem;
+      cudaLaunchAttribute attr[1];
+      attr[0].id = cudaLaunchAttributeClusterDimension;
+      attr[0].val.clusterDim.x = static_cast<unsigned>(S);
+      attr[0].val.clusterDim.y = 1;
+      attr[0].val.clusterDim.z = 1;
+      cfg.attrs = attr;
+      cfg.numAttrs = 1;
+      if (cudaOccupancyMaxActiveClusters(&cap, kern, &cfg) != cudaSuccess) {
+        cudaGetLastError();
+        cap = 0;
+      }
+    }
+    if (cap <= 0) continue;
+    const int64_t cost = ((nrb + cap - 1) / cap) * ((p.nw + S - 1) / S);
+    if (cost < best_cost) {
+      best_cost = cost;
+      best = S;
+    }
+  }
+  p.S = best;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  attr[1].id = cudaLaunchAttributeClusterDimension;
+  attr[1].val.clusterDim.x = static_cast<unsigned>(best);
+  attr[1].val.clusterDim.y = 1;
+  attr[1].val.clusterDim.z = 1;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(nrb * best));
+  cfg.blockDim = dim3(kLtThreads);
+  cfg.dynamicSmemBytes = smem;
   cfg.stream = stream;
   cfg.attrs = attr;
   cfg.numAttrs = best > 1 ? 2 : 1;

@@ -361,6 +361,12 @@ vqb_status vqb_dense_forward(const vqb_linear_desc* desc, const void* x, vqb_dty
       (reinterpret_cast<uintptr_t>(workspace) & 3) == 0 && dense_lut_eligible(geo, x, x_dtype, n))
     return launch_dense_lut(geo, x, x_dtype, n, y, y_dtype, static_cast<int*>(workspace),
                             reinterpret_cast<cudaStream_t>(stream));
+  // a d8 codebook of <= 4096 entries at <= 8 rows (C1's matvec): the same
+  // structure with the whole codebook resident, _decode_matmul arithmetic
+  if (!fused && path == VQB_PATH_AUTO && n <= 8 && !(opts && (opts->decode_variant != 0 || opts->k_split != 0)) &&
+      (reinterpret_cast<uintptr_t>(workspace) & 3) == 0 && dense_lut8_eligible(geo, x, x_dtype, n))
+    return launch_dense_lut8(geo, x, x_dtype, n, y, y_dtype, static_cast<int*>(workspace),
+                             reinterpret_cast<cudaStream_t>(stream));
   return run_linear(geo, x, x_dtype, n, nullptr, 1, n, y, y_dtype, workspace, opts, /*narrow_x_f16=*/fused,
                     /*round_f16_first=*/false, wround, large, reinterpret_cast<cudaStream_t>(stream));
 }

@@ -79,6 +79,11 @@ bool dense_lut_geometry(const LinearGeometry& g);
 bool dense_lut_eligible(const LinearGeometry& g, const void* x, int x_dtype, int T);
 vqb_status launch_dense_lut(const LinearGeometry& g, const void* x, int x_dtype, int T, void* y, int y_dtype,
                             int* status, cudaStream_t stream);
+// The d8 variant (_decode_matmul arithmetic): K <= 4096, even bits, group 64,
+// IN a multiple of 512, up to 8 rows, fp16/bf16 x.
+bool dense_lut8_eligible(const LinearGeometry& g, const void* x, int x_dtype, int T);
+vqb_status launch_dense_lut8(const LinearGeometry& g, const void* x, int x_dtype, int T, void* y, int y_dtype,
+                             int* status, cudaStream_t stream);
 
 // Grouped tcgen05 GEMM for large token counts (vq_prefill_tc.cu).
 bool tc_prefill_supported(const LinearGeometry& geo);
