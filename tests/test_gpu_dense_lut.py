@@ -159,10 +159,12 @@ def _ref8(L, xv, bf16):
 
 @pytest.mark.parametrize("OUT,IN,K,n", [(4096, 4096, 4096, 1), (4096, 4096, 4096, 3), (4096, 4096, 4096, 8),
                                         (1000, 2048, 4096, 2), (512, 512, 4096, 5), (768, 1536, 1000, 4),
-                                        (2048, 1024, 256, 7)])
+                                        (2048, 1024, 256, 7), (37888, 512, 4096, 2)])
 def test_lut8_matches_oracle_bf16(OUT, IN, K, n):
     """C1's matvec at one, three and eight rows; a ragged last row block; one
-    window per row (no split); 10-bit and 8-bit codebooks."""
+    window per row (no split); 10-bit and 8-bit codebooks; 37888 rows of one
+    window, where 256-row CTAs (148 of them) tie 128-row ones and are taken,
+    while the other shapes take 128-row CTAs."""
     L = make_layer(E=1, OUT=OUT, IN=IN, D=8, K=K, G=64, seed=OUT + IN + K + n)
     lin = _lin(L)
     xb = _x(np.random.default_rng(n + 3), n, IN, torch.bfloat16)

@@ -39,6 +39,10 @@
 // long before any wait could expire).
 #include <cuda.h>
 
+#include <map>
+#include <mutex>
+#include <tuple>
+
 #include "vqb_common.cuh"
 #include "vqb_internal.h"
 #include "vqb_tma.cuh"
@@ -417,10 +421,12 @@ __device__ __forceinline__ void l8_mma(float (&d)[4], const uint32_t (&a)[4], ui
         : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
 }
 
-// One staged window for one warp: rows 16 warp + g and + 8, tokens 2t, 2t + 1.
-template <bool XBF16>
+// One staged window for one warp: rows 16 wt + g and + 8, tokens 2t, 2t + 1,
+// scale groups qlo .. qlo + NQ - 1 of the window.
+template <bool XBF16, int NQ>
 __device__ __forceinline__ void l8_window(const unsigned char* table, const unsigned char* sb, const L8Params& p,
-                                          int warp, int g, int t, bool has_x, float (&acc)[4]) {
+                                          int wt, int qlo, int g, int t, bool has_x, float (&acc)[4]) {
+  const int warp = wt;
   const int bits = p.bits;
   const uint32_t mask = (1u << bits) - 1u;
   const int rw = 2 * bits;  // code words per row
@@ -432,7 +438,8 @@ __device__ __forceinline__ void l8_window(const unsigned char* table, const unsi
   const unsigned char* xb = sb + kL8XOff(bits) + g * kLtXStride + 32 * t;
   const int tb = 2 * t * bits;  // bit offset of code 2t inside a group's 8 codes
 #pragma unroll
-  for (int q = 0; q < 8; ++q) {
+  for (int qi = 0; qi < NQ; ++qi) {
+    const int q = qlo + qi;
     const int b0 = 8 * q * bits + tb;
     const int wi = b0 >> 5, sh = b0 & 31;
     const uint32_t v0 = __funnelshift_r(crow0[wi], crow0[wi + 1], sh);
@@ -470,9 +477,14 @@ __device__ __forceinline__ void l8_window(const unsigned char* table, const unsi
   }
 }
 
-template <bool XBF16>
+// KQ = 1: 256 rows per CTA, warp w owns tile w and all 8 groups of a window.
+// KQ = 2: 128 rows per CTA (twice the CTAs for the same work); warps w and
+// w + 8 share tile w % 8 and take groups 0-3 and 4-7, their fp32 partials
+// added in that order before the store.
+template <bool XBF16, int KQ>
 __global__ void __launch_bounds__(kLtThreads, 1) dense_lut8_kernel(const __grid_constant__ LtMaps maps,
                                                                    const __grid_constant__ L8Params p) {
+  constexpr int kRows = kLtRows / KQ, kTiles = kLtWarps / KQ;
   extern __shared__ __align__(16) unsigned char smem[];
   // [table (K + 1 entries)][recv][pad to 1024][stages][barriers]
   float* recv = reinterpret_cast<float*>(smem + p.table_bytes);
@@ -500,8 +512,8 @@ __global__ void __launch_bounds__(kLtThreads, 1) dense_lut8_kernel(const __grid_
     // this CTA's windows into L2 while the previous kernel finishes (a
     // prefetch returns no data, so it cannot observe a stale value)
     for (int w = w0; w < w1; ++w) {
-      lt_prefetch_2d(&maps.codes, w * rw, rb * kLtRows);
-      lt_prefetch_2d(&maps.scales, w * 8, rb * kLtRows);
+      lt_prefetch_2d(&maps.codes, w * rw, rb * kRows);
+      lt_prefetch_2d(&maps.scales, w * 8, rb * kRows);
     }
     // the zero entry at index K
     *reinterpret_cast<uint4*>(smem + static_cast<uint32_t>(p.K) * 16u) = make_uint4(0u, 0u, 0u, 0u);
@@ -522,14 +534,14 @@ __global__ void __launch_bounds__(kLtThreads, 1) dense_lut8_kernel(const __grid_
   pdl_wait();
   pdl_trigger();
   const unsigned char* xg = static_cast<const unsigned char*>(p.x);
-  const uint32_t tx = static_cast<uint32_t>(kLtRows) * 8u * static_cast<uint32_t>(p.bits) + 16u * kLtRows +
+  const uint32_t tx = static_cast<uint32_t>(kRows) * 8u * static_cast<uint32_t>(p.bits) + 16u * kRows +
                       static_cast<uint32_t>(p.T) * kLtWinK * 2u;
   auto issue = [&](int n) {
     unsigned char* sb = stages + (n & 1) * p.stage_bytes;
     const int w = w0 + n;
     mbar_expect_tx(&full[n & 1], tx);
-    tma_load_2d(&maps.codes, &full[n & 1], sb, w * rw, rb * kLtRows);
-    tma_load_2d(&maps.scales, &full[n & 1], sb + kL8ScaleOff(p.bits), w * 8, rb * kLtRows);
+    tma_load_2d(&maps.codes, &full[n & 1], sb, w * rw, rb * kRows);
+    tma_load_2d(&maps.scales, &full[n & 1], sb + kL8ScaleOff(p.bits), w * 8, rb * kRows);
     for (int j = 0; j < p.T; ++j)
       bulk_load(sb + kL8XOff(p.bits) + j * kLtXStride,
                 xg + (static_cast<size_t>(j) * p.IN + static_cast<size_t>(w) * kLtWinK) * 2, kLtWinK * 2, &full[n & 1]);
@@ -549,12 +561,13 @@ __global__ void __launch_bounds__(kLtThreads, 1) dense_lut8_kernel(const __grid_
 
   float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
   const int g = lane >> 2, t = lane & 3;
+  const int wt = warp % kTiles, kq = warp / kTiles;  // MMA tile, group share
   bool alive = warp_wait(tbar, 0, abort_flag);
   for (int n = 0; n < nwin; ++n) {
     const int st = n & 1;
     const unsigned char* sb = stages + st * p.stage_bytes;
     if (alive) alive = warp_wait(&full[st], (n >> 1) & 1, abort_flag);
-    if (alive) l8_window<XBF16>(smem, sb, p, warp, g, t, g < p.T, acc);
+    if (alive) l8_window<XBF16, 8 / KQ>(smem, sb, p, wt, kq * (8 / KQ), g, t, g < p.T, acc);
     __syncwarp();
     if (lane == 0) mbar_arrive(&empty[st]);
     if (tid == 0 && n + kLtStages < nwin && !*abort_flag) {
@@ -564,8 +577,21 @@ __global__ void __launch_bounds__(kLtThreads, 1) dense_lut8_kernel(const __grid_
       }
     }
   }
-  if (p.S == 1) {
-    const int row0 = rb * kLtRows + warp * 16 + g;
+  if constexpr (KQ == 2) {
+    // every warp is past its last window: stage 0's first 4 KB holds the
+    // second group share's partials, added after the first's
+    __syncthreads();
+    float* red = reinterpret_cast<float*>(stages);
+    if (kq == 1)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) red[(wt * 32 + lane) * 4 + e] = acc[e];
+    __syncthreads();
+    if (kq == 0)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) acc[e] = acc[e] + red[(wt * 32 + lane) * 4 + e];
+  }
+  if (p.S == 1 && kq == 0) {
+    const int row0 = rb * kRows + wt * 16 + g;
 #pragma unroll
     for (int e = 0; e < 4; ++e) {
       const int row = row0 + 8 * (e >> 1), tok = 2 * t + (e & 1);
@@ -581,22 +607,22 @@ __global__ void __launch_bounds__(kLtThreads, 1) dense_lut8_kernel(const __grid_
   }
   if (p.S == 1) return;
   // ---- split-K over the cluster: the owner of local row lr is rank lr / R
-  const int R = (kLtRows + p.S - 1) / p.S;
+  const int R = (kRows + p.S - 1) / p.S;
   lt_cluster_wait();
 #pragma unroll
   for (int e = 0; e < 4; ++e) {
-    const int lr = warp * 16 + 8 * (e >> 1) + g, tok = 2 * t + (e & 1);
-    if (tok < p.T) {
+    const int lr = wt * 16 + 8 * (e >> 1) + g, tok = 2 * t + (e & 1);
+    if (kq == 0 && tok < p.T) {
       const int owner = lr / R;
       lt_st_cluster(smem_u32(recv + (split * kLtTok + tok) * R + (lr - owner * R)), static_cast<uint32_t>(owner),
                     acc[e]);
     }
   }
   lt_cluster_sync();
-  const int r0 = split * R, nr = (r0 + R < kLtRows ? R : kLtRows - r0);
+  const int r0 = split * R, nr = (r0 + R < kRows ? R : kRows - r0);
   for (int k = tid; k < p.T * nr; k += kLtThreads) {
     const int tok = k / nr, r = k - tok * nr;
-    const int row = rb * kLtRows + r0 + r;
+    const int row = rb * kRows + r0 + r;
     if (row < p.OUT) {
       float sum = 0.0f;
       for (int q = 0; q < p.S; ++q) sum += recv[(q * kLtTok + tok) * R + r];
@@ -620,39 +646,41 @@ bool dense_lut_eligible(const LinearGeometry& g, const void* x, int x_dtype, int
          a16(g.codes) && a16(g.scales) && (reinterpret_cast<uintptr_t>(g.codebook) & 3) == 0;
 }
 
-// Clusters of S CTAs that fit on the device at once (cached per device and
-// S); 0 when the query fails, and that cluster size is not used.
-static int lt_cluster_capacity(void (*kern)(LtMaps, LtParams), int S, int sms) {
-  static int cache[16][kLtMaxSplit + 1];
-  static bool init = false;
-  if (!init) {
-    for (auto& r : cache)
-      for (int& v : r) v = -1;
-    init = true;
-  }
+// Clusters of S CTAs (kLtThreads threads and `smem` bytes each) that fit on
+// the current device at once; 0 when the query fails, and that cluster size
+// is not used.  Answers are cached per (device, kernel, S, smem) under a lock,
+// so a call costs one map lookup after the first.
+template <typename... KArgs>
+static int lt_cluster_capacity(void (*kern)(KArgs...), int S, uint32_t smem, int sms) {
+  static std::mutex mu;
+  static std::map<std::tuple<int, const void*, int, uint32_t>, int> cache;
   int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 16) return 0;
-  int& c = cache[dev][S];
-  if (c < 0) {
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(static_cast<unsigned>(S * sms));
-    cfg.blockDim = dim3(kLtThreads);
-    cfg.dynamicSmemBytes = kLtSmem;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeClusterDimension;
-    attr[0].val.clusterDim.x = static_cast<unsigned>(S);
-    attr[0].val.clusterDim.y = 1;
-    attr[0].val.clusterDim.z = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
-    int n = 0;
-    if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess || n <= 0) {
-      cudaGetLastError();
-      n = 0;
-    }
-    c = n;
+  if (cudaGetDevice(&dev) != cudaSuccess) return 0;
+  const auto key = std::make_tuple(dev, reinterpret_cast<const void*>(kern), S, smem);
+  {
+    std::lock_guard<std::mutex> lock(mu);
+    const auto it = cache.find(key);
+    if (it != cache.end()) return it->second;
   }
-  return c;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(S * sms));
+  cfg.blockDim = dim3(kLtThreads);
+  cfg.dynamicSmemBytes = smem;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = static_cast<unsigned>(S);
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  int n = 0;
+  if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess || n <= 0) {
+    cudaGetLastError();
+    n = 0;
+  }
+  std::lock_guard<std::mutex> lock(mu);
+  cache[key] = n;
+  return n;
 }
 
 vqb_status launch_dense_lut(const LinearGeometry& g, const void* x, int x_dtype, int T, void* y, int y_dtype,
@@ -690,7 +718,7 @@ vqb_status launch_dense_lut(const LinearGeometry& g, const void* x, int x_dtype,
   int best = 1;
   int64_t best_cost = INT64_MAX;
   for (int S = 1; S <= smax; ++S) {
-    const int cap = S == 1 ? di.sms : lt_cluster_capacity(kern, S, di.sms);
+    const int cap = S == 1 ? di.sms : lt_cluster_capacity(kern, S, kLtSmem, di.sms);
     if (cap <= 0) continue;
     const int64_t waves = (nrb + cap - 1) / cap;
     const int64_t cost = waves * ((p.nw + S - 1) / S);
@@ -739,12 +767,6 @@ vqb_status launch_dense_lut8(const LinearGeometry& g, const void* x, int x_dtype
   if (device_info(&di) != VQB_OK) return VQB_CUDA_ERROR;
   EncodeTiledFn enc = encode_fn();
   if (!enc) return VQB_CUDA_ERROR;
-  LtMaps maps;
-  if (!encode_2d(enc, &maps.codes, CU_TENSOR_MAP_DATA_TYPE_UINT32, 4, g.codes, static_cast<uint64_t>(g.row_words),
-                 static_cast<uint64_t>(g.OUT), static_cast<uint32_t>(2 * g.bits), kLtRows, CU_TENSOR_MAP_SWIZZLE_NONE) ||
-      !encode_2d(enc, &maps.scales, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, g.scales, static_cast<uint64_t>(g.IN / 64),
-                 static_cast<uint64_t>(g.OUT), kLtWinK / 64, kLtRows, CU_TENSOR_MAP_SWIZZLE_NONE))
-    return VQB_CUDA_ERROR;
   L8Params p{};
   p.codebook = static_cast<const uint4*>(g.codebook);
   p.K = g.K;
@@ -761,56 +783,60 @@ vqb_status launch_dense_lut8(const LinearGeometry& g, const void* x, int x_dtype
   p.stage_bytes = kL8StageBytes(g.bits);
   const uint32_t smem = p.table_bytes + kL8RecvBytes + 1024u + kLtStages * p.stage_bytes + 64u;
   if (smem > static_cast<uint32_t>(di.smem_optin)) return VQB_UNSUPPORTED_GEOMETRY;
-  void (*kern)(LtMaps, L8Params) = x_dtype == VQB_BF16 ? dense_lut8_kernel<true> : dense_lut8_kernel<false>;
-  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)) != cudaSuccess)
-    return VQB_CUDA_ERROR;
-  const int nrb = (g.OUT + kLtRows - 1) / kLtRows;
+  using Kern = void (*)(LtMaps, L8Params);
+  const bool bf = x_dtype == VQB_BF16;
+  const Kern kerns[2] = {bf ? dense_lut8_kernel<true, 1> : dense_lut8_kernel<false, 1>,
+                         bf ? dense_lut8_kernel<true, 2> : dense_lut8_kernel<false, 2>};
+  for (Kern k : kerns)
+    if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)) != cudaSuccess)
+      return VQB_CUDA_ERROR;
+  // rows per CTA (256, or 128 with the window's groups split over warp
+  // pairs) and CTAs per row block: the smallest (waves of clusters) x
+  // (windows per CTA) x (rows per CTA), the first found among equals -- C1:
+  // 32 row blocks of 128 x 4 splits, 128 CTAs in one wave
   const int smax = p.nw < kLtMaxSplit ? p.nw : kLtMaxSplit;
-  int best = 1;
+  int best_kq = 1, best_s = 1;
   int64_t best_cost = INT64_MAX;
-  for (int S = 1; S <= smax; ++S) {
-    int cap = di.sms;
-    if (S > 1) {
-      cudaLaunchConfig_t cfg = {};
-      cfg.gridDim = dim3(static_cast<unsigned>(S * di.sms));
-      cfg.blockDim = dim3(kLtThreads);
-      cfg.dynamicSmemBytes = smem;
-      cudaLaunchAttribute attr[1];
-      attr[0].id = cudaLaunchAttributeClusterDimension;
-      attr[0].val.clusterDim.x = static_cast<unsigned>(S);
-      attr[0].val.clusterDim.y = 1;
-      attr[0].val.clusterDim.z = 1;
-      cfg.attrs = attr;
-      cfg.numAttrs = 1;
-      if (cudaOccupancyMaxActiveClusters(&cap, kern, &cfg) != cudaSuccess) {
-        cudaGetLastError();
-        cap = 0;
+  for (int kq = 1; kq <= 2; ++kq) {
+    const int rows = kLtRows / kq;
+    const int nrb = (g.OUT + rows - 1) / rows;
+    for (int S = 1; S <= smax; ++S) {
+      const int cap = S == 1 ? di.sms : lt_cluster_capacity(kerns[kq - 1], S, smem, di.sms);
+      if (cap <= 0) continue;
+      const int64_t cost = ((nrb + cap - 1) / cap) * static_cast<int64_t>((p.nw + S - 1) / S) * rows;
+      if (cost < best_cost) {
+        best_cost = cost;
+        best_kq = kq;
+        best_s = S;
       }
     }
-    if (cap <= 0) continue;
-    const int64_t cost = ((nrb + cap - 1) / cap) * ((p.nw + S - 1) / S);
-    if (cost < best_cost) {
-      best_cost = cost;
-      best = S;
-    }
   }
-  p.S = best;
+  p.S = best_s;
+  const int rows = kLtRows / best_kq;
+  const int nrb = (g.OUT + rows - 1) / rows;
+  LtMaps maps;
+  if (!encode_2d(enc, &maps.codes, CU_TENSOR_MAP_DATA_TYPE_UINT32, 4, g.codes, static_cast<uint64_t>(g.row_words),
+                 static_cast<uint64_t>(g.OUT), static_cast<uint32_t>(2 * g.bits), static_cast<uint32_t>(rows),
+                 CU_TENSOR_MAP_SWIZZLE_NONE) ||
+      !encode_2d(enc, &maps.scales, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, g.scales, static_cast<uint64_t>(g.IN / 64),
+                 static_cast<uint64_t>(g.OUT), kLtWinK / 64, static_cast<uint32_t>(rows), CU_TENSOR_MAP_SWIZZLE_NONE))
+    return VQB_CUDA_ERROR;
   cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   attr[1].id = cudaLaunchAttributeClusterDimension;
-  attr[1].val.clusterDim.x = static_cast<unsigned>(best);
+  attr[1].val.clusterDim.x = static_cast<unsigned>(best_s);
   attr[1].val.clusterDim.y = 1;
   attr[1].val.clusterDim.z = 1;
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(static_cast<unsigned>(nrb * best));
+  cfg.gridDim = dim3(static_cast<unsigned>(nrb * best_s));
   cfg.blockDim = dim3(kLtThreads);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = stream;
   cfg.attrs = attr;
-  cfg.numAttrs = best > 1 ? 2 : 1;
+  cfg.numAttrs = best_s > 1 ? 2 : 1;
   timer_before(stream);
-  const cudaError_t ce = cudaLaunchKernelEx(&cfg, kern, maps, p);
+  const cudaError_t ce = cudaLaunchKernelEx(&cfg, kerns[best_kq - 1], maps, p);
   timer_after(stream);
   if (ce != cudaSuccess) return VQB_CUDA_ERROR;
   note_launch();
