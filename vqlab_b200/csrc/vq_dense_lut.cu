@@ -129,12 +129,14 @@ __device__ __forceinline__ void lt_st_cluster(uint32_t local_smem, uint32_t rank
 }
 
 // One staged window for one warp: rows kLtWarpRows * warp + 8 * r + g (MMA
-// tile j holds r = 2j and 2j + 1), tokens 2t and 2t + 1 of each tile.  Lanes
-// of tokens >= T read no x (their B values are zero).
+// tile j holds r = 2j and 2j + 1), tokens 2t and 2t + 1 of each tile, scale
+// groups qlo .. qlo + NQ - 1 (qlo 0 or 4).  Lanes of tokens >= T read no x
+// (their B values are zero).
 //   off[qq]: swizzled byte offset of this thread's 8 codes of group 4h + qq
 //   inside a 128-byte box row (chunk (2qq + t/2) ^ g, half t & 1).
-__device__ __forceinline__ void lt_window(const unsigned char* table, const unsigned char* sb, int warp, int g, int t,
-                                          uint32_t lane4, const uint32_t (&off)[4], bool has_x,
+template <int NQ>
+__device__ __forceinline__ void lt_window(const unsigned char* table, const unsigned char* sb, int warp, int qlo, int g,
+                                          int t, uint32_t lane4, const uint32_t (&off)[4], bool has_x,
                                           float (&acc)[kLtTiles][4]) {
   const unsigned char* cbase = sb + (warp * kLtWarpRows + g) * 128;
   const unsigned char* xb = sb + kLtXOff + g * kLtXStride + 32 * t;
@@ -143,8 +145,9 @@ __device__ __forceinline__ void lt_window(const unsigned char* table, const unsi
 #pragma unroll
   for (int r = 0; r < 2 * kLtTiles; ++r) sc[r] = *reinterpret_cast<const uint4*>(sbase + r * 8 * 16);
 #pragma unroll
-  for (int q = 0; q < 8; ++q) {
-    const int h = q >> 2, qq = q & 3;
+  for (int qi = 0; qi < NQ; ++qi) {
+    const int q = qlo + qi;            // qlo is 0 or 4: q & 3 == qi & 3
+    const int h = q >> 2, qq = qi & 3;
     uint2 cw[2 * kLtTiles];
 #pragma unroll
     for (int r = 0; r < 2 * kLtTiles; ++r)
@@ -195,20 +198,25 @@ __device__ __forceinline__ void lt_window(const unsigned char* table, const unsi
 // Thread 0: the copies of window w into stage st (codes: two swizzled boxes;
 // scales; the tokens' x rows).
 __device__ __forceinline__ void lt_issue(const LtMaps& maps, const LtParams& p, unsigned char* sb, uint64_t* bar,
-                                         int w, int rb) {
+                                         int w, int rb, int rows) {
   const unsigned char* xg = static_cast<const unsigned char*>(p.x);
-  mbar_expect_tx(bar, 2 * kLtHalfBox + 16 * kLtRows + static_cast<uint32_t>(p.T) * kLtWinK * 2);
-  tma_load_2d(&maps.codes, bar, sb, w * 64, rb * kLtRows);
-  tma_load_2d(&maps.codes, bar, sb + kLtHalfBox, w * 64 + 32, rb * kLtRows);
-  tma_load_2d(&maps.scales, bar, sb + kLtScaleOff, w * 8, rb * kLtRows);
+  mbar_expect_tx(bar, 2u * 128u * rows + 16u * rows + static_cast<uint32_t>(p.T) * kLtWinK * 2);
+  tma_load_2d(&maps.codes, bar, sb, w * 64, rb * rows);
+  tma_load_2d(&maps.codes, bar, sb + kLtHalfBox, w * 64 + 32, rb * rows);
+  tma_load_2d(&maps.scales, bar, sb + kLtScaleOff, w * 8, rb * rows);
   for (int j = 0; j < p.T; ++j)
     bulk_load(sb + kLtXOff + j * kLtXStride, xg + (static_cast<size_t>(j) * p.IN + static_cast<size_t>(w) * kLtWinK) * 2,
               kLtWinK * 2, bar);
 }
 
-template <bool XBF16>
+// KQ = 1: 256 rows per CTA, warp w owns tile w and all 8 groups of a window.
+// KQ = 2: 128 rows per CTA; warps w and w + 8 share tile w % 8 and take
+// groups 0-3 (code box 0) and 4-7 (code box 1), their fp32 partials added in
+// that order before the store.
+template <bool XBF16, int KQ>
 __global__ void __launch_bounds__(kLtThreads, 1) dense_lut_kernel(const __grid_constant__ LtMaps maps,
                                                                   const __grid_constant__ LtParams p) {
+  constexpr int kRows = kLtRows / KQ, kTiles = kLtWarps / KQ;
   extern __shared__ __align__(16) unsigned char smem[];
   unsigned char* stages = smem + kLtTable + ((1024u - ((smem_u32(smem) + kLtTable) & 1023u)) & 1023u);
   uint64_t* full = reinterpret_cast<uint64_t*>(stages + kLtBarOff);
@@ -233,9 +241,9 @@ __global__ void __launch_bounds__(kLtThreads, 1) dense_lut_kernel(const __grid_c
     for (int b = 0; b < p.K * 4; b += 128)
       asm volatile("prefetch.global.L2 [%0];" :: "l"(reinterpret_cast<const char*>(p.codebook) + b));
     for (int w = w0; w < w1; ++w) {
-      lt_prefetch_2d(&maps.codes, w * 64, rb * kLtRows);
-      lt_prefetch_2d(&maps.codes, w * 64 + 32, rb * kLtRows);
-      lt_prefetch_2d(&maps.scales, w * 8, rb * kLtRows);
+      lt_prefetch_2d(&maps.codes, w * 64, rb * kRows);
+      lt_prefetch_2d(&maps.codes, w * 64 + 32, rb * kRows);
+      lt_prefetch_2d(&maps.scales, w * 8, rb * kRows);
     }
   }
   // tokens T..7 read zeros: their x rows are never copied
@@ -254,7 +262,7 @@ __global__ void __launch_bounds__(kLtThreads, 1) dense_lut_kernel(const __grid_c
   pdl_trigger();
   if (tid == 0) {
     if (blockIdx.x == 0) p.status[1] = 0;
-    for (int n = 0; n < kLtStages && n < nwin; ++n) lt_issue(maps, p, stages + n * kLtStageBytes, &full[n], w0 + n, rb);
+    for (int n = 0; n < kLtStages && n < nwin; ++n) lt_issue(maps, p, stages + n * kLtStageBytes, &full[n], w0 + n, rb, kRows);
     sflags[1] = nwin < kLtStages ? nwin : kLtStages;
   }
   // the replicated codebook: entry e for lane l at byte e * 256 + 4 l; codes >= K read zeros.
@@ -275,6 +283,7 @@ __global__ void __launch_bounds__(kLtThreads, 1) dense_lut_kernel(const __grid_c
 #pragma unroll
   for (int j = 0; j < kLtTiles; ++j) acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0.0f;
   const int g = lane >> 2, t = lane & 3;
+  const int wt = warp % kTiles, kq = warp / kTiles;  // MMA tile, group share
   const uint32_t lane4 = static_cast<uint32_t>(lane) * 4u;
   uint32_t off[4];
 #pragma unroll
@@ -299,7 +308,7 @@ __global__ void __launch_bounds__(kLtThreads, 1) dense_lut_kernel(const __grid_c
       }
       __syncthreads();
     }
-    if (alive) lt_window(smem, sb, warp, g, t, lane4, off, g < p.T, acc);
+    if (alive) lt_window<8 / KQ>(smem, sb, wt, kq * (8 / KQ), g, t, lane4, off, g < p.T, acc);
     // the in-place narrowing's writes before the next copy into this stage
     if (XBF16) asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
     __syncwarp();
@@ -307,14 +316,27 @@ __global__ void __launch_bounds__(kLtThreads, 1) dense_lut_kernel(const __grid_c
     if (tid == 0 && n + kLtStages < nwin && !*abort_flag) {
       // refill this stage once every warp has released it
       if (mbar_wait(&empty[st], (n >> 1) & 1, abort_flag)) {
-        lt_issue(maps, p, sb, &full[st], w0 + n + kLtStages, rb);
+        lt_issue(maps, p, sb, &full[st], w0 + n + kLtStages, rb, kRows);
         sflags[1] = n + kLtStages + 1;
       }
     }
   }
-  if (p.S == 1) {
-    // rows kLtWarpRows warp + 16 j + g (+ 8), tokens 2t, 2t + 1
-    const int row0 = rb * kLtRows + warp * kLtWarpRows + g;
+  if constexpr (KQ == 2) {
+    // every warp is past its last window: stage 0's first 4 KB holds the
+    // second group share's partials, added after the first's
+    __syncthreads();
+    float* red = reinterpret_cast<float*>(stages);
+    if (kq == 1)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) red[(wt * 32 + lane) * 4 + e] = acc[0][e];
+    __syncthreads();
+    if (kq == 0)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) acc[0][e] = acc[0][e] + red[(wt * 32 + lane) * 4 + e];
+  }
+  if (p.S == 1 && kq == 0) {
+    // rows kLtWarpRows wt + 16 j + g (+ 8), tokens 2t, 2t + 1
+    const int row0 = rb * kRows + wt * kLtWarpRows + g;
 #pragma unroll
     for (int j = 0; j < kLtTiles; ++j)
 #pragma unroll
@@ -333,14 +355,14 @@ __global__ void __launch_bounds__(kLtThreads, 1) dense_lut_kernel(const __grid_c
   }
   if (p.S == 1) return;
   // ---- split-K over the cluster: the owner of local row lr is rank lr / R
-  const int R = (kLtRows + p.S - 1) / p.S;
+  const int R = (kRows + p.S - 1) / p.S;
   lt_cluster_wait();  // every peer has started: its shared memory may be written
 #pragma unroll
   for (int j = 0; j < kLtTiles; ++j)
 #pragma unroll
     for (int e = 0; e < 4; ++e) {
-      const int lr = warp * kLtWarpRows + 16 * j + 8 * (e >> 1) + g, tok = 2 * t + (e & 1);
-      if (tok < p.T) {
+      const int lr = wt * kLtWarpRows + 16 * j + 8 * (e >> 1) + g, tok = 2 * t + (e & 1);
+      if (kq == 0 && tok < p.T) {
         const int owner = lr / R;
         lt_st_cluster(smem_u32(smem) + lt_recv_off((split * kLtTok + tok) * R + (lr - owner * R)),
                       static_cast<uint32_t>(owner), acc[j][e]);
@@ -348,10 +370,10 @@ __global__ void __launch_bounds__(kLtThreads, 1) dense_lut_kernel(const __grid_c
     }
   lt_cluster_sync();
   // this rank's rows, summed over the S partials in split order
-  const int r0 = split * R, nr = (r0 + R < kLtRows ? R : kLtRows - r0);
+  const int r0 = split * R, nr = (r0 + R < kRows ? R : kRows - r0);
   for (int k = tid; k < p.T * nr; k += kLtThreads) {
     const int tok = k / nr, r = k - tok * nr;
-    const int row = rb * kLtRows + r0 + r;
+    const int row = rb * kRows + r0 + r;
     if (row < p.OUT) {
       float sum = 0.0f;
       for (int q = 0; q < p.S; ++q)
@@ -689,16 +711,14 @@ vqb_status launch_dense_lut(const LinearGeometry& g, const void* x, int x_dtype,
   if (device_info(&di) != VQB_OK) return VQB_CUDA_ERROR;
   EncodeTiledFn enc = encode_fn();
   if (!enc) return VQB_CUDA_ERROR;
-  LtMaps maps;
-  if (!encode_2d(enc, &maps.codes, CU_TENSOR_MAP_DATA_TYPE_UINT32, 4, g.codes, static_cast<uint64_t>(g.row_words),
-                 static_cast<uint64_t>(g.OUT), 32, kLtRows, CU_TENSOR_MAP_SWIZZLE_128B) ||
-      !encode_2d(enc, &maps.scales, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, g.scales, static_cast<uint64_t>(g.IN / 64),
-                 static_cast<uint64_t>(g.OUT), kLtWinK / 64, kLtRows, CU_TENSOR_MAP_SWIZZLE_NONE))
-    return VQB_CUDA_ERROR;
-  void (*kern)(LtMaps, LtParams) = x_dtype == VQB_BF16 ? dense_lut_kernel<true> : dense_lut_kernel<false>;
-  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kLtSmem)) !=
-      cudaSuccess)
-    return VQB_CUDA_ERROR;
+  using Kern = void (*)(LtMaps, LtParams);
+  const bool bf = x_dtype == VQB_BF16;
+  const Kern kerns[2] = {bf ? dense_lut_kernel<true, 1> : dense_lut_kernel<false, 1>,
+                         bf ? dense_lut_kernel<true, 2> : dense_lut_kernel<false, 2>};
+  for (Kern k : kerns)
+    if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kLtSmem)) !=
+        cudaSuccess)
+      return VQB_CUDA_ERROR;
   LtParams p{};
   p.codebook = static_cast<const uint32_t*>(g.codebook);
   p.K = g.K;
@@ -710,41 +730,53 @@ vqb_status launch_dense_lut(const LinearGeometry& g, const void* x, int x_dtype,
   p.IN = g.IN;
   p.nw = g.IN / kLtWinK;
   p.status = status;
-  const int nrb = (g.OUT + kLtRows - 1) / kLtRows;
-  // CTAs per row block: the fewest that reach the smallest (waves of
-  // clusters) x (windows per CTA); e.g. 5120 x 5120: 20 row blocks x 5
-  // splits of 2 windows in one wave
+  // rows per CTA (256, or 128 with the window's groups split over warp pairs)
+  // and CTAs per row block: the smallest (waves of clusters) x (windows per
+  // CTA) x (rows per CTA), the first found among equals -- 5120 x 5120: 20
+  // row blocks of 256 x 5 splits of 2 windows; 1024 x 5120: 8 row blocks of
+  // 128 x 5 splits
   const int smax = p.nw < kLtMaxSplit ? p.nw : kLtMaxSplit;
-  int best = 1;
+  int best_kq = 1, best_s = 1;
   int64_t best_cost = INT64_MAX;
-  for (int S = 1; S <= smax; ++S) {
-    const int cap = S == 1 ? di.sms : lt_cluster_capacity(kern, S, kLtSmem, di.sms);
-    if (cap <= 0) continue;
-    const int64_t waves = (nrb + cap - 1) / cap;
-    const int64_t cost = waves * ((p.nw + S - 1) / S);
-    if (cost < best_cost) {
-      best_cost = cost;
-      best = S;
+  for (int kq = 1; kq <= 2; ++kq) {
+    const int rows = kLtRows / kq;
+    const int nrb = (g.OUT + rows - 1) / rows;
+    for (int S = 1; S <= smax; ++S) {
+      const int cap = S == 1 ? di.sms : lt_cluster_capacity(kerns[kq - 1], S, kLtSmem, di.sms);
+      if (cap <= 0) continue;
+      const int64_t cost = ((nrb + cap - 1) / cap) * static_cast<int64_t>((p.nw + S - 1) / S) * rows;
+      if (cost < best_cost) {
+        best_cost = cost;
+        best_kq = kq;
+        best_s = S;
+      }
     }
   }
-  p.S = best;
-
+  p.S = best_s;
+  const int rows = kLtRows / best_kq;
+  const int nrb = (g.OUT + rows - 1) / rows;
+  LtMaps maps;
+  if (!encode_2d(enc, &maps.codes, CU_TENSOR_MAP_DATA_TYPE_UINT32, 4, g.codes, static_cast<uint64_t>(g.row_words),
+                 static_cast<uint64_t>(g.OUT), 32, static_cast<uint32_t>(rows), CU_TENSOR_MAP_SWIZZLE_128B) ||
+      !encode_2d(enc, &maps.scales, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, g.scales, static_cast<uint64_t>(g.IN / 64),
+                 static_cast<uint64_t>(g.OUT), kLtWinK / 64, static_cast<uint32_t>(rows), CU_TENSOR_MAP_SWIZZLE_NONE))
+    return VQB_CUDA_ERROR;
   cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   attr[1].id = cudaLaunchAttributeClusterDimension;
-  attr[1].val.clusterDim.x = static_cast<unsigned>(best);
+  attr[1].val.clusterDim.x = static_cast<unsigned>(best_s);
   attr[1].val.clusterDim.y = 1;
   attr[1].val.clusterDim.z = 1;
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(static_cast<unsigned>(nrb * best));
+  cfg.gridDim = dim3(static_cast<unsigned>(nrb * best_s));
   cfg.blockDim = dim3(kLtThreads);
   cfg.dynamicSmemBytes = kLtSmem;
   cfg.stream = stream;
   cfg.attrs = attr;
-  cfg.numAttrs = best > 1 ? 2 : 1;
+  cfg.numAttrs = best_s > 1 ? 2 : 1;
   timer_before(stream);
-  const cudaError_t ce = cudaLaunchKernelEx(&cfg, kern, maps, p);
+  const cudaError_t ce = cudaLaunchKernelEx(&cfg, kerns[best_kq - 1], maps, p);
   timer_after(stream);
   if (ce != cudaSuccess) return VQB_CUDA_ERROR;
   note_launch();
