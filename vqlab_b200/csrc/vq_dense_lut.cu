@@ -6,17 +6,19 @@
 // partial sum of each 64-input scale group multiplied by the group's scale,
 // y stored once in the output dtype.
 //
-// One launch of 512-thread CTAs (16 warps of 16 output rows; thread 0 also
-// issues the copies), one CTA per SM at a time:
+// One launch of 512-thread CTAs (16 warps; thread 0 also issues the copies),
+// one CTA per SM at a time:
 //   * the codebook is replicated per lane in shared memory: entry e for lane l
 //     is the word at byte e * 256 + 4 * l, so the 32 lookups of a warp always
 //     hit 32 different banks, and one byte permute (the code byte next to
 //     4 * lane) forms the address;
-//   * a CTA takes 256 output rows and a range of 512-input windows (split s
-//     of S); each window's codes (256 bytes per row: two TMA boxes of 128
-//     bytes x 256 rows with the 128-byte swizzle), its scales (8 x 256 fp16)
-//     and the tokens' x rows (bulk copies) arrive in two stages, refilled
-//     once every warp has released the stage;
+//   * a CTA takes 256 output rows (or 128, warps w and w + 8 then sharing a
+//     16-row tile and taking a window's first and last four scale groups)
+//     and a range of 512-input windows (split s of S); each window's codes
+//     (256 bytes per row: two TMA boxes of 128 bytes x the CTA's rows with
+//     the 128-byte swizzle), its scales (8 fp16 per row) and the tokens' x
+//     rows (bulk copies) arrive in two stages, refilled once every warp has
+//     released the stage;
 //   * inside a scale group (32 codes of a row), thread t of a quad takes codes
 //     8t .. 8t+7 (one 8-byte read per row) and the inputs they cover (two
 //     16-byte reads of x): MMA step m uses codes 8t+2m and 8t+2m+1 as the A
